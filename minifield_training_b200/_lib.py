@@ -1,0 +1,109 @@
+"""ctypes binding of libmfb200.so (the C ABI declared in include/mfb200.h).
+
+The library is loaded from this package directory; if it is missing the import
+fails loudly (there is no CPU fallback). Nonzero statuses become exceptions:
+MFB_ERR_INVALID -> ValueError (the reference raises ValueError for shape and
+argument errors, e.g. src/minifield_training/kernels/attention.py:276-279),
+everything else -> RuntimeError.
+"""
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libmfb200.so")
+
+OK, ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_DEVICE = range(6)
+
+QUANT_KINDS = {
+    "int8-channel-absmax-v1": 0,
+    "int4-g128-absmax-v1": 1,
+    "ternary-g128-absmax-f16-v1": 2,
+    "nf4-g128-absmax-f16-v1": 3,
+}
+MASK_CAUSAL, MASK_PREFIX, MASK_PACKED, MASK_BIDIR, MASK_CACHED = range(5)
+EMPTY_UNIFORM, EMPTY_ZERO = 0, 1
+MAJOR_K, MAJOR_MN = 0, 1
+DTYPE_BF16, DTYPE_F32 = 0, 1
+
+P = ctypes.c_void_p
+I = ctypes.c_int
+F = ctypes.c_float
+SZ = ctypes.c_size_t
+IP = ctypes.POINTER(ctypes.c_int)
+
+# name -> (restype, argtypes); mirrors include/mfb200.h one to one.
+SIGNATURES = {
+    "mfb_last_error": (ctypes.c_char_p, []),
+    "mfb_version": (I, []),
+    "mfb_device_count": (I, [IP]),
+    "mfb_set_device": (I, [I]),
+    "mfb_device_sm_version": (I, [I, IP, IP]),
+    "mfb_malloc": (I, [ctypes.POINTER(P), SZ]),
+    "mfb_free": (I, [P]),
+    "mfb_host_alloc": (I, [ctypes.POINTER(P), SZ]),
+    "mfb_host_free": (I, [P]),
+    "mfb_memcpy_h2d": (I, [P, P, SZ, P]),
+    "mfb_memcpy_d2h": (I, [P, P, SZ, P]),
+    "mfb_memcpy_d2d": (I, [P, P, SZ, P]),
+    "mfb_memset": (I, [P, I, SZ, P]),
+    "mfb_stream_create": (I, [ctypes.POINTER(P)]),
+    "mfb_stream_destroy": (I, [P]),
+    "mfb_stream_sync": (I, [P]),
+    "mfb_device_sync": (I, []),
+    "mfb_event_create": (I, [ctypes.POINTER(P)]),
+    "mfb_event_destroy": (I, [P]),
+    "mfb_event_record": (I, [P, P]),
+    "mfb_event_elapsed_ms": (I, [P, P, ctypes.POINTER(F)]),
+    "mfb_fakequant": (I, [P, I, I, I, P, P, P, P, P, P]),
+    "mfb_attn_ids": (I, [I, P, P, P, P, P, I, I, I, I, IP, IP, IP, P]),
+    "mfb_attn_workspace_size": (SZ, [I, I, I, I, I, I]),
+    "mfb_attn_fwd": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, I, F, P, SZ, P]),
+    "mfb_attn_bwd": (I, [P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, I, F, P, SZ, P]),
+    "mfb_decode_workspace_size": (SZ, [I, I, I, I]),
+    "mfb_decode_attn": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, F, P, SZ, P]),
+    "mfb_gemm_bf16": (I, [P, I, I, P, I, I, P, I, I, I, I, I, F, P, P]),
+    "mfb_gemm_status": (I, [IP]),
+    "mfb_swiglu_fwd": (I, [P, P, I, I, P]),
+    "mfb_swiglu_bwd": (I, [P, P, P, I, I, P]),
+    "mfb_cast_f32_bf16": (I, [P, P, ctypes.c_longlong, P]),
+}
+
+_lib = None
+
+
+def lib():
+    """Load (once) and return the configured ctypes library."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is not built; run `python -m minifield_training_b200.build` "
+                "(the B200 path has no CPU fallback)"
+            )
+        handle = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def last_error() -> str:
+    msg = lib().mfb_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(status: int, what: str = "") -> None:
+    if status == OK:
+        return
+    msg = f"{what}: {last_error()}" if what else last_error()
+    if status == ERR_INVALID:
+        raise ValueError(msg)
+    raise RuntimeError(f"[mfb status {status}] {msg}")
+
+
+def call(name: str, *args):
+    """Call ``name`` and raise on a nonzero status."""
+    check(getattr(lib(), name)(*args), name)

@@ -1,0 +1,148 @@
+// Runtime helpers of the C ABI: error reporting, device memory, streams and
+// events. They let a host without its own device allocator (ctypes + NumPy,
+// or a JAX FFI shim in tests) drive the kernels.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "common.cuh"
+
+namespace mfb {
+
+static thread_local char g_last_error[512] = "";
+
+int set_error(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int cuda_error(cudaError_t err, const char* where) {
+  return set_error(MFB_ERR_CUDA, "%s: %s (%s)", where, cudaGetErrorString(err), cudaGetErrorName(err));
+}
+
+}  // namespace mfb
+
+extern "C" {
+
+const char* mfb_last_error(void) { return mfb::g_last_error; }
+
+int mfb_version(void) { return 1; }
+
+int mfb_device_count(int* count) {
+  MFB_CHECK_ARG(count != nullptr, "count is NULL");
+  MFB_CUDA_TRY(cudaGetDeviceCount(count));
+  return MFB_OK;
+}
+
+int mfb_set_device(int device) {
+  MFB_CUDA_TRY(cudaSetDevice(device));
+  return MFB_OK;
+}
+
+int mfb_device_sm_version(int device, int* major, int* minor) {
+  MFB_CHECK_ARG(major && minor, "NULL out-param");
+  MFB_CUDA_TRY(cudaDeviceGetAttribute(major, cudaDevAttrComputeCapabilityMajor, device));
+  MFB_CUDA_TRY(cudaDeviceGetAttribute(minor, cudaDevAttrComputeCapabilityMinor, device));
+  return MFB_OK;
+}
+
+int mfb_malloc(void** ptr, size_t bytes) {
+  MFB_CHECK_ARG(ptr != nullptr, "ptr is NULL");
+  *ptr = nullptr;
+  if (bytes == 0) return MFB_OK;
+  MFB_CUDA_TRY(cudaMalloc(ptr, bytes));
+  return MFB_OK;
+}
+
+int mfb_free(void* ptr) {
+  if (ptr) MFB_CUDA_TRY(cudaFree(ptr));
+  return MFB_OK;
+}
+
+int mfb_host_alloc(void** ptr, size_t bytes) {
+  MFB_CHECK_ARG(ptr != nullptr, "ptr is NULL");
+  *ptr = nullptr;
+  if (bytes == 0) return MFB_OK;
+  MFB_CUDA_TRY(cudaMallocHost(ptr, bytes));
+  return MFB_OK;
+}
+
+int mfb_host_free(void* ptr) {
+  if (ptr) MFB_CUDA_TRY(cudaFreeHost(ptr));
+  return MFB_OK;
+}
+
+int mfb_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return MFB_OK;
+  MFB_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, (cudaStream_t)stream));
+  return MFB_OK;
+}
+
+int mfb_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return MFB_OK;
+  MFB_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+  return MFB_OK;
+}
+
+int mfb_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return MFB_OK;
+  MFB_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, (cudaStream_t)stream));
+  return MFB_OK;
+}
+
+int mfb_memset(void* dst, int value, size_t bytes, void* stream) {
+  if (bytes == 0) return MFB_OK;
+  MFB_CUDA_TRY(cudaMemsetAsync(dst, value, bytes, (cudaStream_t)stream));
+  return MFB_OK;
+}
+
+int mfb_stream_create(void** stream) {
+  MFB_CHECK_ARG(stream != nullptr, "stream is NULL");
+  cudaStream_t s;
+  MFB_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  *stream = s;
+  return MFB_OK;
+}
+
+int mfb_stream_destroy(void* stream) {
+  if (stream) MFB_CUDA_TRY(cudaStreamDestroy((cudaStream_t)stream));
+  return MFB_OK;
+}
+
+int mfb_stream_sync(void* stream) {
+  MFB_CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));
+  return MFB_OK;
+}
+
+int mfb_device_sync(void) {
+  MFB_CUDA_TRY(cudaDeviceSynchronize());
+  return MFB_OK;
+}
+
+int mfb_event_create(void** event) {
+  MFB_CHECK_ARG(event != nullptr, "event is NULL");
+  cudaEvent_t e;
+  MFB_CUDA_TRY(cudaEventCreate(&e));
+  *event = e;
+  return MFB_OK;
+}
+
+int mfb_event_destroy(void* event) {
+  if (event) MFB_CUDA_TRY(cudaEventDestroy((cudaEvent_t)event));
+  return MFB_OK;
+}
+
+int mfb_event_record(void* event, void* stream) {
+  MFB_CUDA_TRY(cudaEventRecord((cudaEvent_t)event, (cudaStream_t)stream));
+  return MFB_OK;
+}
+
+int mfb_event_elapsed_ms(void* start, void* end, float* ms) {
+  MFB_CHECK_ARG(ms != nullptr, "ms is NULL");
+  MFB_CUDA_TRY(cudaEventElapsedTime(ms, (cudaEvent_t)start, (cudaEvent_t)end));
+  return MFB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,360 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// C[M,N] = alpha * A[M,K] . B[N,K]^T (optionally times a uint8 mask), fp32
+// accumulation in TMEM, bf16 or fp32 output. This is full_linear
+// (src/minifield_training/kernels/linear.py:7-13: x @ W.astype(bf16).T) and the
+// two products of its backward, dX = dY W and dW = dY^T X; with the QAT STE
+// mask fused into the weight-gradient epilogue (the STE of
+// strategies/quantization.py:114-126).
+//
+// Each operand may be K-major (stored [rows, K]) or MN-major (stored
+// [K, rows]); both are loaded by TMA with 128-byte swizzle and described to
+// the tensor core without any transpose pass:
+//   K-major : box {64 K, rows}, 8-row groups 1024 B apart (SBO), K steps of
+//             16 elements advance the start address by 32 B inside the atom.
+//   MN-major: boxes {64 rows, 64 K} placed 8192 B apart (LBO), 8-K-row groups
+//             1024 B apart (SBO), K steps advance by 2048 B.
+//
+// Persistent, warp-specialised CTA (one per SM, 192 threads):
+//   warp 0     TMA producer over a 4-stage smem ring (48 KB per stage),
+//   warp 1     TMEM allocator + single-thread tcgen05.mma issuer (128x256x16),
+//   warps 2-5  epilogue: tcgen05.ld of the 128x256 fp32 accumulator, scale,
+//              mask, convert and store.
+// Two TMEM accumulators (2 x 256 columns) let the epilogue of one tile overlap
+// the main loop of the next. Every mbarrier wait is bounded; a timeout writes a
+// device status word that the host reads back (no trap, no endless spin).
+#include <cudaTypedefs.h>
+
+#include "tc.cuh"
+
+namespace mfb {
+namespace gemm {
+
+// Device status word of the GEMM kernels on each device (0 = ok; otherwise the
+// id of the bounded wait that gave up). Read and cleared by mfb_gemm_status.
+__device__ int g_status;
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int THREADS = 192;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;
+constexpr int TMEM_COLS = 2 * BN;
+
+struct Args {
+  void* C;
+  const uint8_t* mask;
+  long long ldc;
+  int M, N, K;
+  int out_f32;
+  int a_mn, b_mn;
+  int num_m, num_n, num_k;
+  float alpha;
+};
+
+__device__ __forceinline__ void store_chunk(const Args& a, int row, int col0, const uint32_t* r) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * a.alpha;
+  const bool full = col0 + 32 <= a.N;
+  if (a.mask) {
+    const uint8_t* mrow = a.mask + (long long)row * a.N + col0;
+    if (full && (a.N & 15) == 0) {
+      const uint4 m0 = *reinterpret_cast<const uint4*>(mrow);
+      const uint4 m1 = *reinterpret_cast<const uint4*>(mrow + 16);
+      const uint8_t* mb0 = reinterpret_cast<const uint8_t*>(&m0);
+      const uint8_t* mb1 = reinterpret_cast<const uint8_t*>(&m1);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        v[i] *= (float)mb0[i];
+        v[16 + i] *= (float)mb1[i];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < a.N) v[i] *= (float)mrow[i];
+    }
+  }
+  if (a.out_f32) {
+    float* c = reinterpret_cast<float*>(a.C) + (long long)row * a.ldc + col0;
+    if (full) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        reinterpret_cast<float4*>(c)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < a.N) c[i] = v[i];
+    }
+  } else {
+    __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)row * a.ldc + col0;
+    if (full) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 o;
+        o.x = pack_bf16(v[8 * i], v[8 * i + 1]);
+        o.y = pack_bf16(v[8 * i + 2], v[8 * i + 3]);
+        o.z = pack_bf16(v[8 * i + 4], v[8 * i + 5]);
+        o.w = pack_bf16(v[8 * i + 6], v[8 * i + 7]);
+        reinterpret_cast<uint4*>(c)[i] = o;
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < a.N) c[i] = __float2bfloat16_rn(v[i]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + STAGES * STAGE_BYTES;
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return bars + 8u * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return bars + 8u * (2 * STAGES + 2 + a); };
+  const uint32_t done_bar = bars + 8u * (2 * STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + STAGES * STAGE_BYTES + 128);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(full_bar(s), 1);
+      tc::mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(tfull_bar(a), 1);
+      tc::mbar_init(tempty_bar(a), 128);
+    }
+    tc::mbar_init(done_bar, 1);
+    tc::mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::tma_prefetch_desc(&ta);
+    tc::tma_prefetch_desc(&tb);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int num_tiles = args.num_m * args.num_n;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        const int mb = tile % args.num_m, nb = tile / args.num_m;
+        for (int kb = 0; kb < args.num_k; ++kb) {
+          if (!tc::mbar_wait(empty_bar(stage), phase ^ 1, &g_status, 1)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = sbase + stage * STAGE_BYTES, sb = sa + A_BYTES;
+          tc::mbar_expect_tx(full_bar(stage), STAGE_BYTES);
+          if (!args.a_mn) {
+            tc::tma_load_2d(sa, &ta, kb * BK, mb * BM, full_bar(stage));
+          } else {
+#pragma unroll
+            for (int i = 0; i < BM / 64; ++i) tc::tma_load_2d(sa + i * 8192, &ta, mb * BM + 64 * i, kb * BK, full_bar(stage));
+          }
+          if (!args.b_mn) {
+            tc::tma_load_2d(sb, &tb, kb * BK, nb * BN, full_bar(stage));
+          } else {
+#pragma unroll
+            for (int i = 0; i < BN / 64; ++i) tc::tma_load_2d(sb + i * 8192, &tb, nb * BN + 64 * i, kb * BK, full_bar(stage));
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_bf16_f32(BM, BN, args.a_mn, args.b_mn);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        if (!tc::mbar_wait(tempty_bar(acc), acc_phase ^ 1, &g_status, 2)) break;
+        tc::tc_fence_after();
+        const uint32_t d = tmem + acc * BN;
+        for (int kb = 0; kb < args.num_k; ++kb) {
+          if (!tc::mbar_wait(full_bar(stage), phase, &g_status, 3)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t sa = sbase + stage * STAGE_BYTES, sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = args.a_mn ? tc::smem_desc_sw128(sa + k * 2048, 8192, 1024)
+                                          : tc::smem_desc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bd = args.b_mn ? tc::smem_desc_sw128(sb + k * 2048, 8192, 1024)
+                                          : tc::smem_desc_sw128(sb + k * 32, 16, 1024);
+            tc::mma_bf16(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          tc::mma_commit(empty_bar(stage));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        tc::mma_commit(tfull_bar(acc));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      // Drain: every MMA issued above has completed before TMEM is freed.
+      tc::mma_commit(done_bar);
+      tc::mbar_wait(done_bar, 0, &g_status, 4);
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int mb = tile % args.num_m, nb = tile / args.num_m;
+      if (!tc::mbar_wait(tfull_bar(acc), acc_phase, &g_status, 5)) break;
+      tc::tc_fence_after();
+      const int row = mb * BM + q * 32 + lane;
+#pragma unroll 1
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        uint32_t r[32];
+        tc::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + acc * BN + ch * 32, r);
+        tc::tmem_ld_wait();
+        const int col0 = nb * BN + ch * 32;
+        if (row < args.M && col0 < args.N) store_chunk(args, row, col0, r);
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(tempty_bar(acc));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace gemm
+
+namespace tc {
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+int make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
+                   uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(MFB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {64, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(MFB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return MFB_OK;
+}
+
+}  // namespace tc
+}  // namespace mfb
+
+using namespace mfb;
+
+namespace {
+int sm_count(int dev) {
+  static int counts[64] = {0};
+  if (dev < 0 || dev >= 64) return 148;
+  if (!counts[dev]) cudaDeviceGetAttribute(&counts[dev], cudaDevAttrMultiProcessorCount, dev);
+  return counts[dev] ? counts[dev] : 148;
+}
+}  // namespace
+
+extern "C" int mfb_gemm_bf16(const uint16_t* A, int a_major, int lda, const uint16_t* B, int b_major, int ldb,
+                             void* C, int ldc, int out_dtype, int M, int N, int K, float alpha, const uint8_t* mask,
+                             void* stream) {
+  MFB_CHECK_ARG(M > 0 && N > 0 && K > 0, "GEMM needs nonempty M/N/K (%d, %d, %d)", M, N, K);
+  MFB_CHECK_ARG(A && B && C, "NULL operand");
+  MFB_CHECK_ARG(a_major == MFB_MAJOR_K || a_major == MFB_MAJOR_MN, "bad a_major");
+  MFB_CHECK_ARG(b_major == MFB_MAJOR_K || b_major == MFB_MAJOR_MN, "bad b_major");
+  MFB_CHECK_ARG(out_dtype == MFB_DTYPE_BF16 || out_dtype == MFB_DTYPE_F32, "bad out_dtype");
+  MFB_CHECK_ARG(lda % 8 == 0 && ldb % 8 == 0, "lda/ldb must be multiples of 8 elements (16-byte TMA strides)");
+  MFB_CHECK_ARG(lda >= (a_major == MFB_MAJOR_K ? K : M) && ldb >= (b_major == MFB_MAJOR_K ? K : N), "ld too small");
+  MFB_CHECK_ARG(ldc >= N && ldc % (out_dtype == MFB_DTYPE_F32 ? 4 : 8) == 0, "ldc must be >= N and 16-byte aligned");
+  MFB_CHECK_ARG(((uintptr_t)A & 15) == 0 && ((uintptr_t)B & 15) == 0 && ((uintptr_t)C & 15) == 0,
+                "operands must be 16-byte aligned");
+  int dev = 0;
+  MFB_CUDA_TRY(cudaGetDevice(&dev));
+  CUtensorMap ta, tb;
+  int st;
+  if (a_major == MFB_MAJOR_K)
+    st = tc::make_tmap_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, gemm::BM);
+  else
+    st = tc::make_tmap_bf16(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, gemm::BK);
+  if (st) return st;
+  if (b_major == MFB_MAJOR_K)
+    st = tc::make_tmap_bf16(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, gemm::BN);
+  else
+    st = tc::make_tmap_bf16(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, gemm::BK);
+  if (st) return st;
+  gemm::Args a{};
+  a.C = C;
+  a.mask = mask;
+  a.ldc = ldc;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.out_f32 = out_dtype == MFB_DTYPE_F32;
+  a.a_mn = a_major == MFB_MAJOR_MN;
+  a.b_mn = b_major == MFB_MAJOR_MN;
+  a.num_m = cdiv(M, gemm::BM);
+  a.num_n = cdiv(N, gemm::BN);
+  a.num_k = cdiv(K, gemm::BK);
+  a.alpha = alpha;
+  MFB_CUDA_TRY(cudaFuncSetAttribute(gemm::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM));
+  const int tiles = a.num_m * a.num_n;
+  const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
+  gemm::gemm_kernel<<<grid, gemm::THREADS, gemm::SMEM, (cudaStream_t)stream>>>(ta, tb, a);
+  MFB_LAUNCH_CHECK("mfb_gemm_bf16");
+  return MFB_OK;
+}
+
+// Reads and clears the GEMM kernels' device status word for the current
+// device (nonzero: a bounded wait gave up; the value names which one).
+extern "C" int mfb_gemm_status(int* code) {
+  MFB_CHECK_ARG(code != nullptr, "code is NULL");
+  *code = 0;
+  MFB_CUDA_TRY(cudaMemcpyFromSymbol(code, gemm::g_status, sizeof(int)));
+  if (*code) {
+    const int zero = 0;
+    MFB_CUDA_TRY(cudaMemcpyToSymbol(gemm::g_status, &zero, sizeof(int)));
+  }
+  return MFB_OK;
+}

@@ -118,6 +118,20 @@ def decode_lengths(cfg: DecodeConfig, seed: int = 0) -> np.ndarray:
     return rng.integers(cfg.min_len, cfg.capacity + 1, size=cfg.batch).astype(np.int32)
 
 
+def decode_layer_bytes(lengths, cfg: DecodeConfig, elem: int = 2) -> int:
+    """Algorithmic HBM bytes of one layer's decode step.
+
+    Reads of the valid K and V prefix (lengths include the new token), the
+    query read, the output write and the new key/value read + cache write.
+    """
+    lengths = np.asarray(lengths, np.int64)
+    b = lengths.shape[0]
+    kv = int(lengths.sum()) * cfg.kv_heads * cfg.head_dim * 2 * elem
+    qo = b * cfg.heads * cfg.head_dim * 2 * elem
+    new = b * cfg.kv_heads * cfg.head_dim * 2 * elem * 2
+    return kv + qo + new
+
+
 def decode_layer_inputs(cfg: DecodeConfig, seed: int, layer: int = 0, batch=None, capacity=None):
     """(q [B,H,D], k_cache, v_cache [B,cap,Hk,D], new_k, new_v [B,Hk,D]) ~ N(0, 0.02)."""
     b = cfg.batch if batch is None else batch

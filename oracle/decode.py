@@ -20,13 +20,18 @@ from . import attention
 
 
 def append_kv(k_cache, v_cache, new_k, new_v, positions):
-    """Return caches with row b's slot positions[b] replaced (positions < 0: no write)."""
+    """Return caches with row b's slot positions[b] replaced.
+
+    ``jax.lax.dynamic_update_slice`` clamps the start index so the update fits,
+    so the slot is clamped into [0, capacity - 1].
+    """
     k_cache = k_cache.copy()
     v_cache = v_cache.copy()
+    cap = k_cache.shape[1]
     for b, p in enumerate(np.asarray(positions).reshape(-1)):
-        if p >= 0:
-            k_cache[b, p] = new_k[b]
-            v_cache[b, p] = new_v[b]
+        p = min(max(int(p), 0), cap - 1)
+        k_cache[b, p] = new_k[b]
+        v_cache[b, p] = new_v[b]
     return k_cache, v_cache
 
 

@@ -1,0 +1,134 @@
+"""tcgen05 GEMM and the QAT SwiGLU FFN chain vs the oracle."""
+
+import numpy as np
+import pytest
+
+from oracle import linear as olin
+from oracle import quant as oq
+from oracle.bf16 import round_bf16
+from tests._util import assert_close
+from tests.gpu_env import require_gpu
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _gpu():
+    require_gpu()
+
+
+def _dev(x, dtype="bfloat16"):
+    from minifield_training_b200.device import DeviceArray
+
+    return DeviceArray.from_numpy(x, dtype)
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (300, 520, 200), (1000, 768, 1024), (64, 40, 136)])
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_gemm_all_majors(m, n, k, a_mn, b_mn):
+    from minifield_training_b200 import _lib
+    from minifield_training_b200.device import DeviceArray
+    from minifield_training_b200.kernels.linear import _gemm
+
+    rng = np.random.default_rng(m * 7 + n + k + 3 * a_mn + b_mn)
+    a = round_bf16(rng.standard_normal((m, k), dtype=np.float32))
+    b = round_bf16(rng.standard_normal((n, k), dtype=np.float32))
+    ka = np.ascontiguousarray(a.T) if a_mn else a
+    kb = np.ascontiguousarray(b.T) if b_mn else b
+    ad, bd = _dev(ka), _dev(kb)
+    for out_dtype, code in (("float32", _lib.DTYPE_F32), ("bfloat16", _lib.DTYPE_BF16)):
+        ldc = n + (-n) % 8
+        c = DeviceArray((m, ldc), out_dtype)
+        _gemm(ad, a_mn, ka.shape[1], bd, b_mn, kb.shape[1], c, ldc, code, m, n, k)
+        got = c.float32()[:, :n]
+        ref = a.astype(np.float64) @ b.astype(np.float64).T
+        if out_dtype == "float32":
+            np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-4 * np.sqrt(k))
+        else:
+            assert_close(got, ref, scaled=True, what="bf16 gemm")
+    code = np.zeros(1, np.int32)
+    from minifield_training_b200 import _lib as L
+    import ctypes
+
+    st = ctypes.c_int()
+    L.call("mfb_gemm_status", ctypes.byref(st))
+    assert st.value == 0
+
+
+def test_full_linear_reference_kats(golden):
+    from minifield_training_b200.kernels.linear import full_linear, full_linear_bwd
+
+    x = np.zeros((1, 64), np.float32)
+    x[0, :2] = golden["linear_cast_x"][0]
+    w = np.zeros((1, 64), np.float32)
+    w[0, :2] = golden["linear_cast_w"][0]
+    y = full_linear(x, w)
+    np.testing.assert_array_equal(y.float32(), golden["linear_cast_out"])
+    dx, dw = full_linear_bwd(x, w, np.ones((1, 1), np.float32))
+    np.testing.assert_array_equal(dx.float32()[:, :2], golden["linear_cast_dx"])
+    np.testing.assert_array_equal(dw.float32()[:, :2], golden["linear_cast_dw"])
+    gx, gw, probe = golden["linear_x"], golden["linear_w"], golden["linear_probe"]
+    xp = np.zeros((2, 64), np.float32)
+    xp[:, :2] = gx.reshape(2, 2)
+    wp = np.zeros((2, 64), np.float32)
+    wp[:, :2] = gw
+    np.testing.assert_array_equal(full_linear(xp, wp).float32(), golden["linear_out"].reshape(2, 2))
+    dx, dw = full_linear_bwd(xp, wp, probe.reshape(2, 2))
+    np.testing.assert_array_equal(dx.float32()[:, :2], golden["linear_dx"].reshape(2, 2))
+    np.testing.assert_array_equal(dw.float32()[:, :2], golden["linear_dw"])
+
+
+@pytest.mark.parametrize("kind", [oq.KIND_INT8_CHANNEL, oq.KIND_INT4_G128, oq.KIND_NF4_G128])
+def test_swiglu_qat_small(kind):
+    from minifield_training_b200.layers.feed_forward import swiglu_qat_bwd, swiglu_qat_fwd
+
+    rng = np.random.default_rng(17)
+    m, c, f = 384, 256, 640
+    x = rng.standard_normal((m, c), dtype=np.float32)
+    w_gu = (rng.standard_normal((2 * f, c)) * 0.05).astype(np.float32)
+    w_d = (rng.standard_normal((c, f)) * 0.05).astype(np.float32)
+    dy = rng.standard_normal((m, c), dtype=np.float32)
+    y, res = swiglu_qat_fwd(x, w_gu, w_d, kind)
+    dx, dwgu, dwd = swiglu_qat_bwd(res, dy)
+    ry, _, _ = olin.swiglu_qat_forward(x, w_gu, w_d, kind)
+    rdx, rdwgu, rdwd = olin.swiglu_qat_backward(x, w_gu, w_d, kind, dy)
+    assert_close(y.float32(), ry, scaled=True, what="y")
+    assert_close(dx.float32(), rdx, scaled=True, what="dx")
+    assert_close(dwgu.float32(), rdwgu, scaled=True, what="dW_gate_up")
+    assert_close(dwd.float32(), rdwd, scaled=True, what="dW_down")
+
+
+def test_swiglu_qat_config4_full_size():
+    """Full config-4 shapes: forward rows and weight-gradient columns checked exactly
+    against FP64 products of the GPU's own bf16 intermediates (GEMM parity at size)."""
+    from minifield_training_b200 import workloads
+    from minifield_training_b200.layers.feed_forward import swiglu_qat_bwd, swiglu_qat_fwd
+
+    cfg = workloads.CONFIG4
+    x, w_gu, w_d, dy = workloads.qat_inputs(cfg, seed=0)
+    y, res = swiglu_qat_fwd(x, w_gu, w_d, cfg.kind)
+    dx, dwgu, dwd = swiglu_qat_bwd(res, dy)
+    eff_gu, _, eff_d, _ = olin.qat_weights(w_gu, w_d, cfg.kind)
+    rows = np.arange(0, cfg.tokens, 997)
+    ry, _, _ = olin.swiglu_qat_forward(x[rows], w_gu, w_d, cfg.kind, dtype=np.float32)
+    assert_close(y.float32()[rows], ry, scaled=True, what="cfg4 y rows")
+    rdx, _, _ = olin.swiglu_qat_backward(x[rows], w_gu, w_d, cfg.kind, dy[rows], dtype=np.float32)
+    assert_close(dx.float32()[rows], rdx, scaled=True, what="cfg4 dx rows")
+    h = res.h.float32()
+    cols = np.arange(0, cfg.ffn, 331)
+    ref_dwd = round_bf16(dy).astype(np.float64).T @ h[:, cols].astype(np.float64)
+    assert_close(dwd.float32()[:, cols], ref_dwd, scaled=True, what="cfg4 dW_down cols")
+    from minifield_training_b200.device import DeviceArray  # noqa: F401
+
+    xb = round_bf16(x).astype(np.float64)
+    gu = res.gu.float32()
+    # dGU from the GPU's own gate/up output (exact SwiGLU derivative in FP64).
+    dh = round_bf16(dy).astype(np.float64) @ eff_d.astype(np.float64)
+    sub = np.arange(0, 2 * cfg.ffn, 1013)
+    g = gu[:, :cfg.ffn].astype(np.float64)
+    u = gu[:, cfg.ffn:].astype(np.float64)
+    dg = dh * u * olin.silu_grad(g)
+    du = dh * olin.silu(g)
+    dgu = np.concatenate((dg, du), axis=1)[:, sub]
+    ref_dwgu = round_bf16(dgu).T @ xb
+    assert_close(dwgu.float32()[sub], ref_dwgu, scaled=True, what="cfg4 dW_gate_up rows")
