@@ -12,8 +12,12 @@
   ``Quantizer.effective(master)``; the STE passes the effective weight's
   gradient to the master, multiplied by the quantizer's STE mask.
 
-The oracle computes in FP64 (or FP32) from bf16-rounded operands, i.e. the
-reference's FP32 path evaluated on the same bf16 inputs the GPU receives.
+The oracle computes in FP64 (or FP32) from bf16-rounded operands. With
+``bf16_casts=True`` (the default; the benchmark configurations run bf16
+activations) it also rounds to bf16 where the reference's bf16 graph does:
+``full_linear`` returns ``x.dtype`` (kernels/linear.py:9-13), so the gate/up
+output, the SiLU product and, in the backward, dH and dGate/dUp (gradients of
+bf16 tensors) are bf16 values; every product is still exact FP64 arithmetic.
 """
 
 import numpy as np
@@ -43,7 +47,11 @@ def qat_weights(w_gate_up: np.ndarray, w_down: np.ndarray, kind: str):
     return round_bf16(eff_gu), ste_gu, round_bf16(eff_d), ste_d
 
 
-def swiglu_qat_forward(x, w_gate_up, w_down, kind, dtype=np.float64):
+def _cast(a, on, dtype):
+    return round_bf16(a).astype(dtype) if on else a
+
+
+def swiglu_qat_forward(x, w_gate_up, w_down, kind, dtype=np.float64, bf16_casts=True):
     """Return (y, gu, h): gu = x W_gu^T, h = silu(gate) * up, y = h W_d^T.
 
     ``w_gate_up`` is [2F, C] with the gate rows first; ``w_down`` is [C, F].
@@ -53,27 +61,27 @@ def swiglu_qat_forward(x, w_gate_up, w_down, kind, dtype=np.float64):
     eff_gu, _, eff_d, _ = qat_weights(w_gate_up, w_down, kind)
     f = w_down.shape[1]
     xb = round_bf16(x).astype(dtype)
-    gu = xb @ eff_gu.astype(dtype).T
+    gu = _cast(xb @ eff_gu.astype(dtype).T, bf16_casts, dtype)
     g, u = gu[:, :f], gu[:, f:]
     h = round_bf16(silu(g) * u).astype(dtype)
     y = h @ eff_d.astype(dtype).T
     return y, gu, h
 
 
-def swiglu_qat_backward(x, w_gate_up, w_down, kind, d_y, dtype=np.float64):
+def swiglu_qat_backward(x, w_gate_up, w_down, kind, d_y, dtype=np.float64, bf16_casts=True):
     """Return (dx, dw_gate_up, dw_down) of sum(y * d_y) with the STE masks."""
     eff_gu, ste_gu, eff_d, ste_d = qat_weights(w_gate_up, w_down, kind)
     f = w_down.shape[1]
     xb = round_bf16(x).astype(dtype)
-    gu = xb @ eff_gu.astype(dtype).T
+    gu = _cast(xb @ eff_gu.astype(dtype).T, bf16_casts, dtype)
     g, u = gu[:, :f], gu[:, f:]
     h = round_bf16(silu(g) * u).astype(dtype)
     dy = round_bf16(d_y).astype(dtype)
-    dh = dy @ eff_d.astype(dtype)
+    dh = _cast(dy @ eff_d.astype(dtype), bf16_casts, dtype)
     dw_down = (dy.T @ h) * ste_d
     dg = dh * u * silu_grad(g)
     du = dh * silu(g)
-    dgu = np.concatenate((dg, du), axis=1)
+    dgu = _cast(np.concatenate((dg, du), axis=1), bf16_casts, dtype)
     dx = dgu @ eff_gu.astype(dtype)
     dw_gate_up = (dgu.T @ xb) * ste_gu
     return dx, dw_gate_up, dw_down

@@ -23,7 +23,7 @@ def _dev(x, dtype="bfloat16"):
     return DeviceArray.from_numpy(x, dtype)
 
 
-@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (300, 520, 200), (1000, 768, 1024), (64, 40, 136)])
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (296, 520, 200), (1000, 768, 1024), (64, 40, 136)])
 @pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
 def test_gemm_all_majors(m, n, k, a_mn, b_mn):
     from minifield_training_b200 import _lib
@@ -37,7 +37,7 @@ def test_gemm_all_majors(m, n, k, a_mn, b_mn):
     kb = np.ascontiguousarray(b.T) if b_mn else b
     ad, bd = _dev(ka), _dev(kb)
     for out_dtype, code in (("float32", _lib.DTYPE_F32), ("bfloat16", _lib.DTYPE_BF16)):
-        ldc = n + (-n) % 8
+        ldc = n + 3  # unaligned output rows exercise the scalar-store epilogue
         c = DeviceArray((m, ldc), out_dtype)
         _gemm(ad, a_mn, ka.shape[1], bd, b_mn, kb.shape[1], c, ldc, code, m, n, k)
         got = c.float32()[:, :n]
@@ -56,26 +56,41 @@ def test_gemm_all_majors(m, n, k, a_mn, b_mn):
 
 
 def test_full_linear_reference_kats(golden):
+    """KATs of tests/kernels/test_linear.py, zero-padded to the TMA's 8-element
+    stride granularity (padding rows/columns are zero, so the sums are unchanged)."""
     from minifield_training_b200.kernels.linear import full_linear, full_linear_bwd
 
-    x = np.zeros((1, 64), np.float32)
+    x = np.zeros((8, 64), np.float32)
     x[0, :2] = golden["linear_cast_x"][0]
-    w = np.zeros((1, 64), np.float32)
+    w = np.zeros((8, 64), np.float32)
     w[0, :2] = golden["linear_cast_w"][0]
     y = full_linear(x, w)
-    np.testing.assert_array_equal(y.float32(), golden["linear_cast_out"])
-    dx, dw = full_linear_bwd(x, w, np.ones((1, 1), np.float32))
-    np.testing.assert_array_equal(dx.float32()[:, :2], golden["linear_cast_dx"])
-    np.testing.assert_array_equal(dw.float32()[:, :2], golden["linear_cast_dw"])
+    np.testing.assert_array_equal(y.float32()[:1, :1], golden["linear_cast_out"])
+    dy = np.zeros((8, 8), np.float32)
+    dy[0, 0] = 1.0
+    dx, dw = full_linear_bwd(x, w, dy)
+    np.testing.assert_array_equal(dx.float32()[:1, :2], golden["linear_cast_dx"])
+    np.testing.assert_array_equal(dw.float32()[:1, :2], golden["linear_cast_dw"])
     gx, gw, probe = golden["linear_x"], golden["linear_w"], golden["linear_probe"]
-    xp = np.zeros((2, 64), np.float32)
-    xp[:, :2] = gx.reshape(2, 2)
-    wp = np.zeros((2, 64), np.float32)
-    wp[:, :2] = gw
-    np.testing.assert_array_equal(full_linear(xp, wp).float32(), golden["linear_out"].reshape(2, 2))
-    dx, dw = full_linear_bwd(xp, wp, probe.reshape(2, 2))
-    np.testing.assert_array_equal(dx.float32()[:, :2], golden["linear_dx"].reshape(2, 2))
-    np.testing.assert_array_equal(dw.float32()[:, :2], golden["linear_dw"])
+    xp = np.zeros((8, 64), np.float32)
+    xp[:2, :2] = gx.reshape(2, 2)
+    wp = np.zeros((8, 64), np.float32)
+    wp[:2, :2] = gw
+    np.testing.assert_array_equal(full_linear(xp, wp).float32()[:2, :2], golden["linear_out"].reshape(2, 2))
+    dyp = np.zeros((8, 8), np.float32)
+    dyp[:2, :2] = probe.reshape(2, 2)
+    dx, dw = full_linear_bwd(xp, wp, dyp)
+    np.testing.assert_array_equal(dx.float32()[:2, :2], golden["linear_dx"].reshape(2, 2))
+    np.testing.assert_array_equal(dw.float32()[:2, :2], golden["linear_dw"])
+
+
+def test_gemm_rejects_unaligned_tma_strides():
+    from minifield_training_b200.kernels.linear import gemm_tn
+
+    a = _dev(np.zeros((16, 300), np.float32))
+    b = _dev(np.zeros((16, 64), np.float32))
+    with pytest.raises(ValueError, match="multiples of 8"):
+        gemm_tn(a, b)
 
 
 @pytest.mark.parametrize("kind", [oq.KIND_INT8_CHANNEL, oq.KIND_INT4_G128, oq.KIND_NF4_G128])

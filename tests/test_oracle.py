@@ -266,7 +266,7 @@ def test_swiglu_qat_backward_matches_finite_differences():
     w_d = (rng.standard_normal((c, f)) * 0.3).astype(np.float32)
     dy = rng.standard_normal((m, c)).astype(np.float32)
     kind = oq.KIND_INT8_CHANNEL
-    dx, dwgu, dwd = olin.swiglu_qat_backward(x, w_gu, w_d, kind, dy)
+    dx, dwgu, dwd = olin.swiglu_qat_backward(x, w_gu, w_d, kind, dy, bf16_casts=False)
     eff_gu, _, eff_d, _ = olin.qat_weights(w_gu, w_d, kind)
     xb = round_bf16(x).astype(np.float64)
 
