@@ -42,11 +42,13 @@ UNIT = "TFLOP/s"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-secondary", action="store_true", help="skip the decode / QAT secondary measurements")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["attention", "decode", "qat"], default=None,
+                    help="run one workload (profiling); the JSON line then carries only its numbers")
     return ap.parse_args()
 
 
@@ -441,89 +443,86 @@ def measure(dist, fn, steps, warmup, clocks=None):
 
 
 def run_ours(args, dist):
-    from minifield_training_b200 import _lib, device, workloads
+    from minifield_training_b200 import device, workloads
 
     device.set_device(dist.local)
     device.require_b200(dist.local)
     hbm, tf_burst, tf_sus, peak_kind = peaks()
     traffic = traffic_table()
     n = dist.world
-
-    att = AttentionWorkload(workloads.CONFIG2, seed=dist.rank)
+    only = args.only
     clocks = Clocks(dist.local)
-    ms, clk = measure(dist, att.step, args.steps, args.warmup, clocks)
-    value = n * att.total_flops / (ms * 1e-3) / 1e12
+    clocks.start()  # sampled across every timed phase below
 
-    # Per-kernel timing for the roofline: forward alone, backward alone.
-    timer = Timer()
-    fwd_ms = dist.max(timer.time(att.fwd, args.steps))
-    bwd_ms = dist.max(timer.time(att.bwd, args.steps))
-    if bwd_ms >= fwd_ms:
-        dom, dom_ms, dom_flops = "attn_bwd", bwd_ms, 2.5 * att.fwd_flops
-    else:
-        dom, dom_ms, dom_flops = "attn_fwd", fwd_ms, att.fwd_flops
-    achieved = dom_flops / (dom_ms * 1e-3) / 1e12
-    roofline = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s",
-                "frac": achieved / tf_burst, "peak_source": f"{peak_kind} bf16 burst",
-                "traffic": traffic.get(dom), "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
-                "fwd_tflops": att.fwd_flops / (fwd_ms * 1e-3) / 1e12,
-                "bwd_tflops": 2.5 * att.fwd_flops / (bwd_ms * 1e-3) / 1e12}
-
-    # End to end through the C ABI with pinned host buffers.
-    att.e2e_setup()
-    e2e_ms, _ = measure(dist, att.e2e_step, max(3, args.steps // 4), 2)
-    e2e = {"value": n * att.total_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
-           "h2d_bytes_per_step": att.h2d_bytes, "d2h_bytes_per_step": att.d2h_bytes, "ms_per_step": e2e_ms}
-    del att
+    line = {"metric": METRIC, "unit": UNIT, "n_gpus": n, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic"}
+    launches = 0
+    if only in (None, "attention"):
+        att = AttentionWorkload(workloads.CONFIG2, seed=dist.rank)
+        ms, _ = measure(dist, att.step, args.steps, args.warmup)
+        value = n * att.total_flops / (ms * 1e-3) / 1e12
+        launches += AttentionWorkload.launches_per_step * args.steps
+        # Per-kernel timing for the roofline: forward alone, backward alone.
+        timer = Timer()
+        fwd_ms = dist.max(timer.time(att.fwd, args.steps))
+        bwd_ms = dist.max(timer.time(att.bwd, args.steps))
+        if bwd_ms >= fwd_ms:
+            dom, dom_ms, dom_flops = "attn_bwd", bwd_ms, 2.5 * att.fwd_flops
+        else:
+            dom, dom_ms, dom_flops = "attn_fwd", fwd_ms, att.fwd_flops
+        achieved = dom_flops / (dom_ms * 1e-3) / 1e12
+        roofline = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s",
+                    "frac": achieved / tf_burst, "peak_source": f"{peak_kind} bf16 burst",
+                    "traffic": traffic.get(dom), "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+                    "fwd_tflops": att.fwd_flops / (fwd_ms * 1e-3) / 1e12,
+                    "bwd_tflops": 2.5 * att.fwd_flops / (bwd_ms * 1e-3) / 1e12}
+        # End to end through the C ABI with pinned host buffers.
+        att.e2e_setup()
+        e2e_ms, _ = measure(dist, att.e2e_step, max(3, args.steps // 4), 2)
+        e2e = {"value": n * att.total_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
+               "h2d_bytes_per_step": att.h2d_bytes, "d2h_bytes_per_step": att.d2h_bytes, "ms_per_step": e2e_ms}
+        line.update(value=value, ms_per_step=ms, tensor_peak_frac=value / n / tf_burst, roofline=roofline, e2e=e2e)
+        line["config"] = {
+            "workload": workloads.CONFIG2.name, "batch": 8, "seq_len": 2048, "heads": 16, "kv_heads": 8,
+            "head_dim": 64, "segments": "U[32,1024] packed, seed=rank", "flops_per_step": att.total_flops,
+            "per_gpu_work": "fixed (weak scaling, independent replicas)",
+            "l2": "inputs larger than L2 (~250 MB working set per step)"}
+        del att
 
     secondary = {}
-    launches = AttentionWorkload.launches_per_step * args.steps
-    if not args.no_secondary:
+    if only in (None, "decode") and not (only is None and args.no_secondary):
         dec = DecodeWorkload(seed=dist.rank)
         dms, _ = measure(dist, dec.step, args.steps, args.warmup)
         gbs = dec.bytes / (dms * 1e-3) / 1e9
+        launches += DecodeWorkload.launches_per_step * args.steps
         secondary["decode"] = {
             "workload": workloads.CONFIG3.name, "tokens_per_s": n * workloads.CONFIG3.batch / (dms * 1e-3),
             "ms_per_step": dms, "hbm_gbs": gbs, "hbm_frac": gbs / hbm, "peak_gbs": hbm,
             "bytes_per_step": dec.bytes, "traffic": traffic.get("decode")}
         del dec
+    if only in (None, "qat") and not (only is None and args.no_secondary):
         qat = QatWorkload(seed=dist.rank)
-        qms, _ = measure(dist, qat.step, max(3, args.steps // 2), max(3, args.warmup // 2))
+        qsteps = max(3, args.steps // 2)
+        qms, _ = measure(dist, qat.step, qsteps, max(3, args.warmup // 2))
+        launches += QatWorkload.launches_per_step * qsteps
         secondary["qat"] = {
             "workload": workloads.CONFIG4.name, "kind": workloads.CONFIG4.kind,
             "tokens_per_s": n * workloads.CONFIG4.tokens / (qms * 1e-3), "ms_per_step": qms,
             "tflops": qat.flops / (qms * 1e-3) / 1e12, "tensor_frac": qat.flops / (qms * 1e-3) / 1e12 / tf_sus,
             "peak_tflops": tf_sus, "peak_source": f"{peak_kind} bf16 sustained"}
         del qat
+    line["clocks"] = clocks.stop()
 
-    cpu = None
-    if dist.rank == 0 and not args.no_cpu_baseline:
+    if dist.rank == 0 and not args.no_cpu_baseline and only in (None, "attention"):
         v, dt, sample = cpu_attention_sample(2)
-        cpu = {"value": v, "unit": UNIT, "cores": int(os.environ.get("OPENBLAS_NUM_THREADS", os.cpu_count() or 1)),
-               "kind": "port", "sample": sample + f" ({dt:.1f} s)"}
-
+        line["cpu_baseline"] = {"value": v, "unit": UNIT,
+                                "cores": int(os.environ.get("OPENBLAS_NUM_THREADS", os.cpu_count() or 1)),
+                                "kind": "port", "sample": sample + f" ({dt:.1f} s)"}
+    line["gpu_launches"] = launches
+    line["secondary"] = secondary
     if dist.rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": workloads.CONFIG2.name, "batch": 8, "seq_len": 2048, "heads": 16, "kv_heads": 8,
-                       "head_dim": 64, "segments": "U[32,1024] packed, seed=rank", "flops_per_step": att_flops(),
-                       "per_gpu_work": "fixed (weak scaling, independent replicas)",
-                       "l2": "inputs larger than L2 (~250 MB working set per step)"},
-            "tensor_peak_frac": value / n / tf_burst,
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-            "clocks": clk, "secondary": secondary,
-        }
         print(json.dumps(line), flush=True)
     return 0
-
-
-def att_flops():
-    from minifield_training_b200 import workloads
-
-    seg = workloads.packed_segments(0, 8, 2048)
-    return 3.5 * 4.0 * 16 * 64 * workloads.segment_square_sum(seg)
 
 
 def main():
