@@ -138,6 +138,27 @@ int mfb_decode_attn(const uint16_t* q, uint16_t* k_cache, uint16_t* v_cache, con
                     int B, int capacity, int H, int Hk, int D, float scale, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* Allocation-free decode step. No counterpart in the reference: it exists for
+ * callers that cannot call cudaMalloc -- work recorded inside a CUDA-graph
+ * capture, an XLA FFI custom-call handler that may only touch the buffers it
+ * is given, a serving loop that forbids allocation after start-up. Same
+ * inputs, outputs and semantics as mfb_decode_attn, but the split-K scratch is
+ * a fixed array of MFB_DECODE_NOALLOC_SCRATCH_BYTES compiled into the library
+ * (every GPU that loads the library holds it until the process exits);
+ * shapes needing more (mfb_decode_workspace_size > the maximum; config 3,
+ * B=64 x capacity 4096 x 16 heads, needs about 4.3 MB) are rejected with
+ * MFB_ERR_INVALID. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current; make that first
+ * call before any stream capture. Every call on a device shares the one array
+ * and leaves its contents behind (each call clears the parts that must start
+ * at zero), so calls that overlap on the GPU -- concurrent streams, or host
+ * threads on one device -- race and must be serialised by the caller. No
+ * cudaMalloc, cudaFree or allocating library routine is called. */
+#define MFB_DECODE_NOALLOC_SCRATCH_BYTES (8 << 20)
+int mfb_decode_attn_noalloc(const uint16_t* q, uint16_t* k_cache, uint16_t* v_cache, const uint16_t* new_k,
+                            const uint16_t* new_v, const int32_t* positions, const int32_t* valid_length,
+                            uint16_t* o, int B, int capacity, int H, int Hk, int D, float scale, void* stream);
+
 /* ---- GEMM (tcgen05) ----------------------------------------------------------
  * C[M,N] = alpha * op(A) . op(B)^T, bf16 operands, fp32 accumulation in TMEM.
  * a_major / b_major: MFB_MAJOR_K when the operand is stored [rows, K] (K

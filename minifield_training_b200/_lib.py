@@ -62,6 +62,7 @@ SIGNATURES = {
     "mfb_attn_bwd": (I, [P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, I, F, P, SZ, P]),
     "mfb_decode_workspace_size": (SZ, [I, I, I, I]),
     "mfb_decode_attn": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, F, P, SZ, P]),
+    "mfb_decode_attn_noalloc": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, F, P]),
     "mfb_gemm_bf16": (I, [P, I, I, P, I, I, P, I, I, I, I, I, F, P, P]),
     "mfb_gemm_status": (I, [IP]),
     "mfb_swiglu_fwd": (I, [P, P, I, I, P]),

@@ -334,3 +334,92 @@ extern "C" int mfb_decode_attn(const uint16_t* q, uint16_t* k_cache, uint16_t* v
   MFB_LAUNCH_CHECK("mfb_decode_attn");
   return MFB_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// Some callers cannot call cudaMalloc: code running inside a CUDA-graph
+// capture region or a framework's custom-call handler (an XLA FFI handler may
+// only use the buffers the runtime hands it), or a serving loop that forbids
+// allocation after start-up. mfb_decode_attn_noalloc gives them the decode
+// step with its split-K partials in a fixed scratch array compiled into this
+// library instead of a caller workspace.
+// ---------------------------------------------------------------------------
+namespace mfb {
+namespace dec {
+
+// Scratch for the partials and tickets: MFB_DECODE_NOALLOC_SCRATCH_BYTES per
+// device that loads the library, held until the process exits.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[MFB_DECODE_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch per device ordinal, resolved once per
+// device with that device current (the host-side symbol is only a stand-in).
+constexpr int kMaxDevices = 64;
+static void* g_noalloc_ptr[kMaxDevices] = {nullptr};
+
+}  // namespace dec
+}  // namespace mfb
+
+extern "C" int mfb_decode_attn_noalloc(const uint16_t* q, uint16_t* k_cache, uint16_t* v_cache,
+                                       const uint16_t* new_k, const uint16_t* new_v, const int32_t* positions,
+                                       const int32_t* valid_length, uint16_t* o, int B, int capacity, int H, int Hk,
+                                       int D, float scale, void* stream) {
+  MFB_CHECK_ARG(B > 0 && capacity > 0, "Cached attention needs a nonempty batch and cache (B=%d cap=%d)", B, capacity);
+  MFB_CHECK_ARG(D == dec::HD, "Cached attention query/KV shapes are incompatible (head_dim %d; this build needs 64)", D);
+  MFB_CHECK_ARG(H > 0 && Hk > 0 && H % Hk == 0, "Query heads must be divisible by KV heads (H=%d Hk=%d)", H, Hk);
+  MFB_CHECK_ARG(q && k_cache && v_cache && valid_length && o, "NULL tensor argument");
+  MFB_CHECK_ARG((new_k == nullptr) == (new_v == nullptr), "new_k and new_v must both be given or both be NULL");
+  MFB_CHECK_ARG(new_k == nullptr || positions != nullptr, "positions are required with new_k/new_v");
+  const size_t need = dec::carve(nullptr, B, capacity, H).bytes;
+  MFB_CHECK_ARG(need <= (size_t)MFB_DECODE_NOALLOC_SCRATCH_BYTES,
+                "mfb_decode_attn_noalloc: B=%d, capacity=%d, H=%d need %zu scratch bytes, above the fixed %d-byte "
+                "maximum; use mfb_decode_attn with a caller workspace",
+                B, capacity, H, need, (int)MFB_DECODE_NOALLOC_SCRATCH_BYTES);
+  int dev = 0;
+  MFB_CUDA_TRY(cudaGetDevice(&dev));
+  MFB_CHECK_ARG(dev >= 0 && dev < dec::kMaxDevices, "device ordinal %d out of range", dev);
+  if (dec::g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    MFB_CUDA_TRY(cudaGetSymbolAddress(&ptr, dec::g_noalloc_scratch));
+    dec::g_noalloc_ptr[dev] = ptr;
+  }
+  const dec::Workspace w = dec::carve(dec::g_noalloc_ptr[dev], B, capacity, H);
+  dec::Params p{};
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  p.kc = reinterpret_cast<__nv_bfloat16*>(k_cache);
+  p.vc = reinterpret_cast<__nv_bfloat16*>(v_cache);
+  p.nk = reinterpret_cast<const __nv_bfloat16*>(new_k);
+  p.nv = reinterpret_cast<const __nv_bfloat16*>(new_v);
+  p.positions = positions;
+  p.valid_length = valid_length;
+  p.o = reinterpret_cast<__nv_bfloat16*>(o);
+  p.part_o = w.part_o;
+  p.part_ml = w.part_ml;
+  p.tickets = w.tickets;
+  p.B = B;
+  p.cap = capacity;
+  p.H = H;
+  p.Hk = Hk;
+  p.G = H / Hk;
+  p.nch_max = cdiv(capacity, dec::CHUNK);
+  p.scale_log2 = scale * kLog2e;
+  cudaStream_t s = (cudaStream_t)stream;
+  // The array keeps the previous call's contents: the per-row tickets must start at zero.
+  MFB_CUDA_TRY(cudaMemsetAsync(w.tickets, 0, sizeof(int) * (size_t)B, s));
+  dim3 grid(p.nch_max, B);
+  switch (p.G) {
+    case 1:
+      dec::decode_kernel<1><<<grid, dec::THREADS, 0, s>>>(p);
+      break;
+    case 2:
+      dec::decode_kernel<2><<<grid, dec::THREADS, 0, s>>>(p);
+      break;
+    case 4:
+      dec::decode_kernel<4><<<grid, dec::THREADS, 0, s>>>(p);
+      break;
+    default:
+      return set_error(MFB_ERR_UNSUPPORTED, "GQA group size %d unsupported (1, 2 or 4)", p.G);
+  }
+  MFB_LAUNCH_CHECK("mfb_decode_attn_noalloc");
+  return MFB_OK;
+}
