@@ -122,6 +122,11 @@ int mfb_attn_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, const 
                  const int32_t* kid, int B, int T, int S, int H, int Hk, int D, int causal, int causal_offset,
                  int empty_policy, float scale, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Reads (and clears) the attention tensor-core kernels' device status word of
+ * the current device: 0 = ok, otherwise the id of a bounded pipeline wait that
+ * gave up (the kernel then unwound instead of hanging). Synchronous. */
+int mfb_attn_status(int* code);
+
 /* ---- KV-cached decode -------------------------------------------------------
  * One query per sequence: q [B,H,D], caches [B,cap,Hk,D] bf16. If new_k/new_v
  * are non-NULL, row b's new key/value [B,Hk,D] are written at slot positions[b]

@@ -60,6 +60,7 @@ SIGNATURES = {
     "mfb_attn_workspace_size": (SZ, [I, I, I, I, I, I]),
     "mfb_attn_fwd": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, I, F, P, SZ, P]),
     "mfb_attn_bwd": (I, [P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, I, F, P, SZ, P]),
+    "mfb_attn_status": (I, [IP]),
     "mfb_decode_workspace_size": (SZ, [I, I, I, I]),
     "mfb_decode_attn": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, F, P, SZ, P]),
     "mfb_decode_attn_noalloc": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, F, P]),

@@ -25,6 +25,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "tc.cuh"
 
 namespace mfb {
 namespace attn {
@@ -731,6 +732,430 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(const float* __restrict
 }
 
 // ---------------------------------------------------------------------------
+// Forward on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// CTA = (128 query rows, the two query heads of one GQA pair, batch row).
+// Warp roles (320 threads):
+//   warp 0      TMA producer (lane 0): both Q tiles once, then K/V tiles
+//               through a 3-stage ring (128 keys x 64 dims, 128-byte swizzle);
+//               all lanes stage each key tile's ids and run table.
+//   warp 1      TMEM owner and single-thread tcgen05.mma issuer.
+//   warps 2-5   softmax for query head h0, warps 6-9 for h0 + 1: one thread
+//               per query row (TMEM lane quarter = warp % 4), reading its S row
+//               with tcgen05.ld.
+// Per live key tile j and head g:
+//   S_g = Q_g K_j^T           SS MMA, M=128 N=128 K=64 -> TMEM (128 columns)
+//   softmax: the thread loads its 128-value S row with one wait, takes the
+//   row max, and writes P_g = exp2(S * scale * log2e - M) back as bf16 pairs
+//   into the first 64 columns of S_g (tcgen05.st). M is a lazily updated
+//   reference max: it moves (and the thread rescales its O row and row sum in
+//   TMEM) only when the running max exceeds it by more than 8 (P <= 256).
+//   O_g += P_g V_j            TS MMA (A = P from TMEM, B = V MN-major) into a
+//                             64-column accumulator.
+// Masks: full tiles skip masking; otherwise warp 0 publishes the tile's runs of
+// equal nonzero key ids (id, first, last); with at most 8 runs of distinct ids
+// a row's valid keys are one interval, else the thread compares ids per key.
+// The MMA order S_0(j), S_1(j), PV_0(j), S_0(j+1), PV_1(j), S_1(j+1), ... lets
+// one head's softmax run while the other head's products are on the tensor
+// core. TMEM: S_0 [0,128) O_0 [128,192) S_1 [256,384) O_1 [384,448).
+// ---------------------------------------------------------------------------
+__device__ int g_tc_status;
+
+constexpr int TQ = 128, TK = 128;
+constexpr int TF_ST = 3;
+constexpr int TF_THREADS = 320;
+constexpr int TF_Q_OFF = 0;
+constexpr int TF_K_OFF = 2 * 16384;
+constexpr int TF_V_OFF = TF_K_OFF + TF_ST * 16384;
+constexpr int TF_KID_OFF = TF_V_OFF + TF_ST * 16384;
+// Per stage: 128 key ids, then the run table (count, 8 x {id, first, last}).
+constexpr int TF_KID_STRIDE = 128 + 32;
+constexpr int TF_MAX_RUNS = 8;
+constexpr int TF_BAR_OFF = TF_KID_OFF + TF_ST * TF_KID_STRIDE * 4;
+constexpr int TF_SMEM = 1024 + TF_BAR_OFF + 256;
+
+// 128-row tile range from the two 64-row block ranges it covers.
+__device__ __forceinline__ Range range128(const Range* r, int nb64, int tile) {
+  const Range a = r[2 * tile];
+  Range out = a;
+  if (2 * tile + 1 < nb64) {
+    const Range c = r[2 * tile + 1];
+    out.lo = min(a.lo, c.lo);
+    out.hi = max(a.hi, c.hi);
+    out.full = a.full && c.full && a.lo == c.lo;
+  } else {
+    out.full = 0;
+  }
+  return out;
+}
+
+__device__ __forceinline__ bool tile_live128(const Params& p, const Range& qr, const Range& kr, int q0, int s0) {
+  if (p.causal && s0 > min(q0 + TQ - 1, p.T - 1) + p.offset) return false;
+  return max(qr.lo, kr.lo) <= min(qr.hi, kr.hi);
+}
+
+__device__ __forceinline__ bool tile_full128(const Params& p, const Range& qr, const Range& kr, int q0, int s0) {
+  if (!qr.full || !kr.full || qr.lo != kr.lo) return false;
+  return !(p.causal && s0 + TK - 1 > q0 + p.offset);
+}
+
+// 10 warps: the sub-partitions holding 3 warps cap registers at 168 per thread.
+__global__ void __launch_bounds__(TF_THREADS, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                       const __grid_constant__ CUtensorMap tv, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const uint32_t sb = smem_u32(smem);
+  const uint32_t bars = sb + TF_BAR_OFF;
+  const uint32_t q_full = bars;
+  auto kv_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto kv_empty = [&](int s) { return bars + 8u * (1 + TF_ST + s); };
+  auto s_full = [&](int g) { return bars + 8u * (1 + 2 * TF_ST + g); };
+  auto p_full = [&](int g) { return bars + 8u * (3 + 2 * TF_ST + g); };
+  auto o_full = [&](int g) { return bars + 8u * (5 + 2 * TF_ST + g); };
+  const uint32_t done_bar = bars + 8u * (7 + 2 * TF_ST);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TF_BAR_OFF + 8 * (8 + 2 * TF_ST));
+  int* kid_s = reinterpret_cast<int*>(smem + TF_KID_OFF);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, b = blockIdx.z;
+  const int h0 = blockIdx.y * 2;
+  const int hk = h0 / p.G;
+  const int q0 = qt * TQ;
+  const int nkt = cdiv(p.S, TK);
+  const Range qrange = range128(p.qr + (long long)b * p.nqb, p.nqb, qt);
+  const Range* krs = p.kr + (long long)b * p.nkb;
+  int* status = &g_tc_status;
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(q_full, 1);
+    for (int s = 0; s < TF_ST; ++s) {
+      tc::mbar_init(kv_full(s), 1 + 32);
+      tc::mbar_init(kv_empty(s), 1);
+    }
+    for (int g = 0; g < 2; ++g) {
+      tc::mbar_init(s_full(g), 1);
+      tc::mbar_init(p_full(g), 128);
+      tc::mbar_init(o_full(g), 1);
+    }
+    tc::mbar_init(done_bar, 1);
+    tc::mbar_fence_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(smem_u32(tmem_slot), 512);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto next_live = [&](int j) {
+    for (; j < nkt; ++j) {
+      if (p.causal && j * TK > min(q0 + TQ - 1, p.T - 1) + p.offset) return nkt;
+      if (tile_live128(p, qrange, range128(krs, p.nkb, j), q0, j * TK)) return j;
+    }
+    return nkt;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tc::tma_prefetch_desc(&tq);
+      tc::tma_prefetch_desc(&tk);
+      tc::tma_prefetch_desc(&tv);
+      tc::mbar_expect_tx(q_full, 2 * 16384);
+      tc::tma_load_2d(sb + TF_Q_OFF, &tq, h0 * 64, b * p.T + q0, q_full);
+      tc::tma_load_2d(sb + TF_Q_OFF + 16384, &tq, (h0 + 1) * 64, b * p.T + q0, q_full);
+    }
+    int it = 0;
+    for (int j = next_live(0); j < nkt; j = next_live(j + 1), ++it) {
+      const int st = it % TF_ST;
+      const uint32_t ph = (it / TF_ST) & 1;
+      if (!tc::mbar_wait(kv_empty(st), ph ^ 1, status, 11)) break;
+      if (lane == 0) {
+        tc::mbar_expect_tx(kv_full(st), 2 * 16384);
+        tc::tma_load_2d(sb + TF_K_OFF + st * 16384, &tk, hk * 64, b * p.S + j * TK, kv_full(st));
+        tc::tma_load_2d(sb + TF_V_OFF + st * 16384, &tv, hk * 64, b * p.S + j * TK, kv_full(st));
+      }
+      int* kt = kid_s + st * TF_KID_STRIDE;
+      int kv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int s = j * TK + 4 * lane + e;
+        kv[e] = s < p.S ? p.kid[(long long)b * p.S + s] : 0;
+        kt[4 * lane + e] = kv[e];
+      }
+      // Runs of equal nonzero ids: starts / ends per key, ordered prefix index.
+      const int prev = __shfl_up_sync(0xffffffffu, kv[3], 1);
+      const int next = __shfl_down_sync(0xffffffffu, kv[0], 1);
+      unsigned sbits = 0, ebits = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int before = e == 0 ? (lane == 0 ? 0 : prev) : kv[e - 1];
+        const int after = e == 3 ? (lane == 31 ? 0 : next) : kv[e + 1];
+        if (kv[e] != 0 && (e + lane == 0 || before != kv[e])) sbits |= 1u << e;
+        if (kv[e] != 0 && ((e == 3 && lane == 31) || after != kv[e])) ebits |= 1u << e;
+      }
+      const int ns = __popc(sbits), ne = __popc(ebits);
+      int incl_s = ns, incl_e = ne;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int ys = __shfl_up_sync(0xffffffffu, incl_s, o), ye = __shfl_up_sync(0xffffffffu, incl_e, o);
+        if (lane >= o) incl_s += ys, incl_e += ye;
+      }
+      const int total = __shfl_sync(0xffffffffu, incl_s, 31);
+      int* rt = kt + 128;  // [0] = count or -1, then 8 x {id, first, last}
+      if (total <= TF_MAX_RUNS) {
+        int is = incl_s - ns, ie = incl_e - ne;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (sbits & (1u << e)) {
+            rt[1 + 3 * is] = kv[e];
+            rt[2 + 3 * is] = 4 * lane + e;
+            ++is;
+          }
+          if (ebits & (1u << e)) {
+            rt[3 + 3 * ie] = 4 * lane + e;
+            ++ie;
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        int cnt = total <= TF_MAX_RUNS ? total : -1;
+        for (int a = 0; cnt > 0 && a < total; ++a)
+          for (int c = a + 1; c < total; ++c)
+            if (rt[1 + 3 * a] == rt[1 + 3 * c]) cnt = -1;  // an id in two runs: per-key compare
+        rt[0] = cnt;
+      }
+      __syncwarp();
+      tc::mbar_arrive(kv_full(st));
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc_s = tc::idesc_bf16_f32(128, 128, 0, 0);
+      const uint32_t idesc_o = tc::idesc_bf16_f32(128, 64, 0, 1);
+      bool ok = tc::mbar_wait(q_full, 0, status, 13);
+      tc::tc_fence_after();
+      int it = 0, prev = -1;
+      for (int j = next_live(0); ok && j < nkt; j = next_live(j + 1), ++it) {
+        const int st = it % TF_ST;
+        if (!(ok = tc::mbar_wait(kv_full(st), (it / TF_ST) & 1, status, 14))) break;
+        tc::tc_fence_after();
+        for (int g = 0; g < 2; ++g) {
+          const uint32_t s_t = tmem + g * 256, o_t = tmem + g * 256 + 128;
+          if (it > 0) {
+            if (!(ok = tc::mbar_wait(p_full(g), (it - 1) & 1, status, 15))) break;
+            tc::tc_fence_after();
+            const uint32_t vb = sb + TF_V_OFF + prev * 16384;
+#pragma unroll
+            for (int k = 0; k < TK / 16; ++k)
+              tc::mma_bf16_ts(o_t, s_t + k * 8, tc::smem_desc_sw128(vb + k * 2048, 8192, 1024), idesc_o,
+                              (it > 1 || k > 0) ? 1u : 0u);
+          }
+          const uint32_t qb_ = sb + TF_Q_OFF + g * 16384, kb_ = sb + TF_K_OFF + st * 16384;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            tc::mma_bf16(s_t, tc::smem_desc_sw128(qb_ + k * 32, 16, 1024), tc::smem_desc_sw128(kb_ + k * 32, 16, 1024),
+                         idesc_s, k > 0 ? 1u : 0u);
+          tc::mma_commit(s_full(g));
+        }
+        if (!ok) break;
+        if (it > 0) tc::mma_commit(kv_empty(prev));
+        prev = st;
+      }
+      if (ok && it > 0) {
+        for (int g = 0; g < 2; ++g) {
+          const uint32_t s_t = tmem + g * 256, o_t = tmem + g * 256 + 128;
+          if (!tc::mbar_wait(p_full(g), (it - 1) & 1, status, 16)) break;
+          tc::tc_fence_after();
+          const uint32_t vb = sb + TF_V_OFF + prev * 16384;
+#pragma unroll
+          for (int k = 0; k < TK / 16; ++k)
+            tc::mma_bf16_ts(o_t, s_t + k * 8, tc::smem_desc_sw128(vb + k * 2048, 8192, 1024), idesc_o,
+                            (it > 1 || k > 0) ? 1u : 0u);
+          tc::mma_commit(o_full(g));
+        }
+      }
+      tc::mma_commit(done_bar);
+      tc::mbar_wait(done_bar, 0, status, 17);
+    }
+  } else {
+    const int g = (warp - 2) >> 2, quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int t = q0 + r;
+    const int h = h0 + g;
+    const int qid_row = t < p.T ? p.qid[(long long)b * p.T + t] : 0;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t s_t = tmem + lane_off + g * 256, o_t = tmem + lane_off + g * 256 + 128;
+    const float sl2 = p.scale_log2;
+    float M = -INFINITY, l = 0.f;  // reference max (log2 domain) and row sum relative to it
+    int it = 0;
+    bool ok = true;
+    for (int j = next_live(0); j < nkt; j = next_live(j + 1), ++it) {
+      const int st = it % TF_ST;
+      if (!(ok = tc::mbar_wait(s_full(g), it & 1, status, 18))) break;
+      if (!(ok = tc::mbar_wait(kv_full(st), (it / TF_ST) & 1, status, 19))) break;
+      tc::tc_fence_after();
+      const int s0 = j * TK;
+      uint32_t x[TK];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::tmem_ld_32x32b_x32(s_t + c * 32, x + c * 32);
+      tc::tmem_ld_wait();
+      // Mask: full tile / one interval per row / per-key ids.
+      const int* kt = kid_s + st * TF_KID_STRIDE;
+      const bool full = tile_full128(p, qrange, range128(krs, p.nkb, j), q0, s0);
+      int lo = 0, hi = TK - 1;
+      bool per_key = false;
+      if (!full) {
+        const int nr = kt[128];
+        if (nr >= 0) {
+          lo = 1, hi = 0;
+          for (int q = 0; q < nr; ++q)
+            if (kt[129 + 3 * q] == qid_row) lo = kt[130 + 3 * q], hi = kt[131 + 3 * q];
+        } else {
+          per_key = true;
+        }
+        if (p.causal) hi = min(hi, t + p.offset - s0);
+      }
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+      if (!per_key) {
+        // Unmasked tiles have lo = 0, hi = 127: the compares fold away per lane.
+#pragma unroll
+        for (int i = 0; i < TK; i += 4) {
+          float y[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            y[e] = (i + e >= lo && i + e <= hi) ? __uint_as_float(x[i + e]) * sl2 : -INFINITY;
+            x[i + e] = __float_as_uint(y[e]);
+          }
+          mx0 = fmaxf(mx0, y[0]);
+          mx1 = fmaxf(mx1, y[1]);
+          mx2 = fmaxf(mx2, y[2]);
+          mx3 = fmaxf(mx3, y[3]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < TK; i += 4) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const bool valid = i + e <= hi && qid_row != 0 && kt[i + e] == qid_row;
+            const float y = valid ? __uint_as_float(x[i + e]) * sl2 : -INFINITY;
+            x[i + e] = __float_as_uint(y);
+            mx0 = fmaxf(mx0, y);
+          }
+        }
+      }
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      if (mx > M + 8.f) {
+        // Move the reference max; rescale this row's O accumulator and sum.
+        const float sc = ex2(M - mx);
+        if (it > 0 && M != -INFINITY) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t v[16];
+            tc::tmem_ld_32x32b_x16(o_t + c * 16, v);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * sc);
+            tc::tmem_st_32x32b_x16(o_t + c * 16, v);
+          }
+        }
+        l *= sc;
+        M = mx;
+      }
+      const float mu = M == -INFINITY ? 0.f : M;
+      float rs0 = 0.f, rs1 = 0.f, rs2 = 0.f, rs3 = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float e0 = ex2(__uint_as_float(x[c * 32 + i]) - mu), e1 = ex2(__uint_as_float(x[c * 32 + i + 1]) - mu);
+          const float e2 = ex2(__uint_as_float(x[c * 32 + i + 2]) - mu),
+                      e3 = ex2(__uint_as_float(x[c * 32 + i + 3]) - mu);
+          rs0 += e0;
+          rs1 += e1;
+          rs2 += e2;
+          rs3 += e3;
+          pk[i >> 1] = pack_bf16(e0, e1);
+          pk[(i >> 1) + 1] = pack_bf16(e2, e3);
+        }
+        tc::tmem_st_32x32b_x16(s_t + c * 16, pk);
+      }
+      tc::tmem_st_wait();
+      tc::tc_fence_before();
+      tc::mbar_arrive(p_full(g));
+      l += (rs0 + rs1) + (rs2 + rs3);
+    }
+    uint32_t ou[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) ou[i] = 0u;
+    if (ok && it > 0 && tc::mbar_wait(o_full(g), 0, status, 20)) {
+      tc::tc_fence_after();
+      tc::tmem_ld_32x32b_x32(o_t, ou);
+      tc::tmem_ld_32x32b_x32(o_t + 32, ou + 32);
+      tc::tmem_ld_wait();
+    }
+    const float m = M;
+    const float sl2_one = 1.f;
+    // Epilogue: normalise; rows without a valid key follow the empty policy.
+    const bool empty = !(l > 0.f);
+    const float inv = empty ? 0.f : 1.f / l;
+    const bool need_uniform = p.policy == MFB_EMPTY_UNIFORM && __any_sync(0xffffffffu, empty && t < p.T);
+    float vm0 = 0.f, vm1 = 0.f;
+    if (need_uniform) {
+      const __nv_bfloat16* vbase = p.v + ((long long)b * p.S * p.Hk + hk) * HD;
+      for (int s = 0; s < p.S; ++s) {
+        const __nv_bfloat162 x = *reinterpret_cast<const __nv_bfloat162*>(vbase + (long long)s * p.Hk * HD + 2 * lane);
+        vm0 += __bfloat162float(x.x);
+        vm1 += __bfloat162float(x.y);
+      }
+      vm0 /= (float)p.S;
+      vm1 /= (float)p.S;
+    }
+    if (t < p.T) {
+      __nv_bfloat16* orow = p.o + (((long long)b * p.T + t) * p.H + h) * HD;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        uint4 u;
+        uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d = c8 * 8 + 2 * e;
+          float a0 = __uint_as_float(ou[d]) * inv, a1 = __uint_as_float(ou[d + 1]) * inv;
+          w[e] = pack_bf16(a0, a1);
+        }
+        *reinterpret_cast<uint4*>(orow + c8 * 8) = u;
+      }
+      p.lse[((long long)b * p.H + h) * p.T + t] = empty ? -INFINITY : m * sl2_one + __log2f(l);
+    }
+    if (need_uniform) {
+      // Uniform rows: every lane broadcasts its two columns of the V mean.
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        uint4 u;
+        uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d = c8 * 8 + 2 * e;
+          const float u0 = __shfl_sync(0xffffffffu, vm0, d >> 1), u1 = __shfl_sync(0xffffffffu, vm1, d >> 1);
+          w[e] = pack_bf16(u0, u1);
+        }
+        if (empty && t < p.T)
+          *reinterpret_cast<uint4*>(p.o + (((long long)b * p.T + t) * p.H + h) * HD + c8 * 8) = u;
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
 struct Workspace {
@@ -857,6 +1282,19 @@ extern "C" int mfb_attn_ids(int mode, const int32_t* mask, const int32_t* segmen
   return MFB_OK;
 }
 
+// Reads (and clears) the attention tensor-core kernels' device status word of
+// the current device: 0 = ok, otherwise the id of a bounded wait that gave up.
+extern "C" int mfb_attn_status(int* code) {
+  MFB_CHECK_ARG(code != nullptr, "code is NULL");
+  *code = 0;
+  MFB_CUDA_TRY(cudaMemcpyFromSymbol(code, g_tc_status, sizeof(int)));
+  if (*code) {
+    const int zero = 0;
+    MFB_CUDA_TRY(cudaMemcpyToSymbol(g_tc_status, &zero, sizeof(int)));
+  }
+  return MFB_OK;
+}
+
 extern "C" size_t mfb_attn_workspace_size(int B, int T, int S, int H, int Hk, int D) {
   (void)D;
   if (B <= 0 || T <= 0 || S <= 0 || H <= 0 || Hk <= 0) return 0;
@@ -885,9 +1323,15 @@ extern "C" int mfb_attn_fwd(const uint16_t* q, const uint16_t* k, const uint16_t
   p.kid = kid;
   cudaStream_t s = (cudaStream_t)stream;
   if ((st = launch_ranges(p, qid, kid, s))) return st;
-  if ((st = set_smem((const void*)attn_fwd_kernel, FWD_SMEM))) return st;
-  dim3 grid(p.nqb, H / FWD_HPB, B);
-  attn_fwd_kernel<<<grid, FWD_THREADS, FWD_SMEM, s>>>(p);
+  MFB_CHECK_ARG(((uintptr_t)q & 15) == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0,
+                "q/k/v must be 16-byte aligned");
+  CUtensorMap tq, tk, tv;
+  if ((st = tc::make_tmap_bf16(&tq, q, (uint64_t)H * HD, (uint64_t)B * T, (uint64_t)H * HD, TQ))) return st;
+  if ((st = tc::make_tmap_bf16(&tk, k, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
+  if ((st = tc::make_tmap_bf16(&tv, v, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
+  if ((st = set_smem((const void*)attn_fwd_tc_kernel, TF_SMEM))) return st;
+  dim3 grid(cdiv(T, TQ), H / 2, B);
+  attn_fwd_tc_kernel<<<grid, TF_THREADS, TF_SMEM, s>>>(tq, tk, tv, p);
   MFB_LAUNCH_CHECK("mfb_attn_fwd");
   return MFB_OK;
 }
