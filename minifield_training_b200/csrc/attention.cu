@@ -767,11 +767,20 @@ constexpr int TF_THREADS = 320;
 constexpr int TF_Q_OFF = 0;
 constexpr int TF_K_OFF = 2 * 16384;
 constexpr int TF_V_OFF = TF_K_OFF + TF_ST * 16384;
-constexpr int TF_KID_OFF = TF_V_OFF + TF_ST * 16384;
+constexpr int TF_V_STRIDE = 16384;
+// One constant "ones" MN atom (128 key rows x 64 columns, column 0 = 1.0;
+// 16 KB) shared by every V stage: the PV product runs with N = 80 and each
+// stage's B descriptor points its second MN atom here (LBO = ONES - V stage),
+// so column 64 of O accumulates the row sum of P.
+constexpr int TF_ONES_OFF = TF_V_OFF + TF_ST * TF_V_STRIDE;
+constexpr int TF_KID_OFF = TF_ONES_OFF + 16384;
 // Per stage: 128 key ids, then the run table (count, 8 x {id, first, last}).
 constexpr int TF_KID_STRIDE = 128 + 32;
 constexpr int TF_MAX_RUNS = 8;
-constexpr int TF_BAR_OFF = TF_KID_OFF + TF_ST * TF_KID_STRIDE * 4;
+constexpr int TF_LIST_OFF = TF_KID_OFF + TF_ST * TF_KID_STRIDE * 4;
+constexpr int TF_MAX_TILES = 256;  // key tiles per row: S <= 32768
+constexpr int TF_BAR_OFF = TF_LIST_OFF + (TF_MAX_TILES + 4) * 4;
+constexpr int TF_ON = 80;  // PV product width: 64 value columns + the ones column block
 constexpr int TF_SMEM = 1024 + TF_BAR_OFF + 256;
 
 // 128-row tile range from the two 64-row block ranges it covers.
@@ -816,6 +825,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   const uint32_t done_bar = bars + 8u * (7 + 2 * TF_ST);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TF_BAR_OFF + 8 * (8 + 2 * TF_ST));
   int* kid_s = reinterpret_cast<int*>(smem + TF_KID_OFF);
+  int* list = reinterpret_cast<int*>(smem + TF_LIST_OFF);  // [0] = count, then tile | full << 30
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, b = blockIdx.z;
@@ -841,22 +851,40 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     tc::mbar_init(done_bar, 1);
     tc::mbar_fence_init();
   }
-  if (warp == 1) {
+  if (warp == 0) {
+    // Live key tiles of this query tile, in order, with their "no mask" flag.
+    int count = 0;
+    for (int base = 0; base < nkt; base += 32) {
+      const int j = base + lane;
+      bool live = false, full = false;
+      if (j < nkt) {
+        const Range kr = range128(krs, p.nkb, j);
+        live = tile_live128(p, qrange, kr, q0, j * TK);
+        full = live && tile_full128(p, qrange, kr, q0, j * TK);
+      }
+      const unsigned bal = __ballot_sync(0xffffffffu, live);
+      if (live) list[1 + count + __popc(bal & ((1u << lane) - 1))] = j | (full ? 1 << 30 : 0);
+      count += __popc(bal);
+    }
+    if (lane == 0) list[0] = count;
+  } else if (warp == 1) {
     tc::tmem_alloc(smem_u32(tmem_slot), 512);
     tc::tmem_relinquish();
+  } else {
+    // The constant ones atom: column 0 of each of its 128 rows is 1.0.
+    for (int i = threadIdx.x - 64; i < 128 * 8; i += TF_THREADS - 64) {
+      const int row = i / 8, chunk = i % 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (chunk == (row & 7)) v.x = 0x3F80u;  // logical chunk 0 lands at physical chunk row % 8
+      *reinterpret_cast<uint4*>(smem + TF_ONES_OFF + row * 128 + chunk * 16) = v;
+    }
+    tc::fence_proxy_async_smem();
   }
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  auto next_live = [&](int j) {
-    for (; j < nkt; ++j) {
-      if (p.causal && j * TK > min(q0 + TQ - 1, p.T - 1) + p.offset) return nkt;
-      if (tile_live128(p, qrange, range128(krs, p.nkb, j), q0, j * TK)) return j;
-    }
-    return nkt;
-  };
+  const int ntiles = list[0];
 
   if (warp == 0) {
     if (lane == 0) {
@@ -867,16 +895,18 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       tc::tma_load_2d(sb + TF_Q_OFF, &tq, h0 * 64, b * p.T + q0, q_full);
       tc::tma_load_2d(sb + TF_Q_OFF + 16384, &tq, (h0 + 1) * 64, b * p.T + q0, q_full);
     }
-    int it = 0;
-    for (int j = next_live(0); j < nkt; j = next_live(j + 1), ++it) {
+    for (int it = 0; it < ntiles; ++it) {
+      const int j = list[1 + it] & 0xFFFF;
       const int st = it % TF_ST;
       const uint32_t ph = (it / TF_ST) & 1;
       if (!tc::mbar_wait(kv_empty(st), ph ^ 1, status, 11)) break;
       if (lane == 0) {
         tc::mbar_expect_tx(kv_full(st), 2 * 16384);
         tc::tma_load_2d(sb + TF_K_OFF + st * 16384, &tk, hk * 64, b * p.S + j * TK, kv_full(st));
-        tc::tma_load_2d(sb + TF_V_OFF + st * 16384, &tv, hk * 64, b * p.S + j * TK, kv_full(st));
+        tc::tma_load_2d(sb + TF_V_OFF + st * TF_V_STRIDE, &tv, hk * 64, b * p.S + j * TK, kv_full(st));
       }
+      // Key ids and their run table: (id, first, last) of each run of equal
+      // nonzero ids; count -1 when an id recurs or there are more than 8 runs.
       int* kt = kid_s + st * TF_KID_STRIDE;
       int kv[4];
 #pragma unroll
@@ -885,7 +915,6 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         kv[e] = s < p.S ? p.kid[(long long)b * p.S + s] : 0;
         kt[4 * lane + e] = kv[e];
       }
-      // Runs of equal nonzero ids: starts / ends per key, ordered prefix index.
       const int prev = __shfl_up_sync(0xffffffffu, kv[3], 1);
       const int next = __shfl_down_sync(0xffffffffu, kv[0], 1);
       unsigned sbits = 0, ebits = 0;
@@ -904,7 +933,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         if (lane >= o) incl_s += ys, incl_e += ye;
       }
       const int total = __shfl_sync(0xffffffffu, incl_s, 31);
-      int* rt = kt + 128;  // [0] = count or -1, then 8 x {id, first, last}
+      int* rt = kt + 128;
       if (total <= TF_MAX_RUNS) {
         int is = incl_s - ns, ie = incl_e - ne;
 #pragma unroll
@@ -925,7 +954,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         int cnt = total <= TF_MAX_RUNS ? total : -1;
         for (int a = 0; cnt > 0 && a < total; ++a)
           for (int c = a + 1; c < total; ++c)
-            if (rt[1 + 3 * a] == rt[1 + 3 * c]) cnt = -1;  // an id in two runs: per-key compare
+            if (rt[1 + 3 * a] == rt[1 + 3 * c]) cnt = -1;
         rt[0] = cnt;
       }
       __syncwarp();
@@ -934,11 +963,11 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc_s = tc::idesc_bf16_f32(128, 128, 0, 0);
-      const uint32_t idesc_o = tc::idesc_bf16_f32(128, 64, 0, 1);
+      const uint32_t idesc_o = tc::idesc_bf16_f32(128, TF_ON, 0, 1);
       bool ok = tc::mbar_wait(q_full, 0, status, 13);
       tc::tc_fence_after();
       int it = 0, prev = -1;
-      for (int j = next_live(0); ok && j < nkt; j = next_live(j + 1), ++it) {
+      for (; ok && it < ntiles; ++it) {
         const int st = it % TF_ST;
         if (!(ok = tc::mbar_wait(kv_full(st), (it / TF_ST) & 1, status, 14))) break;
         tc::tc_fence_after();
@@ -947,10 +976,10 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
           if (it > 0) {
             if (!(ok = tc::mbar_wait(p_full(g), (it - 1) & 1, status, 15))) break;
             tc::tc_fence_after();
-            const uint32_t vb = sb + TF_V_OFF + prev * 16384;
+            const uint32_t vb = sb + TF_V_OFF + prev * TF_V_STRIDE;
 #pragma unroll
             for (int k = 0; k < TK / 16; ++k)
-              tc::mma_bf16_ts(o_t, s_t + k * 8, tc::smem_desc_sw128(vb + k * 2048, 8192, 1024), idesc_o,
+              tc::mma_bf16_ts(o_t, s_t + k * 8, tc::smem_desc_sw128(vb + k * 2048, TF_ONES_OFF - TF_V_OFF - prev * TF_V_STRIDE, 1024), idesc_o,
                               (it > 1 || k > 0) ? 1u : 0u);
           }
           const uint32_t qb_ = sb + TF_Q_OFF + g * 16384, kb_ = sb + TF_K_OFF + st * 16384;
@@ -969,10 +998,10 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
           const uint32_t s_t = tmem + g * 256, o_t = tmem + g * 256 + 128;
           if (!tc::mbar_wait(p_full(g), (it - 1) & 1, status, 16)) break;
           tc::tc_fence_after();
-          const uint32_t vb = sb + TF_V_OFF + prev * 16384;
+          const uint32_t vb = sb + TF_V_OFF + prev * TF_V_STRIDE;
 #pragma unroll
           for (int k = 0; k < TK / 16; ++k)
-            tc::mma_bf16_ts(o_t, s_t + k * 8, tc::smem_desc_sw128(vb + k * 2048, 8192, 1024), idesc_o,
+            tc::mma_bf16_ts(o_t, s_t + k * 8, tc::smem_desc_sw128(vb + k * 2048, TF_ONES_OFF - TF_V_OFF - prev * TF_V_STRIDE, 1024), idesc_o,
                             (it > 1 || k > 0) ? 1u : 0u);
           tc::mma_commit(o_full(g));
         }
@@ -989,10 +1018,13 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t s_t = tmem + lane_off + g * 256, o_t = tmem + lane_off + g * 256 + 128;
     const float sl2 = p.scale_log2;
-    float M = -INFINITY, l = 0.f;  // reference max (log2 domain) and row sum relative to it
+    float M = -INFINITY;  // reference max of the scaled logits (log2 domain)
     int it = 0;
     bool ok = true;
-    for (int j = next_live(0); j < nkt; j = next_live(j + 1), ++it) {
+    for (; it < ntiles; ++it) {
+      const int entry = list[1 + it];
+      const int j = entry & 0xFFFF;
+      const bool full = (entry >> 30) & 1;
       const int st = it % TF_ST;
       if (!(ok = tc::mbar_wait(s_full(g), it & 1, status, 18))) break;
       if (!(ok = tc::mbar_wait(kv_full(st), (it / TF_ST) & 1, status, 19))) break;
@@ -1002,57 +1034,66 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) tc::tmem_ld_32x32b_x32(s_t + c * 32, x + c * 32);
       tc::tmem_ld_wait();
-      // Mask: full tile / one interval per row / per-key ids.
-      const int* kt = kid_s + st * TF_KID_STRIDE;
-      const bool full = tile_full128(p, qrange, range128(krs, p.nkb, j), q0, s0);
-      int lo = 0, hi = TK - 1;
-      bool per_key = false;
-      if (!full) {
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+      const uint32_t NEG = 0xFF800000u;  // -inf
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < TK; i += 4) {
+          mx0 = fmaxf(mx0, __uint_as_float(x[i]));
+          mx1 = fmaxf(mx1, __uint_as_float(x[i + 1]));
+          mx2 = fmaxf(mx2, __uint_as_float(x[i + 2]));
+          mx3 = fmaxf(mx3, __uint_as_float(x[i + 3]));
+        }
+      } else {
+        const int* kt = kid_s + st * TF_KID_STRIDE;
         const int nr = kt[128];
+        int lo = 1, hi = 0;
         if (nr >= 0) {
-          lo = 1, hi = 0;
           for (int q = 0; q < nr; ++q)
             if (kt[129 + 3 * q] == qid_row) lo = kt[130 + 3 * q], hi = kt[131 + 3 * q];
         } else {
-          per_key = true;
+          lo = 0, hi = TK - 1;
         }
         if (p.causal) hi = min(hi, t + p.offset - s0);
-      }
-      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-      if (!per_key) {
-        // Unmasked tiles have lo = 0, hi = 127: the compares fold away per lane.
+        // Validity bits per 32-key chunk, then one branch-free masking pass.
+        uint32_t vm[4];
 #pragma unroll
-        for (int i = 0; i < TK; i += 4) {
-          float y[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            y[e] = (i + e >= lo && i + e <= hi) ? __uint_as_float(x[i + e]) * sl2 : -INFINITY;
-            x[i + e] = __float_as_uint(y[e]);
-          }
-          mx0 = fmaxf(mx0, y[0]);
-          mx1 = fmaxf(mx1, y[1]);
-          mx2 = fmaxf(mx2, y[2]);
-          mx3 = fmaxf(mx3, y[3]);
+        for (int c = 0; c < 4; ++c) {
+          const int a0 = max(lo - c * 32, 0), b0 = min(hi - c * 32, 31);
+          vm[c] = a0 > b0 ? 0u : ((0xFFFFFFFFu >> (31 - b0)) & (0xFFFFFFFFu << a0));
         }
-      } else {
-#pragma unroll
-        for (int i = 0; i < TK; i += 4) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const bool valid = i + e <= hi && qid_row != 0 && kt[i + e] == qid_row;
-            const float y = valid ? __uint_as_float(x[i + e]) * sl2 : -INFINITY;
-            x[i + e] = __float_as_uint(y);
-            mx0 = fmaxf(mx0, y);
-          }
-        }
-      }
-      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-      if (mx > M + 8.f) {
-        // Move the reference max; rescale this row's O accumulator and sum.
-        const float sc = ex2(M - mx);
-        if (it > 0 && M != -INFINITY) {
+        if (nr < 0) {
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
+            uint32_t bits = 0;
+            for (int i = 0; i < 32; ++i) bits |= (qid_row != 0 && kt[c * 32 + i] == qid_row) ? 1u << i : 0u;
+            vm[c] &= bits;
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            const int k = c * 32 + i;
+            x[k] = (vm[c] >> i) & 1u ? x[k] : NEG;
+            x[k + 1] = (vm[c] >> (i + 1)) & 1u ? x[k + 1] : NEG;
+            x[k + 2] = (vm[c] >> (i + 2)) & 1u ? x[k + 2] : NEG;
+            x[k + 3] = (vm[c] >> (i + 3)) & 1u ? x[k + 3] : NEG;
+            mx0 = fmaxf(mx0, __uint_as_float(x[k]));
+            mx1 = fmaxf(mx1, __uint_as_float(x[k + 1]));
+            mx2 = fmaxf(mx2, __uint_as_float(x[k + 2]));
+            mx3 = fmaxf(mx3, __uint_as_float(x[k + 3]));
+          }
+        }
+      }
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+      if (mx > M + 8.f) {
+        // Move the reference max; rescale this row's O accumulator (its
+        // column 64 is the row sum) once the previous products have landed.
+        if (it > 0 && M != -INFINITY) {
+          const float sc = ex2(M - mx);
+#pragma unroll
+          for (int c = 0; c < TF_ON / 16; ++c) {
             uint32_t v[16];
             tc::tmem_ld_32x32b_x16(o_t + c * 16, v);
             tc::tmem_ld_wait();
@@ -1061,44 +1102,37 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
             tc::tmem_st_32x32b_x16(o_t + c * 16, v);
           }
         }
-        l *= sc;
         M = mx;
       }
-      const float mu = M == -INFINITY ? 0.f : M;
-      float rs0 = 0.f, rs1 = 0.f, rs2 = 0.f, rs3 = 0.f;
+      const float nmu = M == -INFINITY ? 0.f : -M;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float e0 = ex2(__uint_as_float(x[c * 32 + i]) - mu), e1 = ex2(__uint_as_float(x[c * 32 + i + 1]) - mu);
-          const float e2 = ex2(__uint_as_float(x[c * 32 + i + 2]) - mu),
-                      e3 = ex2(__uint_as_float(x[c * 32 + i + 3]) - mu);
-          rs0 += e0;
-          rs1 += e1;
-          rs2 += e2;
-          rs3 += e3;
+        for (int i = 0; i < 32; i += 2) {
+          const float e0 = ex2(fmaf(__uint_as_float(x[c * 32 + i]), sl2, nmu));
+          const float e1 = ex2(fmaf(__uint_as_float(x[c * 32 + i + 1]), sl2, nmu));
           pk[i >> 1] = pack_bf16(e0, e1);
-          pk[(i >> 1) + 1] = pack_bf16(e2, e3);
         }
         tc::tmem_st_32x32b_x16(s_t + c * 16, pk);
       }
       tc::tmem_st_wait();
       tc::tc_fence_before();
       tc::mbar_arrive(p_full(g));
-      l += (rs0 + rs1) + (rs2 + rs3);
     }
     uint32_t ou[64];
+    float l = 0.f;
 #pragma unroll
     for (int i = 0; i < 64; ++i) ou[i] = 0u;
     if (ok && it > 0 && tc::mbar_wait(o_full(g), 0, status, 20)) {
       tc::tc_fence_after();
+      uint32_t lv[16];
       tc::tmem_ld_32x32b_x32(o_t, ou);
       tc::tmem_ld_32x32b_x32(o_t + 32, ou + 32);
+      tc::tmem_ld_32x32b_x16(o_t + 64, lv);
       tc::tmem_ld_wait();
+      l = __uint_as_float(lv[0]);
     }
-    const float m = M;
-    const float sl2_one = 1.f;
     // Epilogue: normalise; rows without a valid key follow the empty policy.
     const bool empty = !(l > 0.f);
     const float inv = empty ? 0.f : 1.f / l;
@@ -1107,45 +1141,31 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     if (need_uniform) {
       const __nv_bfloat16* vbase = p.v + ((long long)b * p.S * p.Hk + hk) * HD;
       for (int s = 0; s < p.S; ++s) {
-        const __nv_bfloat162 x = *reinterpret_cast<const __nv_bfloat162*>(vbase + (long long)s * p.Hk * HD + 2 * lane);
-        vm0 += __bfloat162float(x.x);
-        vm1 += __bfloat162float(x.y);
+        const __nv_bfloat162 v2 = *reinterpret_cast<const __nv_bfloat162*>(vbase + (long long)s * p.Hk * HD + 2 * lane);
+        vm0 += __bfloat162float(v2.x);
+        vm1 += __bfloat162float(v2.y);
       }
       vm0 /= (float)p.S;
       vm1 /= (float)p.S;
     }
-    if (t < p.T) {
-      __nv_bfloat16* orow = p.o + (((long long)b * p.T + t) * p.H + h) * HD;
+    __nv_bfloat16* orow = p.o + (((long long)b * p.T + t) * p.H + h) * HD;
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-        uint4 u;
-        uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+    for (int c8 = 0; c8 < 8; ++c8) {
+      uint4 u;
+      uint32_t* w = reinterpret_cast<uint32_t*>(&u);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int d = c8 * 8 + 2 * e;
-          float a0 = __uint_as_float(ou[d]) * inv, a1 = __uint_as_float(ou[d + 1]) * inv;
-          w[e] = pack_bf16(a0, a1);
-        }
-        *reinterpret_cast<uint4*>(orow + c8 * 8) = u;
-      }
-      p.lse[((long long)b * p.H + h) * p.T + t] = empty ? -INFINITY : m * sl2_one + __log2f(l);
-    }
-    if (need_uniform) {
-      // Uniform rows: every lane broadcasts its two columns of the V mean.
-#pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-        uint4 u;
-        uint32_t* w = reinterpret_cast<uint32_t*>(&u);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int d = c8 * 8 + 2 * e;
+      for (int e = 0; e < 4; ++e) {
+        const int d = c8 * 8 + 2 * e;
+        float a0 = __uint_as_float(ou[d]) * inv, a1 = __uint_as_float(ou[d + 1]) * inv;
+        if (need_uniform) {
           const float u0 = __shfl_sync(0xffffffffu, vm0, d >> 1), u1 = __shfl_sync(0xffffffffu, vm1, d >> 1);
-          w[e] = pack_bf16(u0, u1);
+          if (empty) a0 = u0, a1 = u1;
         }
-        if (empty && t < p.T)
-          *reinterpret_cast<uint4*>(p.o + (((long long)b * p.T + t) * p.H + h) * HD + c8 * 8) = u;
+        w[e] = pack_bf16(a0, a1);
       }
+      if (t < p.T) *reinterpret_cast<uint4*>(orow + c8 * 8) = u;
     }
+    if (t < p.T) p.lse[((long long)b * p.H + h) * p.T + t] = empty ? -INFINITY : M + __log2f(l);
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -1329,6 +1349,7 @@ extern "C" int mfb_attn_fwd(const uint16_t* q, const uint16_t* k, const uint16_t
   if ((st = tc::make_tmap_bf16(&tq, q, (uint64_t)H * HD, (uint64_t)B * T, (uint64_t)H * HD, TQ))) return st;
   if ((st = tc::make_tmap_bf16(&tk, k, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
   if ((st = tc::make_tmap_bf16(&tv, v, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
+  MFB_CHECK_ARG(S <= TF_MAX_TILES * TK, "key length %d above the supported %d", S, TF_MAX_TILES * TK);
   if ((st = set_smem((const void*)attn_fwd_tc_kernel, TF_SMEM))) return st;
   dim3 grid(cdiv(T, TQ), H / 2, B);
   attn_fwd_tc_kernel<<<grid, TF_THREADS, TF_SMEM, s>>>(tq, tk, tv, p);
