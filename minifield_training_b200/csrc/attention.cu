@@ -1176,6 +1176,396 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Backward on tcgen05.
+//
+// CTA = (128 keys, one KV head, batch row); it loops over the group's query
+// heads x live 128-row query tiles ("items"). Warp roles (320 threads):
+//   warp 0      producer: K and V once; per item the Q and dO tiles (TMA, two
+//               stages) and the per-query columns lse, dsum, qid + run table.
+//   warp 1      TMEM owner, single-thread tcgen05.mma issuer.
+//   warps 2-9   softmax-gradient: one key row (TMEM lane) per thread; warps
+//               2-5 take query columns 0-63, warps 6-9 columns 64-127.
+// Per item (q = query tile, all products M = 128):
+//   S^T  = K Q^T        SS, N = 128 -> TMEM [0,128)
+//   dP^T = V dO^T       SS, N = 128 -> TMEM [128,256)
+//   P^T = exp2(S^T * scale*log2e - lse_q) (masked), dS^T = P^T (dP^T - dsum_q):
+//   P^T goes back to TMEM as bf16 pairs in the columns each half has read
+//   ([0,32) and [64,96)); dS^T goes to shared memory in the 128-byte-swizzle
+//   K-major layout (two 64-query atoms of 128 rows).
+//   dV += P^T dO        TS (A = P^T from TMEM), B = dO MN-major -> TMEM [256,320)
+//   dK += dS^T Q        SS, A = dS^T K-major, B = Q MN-major    -> TMEM [320,384)
+//   dQ  = dS K          SS, A = dS^T read MN-major (M = queries), B = K
+//                       MN-major -> TMEM [384,448); the next item's softmax
+//                       warps add it into the FP32 dQ accumulator (vector
+//                       atomics) before touching their own tile.
+// MMAs from one thread run in order, so the next item's S^T / dP^T commit also
+// tells the softmax warps that the previous dV/dK/dQ products are complete.
+// ---------------------------------------------------------------------------
+constexpr int TB_ST = 2;
+constexpr int TB_THREADS = 320;
+constexpr int TB_K_OFF = 0;
+constexpr int TB_V_OFF = 16384;
+constexpr int TB_QD_OFF = 32768;  // stage st: Q at +st*32768, dO at +st*32768+16384
+constexpr int TB_DS_OFF = TB_QD_OFF + TB_ST * 32768;
+constexpr int TB_COL_OFF = TB_DS_OFF + 32768;
+constexpr int TB_COL_STRIDE = 3 * 128 + 32;  // lse[128], dsum[128], qid[128], run table
+constexpr int TB_LIST_OFF = TB_COL_OFF + TB_ST * TB_COL_STRIDE * 4;
+constexpr int TB_BAR_OFF = TB_LIST_OFF + (TF_MAX_TILES + 4) * 4;
+constexpr int TB_SMEM = 1024 + TB_BAR_OFF + 256;
+
+// Run table of equal nonzero ids over a 128-entry tile: rt[0] = count (or -1
+// when an id recurs or there are more than 8 runs), then {id, first, last}.
+// Called by one full warp with its lane's four consecutive ids.
+__device__ __forceinline__ void warp_run_table(const int* v4, int lane, int* rt) {
+  const int prev = __shfl_up_sync(0xffffffffu, v4[3], 1);
+  const int next = __shfl_down_sync(0xffffffffu, v4[0], 1);
+  unsigned sbits = 0, ebits = 0;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int before = e == 0 ? (lane == 0 ? 0 : prev) : v4[e - 1];
+    const int after = e == 3 ? (lane == 31 ? 0 : next) : v4[e + 1];
+    if (v4[e] != 0 && (e + lane == 0 || before != v4[e])) sbits |= 1u << e;
+    if (v4[e] != 0 && ((e == 3 && lane == 31) || after != v4[e])) ebits |= 1u << e;
+  }
+  const int ns = __popc(sbits), ne = __popc(ebits);
+  int incl_s = ns, incl_e = ne;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int ys = __shfl_up_sync(0xffffffffu, incl_s, o), ye = __shfl_up_sync(0xffffffffu, incl_e, o);
+    if (lane >= o) incl_s += ys, incl_e += ye;
+  }
+  const int total = __shfl_sync(0xffffffffu, incl_s, 31);
+  if (total <= TF_MAX_RUNS) {
+    int is = incl_s - ns, ie = incl_e - ne;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (sbits & (1u << e)) {
+        rt[1 + 3 * is] = v4[e];
+        rt[2 + 3 * is] = 4 * lane + e;
+        ++is;
+      }
+      if (ebits & (1u << e)) {
+        rt[3 + 3 * ie] = 4 * lane + e;
+        ++ie;
+      }
+    }
+  }
+  __syncwarp();
+  if (lane == 0) {
+    int cnt = total <= TF_MAX_RUNS ? total : -1;
+    for (int a = 0; cnt > 0 && a < total; ++a)
+      for (int c = a + 1; c < total; ++c)
+        if (rt[1 + 3 * a] == rt[1 + 3 * c]) cnt = -1;
+    rt[0] = cnt;
+  }
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(TB_THREADS, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                       const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const uint32_t sb = smem_u32(smem);
+  const uint32_t bars = sb + TB_BAR_OFF;
+  const uint32_t kv_full = bars;
+  auto qd_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto qd_empty = [&](int s) { return bars + 8u * (1 + TB_ST + s); };
+  const uint32_t s_full = bars + 8u * (1 + 2 * TB_ST);
+  const uint32_t p_full = bars + 8u * (2 + 2 * TB_ST);
+  const uint32_t dq_full = bars + 8u * (3 + 2 * TB_ST);
+  const uint32_t done_bar = bars + 8u * (4 + 2 * TB_ST);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TB_BAR_OFF + 8 * (5 + 2 * TB_ST));
+  int* cols = reinterpret_cast<int*>(smem + TB_COL_OFF);
+  int* list = reinterpret_cast<int*>(smem + TB_LIST_OFF);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int s0 = kt * TK;
+  const int ntq = cdiv(p.T, TQ);
+  const Range krange = range128(p.kr + (long long)b * p.nkb, p.nkb, kt);
+  const Range* qrs = p.qr + (long long)b * p.nqb;
+  int* status = &g_tc_status;
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(kv_full, 1);
+    for (int s = 0; s < TB_ST; ++s) {
+      tc::mbar_init(qd_full(s), 1 + 32);
+      tc::mbar_init(qd_empty(s), 1);
+    }
+    tc::mbar_init(s_full, 1);
+    tc::mbar_init(p_full, 256);
+    tc::mbar_init(dq_full, 1);
+    tc::mbar_init(done_bar, 1);
+    tc::mbar_fence_init();
+  }
+  if (warp == 0) {
+    int count = 0;
+    for (int base = 0; base < ntq; base += 32) {
+      const int i = base + lane;
+      bool live = false, full = false;
+      if (i < ntq) {
+        const Range qr = range128(qrs, p.nqb, i);
+        live = tile_live128(p, qr, krange, i * TQ, s0);
+        full = live && tile_full128(p, qr, krange, i * TQ, s0);
+      }
+      const unsigned bal = __ballot_sync(0xffffffffu, live);
+      if (live) list[1 + count + __popc(bal & ((1u << lane) - 1))] = i | (full ? 1 << 30 : 0);
+      count += __popc(bal);
+    }
+    if (lane == 0) list[0] = count;
+  } else if (warp == 1) {
+    tc::tmem_alloc(smem_u32(tmem_slot), 512);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int nlive = list[0];
+  const int nitems = p.G * nlive;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tc::tma_prefetch_desc(&tq);
+      tc::tma_prefetch_desc(&tk);
+      tc::tma_prefetch_desc(&tv);
+      tc::tma_prefetch_desc(&tdo);
+      tc::mbar_expect_tx(kv_full, 2 * 16384);
+      tc::tma_load_2d(sb + TB_K_OFF, &tk, hk * 64, b * p.S + s0, kv_full);
+      tc::tma_load_2d(sb + TB_V_OFF, &tv, hk * 64, b * p.S + s0, kv_full);
+    }
+    for (int it = 0; it < nitems; ++it) {
+      const int st = it % TB_ST;
+      const uint32_t ph = (it / TB_ST) & 1;
+      const int h = hk * p.G + it / nlive;
+      const int q0 = (list[1 + it % nlive] & 0xFFFF) * TQ;
+      if (!tc::mbar_wait(qd_empty(st), ph ^ 1, status, 31)) break;
+      if (lane == 0) {
+        const uint32_t qb_ = sb + TB_QD_OFF + st * 32768;
+        tc::mbar_expect_tx(qd_full(st), 2 * 16384);
+        tc::tma_load_2d(qb_, &tq, h * 64, b * p.T + q0, qd_full(st));
+        tc::tma_load_2d(qb_ + 16384, &tdo, h * 64, b * p.T + q0, qd_full(st));
+      }
+      int* cs = cols + st * TB_COL_STRIDE;
+      float* lse_s = reinterpret_cast<float*>(cs);
+      float* dsum_s = reinterpret_cast<float*>(cs + 128);
+      int* qid_s = cs + 256;
+      int v4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int c = 4 * lane + e;
+        const int t = q0 + c;
+        const long long li = ((long long)b * p.H + h) * p.T + t;
+        float l = INFINITY, d = 0.f;
+        int q = 0;
+        if (t < p.T) {
+          l = p.lse[li];
+          d = p.dsum[li];
+          q = p.qid[(long long)b * p.T + t];
+          if (l == -INFINITY) l = INFINITY;  // a row without valid keys contributes no P
+        }
+        lse_s[c] = l;
+        dsum_s[c] = d;
+        qid_s[c] = q;
+        v4[e] = q;
+      }
+      warp_run_table(v4, lane, cs + 384);
+      tc::mbar_arrive(qd_full(st));
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc_s = tc::idesc_bf16_f32(128, 128, 0, 0);
+      const uint32_t idesc_kn = tc::idesc_bf16_f32(128, 64, 0, 1);  // K-major A, MN-major B
+      const uint32_t idesc_nn = tc::idesc_bf16_f32(128, 64, 1, 1);  // MN-major A and B
+      const uint32_t st_t = tmem, dp_t = tmem + 128, dv_t = tmem + 256, dk_t = tmem + 320, dq_t = tmem + 384;
+      const uint32_t kb_ = sb + TB_K_OFF, vb_ = sb + TB_V_OFF, ds_ = sb + TB_DS_OFF;
+      bool ok = tc::mbar_wait(kv_full, 0, status, 32);
+      tc::tc_fence_after();
+      for (int it = 0; ok && it < nitems; ++it) {
+        const int st = it % TB_ST;
+        if (!(ok = tc::mbar_wait(qd_full(st), (it / TB_ST) & 1, status, 33))) break;
+        tc::tc_fence_after();
+        const uint32_t qb_ = sb + TB_QD_OFF + st * 32768, dob_ = qb_ + 16384;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc::mma_bf16(st_t, tc::smem_desc_sw128(kb_ + k * 32, 16, 1024), tc::smem_desc_sw128(qb_ + k * 32, 16, 1024),
+                       idesc_s, k > 0 ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc::mma_bf16(dp_t, tc::smem_desc_sw128(vb_ + k * 32, 16, 1024), tc::smem_desc_sw128(dob_ + k * 32, 16, 1024),
+                       idesc_s, k > 0 ? 1u : 0u);
+        tc::mma_commit(s_full);
+        if (!(ok = tc::mbar_wait(p_full, it & 1, status, 34))) break;
+        tc::tc_fence_after();
+        const uint32_t acc0 = it > 0 ? 1u : 0u;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          tc::mma_bf16_ts(dv_t, st_t + 64 * (k >> 2) + 8 * (k & 3), tc::smem_desc_sw128(dob_ + k * 2048, 8192, 1024),
+                          idesc_kn, (acc0 | k) != 0 ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          tc::mma_bf16(dk_t, tc::smem_desc_sw128(ds_ + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
+                       tc::smem_desc_sw128(qb_ + k * 2048, 8192, 1024), idesc_kn, (acc0 | k) != 0 ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          tc::mma_bf16(dq_t, tc::smem_desc_sw128(ds_ + k * 2048, 16384, 1024),
+                       tc::smem_desc_sw128(kb_ + k * 2048, 8192, 1024), idesc_nn, k > 0 ? 1u : 0u);
+        tc::mma_commit(qd_empty(st));
+      }
+      tc::mma_commit(dq_full);
+      tc::mma_commit(done_bar);
+      tc::mbar_wait(done_bar, 0, status, 35);
+    }
+  } else {
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const int r = quarter * 32 + lane;
+    const int s = s0 + r;
+    const int kid_row = s < p.S ? p.kid[(long long)b * p.S + s] : 0;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t st_t = tmem + lane_off, dp_t = tmem + lane_off + 128;
+    const uint32_t dv_t = tmem + lane_off + 256, dk_t = tmem + lane_off + 320, dq_t = tmem + lane_off + 384;
+    uint8_t* ds_row = smem + TB_DS_OFF + half * 16384 + r * 128;
+    const float sl2 = p.scale_log2;
+    const uint32_t NEG = 0xFF800000u;
+    int prev_q0 = -1, prev_h = 0;
+    bool ok = true;
+
+    // Adds the previous item's dQ tile (this thread: one query row, 32 of
+    // its 64 columns) into the FP32 accumulator.
+    auto flush_dq = [&]() {
+      uint32_t v[32];
+      tc::tmem_ld_32x32b_x32(dq_t + half * 32, v);
+      tc::tmem_ld_wait();
+      const int q = prev_q0 + r;
+      if (q < p.T) {
+        float4* dst = reinterpret_cast<float4*>(p.dq_acc + (((long long)b * p.T + q) * p.H + prev_h) * HD + half * 32);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          atomicAdd(dst + e, make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
+                                         __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3])));
+      }
+    };
+
+    for (int it = 0; it < nitems; ++it) {
+      const int st = it % TB_ST;
+      const int entry = list[1 + it % nlive];
+      const int q0 = (entry & 0xFFFF) * TQ;
+      const bool full = (entry >> 30) & 1;
+      const int h = hk * p.G + it / nlive;
+      if (!(ok = tc::mbar_wait(s_full, it & 1, status, 36))) break;
+      if (!(ok = tc::mbar_wait(qd_full(st), (it / TB_ST) & 1, status, 37))) break;
+      tc::tc_fence_after();
+      if (it > 0) flush_dq();
+      const int* cs = cols + st * TB_COL_STRIDE;
+      const float* lse_s = reinterpret_cast<const float*>(cs);
+      const float* dsum_s = reinterpret_cast<const float*>(cs + 128);
+      // Valid query columns of this key row: an interval from the run table
+      // (or per-query ids), cut by causality (t >= s - offset).
+      uint32_t vm[2] = {0xFFFFFFFFu, 0xFFFFFFFFu};
+      if (!full) {
+        const int* rt = cs + 384;
+        const int nr = rt[0];
+        int lo = 1, hi = 0;
+        if (nr >= 0) {
+          for (int q = 0; q < nr; ++q)
+            if (rt[1 + 3 * q] == kid_row) lo = rt[2 + 3 * q], hi = rt[3 + 3 * q];
+        } else {
+          lo = 0, hi = TQ - 1;
+        }
+        if (p.causal) lo = max(lo, s - p.offset - q0);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int base = half * 64 + c * 32;
+          const int a0 = max(lo - base, 0), b0 = min(hi - base, 31);
+          vm[c] = a0 > b0 ? 0u : ((0xFFFFFFFFu >> (31 - b0)) & (0xFFFFFFFFu << a0));
+          if (nr < 0) {
+            uint32_t bits = 0;
+            for (int i = 0; i < 32; ++i) bits |= (kid_row != 0 && cs[256 + base + i] == kid_row) ? 1u << i : 0u;
+            vm[c] &= bits;
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int base = half * 64 + c * 32;
+        uint32_t sx[32], dx[32];
+        tc::tmem_ld_32x32b_x32(st_t + base, sx);
+        tc::tmem_ld_32x32b_x32(dp_t + base, dx);
+        tc::tmem_ld_wait();
+        uint32_t pk[16], dk4[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float2 lse2 = *reinterpret_cast<const float2*>(lse_s + base + i);
+          const float2 ds2 = *reinterpret_cast<const float2*>(dsum_s + base + i);
+          float p0 = ex2(fmaf(__uint_as_float(sx[i]), sl2, -lse2.x));
+          float p1 = ex2(fmaf(__uint_as_float(sx[i + 1]), sl2, -lse2.y));
+          p0 = (vm[c] >> i) & 1u ? p0 : 0.f;
+          p1 = (vm[c] >> (i + 1)) & 1u ? p1 : 0.f;
+          const float d0 = p0 * (__uint_as_float(dx[i]) - ds2.x);
+          const float d1 = p1 * (__uint_as_float(dx[i + 1]) - ds2.y);
+          pk[i >> 1] = pack_bf16(p0, p1);
+          dk4[i >> 1] = pack_bf16(d0, d1);
+        }
+        (void)NEG;
+        tc::tmem_st_32x32b_x16(st_t + half * 64 + c * 16, pk);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int j = c * 4 + jj;  // 16-byte chunk within this half's 128-byte row
+          *reinterpret_cast<uint4*>(ds_row + ((j ^ (r & 7)) << 4)) =
+              make_uint4(dk4[4 * jj], dk4[4 * jj + 1], dk4[4 * jj + 2], dk4[4 * jj + 3]);
+        }
+      }
+      tc::tmem_st_wait();
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      tc::mbar_arrive(p_full);
+      prev_q0 = q0;
+      prev_h = h;
+    }
+    if (ok && tc::mbar_wait(dq_full, 0, status, 38)) {
+      tc::tc_fence_after();
+      if (nitems > 0) flush_dq();
+      // dK (times the logit scale) and dV (plus the uniform-row term) for this key row.
+      uint32_t kv[32], vv[32];
+      tc::tmem_ld_32x32b_x32(dk_t + half * 32, kv);
+      tc::tmem_ld_32x32b_x32(dv_t + half * 32, vv);
+      tc::tmem_ld_wait();
+      if (s < p.S) {
+        const long long off = (((long long)b * p.S + s) * p.Hk + hk) * HD + half * 32;
+        const float* uv = p.uvec + ((long long)b * p.Hk + hk) * HD + half * 32;
+        const bool uni = p.policy == MFB_EMPTY_UNIFORM;
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          uint4 a, c;
+          uint32_t* aw = reinterpret_cast<uint32_t*>(&a);
+          uint32_t* cw = reinterpret_cast<uint32_t*>(&c);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int d = c8 * 8 + 2 * e;
+            const float k0 = nitems > 0 ? __uint_as_float(kv[d]) * p.scale : 0.f;
+            const float k1 = nitems > 0 ? __uint_as_float(kv[d + 1]) * p.scale : 0.f;
+            float v0 = nitems > 0 ? __uint_as_float(vv[d]) : 0.f;
+            float v1 = nitems > 0 ? __uint_as_float(vv[d + 1]) : 0.f;
+            if (uni) v0 += uv[d], v1 += uv[d + 1];
+            aw[e] = pack_bf16(k0, k1);
+            cw[e] = pack_bf16(v0, v1);
+          }
+          *reinterpret_cast<uint4*>(p.dk + off + c8 * 8) = a;
+          *reinterpret_cast<uint4*>(p.dv + off + c8 * 8) = c;
+        }
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
 struct Workspace {
@@ -1387,9 +1777,18 @@ extern "C" int mfb_attn_bwd(const uint16_t* q, const uint16_t* k, const uint16_t
   const long long rows = (long long)B * T * H;
   attn_bwd_pre_kernel<<<(unsigned)((rows + 31) / 32), 256, 0, s>>>(p);
   MFB_LAUNCH_CHECK("attention backward preprocess");
-  if ((st = set_smem((const void*)attn_bwd_main_kernel, BWD_SMEM))) return st;
-  dim3 grid(p.nkb, Hk, B);
-  attn_bwd_main_kernel<<<grid, BWD_THREADS, BWD_SMEM, s>>>(p);
+  MFB_CHECK_ARG(T <= TF_MAX_TILES * TQ, "query length %d above the supported %d", T, TF_MAX_TILES * TQ);
+  MFB_CHECK_ARG(((uintptr_t)q & 15) == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0 &&
+                    ((uintptr_t)d_o & 15) == 0,
+                "q/k/v/d_o must be 16-byte aligned");
+  CUtensorMap tq, tk, tv, tdo;
+  if ((st = tc::make_tmap_bf16(&tq, q, (uint64_t)H * HD, (uint64_t)B * T, (uint64_t)H * HD, TQ))) return st;
+  if ((st = tc::make_tmap_bf16(&tdo, d_o, (uint64_t)H * HD, (uint64_t)B * T, (uint64_t)H * HD, TQ))) return st;
+  if ((st = tc::make_tmap_bf16(&tk, k, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
+  if ((st = tc::make_tmap_bf16(&tv, v, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
+  if ((st = set_smem((const void*)attn_bwd_tc_kernel, TB_SMEM))) return st;
+  dim3 grid(cdiv(S, TK), Hk, B);
+  attn_bwd_tc_kernel<<<grid, TB_THREADS, TB_SMEM, s>>>(tq, tk, tv, tdo, p);
   MFB_LAUNCH_CHECK("attention backward");
   const long long n4 = (long long)B * T * H * HD / 4;
   dq_convert_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, s>>>(w.dq_acc, reinterpret_cast<__nv_bfloat16*>(dq), n4,
