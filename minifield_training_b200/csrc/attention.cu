@@ -192,7 +192,8 @@ constexpr int FWD_SMEM = FWD_HPB * 8192 + 4 * 8192 + 2 * 64 * 4 + 1024;
 
 __global__ void __launch_bounds__(FWD_THREADS) attn_fwd_kernel(Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  // Offset from the __shared__ array itself so accesses keep the shared state space.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sQ = smem_u32(smem);
   const uint32_t sK = sQ + FWD_HPB * 8192;
   const uint32_t sV = sK + 2 * 8192;
@@ -476,7 +477,8 @@ constexpr int BWD_SMEM = 8192 * 7 + 2 * 64 * 4 * 3 + 1024;
 
 __global__ void __launch_bounds__(BWD_THREADS) attn_bwd_main_kernel(Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  // Offset from the __shared__ array itself so accesses keep the shared state space.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sK = smem_u32(smem);
   const uint32_t sV = sK + 8192;
   const uint32_t sQ = sK + 2 * 8192;    // [2]
@@ -813,7 +815,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                        const __grid_constant__ CUtensorMap tv, Params p) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  // Offset from the __shared__ array itself so accesses keep the shared state space.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sb = smem_u32(smem);
   const uint32_t bars = sb + TF_BAR_OFF;
   const uint32_t q_full = bars;
@@ -1179,35 +1182,36 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 // Backward on tcgen05.
 //
 // CTA = (128 keys, one KV head, batch row); it loops over the group's query
-// heads x live 128-row query tiles ("items"). Warp roles (320 threads):
-//   warp 0      producer: K and V once; per item the Q and dO tiles (TMA, two
-//               stages) and the per-query columns lse, dsum, qid + run table.
+// heads x live 128-row query tiles ("items"), each split into two 64-query
+// sub-items so the tensor core works on one sub-item while the
+// softmax-gradient warps work on the other. Warp roles (448 threads):
+//   warp 0      producer: K and V once; per item the Q and dO tiles (TMA, three
+//               stages) and the per-query lse, dsum, qid and run table.
 //   warp 1      TMEM owner, single-thread tcgen05.mma issuer.
-//   warps 2-9   softmax-gradient: one key row (TMEM lane) per thread; warps
-//               2-5 take query columns 0-63, warps 6-9 columns 64-127.
-// Per item (q = query tile, all products M = 128):
-//   S^T  = K Q^T        SS, N = 128 -> TMEM [0,128)
-//   dP^T = V dO^T       SS, N = 128 -> TMEM [128,256)
-//   P^T = exp2(S^T * scale*log2e - lse_q) (masked), dS^T = P^T (dP^T - dsum_q):
-//   P^T goes back to TMEM as bf16 pairs in the columns each half has read
-//   ([0,32) and [64,96)); dS^T goes to shared memory in the 128-byte-swizzle
-//   K-major layout (two 64-query atoms of 128 rows).
-//   dV += P^T dO        TS (A = P^T from TMEM), B = dO MN-major -> TMEM [256,320)
-//   dK += dS^T Q        SS, A = dS^T K-major, B = Q MN-major    -> TMEM [320,384)
-//   dQ  = dS K          SS, A = dS^T read MN-major (M = queries), B = K
-//                       MN-major -> TMEM [384,448); the next item's softmax
-//                       warps add it into the FP32 dQ accumulator (vector
-//                       atomics) before touching their own tile.
-// MMAs from one thread run in order, so the next item's S^T / dP^T commit also
-// tells the softmax warps that the previous dV/dK/dQ products are complete.
+//   warps 2-9   softmax-gradient: one key row (TMEM lane) per thread, 32 of
+//               the sub-item's 64 query columns per warp (two warps per lane
+//               quarter).
+//   warps 10-13 dQ flush: add each item's dQ tile into the FP32 accumulator
+//               (vector reductions) while the next item is computed.
+// Products (M = 128 keys unless noted), issued in the order
+//   S/dP(j), [P ready j-1] dV/dK(j-1), [dQ tile free] dQ(item of j-1), S/dP(j+1)...
+//   S^T_j  = K Q_j^T        N = 64 -> TMEM buffer j%2 [0,64)
+//   dP^T_j = V dO_j^T       N = 64 -> TMEM buffer j%2 [64,128)
+//   P^T_j (bf16) goes back into its warp's own consumed S^T columns; dS^T_j
+//   (bf16) into shared memory (128-byte swizzle, item parity buffer, 64-query
+//   atom per sub-item).
+//   dV += P^T_j dO_j        TS (A from TMEM) -> TMEM [256,320)
+//   dK += dS^T_j Q_j        SS               -> TMEM [320,384)
+//   dQ  = dS K              SS, A = the item's dS^T read MN-major (M = 128
+//                           queries), after both sub-items -> TMEM [384,448)
 // ---------------------------------------------------------------------------
-constexpr int TB_ST = 2;
-constexpr int TB_THREADS = 320;
+constexpr int TB_ST = 3;
+constexpr int TB_THREADS = 448;
 constexpr int TB_K_OFF = 0;
 constexpr int TB_V_OFF = 16384;
 constexpr int TB_QD_OFF = 32768;  // stage st: Q at +st*32768, dO at +st*32768+16384
-constexpr int TB_DS_OFF = TB_QD_OFF + TB_ST * 32768;
-constexpr int TB_COL_OFF = TB_DS_OFF + 32768;
+constexpr int TB_DS_OFF = TB_QD_OFF + TB_ST * 32768;  // two 32 KB dS^T buffers (item parity)
+constexpr int TB_COL_OFF = TB_DS_OFF + 2 * 32768;
 constexpr int TB_COL_STRIDE = 3 * 128 + 32;  // lse[128], dsum[128], qid[128], run table
 constexpr int TB_LIST_OFF = TB_COL_OFF + TB_ST * TB_COL_STRIDE * 4;
 constexpr int TB_BAR_OFF = TB_LIST_OFF + (TF_MAX_TILES + 4) * 4;
@@ -1265,17 +1269,19 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                        const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo, Params p) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  // Offset from the __shared__ array itself so accesses keep the shared state space.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sb = smem_u32(smem);
   const uint32_t bars = sb + TB_BAR_OFF;
   const uint32_t kv_full = bars;
   auto qd_full = [&](int s) { return bars + 8u * (1 + s); };
   auto qd_empty = [&](int s) { return bars + 8u * (1 + TB_ST + s); };
-  const uint32_t s_full = bars + 8u * (1 + 2 * TB_ST);
-  const uint32_t p_full = bars + 8u * (2 + 2 * TB_ST);
-  const uint32_t dq_full = bars + 8u * (3 + 2 * TB_ST);
-  const uint32_t done_bar = bars + 8u * (4 + 2 * TB_ST);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TB_BAR_OFF + 8 * (5 + 2 * TB_ST));
+  auto s_full = [&](int u) { return bars + 8u * (1 + 2 * TB_ST + u); };
+  auto p_full = [&](int u) { return bars + 8u * (3 + 2 * TB_ST + u); };
+  const uint32_t dq_full = bars + 8u * (5 + 2 * TB_ST);
+  const uint32_t dq_free = bars + 8u * (6 + 2 * TB_ST);
+  const uint32_t done_bar = bars + 8u * (7 + 2 * TB_ST);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TB_BAR_OFF + 8 * (8 + 2 * TB_ST));
   int* cols = reinterpret_cast<int*>(smem + TB_COL_OFF);
   int* list = reinterpret_cast<int*>(smem + TB_LIST_OFF);
 
@@ -1293,9 +1299,12 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       tc::mbar_init(qd_full(s), 1 + 32);
       tc::mbar_init(qd_empty(s), 1);
     }
-    tc::mbar_init(s_full, 1);
-    tc::mbar_init(p_full, 256);
+    for (int u = 0; u < 2; ++u) {
+      tc::mbar_init(s_full(u), 1);
+      tc::mbar_init(p_full(u), 256);
+    }
     tc::mbar_init(dq_full, 1);
+    tc::mbar_init(dq_free, 128);
     tc::mbar_init(done_bar, 1);
     tc::mbar_fence_init();
   }
@@ -1375,94 +1384,92 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc_s = tc::idesc_bf16_f32(128, 128, 0, 0);
+      const uint32_t idesc_s = tc::idesc_bf16_f32(128, 64, 0, 0);
       const uint32_t idesc_kn = tc::idesc_bf16_f32(128, 64, 0, 1);  // K-major A, MN-major B
       const uint32_t idesc_nn = tc::idesc_bf16_f32(128, 64, 1, 1);  // MN-major A and B
-      const uint32_t st_t = tmem, dp_t = tmem + 128, dv_t = tmem + 256, dk_t = tmem + 320, dq_t = tmem + 384;
-      const uint32_t kb_ = sb + TB_K_OFF, vb_ = sb + TB_V_OFF, ds_ = sb + TB_DS_OFF;
+      const uint32_t dv_t = tmem + 256, dk_t = tmem + 320, dq_t = tmem + 384;
+      const uint32_t kb_ = sb + TB_K_OFF, vb_ = sb + TB_V_OFF;
+      // K-major K and V descriptors do not change; the per-step advance is
+      // added to the start-address field (bits 0-13, in 16-byte units).
+      const uint64_t kdesc = tc::smem_desc_sw128(kb_, 16, 1024), vdesc = tc::smem_desc_sw128(vb_, 16, 1024);
+      const uint64_t kdesc_mn = tc::smem_desc_sw128(kb_, 8192, 1024);
       bool ok = tc::mbar_wait(kv_full, 0, status, 32);
       tc::tc_fence_after();
-      for (int it = 0; ok && it < nitems; ++it) {
-        const int st = it % TB_ST;
-        if (!(ok = tc::mbar_wait(qd_full(st), (it / TB_ST) & 1, status, 33))) break;
+      const int nsub = 2 * nitems;
+      // Issues dV/dK of sub-item j (its P^T is ready) and, after the second
+      // half of an item, that item's dQ; then frees the item's Q/dO stage.
+      auto finish = [&](int j) -> bool {
+        const int it = j >> 1, hf = j & 1, u = j & 1, st = it % TB_ST;
+        if (!tc::mbar_wait(p_full(u), (j >> 1) & 1, status, 34)) return false;
         tc::tc_fence_after();
-        const uint32_t qb_ = sb + TB_QD_OFF + st * 32768, dob_ = qb_ + 16384;
+        const uint32_t qb_ = sb + TB_QD_OFF + st * 32768 + hf * 8192, dob_ = qb_ + 16384;
+        const uint32_t ds_ = sb + TB_DS_OFF + (it & 1) * 32768;
+        const uint32_t s_t = tmem + u * 128;
+        const uint64_t qd_mn = tc::smem_desc_sw128(qb_, 8192, 1024), dod_mn = tc::smem_desc_sw128(dob_, 8192, 1024);
+        const uint64_t dsd = tc::smem_desc_sw128(ds_ + hf * 16384, 16, 1024);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          tc::mma_bf16(st_t, tc::smem_desc_sw128(kb_ + k * 32, 16, 1024), tc::smem_desc_sw128(qb_ + k * 32, 16, 1024),
-                       idesc_s, k > 0 ? 1u : 0u);
+          tc::mma_bf16_ts(dv_t, s_t + (k >> 1) * 32 + (k & 1) * 8, dod_mn + (uint64_t)(k * 2048 >> 4), idesc_kn,
+                          (j | k) != 0 ? 1u : 0u);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          tc::mma_bf16(dp_t, tc::smem_desc_sw128(vb_ + k * 32, 16, 1024), tc::smem_desc_sw128(dob_ + k * 32, 16, 1024),
-                       idesc_s, k > 0 ? 1u : 0u);
-        tc::mma_commit(s_full);
-        if (!(ok = tc::mbar_wait(p_full, it & 1, status, 34))) break;
-        tc::tc_fence_after();
-        const uint32_t acc0 = it > 0 ? 1u : 0u;
+          tc::mma_bf16(dk_t, dsd + (uint64_t)(k * 32 >> 4), qd_mn + (uint64_t)(k * 2048 >> 4), idesc_kn,
+                       (j | k) != 0 ? 1u : 0u);
+        if (hf == 1) {
+          tc::mma_commit(qd_empty(st));
+          if (it > 0 && !tc::mbar_wait(dq_free, (it - 1) & 1, status, 39)) return false;
+          tc::tc_fence_after();
+          const uint64_t dsn = tc::smem_desc_sw128(ds_, 16384, 1024);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          tc::mma_bf16_ts(dv_t, st_t + 64 * (k >> 2) + 8 * (k & 3), tc::smem_desc_sw128(dob_ + k * 2048, 8192, 1024),
-                          idesc_kn, (acc0 | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < 8; ++k)
+            tc::mma_bf16(dq_t, dsn + (uint64_t)(k * 2048 >> 4), kdesc_mn + (uint64_t)(k * 2048 >> 4), idesc_nn,
+                         k > 0 ? 1u : 0u);
+          tc::mma_commit(dq_full);
+        }
+        return true;
+      };
+      for (int j = 0; ok && j < nsub; ++j) {
+        const int it = j >> 1, hf = j & 1, u = j & 1, st = it % TB_ST;
+        if (hf == 0) {
+          if (!(ok = tc::mbar_wait(qd_full(st), (it / TB_ST) & 1, status, 33))) break;
+          tc::tc_fence_after();
+        }
+        const uint32_t qb_ = sb + TB_QD_OFF + st * 32768 + hf * 8192, dob_ = qb_ + 16384;
+        const uint32_t s_t = tmem + u * 128, dp_t = s_t + 64;
+        const uint64_t qd = tc::smem_desc_sw128(qb_, 16, 1024), dod = tc::smem_desc_sw128(dob_, 16, 1024);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          tc::mma_bf16(dk_t, tc::smem_desc_sw128(ds_ + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
-                       tc::smem_desc_sw128(qb_ + k * 2048, 8192, 1024), idesc_kn, (acc0 | k) != 0 ? 1u : 0u);
+        for (int k = 0; k < 4; ++k)
+          tc::mma_bf16(s_t, kdesc + (uint64_t)(k * 32 >> 4), qd + (uint64_t)(k * 32 >> 4), idesc_s, k > 0 ? 1u : 0u);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          tc::mma_bf16(dq_t, tc::smem_desc_sw128(ds_ + k * 2048, 16384, 1024),
-                       tc::smem_desc_sw128(kb_ + k * 2048, 8192, 1024), idesc_nn, k > 0 ? 1u : 0u);
-        tc::mma_commit(qd_empty(st));
+        for (int k = 0; k < 4; ++k)
+          tc::mma_bf16(dp_t, vdesc + (uint64_t)(k * 32 >> 4), dod + (uint64_t)(k * 32 >> 4), idesc_s, k > 0 ? 1u : 0u);
+        tc::mma_commit(s_full(u));
+        if (j > 0 && !(ok = finish(j - 1))) break;
       }
-      tc::mma_commit(dq_full);
+      if (ok && nsub > 0) finish(nsub - 1);
       tc::mma_commit(done_bar);
       tc::mbar_wait(done_bar, 0, status, 35);
     }
-  } else {
-    const int quarter = warp & 3, half = (warp - 2) >> 2;
+  } else if (warp < 10) {
+    const int quarter = warp & 3, wh = (warp - 2) >> 2;  // wh: which 32 of the sub-item's 64 columns
     const int r = quarter * 32 + lane;
     const int s = s0 + r;
     const int kid_row = s < p.S ? p.kid[(long long)b * p.S + s] : 0;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t st_t = tmem + lane_off, dp_t = tmem + lane_off + 128;
-    const uint32_t dv_t = tmem + lane_off + 256, dk_t = tmem + lane_off + 320, dq_t = tmem + lane_off + 384;
-    uint8_t* ds_row = smem + TB_DS_OFF + half * 16384 + r * 128;
     const float sl2 = p.scale_log2;
-    const uint32_t NEG = 0xFF800000u;
-    int prev_q0 = -1, prev_h = 0;
     bool ok = true;
-
-    // Adds the previous item's dQ tile (this thread: one query row, 32 of
-    // its 64 columns) into the FP32 accumulator.
-    auto flush_dq = [&]() {
-      uint32_t v[32];
-      tc::tmem_ld_32x32b_x32(dq_t + half * 32, v);
-      tc::tmem_ld_wait();
-      const int q = prev_q0 + r;
-      if (q < p.T) {
-        float4* dst = reinterpret_cast<float4*>(p.dq_acc + (((long long)b * p.T + q) * p.H + prev_h) * HD + half * 32);
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          atomicAdd(dst + e, make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
-                                         __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3])));
-      }
-    };
-
-    for (int it = 0; it < nitems; ++it) {
-      const int st = it % TB_ST;
+    const int nsub = 2 * nitems;
+    for (int j = 0; j < nsub; ++j) {
+      const int it = j >> 1, hf = j & 1, u = j & 1, st = it % TB_ST;
       const int entry = list[1 + it % nlive];
       const int q0 = (entry & 0xFFFF) * TQ;
       const bool full = (entry >> 30) & 1;
-      const int h = hk * p.G + it / nlive;
-      if (!(ok = tc::mbar_wait(s_full, it & 1, status, 36))) break;
-      if (!(ok = tc::mbar_wait(qd_full(st), (it / TB_ST) & 1, status, 37))) break;
+      if (!(ok = tc::mbar_wait(s_full(u), (j >> 1) & 1, status, 36))) break;
+      if (hf == 0 && !(ok = tc::mbar_wait(qd_full(st), (it / TB_ST) & 1, status, 37))) break;
       tc::tc_fence_after();
-      if (it > 0) flush_dq();
       const int* cs = cols + st * TB_COL_STRIDE;
-      const float* lse_s = reinterpret_cast<const float*>(cs);
-      const float* dsum_s = reinterpret_cast<const float*>(cs + 128);
-      // Valid query columns of this key row: an interval from the run table
-      // (or per-query ids), cut by causality (t >= s - offset).
-      uint32_t vm[2] = {0xFFFFFFFFu, 0xFFFFFFFFu};
+      const int cbase = hf * 64 + wh * 32;  // this warp's 32 query columns within the item
+      uint32_t vm = 0xFFFFFFFFu;
       if (!full) {
         const int* rt = cs + 384;
         const int nr = rt[0];
@@ -1474,66 +1481,64 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
           lo = 0, hi = TQ - 1;
         }
         if (p.causal) lo = max(lo, s - p.offset - q0);
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int base = half * 64 + c * 32;
-          const int a0 = max(lo - base, 0), b0 = min(hi - base, 31);
-          vm[c] = a0 > b0 ? 0u : ((0xFFFFFFFFu >> (31 - b0)) & (0xFFFFFFFFu << a0));
-          if (nr < 0) {
-            uint32_t bits = 0;
-            for (int i = 0; i < 32; ++i) bits |= (kid_row != 0 && cs[256 + base + i] == kid_row) ? 1u << i : 0u;
-            vm[c] &= bits;
-          }
+        const int a0 = max(lo - cbase, 0), b0 = min(hi - cbase, 31);
+        vm = a0 > b0 ? 0u : ((0xFFFFFFFFu >> (31 - b0)) & (0xFFFFFFFFu << a0));
+        if (nr < 0) {
+          uint32_t bits = 0;
+          for (int i = 0; i < 32; ++i) bits |= (kid_row != 0 && cs[256 + cbase + i] == kid_row) ? 1u << i : 0u;
+          vm &= bits;
         }
       }
+      const uint32_t s_t = tmem + lane_off + u * 128 + wh * 32, dp_t = tmem + lane_off + u * 128 + 64 + wh * 32;
+      uint32_t sx[32], dx[32];
+      tc::tmem_ld_32x32b_x32(s_t, sx);
+      tc::tmem_ld_32x32b_x32(dp_t, dx);
+      tc::tmem_ld_wait();
+      const float* lse_s = reinterpret_cast<const float*>(cs) + cbase;
+      const float* dsum_s = reinterpret_cast<const float*>(cs + 128) + cbase;
+      uint32_t pk[16], dk4[16];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int base = half * 64 + c * 32;
-        uint32_t sx[32], dx[32];
-        tc::tmem_ld_32x32b_x32(st_t + base, sx);
-        tc::tmem_ld_32x32b_x32(dp_t + base, dx);
-        tc::tmem_ld_wait();
-        uint32_t pk[16], dk4[16];
+      for (int i = 0; i < 32; i += 4) {
+        const float4 l4 = *reinterpret_cast<const float4*>(lse_s + i);
+        const float4 d4 = *reinterpret_cast<const float4*>(dsum_s + i);
+        const float ls[4] = {l4.x, l4.y, l4.z, l4.w}, dsm[4] = {d4.x, d4.y, d4.z, d4.w};
+        float pv[4], dv4[4];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float2 lse2 = *reinterpret_cast<const float2*>(lse_s + base + i);
-          const float2 ds2 = *reinterpret_cast<const float2*>(dsum_s + base + i);
-          float p0 = ex2(fmaf(__uint_as_float(sx[i]), sl2, -lse2.x));
-          float p1 = ex2(fmaf(__uint_as_float(sx[i + 1]), sl2, -lse2.y));
-          p0 = (vm[c] >> i) & 1u ? p0 : 0.f;
-          p1 = (vm[c] >> (i + 1)) & 1u ? p1 : 0.f;
-          const float d0 = p0 * (__uint_as_float(dx[i]) - ds2.x);
-          const float d1 = p1 * (__uint_as_float(dx[i + 1]) - ds2.y);
-          pk[i >> 1] = pack_bf16(p0, p1);
-          dk4[i >> 1] = pack_bf16(d0, d1);
+        for (int e = 0; e < 4; ++e) {
+          const float pe = ex2(fmaf(__uint_as_float(sx[i + e]), sl2, -ls[e]));
+          pv[e] = (vm >> (i + e)) & 1u ? pe : 0.f;
+          dv4[e] = pv[e] * (__uint_as_float(dx[i + e]) - dsm[e]);
         }
-        (void)NEG;
-        tc::tmem_st_32x32b_x16(st_t + half * 64 + c * 16, pk);
+        pk[i >> 1] = pack_bf16(pv[0], pv[1]);
+        pk[(i >> 1) + 1] = pack_bf16(pv[2], pv[3]);
+        dk4[i >> 1] = pack_bf16(dv4[0], dv4[1]);
+        dk4[(i >> 1) + 1] = pack_bf16(dv4[2], dv4[3]);
+      }
+      // P^T into the first 16 of this warp's own 32 consumed S^T columns.
+      tc::tmem_st_32x32b_x16(s_t, pk);
+      uint8_t* ds_row = smem + TB_DS_OFF + (it & 1) * 32768 + hf * 16384 + r * 128;
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const int j = c * 4 + jj;  // 16-byte chunk within this half's 128-byte row
-          *reinterpret_cast<uint4*>(ds_row + ((j ^ (r & 7)) << 4)) =
-              make_uint4(dk4[4 * jj], dk4[4 * jj + 1], dk4[4 * jj + 2], dk4[4 * jj + 3]);
-        }
+      for (int jj = 0; jj < 4; ++jj) {
+        const int c16 = wh * 4 + jj;  // 16-byte chunk of the 64-query atom row
+        *reinterpret_cast<uint4*>(ds_row + ((c16 ^ (r & 7)) << 4)) =
+            make_uint4(dk4[4 * jj], dk4[4 * jj + 1], dk4[4 * jj + 2], dk4[4 * jj + 3]);
       }
       tc::tmem_st_wait();
       tc::fence_proxy_async_smem();
       tc::tc_fence_before();
-      tc::mbar_arrive(p_full);
-      prev_q0 = q0;
-      prev_h = h;
+      tc::mbar_arrive(p_full(u));
     }
-    if (ok && tc::mbar_wait(dq_full, 0, status, 38)) {
+    // Epilogue: after the last products, dK (times the logit scale) and dV
+    // (plus the uniform-row term) for this key row, this warp's 32 columns.
+    if (ok && tc::mbar_wait(done_bar, 0, status, 38)) {
       tc::tc_fence_after();
-      if (nitems > 0) flush_dq();
-      // dK (times the logit scale) and dV (plus the uniform-row term) for this key row.
       uint32_t kv[32], vv[32];
-      tc::tmem_ld_32x32b_x32(dk_t + half * 32, kv);
-      tc::tmem_ld_32x32b_x32(dv_t + half * 32, vv);
+      tc::tmem_ld_32x32b_x32(tmem + lane_off + 320 + wh * 32, kv);
+      tc::tmem_ld_32x32b_x32(tmem + lane_off + 256 + wh * 32, vv);
       tc::tmem_ld_wait();
       if (s < p.S) {
-        const long long off = (((long long)b * p.S + s) * p.Hk + hk) * HD + half * 32;
-        const float* uv = p.uvec + ((long long)b * p.Hk + hk) * HD + half * 32;
+        const long long off = (((long long)b * p.S + s) * p.Hk + hk) * HD + wh * 32;
+        const float* uv = p.uvec + ((long long)b * p.Hk + hk) * HD + wh * 32;
         const bool uni = p.policy == MFB_EMPTY_UNIFORM;
 #pragma unroll
         for (int c8 = 0; c8 < 4; ++c8) {
@@ -1554,6 +1559,30 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
           *reinterpret_cast<uint4*>(p.dk + off + c8 * 8) = a;
           *reinterpret_cast<uint4*>(p.dv + off + c8 * 8) = c;
         }
+      }
+    }
+  } else {
+    // dQ flush warps: query row = TMEM lane, all 64 columns.
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t dq_t = tmem + ((uint32_t)(quarter * 32) << 16) + 384;
+    for (int it = 0; it < nitems; ++it) {
+      if (!tc::mbar_wait(dq_full, it & 1, status, 40)) break;
+      tc::tc_fence_after();
+      const int h = hk * p.G + it / nlive;
+      const int q = (list[1 + it % nlive] & 0xFFFF) * TQ + r;
+      uint32_t v[64];
+      tc::tmem_ld_32x32b_x32(dq_t, v);
+      tc::tmem_ld_32x32b_x32(dq_t + 32, v + 32);
+      tc::tmem_ld_wait();
+      tc::tc_fence_before();
+      tc::mbar_arrive(dq_free);
+      if (q < p.T) {
+        float* dst = p.dq_acc + (((long long)b * p.T + q) * p.H + h) * HD;
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          red_add_v4(dst + 4 * e, __uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
+                     __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
       }
     }
   }

@@ -110,7 +110,8 @@ __device__ __forceinline__ void store_chunk(const Args& a, int row, int col0, co
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, Args args) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  // Offset from the __shared__ array itself so accesses keep the shared state space.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bars = sbase + STAGES * STAGE_BYTES;
   auto full_bar = [&](int s) { return bars + 8u * s; };
