@@ -135,8 +135,11 @@ int mfb_attn_status(int* code);
  * (src/minifield_training/layers/attention.py:309-314).
  * The query attends to slots < valid_length[b] (dense_cached_attention,
  * kernels/attention.py:264-282; valid_length 0 = uniform over all slots).
- * Output o [B,H,D] bf16. Split over the cache length; partials go to the
- * workspace and the last chunk of each row combines them. D must be 64. */
+ * Output o [B,H,D] bf16. The launch is stream-K over all valid positions of
+ * all rows: every CTA takes an equal contiguous share, partials of the rows a
+ * share cuts go to the workspace, and the last CTA of each such row combines
+ * them. The workspace depends on B and H only, not on the capacity.
+ * D must be 64; H/Hk in {1,2,4}; Hk in {1,2,4,8}; B <= 8192. */
 size_t mfb_decode_workspace_size(int B, int capacity, int H, int D);
 int mfb_decode_attn(const uint16_t* q, uint16_t* k_cache, uint16_t* v_cache, const uint16_t* new_k,
                     const uint16_t* new_v, const int32_t* positions, const int32_t* valid_length, uint16_t* o,
@@ -147,11 +150,11 @@ int mfb_decode_attn(const uint16_t* q, uint16_t* k_cache, uint16_t* v_cache, con
  * callers that cannot call cudaMalloc -- work recorded inside a CUDA-graph
  * capture, an XLA FFI custom-call handler that may only touch the buffers it
  * is given, a serving loop that forbids allocation after start-up. Same
- * inputs, outputs and semantics as mfb_decode_attn, but the split-K scratch is
+ * inputs, outputs and semantics as mfb_decode_attn, but the partial scratch is
  * a fixed array of MFB_DECODE_NOALLOC_SCRATCH_BYTES compiled into the library
  * (every GPU that loads the library holds it until the process exits);
- * shapes needing more (mfb_decode_workspace_size > the maximum; config 3,
- * B=64 x capacity 4096 x 16 heads, needs about 4.3 MB) are rejected with
+ * shapes needing more (mfb_decode_workspace_size > the maximum; B=64 rows
+ * of 16 query heads need about 4.6 MB at any capacity) are rejected with
  * MFB_ERR_INVALID. The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress) with that device current; make that first
  * call before any stream capture. Every call on a device shares the one array
