@@ -139,7 +139,8 @@ int mfb_attn_status(int* code);
  * all rows: every CTA takes an equal contiguous share, partials of the rows a
  * share cuts go to the workspace, and the last CTA of each such row combines
  * them. The workspace depends on B and H only, not on the capacity.
- * D must be 64; H/Hk in {1,2,4}; Hk in {1,2,4,8}; B <= 8192. */
+ * D must be 64; H/Hk in {1,2,4}; Hk in {1,2,4,8}; B <= 8192; B x capacity
+ * < 2^31; q, o, the caches and new_k/new_v 16-byte aligned. */
 size_t mfb_decode_workspace_size(int B, int capacity, int H, int D);
 int mfb_decode_attn(const uint16_t* q, uint16_t* k_cache, uint16_t* v_cache, const uint16_t* new_k,
                     const uint16_t* new_v, const int32_t* positions, const int32_t* valid_length, uint16_t* o,

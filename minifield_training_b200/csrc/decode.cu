@@ -12,17 +12,24 @@
 // positions of all KV heads are contiguous (Hk x 128 bytes each).
 //
 // Work split ("stream-K" over positions): the valid positions of all rows,
-// sum_b len_b, are divided into equal contiguous shares, one per CTA (two CTAs
-// per SM); a share is cut at row boundaries into segments. A producer warp
-// streams each segment's K and V through a 3-stage shared-memory ring with
-// per-head 2-D TMA boxes (16 positions x 64 dims, 128-byte swizzle, no
-// multicast), without draining between segments. Eight compute warps (one KV
-// head each) run the scores and P.V on the warp-level tensor-core MMA with the
-// GQA group's query heads as rows -- the kernel is bandwidth-bound, the MMA
-// only removes the per-element conversions and shuffles -- and an FP32 online
-// softmax. Each (CTA, row) segment writes one (m, l, o) partial; the last
-// segment of a row to finish (atomic ticket, no waiting) combines them.
+// sum_b len_b, are divided into equal contiguous shares, one per resident CTA;
+// a share is cut at row boundaries into segments. A producer thread streams
+// each segment's K and V through a 3-stage shared-memory ring, one 3-D TMA box
+// {64 dims, 16 positions, Hk heads} per operand and stage (128-byte swizzle,
+// no multicast), and brings the segment's query row -- and, at the stage that
+// holds the append slot, the new key/value row -- into a side slot of the same
+// stage with bulk copies, so the compute warps issue no global loads. Eight
+// compute warps (one KV head each) run the scores and P.V on the warp-level
+// tensor-core MMA with the GQA group's query heads as rows -- the kernel is
+// bandwidth-bound, the MMA only removes per-element conversions and shuffles --
+// and an FP32 online softmax. A row that lies inside one share is written
+// directly. Only the first and last row of a share can be cut; their (m, l, o)
+// partials go to the workspace, and once the CTA has finished all its stages
+// it takes one ticket per cut row; the last CTA of a row (atomic ticket, no
+// waiting) combines its partials.
 #include <math.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "tc.cuh"
@@ -31,15 +38,39 @@ namespace mfb {
 namespace dec {
 
 constexpr int HD = 64;
-constexpr int WARPS = 8;                  // compute warps
+constexpr int WARPS = 8;                   // compute warps
 constexpr int THREADS = 32 * (WARPS + 1);  // + one producer warp
 constexpr int MAXG = 4;
-constexpr int NST = 3;                    // ring stages
-constexpr int SP = 16;                    // positions per stage
-constexpr int STAGE_K = SP * 8 * 128;     // bytes of K (and of V) per stage: 16 positions x up to 8 heads
-constexpr int MAX_GRID = 1024;            // CTAs per launch (partial slots reserved per call)
+constexpr int NST = 3;                     // ring stages
+constexpr int SP = 16;                     // positions per stage
+constexpr int HEAD_TILE = SP * 128;        // one KV head's 16 positions x 64 dims
+constexpr int STAGE_K = 8 * HEAD_TILE;     // K (and V) bytes per stage for up to 8 KV heads
+constexpr int MAX_GRID = 1024;             // CTAs per launch (partial slots reserved per call)
 constexpr int MAX_B = 8192;
-constexpr int SMEM_BASE = 1024 + NST * 2 * STAGE_K + 64;
+constexpr int MAX_H = 8 * MAXG;
+
+// Dynamic shared memory, offsets from the 1024-byte-aligned base:
+//   ring   NST x {K [Hk][16][64], V [Hk][16][64]}, 128-byte swizzled
+//   side   NST x {q row [H][64], new k [Hk][64], new v [Hk][64]}
+//   bars   NST full + NST empty mbarriers
+//   pref   [B + 1] int: exclusive prefix of the rows' valid lengths
+//   wslot  [B] int: each row's append slot (-1: no append)
+//   uflag  [B] uint8: 1 when valid_length <= 0 (uniform row)
+struct Layout {
+  uint32_t side, side_bytes, bars, pref, wslot, uflag, total;
+};
+
+__host__ __device__ inline Layout layout(int B, int H, int Hk) {
+  Layout L;
+  L.side = NST * 2 * STAGE_K;
+  L.side_bytes = (uint32_t)(H + 2 * Hk) * 128u;
+  L.bars = L.side + NST * L.side_bytes;
+  L.pref = L.bars + 2 * NST * 8;
+  L.wslot = L.pref + 4u * (uint32_t)(B + 1);
+  L.uflag = L.wslot + 4u * (uint32_t)B;
+  L.total = L.uflag + (uint32_t)B;
+  return L;
+}
 
 // Bounded-wait status word of the decode kernel on each device.
 __device__ int g_dec_status;
@@ -56,7 +87,7 @@ struct Params {
   float* part_o;    // [MAX_GRID + B][H][64]: slot (cta + row)
   float2* part_ml;  // [MAX_GRID + B][H]
   int* tickets;     // [B]
-  int B, cap, H, Hk, G;
+  int B, cap, H, Hk;
   float scale_log2;
 };
 
@@ -66,31 +97,69 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__device__ __forceinline__ void unpack8(const uint4& u, float* f) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 x = __bfloat1622float2(h[i]);
-    f[2 * i] = x.x;
-    f[2 * i + 1] = x.y;
-  }
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];\n" : "=r"(v) : "r"(a));
+  return v;
 }
 
-__device__ __forceinline__ int row_len(const Params& p, int b) {
-  const int L = p.valid_length[b];
-  return L <= 0 ? p.cap : min(L, p.cap);
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];\n" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
 }
 
-__device__ __forceinline__ int row_slot(const Params& p, int b) {
-  return (p.nk != nullptr && p.positions != nullptr) ? min(max(p.positions[b], 0), p.cap - 1) : -1;
+__device__ __forceinline__ void sts128(uint32_t a, const uint4& v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};\n" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
 }
 
 // The CTA whose share [floor(i*T/g), floor((i+1)*T/g)) holds position x.
-__device__ __forceinline__ int cta_of(long long x, long long total, int g) {
-  return (int)(((x + 1) * g + total - 1) / total) - 1;
+__device__ __forceinline__ int cta_of(int x, int total, int g) {
+  return (int)(((long long)(x + 1) * g + total - 1) / total) - 1;
 }
 
 __device__ __forceinline__ void compute_bar() { asm volatile("bar.sync 1, 256;\n" ::: "memory"); }
+
+// Merges the partials of row b written by CTAs c0..c1 (one pass, online max;
+// four partials' loads in flight at a time) and writes the bf16 output row.
+__device__ __forceinline__ void combine_row(const Params& p, int b, int c0, int c1, int tid) {
+  for (int item = tid; item < p.H * (HD / 4); item += 32 * WARPS) {
+    const int h = item / (HD / 4), d4 = (item % (HD / 4)) * 4;
+    float m = -INFINITY, den = 0.f, n0 = 0.f, n1 = 0.f, n2 = 0.f, n3 = 0.f;
+    for (int c = c0; c <= c1; c += 4) {
+      float2 ml[4];
+      float4 ov[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        ml[u] = make_float2(-INFINITY, 0.f);
+        ov[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c + u <= c1) {
+          const long long pi = ((long long)c + u + b) * p.H + h;
+          ml[u] = __ldcg(p.part_ml + pi);
+          ov[u] = __ldcg(reinterpret_cast<const float4*>(p.part_o + pi * HD + d4));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (c + u <= c1) {
+          const float mn = fmaxf(m, ml[u].x);
+          const float a = ex2(m - mn), w = ex2(ml[u].x - mn);
+          den = den * a + ml[u].y * w;
+          n0 = n0 * a + ov[u].x * w;
+          n1 = n1 * a + ov[u].y * w;
+          n2 = n2 * a + ov[u].z * w;
+          n3 = n3 * a + ov[u].w * w;
+          m = mn;
+        }
+      }
+    }
+    const float inv = 1.f / den;
+    uint2 out;
+    out.x = pack_bf16(n0 * inv, n1 * inv);
+    out.y = pack_bf16(n2 * inv, n3 * inv);
+    *reinterpret_cast<uint2*>(p.o + ((long long)b * p.H + h) * HD + d4) = out;
+  }
+}
 
 template <int G>
 __global__ void __launch_bounds__(THREADS, 2)
@@ -98,22 +167,33 @@ __global__ void __launch_bounds__(THREADS, 2)
   extern __shared__ uint8_t smem_raw[];
   // Offset from the __shared__ array itself so accesses keep the shared state space.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  int* pref = reinterpret_cast<int*>(smem + NST * 2 * STAGE_K + 64);  // [B + 1] exclusive prefix of lengths
-  __shared__ int s_wsum[WARPS + 1], s_last;
+  const Layout lay = layout(p.B, p.H, p.Hk);
+  int* pref = reinterpret_cast<int*>(smem + lay.pref);
+  int* wslot = reinterpret_cast<int*>(smem + lay.wslot);
+  uint8_t* uflag = smem + lay.uflag;
+  __shared__ int s_wsum[WARPS + 1], s_comb[2];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t sb = smem_u32(smem);
-  const uint32_t bars = sb + NST * 2 * STAGE_K;
+  const uint32_t bars = sb + lay.bars;
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (NST + s); };
   int* status = &g_dec_status;
-  const long long row_elems = (long long)p.Hk * HD;
+  const int row_elems = p.Hk * HD;
+  const bool append = p.nk != nullptr;
 
-  // Exclusive prefix of the rows' valid lengths.
+  // Prologue: the rows' valid lengths (prefix), append slots and uniform flags.
   {
     const int per = cdiv(p.B, THREADS);
     const int r0 = min(p.B, tid * per), r1 = min(p.B, r0 + per);
     int local = 0;
-    for (int r = r0; r < r1; ++r) local += row_len(p, r);
+    for (int r = r0; r < r1; ++r) {
+      const int L = p.valid_length[r];
+      const int len = L <= 0 ? p.cap : min(L, p.cap);
+      pref[r] = len;
+      uflag[r] = L <= 0;
+      wslot[r] = append ? min(max(p.positions[r], 0), p.cap - 1) : -1;
+      local += len;
+    }
     int incl = local;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -132,30 +212,18 @@ __global__ void __launch_bounds__(THREADS, 2)
     int off = incl - local;
     for (int w = 0; w < warp; ++w) off += s_wsum[w];
     for (int r = r0; r < r1; ++r) {
+      const int len = pref[r];
       pref[r] = off;
-      off += row_len(p, r);
+      off += len;
     }
     if (tid == THREADS - 1) pref[p.B] = off;
     __syncthreads();
   }
-  const long long total = pref[p.B];
-  // Appends whose slot is not a valid position of the row (at or beyond
-  // valid_length): one CTA per row, nothing reads that slot this step.
-  for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
-    const int wpos = row_slot(p, b);
-    if (wpos >= 0 && wpos >= row_len(p, b) && tid < (int)(row_elems / 8)) {
-      for (int i = tid; i < (int)(row_elems / 8); i += THREADS) {
-        *reinterpret_cast<uint4*>(p.kc + ((long long)b * p.cap + wpos) * row_elems + i * 8) =
-            *reinterpret_cast<const uint4*>(p.nk + (long long)b * row_elems + i * 8);
-        *reinterpret_cast<uint4*>(p.vc + ((long long)b * p.cap + wpos) * row_elems + i * 8) =
-            *reinterpret_cast<const uint4*>(p.nv + (long long)b * row_elems + i * 8);
-      }
-    }
-  }
-  const int g = (int)min((long long)gridDim.x, total);  // every share is nonempty
+  const int total = pref[p.B];
+  const int g = min((int)gridDim.x, total);  // every share is nonempty
   const int i = blockIdx.x;
   if (i >= g) return;
-  const long long x0 = i * total / g, x1 = (i + 1) * total / g;
+  const int x0 = (int)((long long)i * total / g), x1 = (int)((long long)(i + 1) * total / g);
   int b0 = 0;
   {
     int lo = 0, hi = p.B - 1;
@@ -168,24 +236,31 @@ __global__ void __launch_bounds__(THREADS, 2)
   }
 
   if (warp == WARPS) {
-    // Producer: per stage and KV head, one 16-position x 64-dim TMA box of K
-    // and one of V (128-byte swizzle), so each head's tile is conflict-free
-    // for ldmatrix.
+    // Producer: per stage one K box and one V box (all KV heads), plus the
+    // query row on a segment's first stage and the new key/value rows on the
+    // stage that holds the append slot, all counted on the stage's barrier.
     if (lane == 0) {
       tc::tma_prefetch_desc(&tk);
       tc::tma_prefetch_desc(&tv);
+      const uint32_t kv_bytes = 2u * p.Hk * HEAD_TILE, q_bytes = p.H * 128u, n_bytes = p.Hk * 128u;
       int it = 0;
       bool ok = true;
       for (int b = b0; ok && b < p.B && pref[b] < x1; ++b) {
-        const int lo = (int)(max(x0, (long long)pref[b]) - pref[b]);
-        const int hi = (int)(min(x1, (long long)pref[b + 1]) - pref[b]);
+        const int lo = max(x0, pref[b]) - pref[b], hi = min(x1, pref[b + 1]) - pref[b];
+        const int ws = wslot[b];
         for (int p0 = lo; p0 < hi; p0 += SP, ++it) {
           const int st = it % NST;
           if (!(ok = tc::mbar_wait(empty_bar(st), ((it / NST) & 1) ^ 1, status, 1))) break;
-          tc::mbar_expect_tx(full_bar(st), 2 * p.Hk * SP * 128);
-          for (int h = 0; h < p.Hk; ++h) {
-            tc::tma_load_2d(sb + st * 2 * STAGE_K + h * 2048, &tk, h * HD, b * p.cap + p0, full_bar(st));
-            tc::tma_load_2d(sb + st * 2 * STAGE_K + STAGE_K + h * 2048, &tv, h * HD, b * p.cap + p0, full_bar(st));
+          const int np = min(SP, hi - p0);
+          const bool first = p0 == lo, patch = ws >= p0 && ws < p0 + np;
+          const uint32_t side = sb + lay.side + st * lay.side_bytes;
+          tc::mbar_expect_tx(full_bar(st), kv_bytes + (first ? q_bytes : 0u) + (patch ? 2u * n_bytes : 0u));
+          tc::tma_load_3d(sb + st * 2 * STAGE_K, &tk, 0, b * p.cap + p0, 0, full_bar(st));
+          tc::tma_load_3d(sb + st * 2 * STAGE_K + STAGE_K, &tv, 0, b * p.cap + p0, 0, full_bar(st));
+          if (first) tc::bulk_load(side, p.q + (long long)b * p.H * HD, q_bytes, full_bar(st));
+          if (patch) {
+            tc::bulk_load(side + q_bytes, p.nk + (long long)b * row_elems, n_bytes, full_bar(st));
+            tc::bulk_load(side + q_bytes + n_bytes, p.nv + (long long)b * row_elems, n_bytes, full_bar(st));
           }
         }
       }
@@ -202,41 +277,21 @@ __global__ void __launch_bounds__(THREADS, 2)
   const int hk = warp;
   const bool active = hk < p.Hk;
   const int g4 = lane >> 2, c4 = lane & 3;  // fragment row (query head in the group) and column pair
-  int it = 0;
+  const float sl2 = p.scale_log2;
+  int it = 0, b_last = b0;
   bool ok = true;
   for (int b = b0; b < p.B && pref[b] < x1; ++b) {
-    const int lo = (int)(max(x0, (long long)pref[b]) - pref[b]);
-    const int hi = (int)(min(x1, (long long)pref[b + 1]) - pref[b]);
-    const int L = p.valid_length[b];
-    const bool uniform = L <= 0;
-    const int wpos = row_slot(p, b);
-    const bool own_slot = wpos >= lo && wpos < hi;
-    if (own_slot) {
-      // The cache append of this row; stage tiles may hold the old row at
-      // wpos, which each warp overwrites in shared memory below.
-      for (int e = tid; e < (int)(row_elems / 8); e += 32 * WARPS) {
-        *reinterpret_cast<uint4*>(p.kc + ((long long)b * p.cap + wpos) * row_elems + e * 8) =
-            *reinterpret_cast<const uint4*>(p.nk + (long long)b * row_elems + e * 8);
-        *reinterpret_cast<uint4*>(p.vc + ((long long)b * p.cap + wpos) * row_elems + e * 8) =
-            *reinterpret_cast<const uint4*>(p.nv + (long long)b * row_elems + e * 8);
-      }
-    }
-    // Q fragments (unscaled bf16; rows >= G are zero).
+    b_last = b;
+    const int lo = max(x0, pref[b]) - pref[b], hi = min(x1, pref[b + 1]) - pref[b];
+    const bool uniform = uflag[b] != 0;
+    const int ws = wslot[b];
     uint32_t qa[4][4];
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      qa[kk][0] = qa[kk][1] = qa[kk][2] = qa[kk][3] = 0u;
-      if (active && g4 < G) {
-        const __nv_bfloat16* qr = p.q + ((long long)b * p.H + hk * G + g4) * HD + kk * 16 + 2 * c4;
-        qa[kk][0] = *reinterpret_cast<const uint32_t*>(qr);
-        qa[kk][2] = *reinterpret_cast<const uint32_t*>(qr + 8);
-      }
-    }
+    for (int kk = 0; kk < 4; ++kk) qa[kk][0] = qa[kk][1] = qa[kk][2] = qa[kk][3] = 0u;
     float o[8][4];
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
     float m = -INFINITY, l = 0.f;
-    const float sl2 = p.scale_log2;
     for (int p0 = lo; p0 < hi; p0 += SP, ++it) {
       const int st = it % NST;
       // After a timed-out wait the warp skips the remaining waits but keeps
@@ -244,17 +299,29 @@ __global__ void __launch_bounds__(THREADS, 2)
       if (ok) ok = tc::mbar_wait(full_bar(st), (it / NST) & 1, status, 2);
       if (ok && active) {
         const int np = min(SP, hi - p0);
-        const uint32_t kt = sb + st * 2 * STAGE_K + hk * 2048, vt = kt + STAGE_K;
-        if (own_slot && wpos >= p0 && wpos < p0 + np) {
-          // Patch the new token's key / value row into this head's tiles.
-          const int r = wpos - p0;
+        const uint32_t kt = sb + st * 2 * STAGE_K + hk * HEAD_TILE, vt = kt + STAGE_K;
+        const uint32_t side = sb + lay.side + st * lay.side_bytes;
+        if (p0 == lo && g4 < G) {
+          // Q fragments (unscaled bf16) of query head hk*G + g4 from the side slot.
+          const uint32_t qrow = side + (hk * G + g4) * 128u + 4u * c4;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            qa[kk][0] = lds32(qrow + kk * 32);
+            qa[kk][2] = lds32(qrow + kk * 32 + 16);
+          }
+        }
+        if (ws >= p0 && ws < p0 + np) {
+          // The new token: patch its key / value row into this head's tiles
+          // (the stage holds the old row) and append it to the caches in HBM.
+          const int r = ws - p0;
           if (lane < 8) {
-            const uint4 nk4 = *reinterpret_cast<const uint4*>(p.nk + ((long long)b * p.Hk + hk) * HD + lane * 8);
-            const uint4 nv4 = *reinterpret_cast<const uint4*>(p.nv + ((long long)b * p.Hk + hk) * HD + lane * 8);
-            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};\n" ::"r"(kt + swz64(r, lane * 8)), "r"(nk4.x), "r"(nk4.y),
-                         "r"(nk4.z), "r"(nk4.w));
-            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};\n" ::"r"(vt + swz64(r, lane * 8)), "r"(nv4.x), "r"(nv4.y),
-                         "r"(nv4.z), "r"(nv4.w));
+            const uint32_t nrow = side + p.H * 128u + hk * 128u + lane * 16u;
+            const uint4 nk4 = lds128(nrow), nv4 = lds128(nrow + p.Hk * 128u);
+            sts128(kt + swz64(r, lane * 8), nk4);
+            sts128(vt + swz64(r, lane * 8), nv4);
+            const long long at = ((long long)b * p.cap + ws) * row_elems + hk * HD + lane * 8;
+            *reinterpret_cast<uint4*>(p.kc + at) = nk4;
+            *reinterpret_cast<uint4*>(p.vc + at) = nv4;
             tc::fence_proxy_async_smem();  // the ring's next TMA write to this stage must follow
           }
           __syncwarp();
@@ -310,42 +377,64 @@ __global__ void __launch_bounds__(THREADS, 2)
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(empty_bar(st));
     }
-    // Segment partial of rows g4 < G: the quad's four lanes hold 16 dims each.
-    const long long slot = (long long)i + b;
+    // Segment end, rows g4 < G (the quad's four lanes hold 16 dims each): a
+    // row inside this share is finished here; a cut row leaves its partial.
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
     if (active && g4 < G) {
-      const long long pi = slot * p.H + hk * G + g4;
+      const int c0 = cta_of(pref[b], total, g), c1 = cta_of(pref[b + 1] - 1, total, g);
+      const int h = hk * G + g4;
+      if (c0 == c1) {
+        const float inv = 1.f / l;
+        __nv_bfloat16* orow = p.o + ((long long)b * p.H + h) * HD + 2 * c4;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
-        *reinterpret_cast<float2*>(p.part_o + pi * HD + nt * 8 + 2 * c4) = make_float2(o[nt][0], o[nt][1]);
-      if (c4 == 0) p.part_ml[pi] = make_float2(m, l);
-    }
-    // The last segment of row b to finish combines the row's partials.
-    const int c0 = cta_of(pref[b], total, g), c1 = cta_of((long long)pref[b + 1] - 1, total, g);
-    __threadfence();
-    compute_bar();
-    if (tid == 0) s_last = atomicAdd(p.tickets + b, 1) == c1 - c0;
-    compute_bar();
-    if (s_last) {
-      __threadfence();
-      for (int idx = tid; idx < p.H * HD; idx += 32 * WARPS) {
-        const int h = idx / HD, d = idx % HD;
-        float mx = -INFINITY;
-        for (int c = c0; c <= c1; ++c) mx = fmaxf(mx, __ldcg(p.part_ml + ((long long)c + b) * p.H + h).x);
-        float num = 0.f, den = 0.f;
-        for (int c = c0; c <= c1; ++c) {
-          const long long pi = ((long long)c + b) * p.H + h;
-          const float2 ml = __ldcg(p.part_ml + pi);
-          const float w = ex2(ml.x - mx);
-          den += ml.y * w;
-          num += __ldcg(p.part_o + pi * HD + d) * w;
-        }
-        p.o[((long long)b * p.H + h) * HD + d] = __float2bfloat16_rn(num / den);
+        for (int nt = 0; nt < 8; ++nt)
+          *reinterpret_cast<uint32_t*>(orow + nt * 8) = pack_bf16(o[nt][0] * inv, o[nt][1] * inv);
+      } else {
+        const long long pi = ((long long)i + b) * p.H + h;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+          *reinterpret_cast<float2*>(p.part_o + pi * HD + nt * 8 + 2 * c4) = make_float2(o[nt][0], o[nt][1]);
+        if (c4 == 0) p.part_ml[pi] = make_float2(m, l);
       }
-      if (tid == 0) p.tickets[b] = 0;
     }
-    compute_bar();
+  }
+
+  // All stages done: one ticket per cut row (at most the share's first and
+  // last row); the last CTA of a row to arrive combines the row's partials.
+  __threadfence();
+  compute_bar();
+  if (tid < 2) {
+    int row = -1;
+    const int b = tid == 0 ? b0 : b_last;
+    if (tid == 0 || b_last != b0) {
+      const int c0 = cta_of(pref[b], total, g), c1 = cta_of(pref[b + 1] - 1, total, g);
+      if (c0 != c1 && atomicAdd(p.tickets + b, 1) == c1 - c0) row = b;
+    }
+    s_comb[tid] = row;
+  }
+  compute_bar();
+#pragma unroll 1
+  for (int k = 0; k < 2; ++k) {
+    const int b = s_comb[k];
+    if (b < 0) continue;
+    __threadfence();
+    combine_row(p, b, cta_of(pref[b], total, g), cta_of(pref[b + 1] - 1, total, g), tid);
+    if (tid == 0) p.tickets[b] = 0;
+  }
+  // Appends whose slot is not a valid position of its row (at or beyond
+  // valid_length): nothing reads that slot this step; row b goes to CTA b % g.
+  if (append) {
+    for (int b = i; b < p.B; b += g) {
+      const int ws = wslot[b];
+      if (ws >= pref[b + 1] - pref[b]) {
+        for (int e = tid; e < row_elems / 8; e += 32 * WARPS) {
+          const long long at = ((long long)b * p.cap + ws) * row_elems + e * 8;
+          *reinterpret_cast<uint4*>(p.kc + at) = *reinterpret_cast<const uint4*>(p.nk + (long long)b * row_elems + e * 8);
+          *reinterpret_cast<uint4*>(p.vc + at) = *reinterpret_cast<const uint4*>(p.nv + (long long)b * row_elems + e * 8);
+        }
+      }
+    }
   }
 }
 
@@ -385,7 +474,37 @@ int check(const void* q, const void* kc, const void* vc, const void* nk, const v
   MFB_CHECK_ARG(q && kc && vc && vl && o, "NULL tensor argument");
   MFB_CHECK_ARG((nk == nullptr) == (nv == nullptr), "new_k and new_v must both be given or both be NULL");
   MFB_CHECK_ARG(nk == nullptr || positions != nullptr, "positions are required with new_k/new_v");
+  MFB_CHECK_ARG((long long)B * capacity < (1LL << 31), "decode needs B x capacity < 2^31 cache positions (%lld)",
+                (long long)B * capacity);
   MFB_CHECK_ARG(((uintptr_t)kc & 15) == 0 && ((uintptr_t)vc & 15) == 0, "caches must be 16-byte aligned");
+  MFB_CHECK_ARG(((uintptr_t)q & 15) == 0 && ((uintptr_t)o & 15) == 0 && ((uintptr_t)nk & 15) == 0 &&
+                    ((uintptr_t)nv & 15) == 0,
+                "q, o, new_k and new_v must be 16-byte aligned");
+  return MFB_OK;
+}
+
+// Sets the kernel's dynamic shared-memory limit once per device and returns
+// how many CTAs of `smem` bytes fit on one SM.
+template <int G>
+int resident_ctas(int dev, size_t smem, int* occ) {
+  static bool configured[64] = {false};
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    const int smem_max = 1024 + (int)layout(MAX_B, MAX_H, 8).total;
+    MFB_CUDA_TRY(cudaFuncSetAttribute(decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max));
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  MFB_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, decode_kernel<G>, THREADS, smem));
+  return MFB_OK;
+}
+
+template <int G>
+int launch(const CUtensorMap& tk, const CUtensorMap& tv, const Params& p, int dev, int sms, size_t smem,
+           cudaStream_t s) {
+  int occ = 0, st;
+  if ((st = resident_ctas<G>(dev, smem, &occ))) return st;
+  const int grid = std::min(std::max(occ, 1) * sms, MAX_GRID);
+  decode_kernel<G><<<grid, THREADS, smem, s>>>(tk, tv, p);
+  MFB_LAUNCH_CHECK("decode kernel");
   return MFB_OK;
 }
 
@@ -409,36 +528,22 @@ int run(const uint16_t* q, uint16_t* k_cache, uint16_t* v_cache, const uint16_t*
   p.cap = capacity;
   p.H = H;
   p.Hk = Hk;
-  p.G = H / Hk;
   p.scale_log2 = scale * kLog2e;
   int dev = 0, sms = 148;
   MFB_CUDA_TRY(cudaGetDevice(&dev));
   MFB_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  const int grid = 2 * sms < MAX_GRID ? 2 * sms : MAX_GRID;
-  const size_t smem = SMEM_BASE + sizeof(int) * (size_t)(B + 1);
-  const int smem_max = SMEM_BASE + (int)sizeof(int) * (MAX_B + 1);
+  const size_t smem = 1024 + layout(B, H, Hk).total;
   CUtensorMap tk, tv;
   int st;
-  const uint64_t rows = (uint64_t)B * capacity, cols = (uint64_t)Hk * HD;
-  if ((st = tc::make_tmap_bf16(&tk, k_cache, cols, rows, cols, SP))) return st;
-  if ((st = tc::make_tmap_bf16(&tv, v_cache, cols, rows, cols, SP))) return st;
+  const uint64_t rows = (uint64_t)B * capacity;
+  if ((st = tc::make_tmap_bf16_heads(&tk, k_cache, rows, Hk, SP))) return st;
+  if ((st = tc::make_tmap_bf16_heads(&tv, v_cache, rows, Hk, SP))) return st;
   MFB_CUDA_TRY(cudaMemsetAsync(w.tickets, 0, sizeof(int) * (size_t)B, s));
-  switch (p.G) {
-    case 1:
-      MFB_CUDA_TRY(cudaFuncSetAttribute(decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max));
-      decode_kernel<1><<<grid, THREADS, smem, s>>>(tk, tv, p);
-      break;
-    case 2:
-      MFB_CUDA_TRY(cudaFuncSetAttribute(decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max));
-      decode_kernel<2><<<grid, THREADS, smem, s>>>(tk, tv, p);
-      break;
-    default:
-      MFB_CUDA_TRY(cudaFuncSetAttribute(decode_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max));
-      decode_kernel<4><<<grid, THREADS, smem, s>>>(tk, tv, p);
-      break;
+  switch (H / Hk) {
+    case 1: return launch<1>(tk, tv, p, dev, sms, smem, s);
+    case 2: return launch<2>(tk, tv, p, dev, sms, smem, s);
+    default: return launch<4>(tk, tv, p, dev, sms, smem, s);
   }
-  MFB_LAUNCH_CHECK("decode kernel");
-  return MFB_OK;
 }
 
 }  // namespace dec

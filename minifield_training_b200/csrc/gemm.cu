@@ -286,6 +286,20 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t 
   return MFB_OK;
 }
 
+int make_tmap_bf16_heads(CUtensorMap* map, const void* base, uint64_t rows, int heads, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(MFB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  cuuint64_t dims[3] = {64, rows, (cuuint64_t)heads};
+  cuuint64_t strides[2] = {(cuuint64_t)heads * 128, 128};
+  cuuint32_t box[3] = {64, box_rows, (cuuint32_t)heads};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(MFB_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+  return MFB_OK;
+}
+
 }  // namespace tc
 }  // namespace mfb
 

@@ -53,6 +53,21 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
       : "memory");
 }
+// 3-D tiled load (coordinates innermost first), no multicast.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+// Untiled bulk copy global -> shared; both addresses 16-byte aligned, bytes a
+// multiple of 16; completion counted on the mbarrier. No multicast.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -164,6 +179,11 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 // `ld` elements; box = {64 inner (128 bytes), box_outer}; 128-byte swizzle.
 int make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
                    uint32_t box_outer);
+// 3-D bf16 tensor map over a [rows, heads, 64] array (one 64-element head
+// vector per (row, head), rows heads*128 bytes apart), addressed as
+// {dim, row, head} so that box {64, box_rows, heads} lands in shared memory as
+// [head][box_rows][64]: one 128-byte-swizzled tile per head.
+int make_tmap_bf16_heads(CUtensorMap* map, const void* base, uint64_t rows, int heads, uint32_t box_rows);
 
 }  // namespace tc
 }  // namespace mfb
