@@ -185,6 +185,90 @@ int mfb_gemm_bf16(const uint16_t* A, int a_major, int lda, const uint16_t* B, in
  * up (the kernel then unwound instead of hanging). Synchronous. */
 int mfb_gemm_status(int* code);
 
+/* ---- Transactional AdamW (src/minifield_training/optimizers/adamw.py:384-571)
+ * One all-or-nothing clipped AdamW update over flat FP32 arenas ordered
+ * [decayed trainable | undecayed trainable | frozen]: params, m and v hold
+ * n_total elements, grads the first n_train (n_decayed <= n_train). Device
+ * scalars: step (int32, incremented on commit), loss, accumulation_valid
+ * (uint8) and, when non-NULL, grad_divisor (the logical step's denominator;
+ * gradients are divided by it before anything else, as
+ * src/minifield_training/engine/step.py:389 does). Codes and their precedence
+ * follow CommitCode (adamw.py:30-39, :437-461); the gradient norm, clip scale
+ * and update norm follow adamw.py:476-541; a candidate with a non-finite norm
+ * or leaf is rejected (adamw.py:543-569). A rejected update writes nothing.
+ * `result` is a device mfb_adamw_result written by the call. Arenas must be
+ * 16-byte aligned. Calls on one workspace must not overlap. */
+typedef struct {
+  int32_t code; /* 0 committed, 1 accumulation invalid, 2 non-finite loss, 3 invalid state,
+                   4 non-finite gradient, 5 step overflow, 6 candidate invalid */
+  int32_t committed;
+  float loss, gradient_norm, clipped_gradient_norm, update_norm; /* NaN norms when rejected before the attempt */
+} mfb_adamw_result;
+size_t mfb_adamw_workspace_size(void);
+int mfb_adamw_commit(float* params, float* m, float* v, const float* grads, long long n_train, long long n_decayed,
+                     long long n_total, int32_t* step, const float* loss, const uint8_t* accumulation_valid,
+                     const float* grad_divisor, float learning_rate, float beta1, float beta2, float epsilon,
+                     float weight_decay, float clip_norm, void* result, void* workspace, size_t workspace_bytes,
+                     void* stream);
+/* Logical-step normalization (src/minifield_training/engine/step.py:384-389):
+ * accumulation_valid = counts_valid && isfinite(count_sum) && count_sum > 0;
+ * divisor = count_sum if valid else 1; loss = loss_sum / divisor. All device
+ * scalars; counts_valid may be NULL (true). */
+int mfb_step_normalize(const float* loss_sum, const float* count_sum, const uint8_t* counts_valid, float* loss,
+                       float* divisor, uint8_t* accumulation_valid, void* stream);
+
+/* ---- Encoder training-step kernels -------------------------------------------
+ * bf16 activations [M, C] (M = B*T packed tokens), FP32 masters and FP32
+ * weight gradients. Weight-gradient outputs are written, or added to when
+ * `accumulate` is nonzero. Workspaces hold per-block partial sums.
+ *
+ * rms_norm (src/minifield_training/kernels/normalization.py:7-22) with the
+ * encoder block's bf16 residual add fused in front (encoder.py:64-110): when
+ * `residual` is non-NULL, sum_out = bf16(x + residual) is written and
+ * normalized; y = bf16(bf16(s * rstd) * bf16(weight)), times row_mask[m] when
+ * row_mask is non-NULL (conv_input_projection, layers/convolution.py:29-37);
+ * rstd [M] FP32 is saved for the backward. C a multiple of 256, <= 2048. */
+size_t mfb_norm_workspace_size(int M, int C);
+int mfb_rmsnorm_fwd(const uint16_t* x, const uint16_t* residual, const float* weight, const int32_t* row_mask,
+                    uint16_t* sum_out, uint16_t* y, float* rstd, int M, int C, float eps, void* stream);
+/* dx = dres + d(rms_norm)/dx . dy (dres may be NULL); dweight [C]. C <= 1024. */
+int mfb_rmsnorm_bwd(const uint16_t* x, const float* weight, const float* rstd, const int32_t* row_mask,
+                    const uint16_t* dy, const uint16_t* dres, uint16_t* dx, float* dweight, int accumulate, int M,
+                    int C, void* workspace, size_t workspace_bytes, void* stream);
+/* Per-head q/k RMSNorm (project_qkv, layers/attention.py:61-77) and rotary
+ * embedding (apply_rotary, kernels/rotary.py:7-39) on the fused projection
+ * output qkv [M, ld_qkv] = [q heads | k heads | v heads] x 64: writes q
+ * [M,H,64], k and v [M,Hk,64]. freqs [32] = theta^(-2i/64) in FP32;
+ * positions [M]. The backward writes d_qkv [M, ld_qkv] and the 64-wide gain
+ * gradients. */
+int mfb_qknorm_rope_fwd(const uint16_t* qkv, int ld_qkv, const float* wq, const float* wk, const int32_t* positions,
+                        const float* freqs, uint16_t* q, uint16_t* k, uint16_t* v, float* rstd_q, float* rstd_k,
+                        int M, int H, int Hk, float eps, void* stream);
+int mfb_qknorm_rope_bwd(const uint16_t* qkv, int ld_qkv, const float* wq, const float* wk, const int32_t* positions,
+                        const float* freqs, const float* rstd_q, const float* rstd_k, const uint16_t* dq,
+                        const uint16_t* dk, const uint16_t* dv, uint16_t* dqkv, float* dwq, float* dwk, int accumulate,
+                        int M, int H, int Hk, void* workspace, size_t workspace_bytes, void* stream);
+/* Frozen token embedding rows cast to bf16 (encoder.py:231); ids clamped to [0, V). */
+int mfb_embed_gather(const float* table, const int32_t* ids, uint16_t* out, long long M, int C, int V, void* stream);
+/* Gated centered short convolution (encoder.py:76-86,
+ * kernels/bidirectional.py:38-58): bcx [M, 3C] = [b | c | values] from the
+ * in-projection, taps [C, 3] FP32, segment_ids [M] (rows of T tokens; 0 =
+ * padding) -> mixed [M, C] = c * conv(b * values). */
+int mfb_conv_fwd(const uint16_t* bcx, const float* taps, const int32_t* segment_ids, uint16_t* mixed, long long M,
+                 int T, int C, void* stream);
+size_t mfb_encoder_workspace_size(int C, int classes);
+int mfb_conv_bwd(const uint16_t* bcx, const float* taps, const int32_t* segment_ids, const uint16_t* dmixed,
+                 uint16_t* dbcx, float* dtaps, int accumulate, long long M, int T, int C, void* workspace,
+                 size_t workspace_bytes, void* stream);
+/* Token classification head and summed cross-entropy, forward and backward in
+ * one pass: logits = bf16(encoded . bf16(weight)^T) [M, classes];
+ * loss_count[0] = sum over rows with valid != 0 of logsumexp(logits) -
+ * logits[label], loss_count[1] = number of such rows; d_encoded and d_weight
+ * [classes, C] are the gradients of loss_count[0]. C = 1024, classes <= 4. */
+int mfb_head_loss(const uint16_t* encoded, const float* weight, const int32_t* labels, const int32_t* valid,
+                  uint16_t* d_encoded, float* d_weight, float* loss_count, int M, int C, int classes, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
 /* ---- SwiGLU glue between the QAT GEMMs (layers/feed_forward.py:24-35) ------
  * gu [M, 2F] bf16 (gate columns first) -> h [M,F] = silu(gate) * up, bf16.
  * Backward: dh [M,F] -> dgu [M,2F] bf16. */

@@ -30,6 +30,7 @@ P = ctypes.c_void_p
 I = ctypes.c_int
 F = ctypes.c_float
 SZ = ctypes.c_size_t
+LL = ctypes.c_longlong
 IP = ctypes.POINTER(ctypes.c_int)
 
 # name -> (restype, argtypes); mirrors include/mfb200.h one to one.
@@ -66,6 +67,19 @@ SIGNATURES = {
     "mfb_decode_attn_noalloc": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, F, P]),
     "mfb_gemm_bf16": (I, [P, I, I, P, I, I, P, I, I, I, I, I, F, P, P]),
     "mfb_gemm_status": (I, [IP]),
+    "mfb_adamw_workspace_size": (SZ, []),
+    "mfb_adamw_commit": (I, [P, P, P, P, LL, LL, LL, P, P, P, P, F, F, F, F, F, F, P, P, SZ, P]),
+    "mfb_step_normalize": (I, [P, P, P, P, P, P, P]),
+    "mfb_norm_workspace_size": (SZ, [I, I]),
+    "mfb_rmsnorm_fwd": (I, [P, P, P, P, P, P, P, I, I, F, P]),
+    "mfb_rmsnorm_bwd": (I, [P, P, P, P, P, P, P, P, I, I, I, P, SZ, P]),
+    "mfb_qknorm_rope_fwd": (I, [P, I, P, P, P, P, P, P, P, P, P, I, I, I, F, P]),
+    "mfb_qknorm_rope_bwd": (I, [P, I, P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, P, SZ, P]),
+    "mfb_embed_gather": (I, [P, P, P, LL, I, I, P]),
+    "mfb_conv_fwd": (I, [P, P, P, P, LL, I, I, P]),
+    "mfb_encoder_workspace_size": (SZ, [I, I]),
+    "mfb_conv_bwd": (I, [P, P, P, P, P, P, I, LL, I, I, P, SZ, P]),
+    "mfb_head_loss": (I, [P, P, P, P, P, P, P, I, I, I, P, SZ, P]),
     "mfb_swiglu_fwd": (I, [P, P, I, I, P]),
     "mfb_swiglu_bwd": (I, [P, P, P, I, I, P]),
     "mfb_cast_f32_bf16": (I, [P, P, ctypes.c_longlong, P]),

@@ -121,6 +121,18 @@ class DeviceArray:
         view._base = self  # a view keeps its owner alive
         return view
 
+    def view(self, offset: int, shape, dtype=None):
+        """A view of ``shape`` starting ``offset`` elements (of this dtype) in."""
+        dtype = _canon(dtype or self.dtype)
+        shape = tuple(int(x) for x in ((shape,) if np.isscalar(shape) else shape))
+        nbytes = int(np.prod(shape, dtype=np.int64)) * DTYPES[dtype].itemsize
+        start = int(offset) * self.itemsize
+        if offset < 0 or start + nbytes > self.nbytes:
+            raise ValueError(f"view [{start}, {start + nbytes}) bytes outside a {self.nbytes}-byte array")
+        v = DeviceArray(shape, dtype, ptr=self.ptr + start, owner=False)
+        v._base = self
+        return v
+
     def copy_(self, other: "DeviceArray", stream=None):
         if other.nbytes != self.nbytes:
             raise ValueError("size mismatch")

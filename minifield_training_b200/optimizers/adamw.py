@@ -1,0 +1,286 @@
+"""Transactional full-weight AdamW over device arenas.
+
+Mirrors src/minifield_training/optimizers/adamw.py: ``CommitCode`` (:30-39),
+``AdamWConfig`` and its validation (:42-110), ``CommitResult`` (:113-122),
+``initialize_state`` (:300-322) and ``make_transaction(inventory, config)`` ->
+``transition(state, gradients, active_loss, accumulation_valid)`` (:384-571).
+The inventory mirrors ``core/parameters.py:12-57`` (name, shape, trainable,
+decayed). The update itself is ``mfb_adamw_commit`` in libmfb200.so.
+
+Layout: a ``State`` keeps params, m and v in three FP32 device arenas ordered
+[decayed trainable | undecayed trainable | frozen] (names sorted inside each
+group), plus a grads arena over the trainable prefix and an int32 device step.
+``state["params"][name]`` etc. are views into the arenas. The transaction
+updates the arenas in place only when it commits (the reference's donated
+transaction, adamw.py:574-591); a rejected update leaves them untouched, so
+``result.state`` is the same object either way.
+"""
+
+import ctypes
+import dataclasses
+import enum
+import math
+
+import numpy as np
+
+from .. import _lib
+from ..device import DeviceArray
+
+_INT32_MAX = np.iinfo(np.int32).max
+
+
+class CommitCode(enum.IntEnum):
+    """Result codes, as adamw.py:30-39."""
+
+    COMMITTED = 0
+    ACCUMULATION_INVALID = 1
+    NONFINITE_LOSS = 2
+    INVALID_STATE = 3
+    NONFINITE_GRADIENT = 4
+    STEP_OVERFLOW = 5
+    CANDIDATE_INVALID = 6
+
+
+@dataclasses.dataclass(frozen=True)
+class AdamWConfig:
+    """Validated float32 settings (adamw.py:42-92)."""
+
+    learning_rate: float
+    beta1: float = 0.9
+    beta2: float = 0.95
+    epsilon: float = 1e-8
+    weight_decay: float = 0.01
+    clip_norm: float = 1.0
+
+    def __post_init__(self):
+        converted = {}
+        for name in ("learning_rate", "beta1", "beta2", "epsilon", "weight_decay", "clip_norm"):
+            value = getattr(self, name)
+            if isinstance(value, bool) or not isinstance(value, (int, float)):
+                raise ValueError(f"{name} must be a non-boolean finite number")
+            number = float(value)
+            if not math.isfinite(number) or abs(number) > float(np.finfo(np.float32).max):
+                raise ValueError(f"{name} must be a finite float32 scalar")
+            effective = float(np.float32(number))
+            if number and effective == 0:
+                raise ValueError(f"{name} must be representable in float32")
+            if effective and abs(effective) < float(np.finfo(np.float32).tiny):
+                raise ValueError(f"{name} must be zero or a normal float32 scalar")
+            converted[name] = effective
+        if converted["learning_rate"] <= 0:
+            raise ValueError("learning_rate must be positive")
+        if not 0 <= converted["beta1"] < 1:
+            raise ValueError("beta1 must be in [0, 1)")
+        if not 0 <= converted["beta2"] < 1:
+            raise ValueError("beta2 must be in [0, 1)")
+        if converted["epsilon"] <= 0:
+            raise ValueError("epsilon must be positive")
+        if converted["weight_decay"] < 0:
+            raise ValueError("weight_decay must be nonnegative")
+        if converted["clip_norm"] <= 0:
+            raise ValueError("clip_norm must be positive")
+        for name, value in converted.items():
+            object.__setattr__(self, name, value)
+
+
+@dataclasses.dataclass(frozen=True)
+class ParameterSpec:
+    """One stored leaf (core/parameters.py:12-22)."""
+
+    name: str
+    shape: tuple
+    trainable: bool
+    decayed: bool
+
+
+@dataclasses.dataclass(frozen=True)
+class Inventory:
+    """Leaf metadata with the derived membership views (core/parameters.py:25-57)."""
+
+    specs: tuple
+
+    @property
+    def names(self):
+        return tuple(s.name for s in self.specs)
+
+    @property
+    def trainable_names(self):
+        return tuple(s.name for s in self.specs if s.trainable)
+
+    @property
+    def frozen_names(self):
+        return tuple(s.name for s in self.specs if not s.trainable)
+
+
+def build_inventory(shapes, *, decayed_names=frozenset(), frozen_names=frozenset()) -> Inventory:
+    """Inventory over ``shapes`` (name -> shape); frozen leaves cannot decay (core/parameters.py:58-125)."""
+    unknown = (set(decayed_names) | set(frozen_names)) - set(shapes)
+    if unknown:
+        raise ValueError(f"Inventory names are not parameters: {sorted(unknown)}")
+    if set(decayed_names) & set(frozen_names):
+        raise ValueError("Frozen parameters cannot be decayed")
+    specs = tuple(
+        ParameterSpec(name, tuple(int(x) for x in shapes[name]), name not in frozen_names, name in decayed_names)
+        for name in sorted(shapes))
+    if not specs:
+        raise ValueError("Full-weight inventory must not be empty")
+    return Inventory(specs)
+
+
+class Layout:
+    """Arena offsets: [decayed trainable | undecayed trainable | frozen]."""
+
+    def __init__(self, inventory: Inventory):
+        groups = ([s for s in inventory.specs if s.trainable and s.decayed],
+                  [s for s in inventory.specs if s.trainable and not s.decayed],
+                  [s for s in inventory.specs if not s.trainable])
+        self.specs = {s.name: s for s in inventory.specs}
+        self.offsets = {}
+        off = 0
+        sizes = []
+        for group in groups:
+            for s in group:
+                # 4-element (16-byte) alignment for every leaf keeps vector access aligned.
+                self.offsets[s.name] = off
+                off += _round4(int(np.prod(s.shape, dtype=np.int64)))
+            sizes.append(off)
+        self.n_decayed, self.n_train, self.n_total = sizes
+        self.trainable = tuple(s.name for s in groups[0] + groups[1])
+
+    def size(self, name):
+        return int(np.prod(self.specs[name].shape, dtype=np.int64))
+
+    def views(self, arena: DeviceArray, names):
+        return {n: arena.view(self.offsets[n], self.specs[n].shape) for n in names}
+
+
+def _round4(n):
+    return (n + 3) // 4 * 4
+
+
+class State(dict):
+    """``{"params", "m", "v", "step"}`` (optimizers/state.py:11-17) backed by arenas."""
+
+    def __init__(self, layout: Layout, arenas):
+        self.layout = layout
+        self.arenas = arenas  # params, m, v, grads, step
+        names = list(layout.specs)
+        super().__init__(params=layout.views(arenas["params"], names), m=layout.views(arenas["m"], names),
+                         v=layout.views(arenas["v"], names), step=arenas["step"])
+
+    def gradient_tree(self):
+        """Views of the grads arena for the trainable leaves (the transition's input layout)."""
+        return self.layout.views(self.arenas["grads"], self.layout.trainable)
+
+
+def initialize_state(parameters, inventory: Inventory) -> State:
+    """Zero-moment FP32 state (adamw.py:300-322); rejects non-finite masters."""
+    layout = Layout(inventory)
+    if set(parameters) != set(layout.specs):
+        raise ValueError("Full-weight parameter tree mismatch")
+    arenas = {k: DeviceArray.zeros((max(layout.n_total, 4),), "float32") for k in ("params", "m", "v")}
+    arenas["grads"] = DeviceArray.zeros((max(layout.n_train, 4),), "float32")
+    arenas["step"] = DeviceArray.zeros((1,), "int32")
+    for name, value in parameters.items():
+        host = np.asarray(value, np.float32)
+        if host.shape != layout.specs[name].shape:
+            raise ValueError(f"Full-weight parameter shape mismatch: {name}")
+        if not np.isfinite(host).all():
+            raise ValueError(f"Full-weight parameter is non-finite: {name}")
+        dst = arenas["params"].view(layout.offsets[name], host.shape)
+        _lib.call("mfb_memcpy_h2d", ctypes.c_void_p(dst.ptr), host.ctypes.data_as(ctypes.c_void_p), host.nbytes, None)
+    return State(layout, arenas)
+
+
+class _ResultStruct(ctypes.Structure):
+    _fields_ = [("code", ctypes.c_int32), ("committed", ctypes.c_int32), ("loss", ctypes.c_float),
+                ("gradient_norm", ctypes.c_float), ("clipped_gradient_norm", ctypes.c_float),
+                ("update_norm", ctypes.c_float)]
+
+
+class CommitResult:
+    """State and diagnostics of one transaction (adamw.py:113-122); fields read on first access."""
+
+    def __init__(self, state, device_result: DeviceArray, stream):
+        self.state = state
+        self._dev = device_result
+        self._stream = stream
+        self._host = None
+
+    def _fetch(self):
+        if self._host is None:
+            r = _ResultStruct()
+            _lib.call("mfb_memcpy_d2h", ctypes.c_void_p(ctypes.addressof(r)), ctypes.c_void_p(self._dev.ptr),
+                      ctypes.sizeof(r), self._stream)
+            _lib.call("mfb_stream_sync", self._stream)
+            self._host = r
+        return self._host
+
+    committed = property(lambda self: bool(self._fetch().committed))
+    code = property(lambda self: CommitCode(self._fetch().code))
+    loss = property(lambda self: float(self._fetch().loss))
+    gradient_norm = property(lambda self: float(self._fetch().gradient_norm))
+    clipped_gradient_norm = property(lambda self: float(self._fetch().clipped_gradient_norm))
+    update_norm = property(lambda self: float(self._fetch().update_norm))
+
+
+def _device_scalar(value, dtype, cache, key):
+    if isinstance(value, DeviceArray):
+        return value
+    arr = cache.get(key)
+    if arr is None:
+        arr = cache[key] = DeviceArray((1,), dtype)
+    host = np.asarray([value], dtype=np.float32 if dtype == "float32" else np.uint8)
+    _lib.call("mfb_memcpy_h2d", ctypes.c_void_p(arr.ptr), host.ctypes.data_as(ctypes.c_void_p), host.nbytes, None)
+    return arr
+
+
+def make_transaction(inventory: Inventory, config: AdamWConfig):
+    """Build the commit (adamw.py:384-415): ``transition(state, gradients, active_loss, accumulation_valid, *, divisor=None, stream=None)``.
+
+    ``gradients`` is ``state.gradient_tree()`` (already in the arena) or any
+    name -> array mapping over exactly the trainable leaves, which is copied
+    into the arena first. ``active_loss`` / ``accumulation_valid`` are Python
+    scalars or device scalars; ``divisor`` (device float32) optionally divides
+    the gradients first (the logical step's normalization).
+    """
+    layout = Layout(inventory)
+    workspace = DeviceArray((_lib.lib().mfb_adamw_workspace_size(),), "uint8")
+    result_dev = DeviceArray((6,), "int32")
+    scalars = {}
+
+    def transition(state: State, gradients, active_loss, accumulation_valid, *, divisor=None, stream=None):
+        if not isinstance(state, State) or state.layout.offsets != layout.offsets:
+            raise ValueError("Full-weight state does not match the inventory")
+        if set(gradients) != set(layout.trainable):
+            missing = sorted(set(layout.trainable) - set(gradients))
+            extra = sorted(set(gradients) - set(layout.trainable))
+            raise ValueError(f"Full-weight gradient tree mismatch; missing={missing}, extra={extra}")
+        grads = state.arenas["grads"]
+        for name, g in gradients.items():
+            dst = grads.view(layout.offsets[name], layout.specs[name].shape)
+            if isinstance(g, DeviceArray):
+                if g.ptr != dst.ptr:
+                    if g.dtype != "float32" or g.shape != dst.shape:
+                        raise ValueError(f"Full-weight gradient must be float32 of shape {dst.shape}: {name}")
+                    dst.copy_(g, stream)
+            else:
+                host = np.asarray(g)
+                if host.shape != dst.shape or host.dtype != np.float32:
+                    raise ValueError(f"Full-weight gradient must be float32 of shape {dst.shape}: {name}")
+                host = np.ascontiguousarray(host)
+                _lib.call("mfb_memcpy_h2d", ctypes.c_void_p(dst.ptr), host.ctypes.data_as(ctypes.c_void_p),
+                          host.nbytes, stream)
+        loss = _device_scalar(active_loss, "float32", scalars, "loss")
+        valid = _device_scalar(bool(accumulation_valid) if not isinstance(accumulation_valid, DeviceArray)
+                               else accumulation_valid, "uint8", scalars, "valid")
+        P = ctypes.c_void_p
+        a = state.arenas
+        _lib.call("mfb_adamw_commit", P(a["params"].ptr), P(a["m"].ptr), P(a["v"].ptr), P(grads.ptr), layout.n_train,
+                  layout.n_decayed, layout.n_total, P(a["step"].ptr), P(loss.ptr), P(valid.ptr),
+                  P(divisor.ptr) if divisor is not None else None, config.learning_rate, config.beta1, config.beta2,
+                  config.epsilon, config.weight_decay, config.clip_norm, P(result_dev.ptr), P(workspace.ptr),
+                  workspace.nbytes, stream)
+        return CommitResult(state, result_dev, stream)
+
+    return transition

@@ -1,0 +1,172 @@
+"""AdamW transaction on the GPU (mfb_adamw_commit via optimizers.adamw) against oracle/adamw.py.
+
+Without clipping both sides run the same float32 operations in the same order,
+so committed leaves must match bit for bit; with clipping the device's FP64
+norm can move the clip scale by an ulp, so leaves are compared at rtol 2e-6.
+Rejections must leave every arena byte unchanged.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from oracle import adamw as oa
+from tests.gpu_env import require_gpu
+
+pytestmark = pytest.mark.gpu
+F = np.float32
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _gpu():
+    require_gpu()
+
+
+def _upload(view, host):
+    from minifield_training_b200 import _lib
+    host = np.ascontiguousarray(np.asarray(host, F))
+    _lib.call("mfb_memcpy_h2d", ctypes.c_void_p(view.ptr), host.ctypes.data_as(ctypes.c_void_p), host.nbytes, None)
+
+
+def _make(shapes, decayed, frozen, params, m, v, step=0):
+    from minifield_training_b200.optimizers import adamw
+    inv = adamw.build_inventory(shapes, decayed_names=frozenset(decayed), frozen_names=frozenset(frozen))
+    st = adamw.initialize_state(params, inv)
+    for name in shapes:
+        _upload(st["m"][name], m[name])
+        _upload(st["v"][name], v[name])
+    np_step = np.array([step], np.int32)
+    from minifield_training_b200 import _lib
+    _lib.call("mfb_memcpy_h2d", ctypes.c_void_p(st["step"].ptr), np_step.ctypes.data_as(ctypes.c_void_p), 4, None)
+    return inv, st
+
+
+def _read(st):
+    return ({g: {n: st[g][n].numpy() for n in st[g]} for g in ("params", "m", "v")}, int(st["step"].numpy()[0]))
+
+
+def _fixture():
+    from tests.test_adamw_oracle import _grads, _state
+    s = _state()
+    shapes = {k: v.shape for k, v in s["params"].items()}
+    return shapes, s, _grads()
+
+
+def _cfg(**kw):
+    c = dict(learning_rate=0.1, beta1=0.9, beta2=0.95, epsilon=1e-8, weight_decay=0.01, clip_norm=1.0)
+    c.update(kw)
+    return c
+
+
+def _run_gpu(shapes, decayed, frozen, s, grads, loss=1.0, valid=True, **kw):
+    from minifield_training_b200.optimizers import adamw
+    inv, st = _make(shapes, decayed, frozen, s["params"], s["m"], s["v"], s["step"])
+    before = _read(st)
+    tr = adamw.make_transaction(inv, adamw.AdamWConfig(**_cfg(**kw)))
+    res = tr(st, grads, F(loss), valid)
+    return res, before, _read(st)
+
+
+def test_reference_fixture_commits_bit_exactly():
+    shapes, s, grads = _fixture()
+    res, _, (after, step) = _run_gpu(shapes, {"w.matrix"}, {"w.frozen_matrix", "w.frozen_vector"}, s, grads,
+                                     clip_norm=10.0)
+    ref = oa.transition(s, grads, 1.0, True, _cfg(clip_norm=10.0), {"w.matrix", "w.vector"}, {"w.matrix"})
+    assert res.committed and res.code == 0 and step == 1
+    for g in ("params", "m", "v"):
+        for n in shapes:
+            np.testing.assert_array_equal(after[g][n], ref[0][g][n], err_msg=f"{g}/{n}")
+    np.testing.assert_allclose(res.gradient_norm, ref[4], rtol=1e-6)
+    np.testing.assert_allclose(res.clipped_gradient_norm, ref[5], rtol=1e-6)
+    np.testing.assert_allclose(res.update_norm, ref[6], rtol=1e-5)
+
+
+@pytest.mark.parametrize("case,code", [("grad", 4), ("loss", 2), ("acc", 1), ("m_inf", 3), ("v_neg", 3),
+                                       ("v_nan", 3), ("step", 5), ("candidate", 6)])
+def test_rejections_write_nothing(case, code):
+    shapes, s, grads = _fixture()
+    loss, valid, kw = 1.0, True, {}
+    if case == "grad":
+        grads["w.vector"] = np.array([np.nan, 0, 0], F)
+    elif case == "loss":
+        loss = np.nan
+    elif case == "acc":
+        valid = False
+    elif case == "m_inf":
+        s["m"]["w.vector"] = np.array([np.inf, 0, 0], F)
+    elif case == "v_neg":
+        s["v"]["w.vector"] = np.array([-1.0, 0, 0], F)
+    elif case == "v_nan":
+        s["v"]["w.frozen_vector"] = np.array([0, np.nan, 0, 0], F)
+    elif case == "step":
+        s["step"] = 2**31 - 1
+    elif case == "candidate":
+        s["params"]["w.matrix"] = np.full((2, 3), 1e38, F)
+        grads = {k: np.zeros_like(v) for k, v in grads.items()}
+        kw = dict(learning_rate=1.0, weight_decay=4.0, clip_norm=1e30)
+    from minifield_training_b200.optimizers import adamw
+    inv, st = _make(shapes, {"w.matrix"}, {"w.frozen_matrix", "w.frozen_vector"}, s["params"], s["m"], s["v"],
+                    s["step"])
+    before = _read(st)
+    res = adamw.make_transaction(inv, adamw.AdamWConfig(**_cfg(**kw)))(st, grads, F(loss), valid)
+    assert not res.committed and int(res.code) == code
+    after = _read(st)
+    assert after[1] == before[1]
+    for g in ("params", "m", "v"):
+        for n in shapes:
+            np.testing.assert_array_equal(after[0][g][n].view(np.uint32), before[0][g][n].view(np.uint32))
+    if code != 6:
+        assert np.isnan(res.gradient_norm) and np.isnan(res.update_norm)
+
+
+@pytest.mark.parametrize("clip", [1e6, 0.5])
+def test_large_ragged_arena_matches_oracle(clip):
+    rng = np.random.default_rng(7)
+    shapes = {"a.decayed": (1023, 517), "b.decayed": (3, 5), "c.plain": (1001,), "d.plain": (64, 3, 7),
+              "e.frozen": (333, 129), "f.plain": (7,)}
+    decayed, frozen = {"a.decayed", "b.decayed"}, {"e.frozen"}
+    s = {"params": {k: rng.standard_normal(sh, dtype=F) for k, sh in shapes.items()},
+         "m": {k: (rng.standard_normal(sh, dtype=F) * F(0.01)) for k, sh in shapes.items()},
+         "v": {k: np.abs(rng.standard_normal(sh, dtype=F)) * F(1e-4) for k, sh in shapes.items()}, "step": 41}
+    for k in frozen:
+        s["m"][k][:] = 0
+        s["v"][k][:] = 0
+    grads = {k: rng.standard_normal(sh, dtype=F) * F(1e-3) for k, sh in shapes.items() if k not in frozen}
+    grads["c.plain"][:10] = 0  # m_hat == 0 where the moment is also zero
+    s["m"]["c.plain"][:10] = 0
+    res, _, (after, step) = _run_gpu(shapes, decayed, frozen, s, grads, clip_norm=clip, weight_decay=0.1)
+    ref = oa.transition(s, grads, 1.0, True, _cfg(clip_norm=clip, weight_decay=0.1), set(grads), decayed)
+    assert res.committed and ref[1] and step == 42
+    np.testing.assert_allclose(res.gradient_norm, ref[4], rtol=1e-5)
+    np.testing.assert_allclose(res.update_norm, ref[6], rtol=1e-4)
+    for g in ("params", "m", "v"):
+        for n in shapes:
+            if clip > 1e5:
+                np.testing.assert_array_equal(after[g][n], ref[0][g][n], err_msg=f"{g}/{n}")
+            else:
+                np.testing.assert_allclose(after[g][n], ref[0][g][n], rtol=2e-6, atol=1e-12, err_msg=f"{g}/{n}")
+
+
+def test_normalized_step_divides_gradients_and_loss():
+    from minifield_training_b200 import _lib
+    from minifield_training_b200.device import DeviceArray
+    from minifield_training_b200.optimizers import adamw
+    shapes, s, grads = _fixture()
+    count = F(6.0)
+    sums = {k: v * count for k, v in grads.items()}
+    inv, st = _make(shapes, {"w.matrix"}, {"w.frozen_matrix", "w.frozen_vector"}, s["params"], s["m"], s["v"])
+    dev = lambda x, dt: DeviceArray.from_numpy(np.array([x]), dt)
+    ls, cs = dev(F(12.0), "float32"), dev(count, "float32")
+    loss, div, ok = DeviceArray((1,), "float32"), DeviceArray((1,), "float32"), DeviceArray((1,), "uint8")
+    P = ctypes.c_void_p
+    _lib.call("mfb_step_normalize", P(ls.ptr), P(cs.ptr), None, P(loss.ptr), P(div.ptr), P(ok.ptr), None)
+    res = adamw.make_transaction(inv, adamw.AdamWConfig(**_cfg(clip_norm=10.0)))(st, sums, loss, ok, divisor=div)
+    ref_loss, ref_grads, ref_valid = oa.normalize(F(12.0), count, sums)
+    ref = oa.transition(s, ref_grads, ref_loss, ref_valid, _cfg(clip_norm=10.0), {"w.matrix", "w.vector"},
+                        {"w.matrix"})
+    assert res.committed and res.loss == pytest.approx(2.0)
+    after, _ = _read(st)
+    for g in ("params", "m", "v"):
+        for n in shapes:
+            np.testing.assert_array_equal(after[g][n], ref[0][g][n], err_msg=f"{g}/{n}")
