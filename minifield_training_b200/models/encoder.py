@@ -1,0 +1,479 @@
+"""LFM2.5-style encoder training step (config 5) on B200: QAT forward, backward,
+data-parallel gradient allreduce and the transactional AdamW commit.
+
+Mirrors, with the reference's parameter names and block equations:
+  encode / _block        src/minifield_training/models/lfm2_5/encoder.py:64-240
+  conv_input_projection  src/minifield_training/layers/convolution.py:29-37
+  project_qkv, rope      src/minifield_training/layers/attention.py:61-97
+  swiglu_ffn             src/minifield_training/layers/feed_forward.py:24-35
+  QAT on projections     src/minifield_training/strategies/quantization.py:114-126
+                         over model.projection_names (models/lfm2_5/model.py:169-184)
+  step normalization     src/minifield_training/engine/step.py:36-78, :367-395
+  AdamW transaction      src/minifield_training/optimizers/adamw.py:384-571
+The reference's encoder ships no training head; this step adds a token
+classification head ("head.weight" [classes, hidden], a decayed trainable
+matrix, not quantized) with a summed cross-entropy over valid tokens and the
+valid-token count as the loss terms (engine/step.py:17-19 contract).
+
+Every activation and weight buffer is allocated once per EncoderStep. Each
+layer's projections are fake-quantized into fused bf16 weight buffers
+(q|k|v and gate|up rows adjacent), and the parameter arenas are ordered so the
+fused weight gradients land, FP32, straight in the gradient arena. Activations
+are kept for the backward (no rematerialization: 180 GB of HBM holds them).
+With a process group the gradient arena (plus the loss and count in its
+tail) is all-reduced bucket by bucket as each layer's backward finishes,
+overlapping the remaining backward; the AdamW commit then runs replicated.
+"""
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from .. import _lib
+from ..device import DeviceArray
+from ..optimizers import adamw
+
+P = ctypes.c_void_p
+
+
+def _prefix(i):
+    return f"lfm2.layers.{i}."
+
+
+def parameter_shapes(cfg) -> dict:
+    """Reference names and shapes (model.py:127-166 with the encoder's lfm2. prefix) plus the head."""
+    c, f, kv = cfg.hidden, cfg.ffn, cfg.kv_heads * cfg.head_dim
+    shapes = {"lfm2.embed_tokens.weight": (cfg.vocab, c), "lfm2.embedding_norm.weight": (c,),
+              "head.weight": (cfg.classes, c)}
+    for i, kind in enumerate(cfg.layer_types):
+        p = _prefix(i)
+        shapes.update({p + "operator_norm.weight": (c,), p + "ffn_norm.weight": (c,),
+                       p + "feed_forward.w1.weight": (f, c), p + "feed_forward.w3.weight": (f, c),
+                       p + "feed_forward.w2.weight": (c, f)})
+        if kind == "conv":
+            shapes.update({p + "conv.in_proj.weight": (3 * c, c), p + "conv.out_proj.weight": (c, c),
+                           p + "conv.conv.weight": (c, 1, 3)})
+        else:
+            shapes.update({p + "self_attn.q_proj.weight": (c, c), p + "self_attn.k_proj.weight": (kv, c),
+                           p + "self_attn.v_proj.weight": (kv, c), p + "self_attn.out_proj.weight": (c, c),
+                           p + "self_attn.q_layernorm.weight": (cfg.head_dim,),
+                           p + "self_attn.k_layernorm.weight": (cfg.head_dim,)})
+    return shapes
+
+
+PROJECTION_SUFFIXES = ("self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight",
+                       "self_attn.out_proj.weight", "conv.in_proj.weight", "conv.out_proj.weight",
+                       "feed_forward.w1.weight", "feed_forward.w2.weight", "feed_forward.w3.weight")
+
+
+def projection_names(cfg) -> frozenset:
+    return frozenset(n for n in parameter_shapes(cfg) if n.endswith(PROJECTION_SUFFIXES))
+
+
+def inventory(cfg) -> adamw.Inventory:
+    """Decay every unfrozen matrix (model.py:187-209); the token embeddings are frozen."""
+    shapes = parameter_shapes(cfg)
+    frozen = frozenset({"lfm2.embed_tokens.weight"})
+    return adamw.build_inventory(shapes, decayed_names=frozenset(n for n, s in shapes.items()
+                                                                 if len(s) == 2 and n not in frozen),
+                                 frozen_names=frozen)
+
+
+def arena_order(cfg):
+    """Head first, then layers last to first (the backward's order), fused groups adjacent."""
+    order = ["head.weight", "lfm2.embedding_norm.weight"]
+    for i in reversed(range(len(cfg.layer_types))):
+        p = _prefix(i)
+        order += [p + "feed_forward.w1.weight", p + "feed_forward.w3.weight", p + "feed_forward.w2.weight",
+                  p + "ffn_norm.weight"]
+        if cfg.layer_types[i] == "conv":
+            order += [p + "conv.out_proj.weight", p + "conv.in_proj.weight", p + "conv.conv.weight"]
+        else:
+            order += [p + "self_attn.out_proj.weight", p + "self_attn.q_proj.weight", p + "self_attn.k_proj.weight",
+                      p + "self_attn.v_proj.weight", p + "self_attn.q_layernorm.weight",
+                      p + "self_attn.k_layernorm.weight"]
+        order.append(p + "operator_norm.weight")
+    order.append("lfm2.embed_tokens.weight")
+    return order
+
+
+def init_parameters(cfg, seed: int = 0) -> dict:
+    """Random init: N(0, 0.02) for matrices, taps, embeddings and the head; ones for norm gains."""
+    rng = np.random.default_rng(seed)
+    out = {}
+    for name, shape in parameter_shapes(cfg).items():
+        if name.endswith("norm.weight") or name.endswith("layernorm.weight"):
+            out[name] = np.ones(shape, np.float32)
+        else:
+            out[name] = (rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02))
+    return out
+
+
+def rope_freqs(theta: float, head_dim: int = 64) -> np.ndarray:
+    """theta ** (-arange(0, D, 2) / D) in float32 (kernels/rotary.py:31-33)."""
+    return (np.float32(theta) ** (-np.arange(0, head_dim, 2, dtype=np.float32) / np.float32(head_dim))).astype(
+        np.float32)
+
+
+def _gemm(a, a_major, lda, b, b_major, ldb, c, ldc, f32, m, n, k, mask=None, stream=None):
+    _lib.call("mfb_gemm_bf16", P(a), a_major, lda, P(b), b_major, ldb, P(c), ldc,
+              _lib.DTYPE_F32 if f32 else _lib.DTYPE_BF16, m, n, k, ctypes.c_float(1.0),
+              P(mask) if mask is not None else None, stream)
+
+
+def _fwd(x, w, out, m, n, k, stream):
+    """out[m, n] = x[m, k] . w[n, k]^T (bf16)."""
+    _gemm(x.ptr, _lib.MAJOR_K, k, w.ptr, _lib.MAJOR_K, k, out.ptr, n, False, m, n, k, stream=stream)
+
+
+def _dgrad(dy, w, out, m, n, k, stream):
+    """out[m, k] = dy[m, n] . w[n, k] (bf16)."""
+    _gemm(dy.ptr, _lib.MAJOR_K, n, w.ptr, _lib.MAJOR_MN, k, out.ptr, k, False, m, k, n, stream=stream)
+
+
+def _wgrad(dy, x, out_ptr, ste, m, n, k, stream):
+    """out[n, k] (FP32) = dy[m, n]^T . x[m, k], times the STE mask."""
+    _gemm(dy.ptr, _lib.MAJOR_MN, n, x.ptr, _lib.MAJOR_MN, k, out_ptr, k, True, n, k, m,
+          mask=ste.ptr if ste is not None else None, stream=stream)
+
+
+@dataclass
+class _Layer:
+    kind: str
+    x: DeviceArray         # layer input (sum), [M, C]
+    h: DeviceArray         # operator-normed input
+    rstd_op: DeviceArray
+    mid: DeviceArray       # x + operator residual
+    h2: DeviceArray        # ffn-normed
+    rstd_ffn: DeviceArray
+    gu: DeviceArray        # [M, 2F]
+    a: DeviceArray         # [M, F]
+    y: DeviceArray         # ffn output [M, C]
+    r: DeviceArray         # operator output [M, C]
+    proj: DeviceArray      # conv: bcx [M, 3C]; attention: raw qkv [M, 2048]
+    mixed: DeviceArray = None  # conv
+    q: DeviceArray = None
+    k: DeviceArray = None
+    v: DeviceArray = None
+    o: DeviceArray = None
+    lse: DeviceArray = None
+    rstd_q: DeviceArray = None
+    rstd_k: DeviceArray = None
+    w_in: DeviceArray = None   # fused eff bf16 [3C | 2048, C]
+    ste_in: DeviceArray = None
+    w_out: DeviceArray = None
+    ste_out: DeviceArray = None
+    w13: DeviceArray = None
+    ste13: DeviceArray = None
+    w2: DeviceArray = None
+    ste2: DeviceArray = None
+
+
+class EncoderStep:
+    """One logical training step over ``rows`` local sequences of the global batch.
+
+    ``group`` (a torch.distributed process group, or None) all-reduces the
+    gradient sums, loss and count; ``stream`` is the CUDA stream handle all
+    kernels run on (and, with a group, the stream the collectives order after).
+    """
+
+    def __init__(self, cfg, rows: int, *, seed: int = 0, group=None, stream=None, torch_grads=None):
+        self.cfg, self.rows, self.T = cfg, rows, cfg.length
+        self.M = m = rows * cfg.length
+        self.group, self.stream = group, stream
+        c, f, h, hk = cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads
+        self.nq = (h + 2 * hk) * cfg.head_dim
+        inv = inventory(cfg)
+        self.layout = adamw.Layout(inv, arena_order(cfg))
+        n_grad = self.layout.n_train + 4  # tail: loss sum, count
+        if torch_grads is not None:
+            grads = DeviceArray((n_grad,), "float32", ptr=torch_grads.data_ptr(), owner=False)
+            grads._base = torch_grads
+        else:
+            grads = DeviceArray.zeros((n_grad,), "float32")
+        self.grads = grads
+        self.state = adamw.initialize_state(init_parameters(cfg, seed), inv, order=arena_order(cfg), grads=grads)
+        self.loss_count = grads.view(self.layout.n_train, (2,))
+        self.transition = adamw.make_transaction(inv, adamw.AdamWConfig(
+            cfg.learning_rate, beta1=cfg.beta1, beta2=cfg.beta2, epsilon=cfg.epsilon, weight_decay=cfg.weight_decay,
+            clip_norm=cfg.clip_norm))
+        self.params = self.state["params"]
+        self.gviews = self.state.gradient_tree()
+        self.quant = _lib.QUANT_KINDS[cfg.quant] if cfg.quant else None
+        bf, f32 = "bfloat16", "float32"
+        E = DeviceArray
+        # Shared step inputs and scratch.
+        self.ids, self.mask, self.seg, self.pos, self.labels = (E((m,), "int32") for _ in range(5))
+        self.freqs = E.from_numpy(rope_freqs(cfg.rope_theta, cfg.head_dim), f32)
+        self.qid, self.kid = E((rows, self.T), "int32"), E((rows, self.T), "int32")
+        self.x0 = E((m, c), bf)
+        self.final = E((m, c), bf)
+        self.enc = E((m, c), bf)
+        self.rstd_final = E((m,), f32)
+        self.d_a, self.d_b = E((m, c), bf), E((m, c), bf)   # residual-stream gradients (ping-pong)
+        self.d_mid = E((m, c), bf)
+        self.d_h = E((m, c), bf)
+        self.d_gu = E((m, 2 * f), bf)
+        self.d_f = E((m, f), bf)
+        self.d_proj = E((m, max(3 * c, self.nq)), bf)
+        self.d_q, self.d_k, self.d_v = E((m, h, 64), bf), E((m, hk, 64), bf), E((m, hk, 64), bf)
+        self.d_o = E((m, c), bf)
+        ws = max(_lib.lib().mfb_norm_workspace_size(m, c), _lib.lib().mfb_encoder_workspace_size(c, cfg.classes))
+        self.ws = E((ws,), "uint8")
+        aws = _lib.lib().mfb_attn_workspace_size(rows, self.T, self.T, h, hk, cfg.head_dim)
+        self.attn_ws = E((max(aws, 16),), "uint8")
+        self.result = None
+        self.layers = []
+        for kind in cfg.layer_types:
+            L = _Layer(kind, x=E((m, c), bf), h=E((m, c), bf), rstd_op=E((m,), f32), mid=E((m, c), bf),
+                       h2=E((m, c), bf), rstd_ffn=E((m,), f32), gu=E((m, 2 * f), bf), a=E((m, f), bf),
+                       y=E((m, c), bf), r=E((m, c), bf),
+                       proj=E((m, 3 * c if kind == "conv" else self.nq), bf))
+            if kind == "conv":
+                L.mixed = E((m, c), bf)
+                L.w_in, L.ste_in = E((3 * c, c), bf), E((3 * c, c), "uint8")
+            else:
+                L.q, L.k, L.v, L.o = E((m, h, 64), bf), E((m, hk, 64), bf), E((m, hk, 64), bf), E((m, c), bf)
+                L.lse, L.rstd_q, L.rstd_k = E((rows, h, self.T), f32), E((m, h), f32), E((m, hk), f32)
+                L.w_in, L.ste_in = E((self.nq, c), bf), E((self.nq, c), "uint8")
+            L.w_out, L.ste_out = E((c, c), bf), E((c, c), "uint8")
+            L.w13, L.ste13 = E((2 * f, c), bf), E((2 * f, c), "uint8")
+            L.w2, L.ste2 = E((c, f), bf), E((c, f), "uint8")
+            self.layers.append(L)
+        self.head_eff = E((cfg.classes, c), bf)
+        self._buckets = reduction_plan(self.layout, len(self.layers), self.grads.size)
+
+    # ---- helpers -----------------------------------------------------------------
+    def _p(self, name):
+        return self.params[name]
+
+    def _g(self, name):
+        return self.gviews[name]
+
+    def _quantize(self, name, eff: DeviceArray, ste: DeviceArray, row0: int):
+        w = self._p(name)
+        rows, cols = w.shape
+        e = eff.view(row0 * cols, (rows, cols))
+        s = ste.view(row0 * cols, (rows, cols))
+        if self.quant is None:
+            _lib.call("mfb_cast_f32_bf16", P(w.ptr), P(e.ptr), rows * cols, self.stream)
+            _lib.call("mfb_memset", P(s.ptr), 1, rows * cols, self.stream)
+        else:
+            _lib.call("mfb_fakequant", P(w.ptr), self.quant, rows, cols, None, None, P(s.ptr), None, P(e.ptr),
+                      self.stream)
+
+    def quantize(self):
+        """Effective bf16 weights and STE masks of every projection for this step."""
+        c, f = self.cfg.hidden, self.cfg.ffn
+        for i, L in enumerate(self.layers):
+            p = _prefix(i)
+            self._quantize(p + "feed_forward.w1.weight", L.w13, L.ste13, 0)
+            self._quantize(p + "feed_forward.w3.weight", L.w13, L.ste13, f)
+            self._quantize(p + "feed_forward.w2.weight", L.w2, L.ste2, 0)
+            if L.kind == "conv":
+                self._quantize(p + "conv.in_proj.weight", L.w_in, L.ste_in, 0)
+                self._quantize(p + "conv.out_proj.weight", L.w_out, L.ste_out, 0)
+            else:
+                kv = self.cfg.kv_heads * self.cfg.head_dim
+                self._quantize(p + "self_attn.q_proj.weight", L.w_in, L.ste_in, 0)
+                self._quantize(p + "self_attn.k_proj.weight", L.w_in, L.ste_in, c)
+                self._quantize(p + "self_attn.v_proj.weight", L.w_in, L.ste_in, c + kv)
+                self._quantize(p + "self_attn.out_proj.weight", L.w_out, L.ste_out, 0)
+        # The head is not a model projection: full_linear casts its master to bf16.
+        hw = self._p("head.weight")
+        _lib.call("mfb_cast_f32_bf16", P(hw.ptr), P(self.head_eff.ptr), hw.size, self.stream)
+
+    def set_batch(self, ids, mask, seg, pos, labels):
+        """Upload one local batch (int32 [rows, T] host arrays) and build the attention ids."""
+        for dst, src in ((self.ids, ids), (self.mask, mask), (self.seg, seg), (self.pos, pos),
+                         (self.labels, labels)):
+            a = np.ascontiguousarray(np.asarray(src, np.int32).reshape(-1))
+            _lib.call("mfb_memcpy_h2d", P(dst.ptr), a.ctypes.data_as(P), a.nbytes, self.stream)
+        self._build_ids()
+
+    def _build_ids(self):
+        c_, o_, p_ = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        _lib.call("mfb_attn_ids", _lib.MASK_BIDIR, P(self.mask.ptr), P(self.seg.ptr), None, P(self.qid.ptr),
+                  P(self.kid.ptr), self.rows, self.T, self.T, 0, ctypes.byref(c_), ctypes.byref(o_),
+                  ctypes.byref(p_), self.stream)
+        self.attn_flags = (c_.value, o_.value, p_.value)
+
+    # ---- forward -------------------------------------------------------------------
+    def _rms(self, x, res, w, mask, sum_out, y, rstd):
+        _lib.call("mfb_rmsnorm_fwd", P(x.ptr), P(res.ptr) if res is not None else None, P(w.ptr),
+                  P(mask.ptr) if mask is not None else None, P(sum_out.ptr) if res is not None else None, P(y.ptr),
+                  P(rstd.ptr), self.M, self.cfg.hidden, ctypes.c_float(self.cfg.norm_eps), self.stream)
+
+    def forward(self):
+        cfg, m, c, f, s = self.cfg, self.M, self.cfg.hidden, self.cfg.ffn, self.stream
+        emb = self._p("lfm2.embed_tokens.weight")
+        _lib.call("mfb_embed_gather", P(emb.ptr), P(self.ids.ptr), P(self.x0.ptr), m, c, cfg.vocab, s)
+        prev = None
+        for i, L in enumerate(self.layers):
+            p = _prefix(i)
+            opmask = self.mask if L.kind == "conv" else None
+            if prev is None:
+                _lib.call("mfb_memcpy_d2d", P(L.x.ptr), P(self.x0.ptr), L.x.nbytes, s)
+                self._rms(L.x, None, self._p(p + "operator_norm.weight"), opmask, None, L.h, L.rstd_op)
+            else:
+                self._rms(prev.mid, prev.y, self._p(p + "operator_norm.weight"), opmask, L.x, L.h, L.rstd_op)
+            if L.kind == "conv":
+                _fwd(L.h, L.w_in, L.proj, m, 3 * c, c, s)
+                _lib.call("mfb_conv_fwd", P(L.proj.ptr), P(self._p(p + "conv.conv.weight").ptr), P(self.seg.ptr),
+                          P(L.mixed.ptr), m, self.T, c, s)
+                _fwd(L.mixed, L.w_out, L.r, m, c, c, s)
+            else:
+                _fwd(L.h, L.w_in, L.proj, m, self.nq, c, s)
+                _lib.call("mfb_qknorm_rope_fwd", P(L.proj.ptr), self.nq, P(self._p(p + "self_attn.q_layernorm.weight").ptr),
+                          P(self._p(p + "self_attn.k_layernorm.weight").ptr), P(self.pos.ptr), P(self.freqs.ptr),
+                          P(L.q.ptr), P(L.k.ptr), P(L.v.ptr), P(L.rstd_q.ptr), P(L.rstd_k.ptr), m, cfg.heads,
+                          cfg.kv_heads, ctypes.c_float(cfg.norm_eps), s)
+                causal, off, pol = self.attn_flags
+                _lib.call("mfb_attn_fwd", P(L.q.ptr), P(L.k.ptr), P(L.v.ptr), P(L.o.ptr), P(L.lse.ptr),
+                          P(self.qid.ptr), P(self.kid.ptr), self.rows, self.T, self.T, cfg.heads, cfg.kv_heads,
+                          cfg.head_dim, causal, off, pol, ctypes.c_float(cfg.head_dim ** -0.5), P(self.attn_ws.ptr),
+                          self.attn_ws.nbytes, s)
+                _fwd(L.o, L.w_out, L.r, m, c, c, s)
+            self._rms(L.x, L.r, self._p(p + "ffn_norm.weight"), None, L.mid, L.h2, L.rstd_ffn)
+            _fwd(L.h2, L.w13, L.gu, m, 2 * f, c, s)
+            _lib.call("mfb_swiglu_fwd", P(L.gu.ptr), P(L.a.ptr), m, f, s)
+            _fwd(L.a, L.w2, L.y, m, c, f, s)
+            prev = L
+        self._rms(prev.mid, prev.y, self._p("lfm2.embedding_norm.weight"), self.mask, self.final, self.enc,
+                  self.rstd_final)
+
+    # ---- backward ------------------------------------------------------------------
+    def _rms_bwd(self, x, w, rstd, mask, dy, dres, dx, dw):
+        _lib.call("mfb_rmsnorm_bwd", P(x.ptr), P(w.ptr), P(rstd.ptr), P(mask.ptr) if mask is not None else None,
+                  P(dy.ptr), P(dres.ptr) if dres is not None else None, P(dx.ptr), P(dw.ptr), 0, self.M,
+                  self.cfg.hidden, P(self.ws.ptr), self.ws.nbytes, self.stream)
+
+    def backward(self, on_layer_done=None):
+        cfg, m, c, f, s = self.cfg, self.M, self.cfg.hidden, self.cfg.ffn, self.stream
+        lc = self.loss_count
+        _lib.call("mfb_head_loss", P(self.enc.ptr), P(self._p("head.weight").ptr), P(self.labels.ptr),
+                  P(self.mask.ptr), P(self.d_h.ptr), P(self._g("head.weight").ptr), P(lc.ptr), m, c, cfg.classes,
+                  P(self.ws.ptr), self.ws.nbytes, s)
+        d, spare = self.d_a, self.d_b
+        self._rms_bwd(self.final, self._p("lfm2.embedding_norm.weight"), self.rstd_final, self.mask, self.d_h, None,
+                      d, self._g("lfm2.embedding_norm.weight"))
+        for i in reversed(range(len(self.layers))):
+            L, p = self.layers[i], _prefix(i)
+            # FFN: x_next = mid + y.
+            _dgrad(d, L.w2, self.d_f, m, c, f, s)
+            _wgrad(d, L.a, self._g(p + "feed_forward.w2.weight").ptr, L.ste2, m, c, f, s)
+            _lib.call("mfb_swiglu_bwd", P(L.gu.ptr), P(self.d_f.ptr), P(self.d_gu.ptr), m, f, s)
+            _dgrad(self.d_gu, L.w13, self.d_h, m, 2 * f, c, s)
+            _wgrad(self.d_gu, L.h2, self._g(p + "feed_forward.w1.weight").ptr, L.ste13, m, 2 * f, c, s)
+            self._rms_bwd(L.mid, self._p(p + "ffn_norm.weight"), L.rstd_ffn, None, self.d_h, d, self.d_mid,
+                          self._g(p + "ffn_norm.weight"))
+            # Operator: mid = x + r.
+            if L.kind == "conv":
+                _dgrad(self.d_mid, L.w_out, self.d_o, m, c, c, s)
+                _wgrad(self.d_mid, L.mixed, self._g(p + "conv.out_proj.weight").ptr, L.ste_out, m, c, c, s)
+                _lib.call("mfb_conv_bwd", P(L.proj.ptr), P(self._p(p + "conv.conv.weight").ptr), P(self.seg.ptr),
+                          P(self.d_o.ptr), P(self.d_proj.ptr), P(self._g(p + "conv.conv.weight").ptr), 0, m, self.T,
+                          c, P(self.ws.ptr), self.ws.nbytes, s)
+                _dgrad(self.d_proj, L.w_in, self.d_h, m, 3 * c, c, s)
+                _wgrad(self.d_proj, L.h, self._g(p + "conv.in_proj.weight").ptr, L.ste_in, m, 3 * c, c, s)
+            else:
+                _dgrad(self.d_mid, L.w_out, self.d_o, m, c, c, s)
+                _wgrad(self.d_mid, L.o, self._g(p + "self_attn.out_proj.weight").ptr, L.ste_out, m, c, c, s)
+                causal, off, pol = self.attn_flags
+                _lib.call("mfb_attn_bwd", P(L.q.ptr), P(L.k.ptr), P(L.v.ptr), P(L.o.ptr), P(L.lse.ptr),
+                          P(self.d_o.ptr), P(self.d_q.ptr), P(self.d_k.ptr), P(self.d_v.ptr), P(self.qid.ptr),
+                          P(self.kid.ptr), self.rows, self.T, self.T, cfg.heads, cfg.kv_heads, cfg.head_dim, causal,
+                          off, pol, ctypes.c_float(cfg.head_dim ** -0.5), P(self.attn_ws.ptr), self.attn_ws.nbytes, s)
+                _lib.call("mfb_qknorm_rope_bwd", P(L.proj.ptr), self.nq,
+                          P(self._p(p + "self_attn.q_layernorm.weight").ptr),
+                          P(self._p(p + "self_attn.k_layernorm.weight").ptr), P(self.pos.ptr), P(self.freqs.ptr),
+                          P(L.rstd_q.ptr), P(L.rstd_k.ptr), P(self.d_q.ptr), P(self.d_k.ptr), P(self.d_v.ptr),
+                          P(self.d_proj.ptr), P(self._g(p + "self_attn.q_layernorm.weight").ptr),
+                          P(self._g(p + "self_attn.k_layernorm.weight").ptr), 0, m, cfg.heads, cfg.kv_heads,
+                          P(self.ws.ptr), self.ws.nbytes, s)
+                _dgrad(self.d_proj, L.w_in, self.d_h, m, self.nq, c, s)
+                _wgrad(self.d_proj, L.h, self._g(p + "self_attn.q_proj.weight").ptr, L.ste_in, m, self.nq, c, s)
+            opmask = self.mask if L.kind == "conv" else None
+            self._rms_bwd(L.x, self._p(p + "operator_norm.weight"), L.rstd_op, opmask, self.d_h, self.d_mid, spare,
+                          self._g(p + "operator_norm.weight"))
+            d, spare = spare, d
+            if on_layer_done is not None:
+                on_layer_done(i)
+        self.d_x0 = d  # the embeddings are frozen: this gradient is not used
+
+    # ---- the logical step ------------------------------------------------------------
+    def step(self):
+        """quantize -> forward -> backward (+ bucketed allreduce) -> normalize -> AdamW commit."""
+        self.quantize()
+        self.forward()
+        if self.group is not None:
+            reducer = BucketReducer(self.grads._base, self._buckets, self.group)
+            self.backward(reducer.layer_done)
+            reducer.finish()
+        else:
+            self.backward()
+        self._commit()
+        return self.result
+
+    def _commit(self):
+        if not hasattr(self, "_scalars"):
+            self._scalars = (DeviceArray((1,), "float32"), DeviceArray((1,), "float32"), DeviceArray((1,), "uint8"))
+        loss, div, ok = self._scalars
+        lc = self.loss_count
+        _lib.call("mfb_step_normalize", P(lc.ptr), P(lc.ptr + 4), None, P(loss.ptr), P(div.ptr), P(ok.ptr),
+                  self.stream)
+        self.result = self.transition(self.state, self.gviews, loss, ok, divisor=div, stream=self.stream)
+
+
+def reduction_plan(layout, n_layers: int, total: int):
+    """Allreduce ranges of the flat gradient buffer, in launch order.
+
+    One range per layer, backward order: the layer's matrices, contiguous in
+    the decayed region (arena_order puts layers last to first). Then the rest
+    in one or two ranges: the head before the first layer range, and after the
+    last one every vector leaf plus the loss/count tail. Together the ranges
+    partition [0, total) (checked by the tests).
+    """
+    plan = []
+    for i in reversed(range(n_layers)):
+        names = [n for n in layout.trainable if n.startswith(_prefix(i)) and len(layout.specs[n].shape) == 2]
+        lo = min(layout.offsets[n] for n in names)
+        hi = max(layout.offsets[n] + layout.size(n) for n in names)
+        plan.append(("layer", i, lo, hi))
+    lo_all = min(p[2] for p in plan)
+    hi_all = max(p[3] for p in plan)
+    if lo_all > 0:
+        plan.append(("rest", -1, 0, lo_all))
+    if total > hi_all:
+        plan.append(("rest", -1, hi_all, total))
+    return plan
+
+
+class BucketReducer:
+    """SUM-allreduces a flat torch tensor bucket by bucket (engine/step.py:62's psum).
+
+    ``layer_done(i)`` is called after layer i's backward is enqueued on the
+    current torch stream; its bucket's collective is then enqueued and runs
+    while the backward of the layers below it continues. ``finish()``
+    reduces the remaining ranges and makes the current stream wait for all.
+    """
+
+    def __init__(self, flat, plan, group):
+        self.flat, self.group, self.works = flat, group, []
+        self.by_layer = {i: (lo, hi) for kind, i, lo, hi in plan if kind == "layer"}
+        self.rest = [(lo, hi) for kind, _, lo, hi in plan if kind == "rest"]
+
+    def _reduce(self, lo, hi):
+        import torch.distributed as dist
+        self.works.append(dist.all_reduce(self.flat[lo:hi], group=self.group, async_op=True))
+
+    def layer_done(self, i):
+        self._reduce(*self.by_layer[i])
+
+    def finish(self):
+        for lo, hi in self.rest:
+            self._reduce(lo, hi)
+        for w in self.works:
+            w.wait()
+        self.works = []

@@ -128,12 +128,20 @@ def build_inventory(shapes, *, decayed_names=frozenset(), frozen_names=frozenset
 
 
 class Layout:
-    """Arena offsets: [decayed trainable | undecayed trainable | frozen]."""
+    """Arena offsets: [decayed trainable | undecayed trainable | frozen].
 
-    def __init__(self, inventory: Inventory):
-        groups = ([s for s in inventory.specs if s.trainable and s.decayed],
-                  [s for s in inventory.specs if s.trainable and not s.decayed],
-                  [s for s in inventory.specs if not s.trainable])
+    Inside each group leaves follow ``order`` (names, default sorted), so a
+    caller can make leaves that one kernel writes together adjacent.
+    """
+
+    def __init__(self, inventory: Inventory, order=None):
+        rank = {n: i for i, n in enumerate(order if order is not None else sorted(inventory.names))}
+        if set(rank) != set(inventory.names):
+            raise ValueError("arena order must list every inventory name once")
+        specs = sorted(inventory.specs, key=lambda s: rank[s.name])
+        groups = ([s for s in specs if s.trainable and s.decayed],
+                  [s for s in specs if s.trainable and not s.decayed],
+                  [s for s in specs if not s.trainable])
         self.specs = {s.name: s for s in inventory.specs}
         self.offsets = {}
         off = 0
@@ -173,13 +181,23 @@ class State(dict):
         return self.layout.views(self.arenas["grads"], self.layout.trainable)
 
 
-def initialize_state(parameters, inventory: Inventory) -> State:
-    """Zero-moment FP32 state (adamw.py:300-322); rejects non-finite masters."""
-    layout = Layout(inventory)
+def initialize_state(parameters, inventory: Inventory, *, order=None, grads=None) -> State:
+    """Zero-moment FP32 state (adamw.py:300-322); rejects non-finite masters.
+
+    ``order`` sets the arena order (see Layout); ``grads`` optionally supplies
+    the gradient arena (FP32, at least n_train elements, 16-byte aligned), e.g.
+    a buffer that a collective library also addresses.
+    """
+    layout = Layout(inventory, order)
     if set(parameters) != set(layout.specs):
         raise ValueError("Full-weight parameter tree mismatch")
     arenas = {k: DeviceArray.zeros((max(layout.n_total, 4),), "float32") for k in ("params", "m", "v")}
-    arenas["grads"] = DeviceArray.zeros((max(layout.n_train, 4),), "float32")
+    if grads is not None:
+        if grads.dtype != "float32" or grads.size < layout.n_train or grads.ptr % 16:
+            raise ValueError("gradient arena must be 16-byte aligned float32 with n_train elements")
+        arenas["grads"] = grads
+    else:
+        arenas["grads"] = DeviceArray.zeros((max(layout.n_train, 4),), "float32")
     arenas["step"] = DeviceArray.zeros((1,), "int32")
     for name, value in parameters.items():
         host = np.asarray(value, np.float32)
@@ -244,14 +262,16 @@ def make_transaction(inventory: Inventory, config: AdamWConfig):
     scalars or device scalars; ``divisor`` (device float32) optionally divides
     the gradients first (the logical step's normalization).
     """
-    layout = Layout(inventory)
     workspace = DeviceArray((_lib.lib().mfb_adamw_workspace_size(),), "uint8")
     result_dev = DeviceArray((6,), "int32")
     scalars = {}
 
+    names = set(inventory.names)
+
     def transition(state: State, gradients, active_loss, accumulation_valid, *, divisor=None, stream=None):
-        if not isinstance(state, State) or state.layout.offsets != layout.offsets:
+        if not isinstance(state, State) or set(state.layout.specs) != names:
             raise ValueError("Full-weight state does not match the inventory")
+        layout = state.layout
         if set(gradients) != set(layout.trainable):
             missing = sorted(set(layout.trainable) - set(gradients))
             extra = sorted(set(gradients) - set(layout.trainable))

@@ -168,3 +168,78 @@ def qat_inputs(cfg: QatConfig, seed: int = 0, tokens=None):
     w_d = rng.standard_normal((cfg.hidden, cfg.ffn), dtype=np.float32) * s
     d_y = rng.standard_normal((m, cfg.hidden), dtype=np.float32)
     return x, w_gu, w_d, d_y
+
+
+# ---- config 5: data-parallel encoder training step -------------------------------
+ENCODER_LAYERS = ("conv", "conv", "full_attention", "conv", "conv", "full_attention", "conv", "conv",
+                  "full_attention", "conv", "full_attention", "conv", "full_attention", "conv", "full_attention",
+                  "conv")  # tests/models/lfm2_5/fixtures/encoder_config.json layer_types
+
+
+@dataclass(frozen=True)
+class EncoderStepConfig:
+    name: str = "cfg5-encoder-dp-qat-train-step"
+    global_batch: int = 32
+    length: int = 2048
+    hidden: int = 1024
+    ffn: int = 6656
+    heads: int = 16
+    kv_heads: int = 8
+    head_dim: int = 64
+    layer_types: tuple = ENCODER_LAYERS
+    vocab: int = 65536
+    classes: int = 2
+    norm_eps: float = 1e-5
+    rope_theta: float = 1e6
+    quant: str = "int8-channel-absmax-v1"
+    learning_rate: float = 3e-4
+    beta1: float = 0.9
+    beta2: float = 0.95
+    weight_decay: float = 0.1
+    epsilon: float = 1e-8
+    clip_norm: float = 1.0
+
+
+CONFIG5 = EncoderStepConfig()
+
+
+def encoder_batch(cfg: EncoderStepConfig, seed: int, rows=None, row0: int = 0):
+    """Synthetic packed batch rows [row0, row0 + rows) of the global batch of step ``seed``.
+
+    Returns int32 arrays [rows, T]: token ids ~ U[0, vocab), attention mask
+    (segment != 0), segment ids (config-2 packing), per-segment positions and
+    class labels ~ U[0, classes).
+    """
+    rows = cfg.global_batch if rows is None else rows
+    seg = packed_segments(seed, cfg.global_batch, cfg.length)[row0:row0 + rows]
+    rng = np.random.default_rng(seed + 1_000_003)
+    ids = rng.integers(0, cfg.vocab, (cfg.global_batch, cfg.length)).astype(np.int32)[row0:row0 + rows]
+    labels = rng.integers(0, cfg.classes, (cfg.global_batch, cfg.length)).astype(np.int32)[row0:row0 + rows]
+    mask = (seg != 0).astype(np.int32)
+    pos = np.zeros_like(seg)
+    for r in range(rows):
+        start = 0
+        for t in range(1, cfg.length + 1):
+            if t == cfg.length or seg[r, t] != seg[r, start]:
+                pos[r, start:t] = np.arange(t - start)
+                start = t
+    pos[seg == 0] = 0
+    return ids, mask, seg.astype(np.int32), pos.astype(np.int32), labels
+
+
+def encoder_matmul_params(cfg: EncoderStepConfig) -> int:
+    """Parameters that take part in a matrix product per token (the head excluded)."""
+    c, f, kv = cfg.hidden, cfg.ffn, cfg.kv_heads * cfg.head_dim
+    n = 0
+    for kind in cfg.layer_types:
+        n += 3 * c * f
+        n += (3 * c * c + c * c) if kind == "conv" else (c * c + 2 * kv * c + c * c)
+    return n
+
+
+def encoder_step_flops(cfg: EncoderStepConfig, segment_ids) -> float:
+    """6 * matmul params * tokens + attention fwd+bwd (3.5 x 4 H D sum L^2 per attention layer)."""
+    tokens = segment_ids.size
+    attn = sum(1 for k in cfg.layer_types if k != "conv") * 3.5 * 4 * cfg.heads * cfg.head_dim * \
+        segment_square_sum(segment_ids)
+    return 6.0 * encoder_matmul_params(cfg) * tokens + attn

@@ -1,0 +1,80 @@
+"""Host logic of the data-parallel encoder step, on the CPU.
+
+The allreduce plan must partition the gradient buffer (plus the loss/count
+tail) exactly once, and the bucket-wise SUM allreduce must equal a plain
+full allreduce -- checked with two gloo ranks (engine/step.py:62 psums the
+loss, count and gradient tree together).
+"""
+
+import dataclasses
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from minifield_training_b200 import workloads
+from minifield_training_b200.models import encoder as me
+from minifield_training_b200.optimizers import adamw
+
+TINY = dataclasses.replace(workloads.CONFIG5, global_batch=2, length=128, ffn=256,
+                           layer_types=("conv", "full_attention", "conv"), vocab=1000)
+
+
+@pytest.mark.parametrize("cfg", [workloads.CONFIG5, TINY], ids=["config5", "tiny"])
+def test_plan_partitions_the_gradient_buffer(cfg):
+    layout = adamw.Layout(me.inventory(cfg), me.arena_order(cfg))
+    total = layout.n_train + 4
+    plan = me.reduction_plan(layout, len(cfg.layer_types), total)
+    cover = np.zeros(total, np.int32)
+    for _, _, lo, hi in plan:
+        cover[lo:hi] += 1
+    assert (cover == 1).all()
+    layers = [p for p in plan if p[0] == "layer"]
+    assert [p[1] for p in layers] == list(reversed(range(len(cfg.layer_types))))
+    # Fused groups are adjacent in the arena: gate|up and q|k|v.
+    for i, kind in enumerate(cfg.layer_types):
+        p = f"lfm2.layers.{i}."
+        assert layout.offsets[p + "feed_forward.w3.weight"] == layout.offsets[p + "feed_forward.w1.weight"] + \
+            layout.size(p + "feed_forward.w1.weight")
+        if kind != "conv":
+            q, k, v = (p + f"self_attn.{n}_proj.weight" for n in "qkv")
+            assert layout.offsets[k] == layout.offsets[q] + layout.size(q)
+            assert layout.offsets[v] == layout.offsets[k] + layout.size(k)
+
+
+def test_matmul_parameter_count_matches_the_published_figure():
+    assert workloads.encoder_matmul_params(workloads.CONFIG5) == 387_973_120
+
+
+def _worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    layout = adamw.Layout(me.inventory(TINY), me.arena_order(TINY))
+    total = layout.n_train + 4
+    plan = me.reduction_plan(layout, len(TINY.layer_types), total)
+    g = torch.Generator().manual_seed(rank)
+    flat = torch.randn(total, generator=g)
+    expected = flat.clone()
+    dist.all_reduce(expected)
+    red = me.BucketReducer(flat, plan, None)
+    for i in reversed(range(len(TINY.layer_types))):
+        red.layer_done(i)
+    red.finish()
+    out[rank] = float((flat - expected).abs().max())
+    dist.destroy_process_group()
+
+
+def test_bucketed_allreduce_equals_full_allreduce_on_two_gloo_ranks():
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    port = 29400 + os.getpid() % 500
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    assert out[0] == 0.0 and out[1] == 0.0
