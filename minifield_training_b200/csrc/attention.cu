@@ -1029,8 +1029,12 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       const int j = entry & 0xFFFF;
       const bool full = (entry >> 30) & 1;
       const int st = it % TF_ST;
-      if (!(ok = tc::mbar_wait(s_full(g), it & 1, status, 18))) break;
-      if (!(ok = tc::mbar_wait(kv_full(st), (it / TF_ST) & 1, status, 19))) break;
+      // Wait outcomes are made warp-uniform: the TMEM accesses below are
+      // warp-collective.
+      ok = tc::mbar_wait(s_full(g), it & 1, status, 18);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      ok = tc::mbar_wait(kv_full(st), (it / TF_ST) & 1, status, 19);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
       tc::tc_fence_after();
       const int s0 = j * TK;
       uint32_t x[TK];
@@ -1090,23 +1094,25 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         }
       }
       const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
-      if (mx > M + 8.f) {
-        // Move the reference max; rescale this row's O accumulator (its
-        // column 64 is the row sum) once the previous products have landed.
-        if (it > 0 && M != -INFINITY) {
-          const float sc = ex2(M - mx);
+      // Lazy rescale: a row whose max rose by more than 2^8 moves its
+      // reference max and rescales its O accumulator (column 64 holds the row
+      // sum); the previous products have landed (s_full follows them).
+      // tcgen05.ld/st are warp-collective, so the warp rescales together when
+      // any of its rows moves; the other rows scale by exactly 1.
+      const bool up = mx > M + 8.f;
+      if (it > 0 && __any_sync(0xffffffffu, up && M != -INFINITY)) {
+        const float sc = (up && M != -INFINITY) ? ex2(M - mx) : 1.f;
 #pragma unroll
-          for (int c = 0; c < TF_ON / 16; ++c) {
-            uint32_t v[16];
-            tc::tmem_ld_32x32b_x16(o_t + c * 16, v);
-            tc::tmem_ld_wait();
+        for (int c = 0; c < TF_ON / 16; ++c) {
+          uint32_t v[16];
+          tc::tmem_ld_32x32b_x16(o_t + c * 16, v);
+          tc::tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * sc);
-            tc::tmem_st_32x32b_x16(o_t + c * 16, v);
-          }
+          for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * sc);
+          tc::tmem_st_32x32b_x16(o_t + c * 16, v);
         }
-        M = mx;
       }
+      if (up) M = mx;
       const float nmu = M == -INFINITY ? 0.f : -M;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -1127,7 +1133,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     float l = 0.f;
 #pragma unroll
     for (int i = 0; i < 64; ++i) ou[i] = 0u;
-    if (ok && it > 0 && tc::mbar_wait(o_full(g), 0, status, 20)) {
+    const bool o_ready = ok && it > 0 && tc::mbar_wait(o_full(g), 0, status, 20);
+    if (__all_sync(0xffffffffu, o_ready)) {
       tc::tc_fence_after();
       uint32_t lv[16];
       tc::tmem_ld_32x32b_x32(o_t, ou);
@@ -1464,8 +1471,13 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       const int entry = list[1 + it % nlive];
       const int q0 = (entry & 0xFFFF) * TQ;
       const bool full = (entry >> 30) & 1;
-      if (!(ok = tc::mbar_wait(s_full(u), (j >> 1) & 1, status, 36))) break;
-      if (hf == 0 && !(ok = tc::mbar_wait(qd_full(st), (it / TB_ST) & 1, status, 37))) break;
+      // Warp-uniform wait outcomes: the TMEM accesses below are warp-collective.
+      ok = tc::mbar_wait(s_full(u), (j >> 1) & 1, status, 36);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      if (hf == 0) {
+        ok = tc::mbar_wait(qd_full(st), (it / TB_ST) & 1, status, 37);
+        if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      }
       tc::tc_fence_after();
       const int* cs = cols + st * TB_COL_STRIDE;
       const int cbase = hf * 64 + wh * 32;  // this warp's 32 query columns within the item
@@ -1530,7 +1542,8 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
     }
     // Epilogue: after the last products, dK (times the logit scale) and dV
     // (plus the uniform-row term) for this key row, this warp's 32 columns.
-    if (ok && tc::mbar_wait(done_bar, 0, status, 38)) {
+    const bool done_ok = ok && tc::mbar_wait(done_bar, 0, status, 38);
+    if (__all_sync(0xffffffffu, done_ok)) {
       tc::tc_fence_after();
       uint32_t kv[32], vv[32];
       tc::tmem_ld_32x32b_x32(tmem + lane_off + 320 + wh * 32, kv);
@@ -1567,7 +1580,7 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
     const int r = quarter * 32 + lane;
     const uint32_t dq_t = tmem + ((uint32_t)(quarter * 32) << 16) + 384;
     for (int it = 0; it < nitems; ++it) {
-      if (!tc::mbar_wait(dq_full, it & 1, status, 40)) break;
+      if (!__all_sync(0xffffffffu, tc::mbar_wait(dq_full, it & 1, status, 40))) break;
       tc::tc_fence_after();
       const int h = hk * p.G + it / nlive;
       const int q = (list[1 + it % nlive] & 0xFFFF) * TQ + r;

@@ -244,3 +244,30 @@ def test_config2_segment_bidirectional_full_batch_rows_checked():
     out, grads = oracle_attention(q[rows], k[rows], v[rows], sub, do[rows], dtype=np.float32)
     got = {key: r[key][rows] for key in ("out", "dq", "dk", "dv")}
     _check(got, out, grads, "config2")
+
+
+def test_rows_of_one_warp_that_rescale_differently():
+    """The forward's lazy rescale must stay warp-collective when rows diverge.
+
+    Keys of the first 128-key tile score 0 for every query; keys of the later
+    tiles score about 50 (> 2^8 in the log2 domain after the 1/8 scale) for
+    even query rows only, so in every warp half the rows move their reference
+    max after the first tile and half do not.
+    """
+    rng = np.random.default_rng(11)
+    t, d = 512, 64
+    u = np.zeros(d, np.float32)
+    u[0] = np.sqrt(50.0)
+    q = np.zeros((1, t, 2, d), np.float32)
+    q[0, 0::2, :, :] = u
+    q[0, 1::2, :, 1] = np.sqrt(50.0)  # orthogonal to every key
+    k = np.zeros((1, t, 1, d), np.float32)
+    k[0, 128:, 0, :] = u
+    k += rng.standard_normal(k.shape).astype(np.float32) * 0.01
+    v = rng.standard_normal((1, t, 1, d)).astype(np.float32)
+    do = rng.standard_normal((1, t, 2, d)).astype(np.float32)
+    mask = np.ones((1, t), np.int32)
+    r = gpu_attention(BIDIR, q, k, v, do, mask=mask)
+    ids = oatt.bidirectional_ids(mask, None)
+    out, grads = oracle_attention(q, k, v, ids, do)
+    _check(r, out, grads, "divergent rescale")
