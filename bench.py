@@ -8,12 +8,16 @@ A step = one forward + backward over the batch through the C ABI
 (ids -> forward -> backward). ``value`` = algorithmic TFLOP/s (4*H*D per valid
 query/key pair forward, x3.5 forward+backward) over all ranks. Secondary
 measurements in the same line: KV-cached decode over 6 layers (config 3,
-tokens/s and HBM GB/s) and the QAT SwiGLU FFN forward+backward (config 4,
-tokens/s and TFLOP/s).
+tokens/s and HBM GB/s), the QAT SwiGLU FFN forward+backward (config 4,
+tokens/s and TFLOP/s) and the data-parallel encoder training step (config 5:
+16-layer QAT encoder forward+backward, gradient allreduce, AdamW commit;
+tokens/s of the fixed global batch of 32 x 2048).
 
-Multi-GPU: one process per GPU (torchrun); every rank runs its own copy of the
-workload (weak scaling, no collective on the data path); timing is the max
-over ranks of CUDA-event time between barriers.
+Multi-GPU: one process per GPU (torchrun). Configs 2-4 run one copy per rank
+(weak scaling, no collective on their data path). Config 5 splits the global
+batch's rows over the ranks (strong scaling) and all-reduces the gradient sums
+over NCCL, bucket by bucket during the backward. Timing is the max over ranks
+of CUDA-event time between barriers.
 
 ``--impl reference`` times the reference algorithm's CPU restatement (the
 NumPy oracle; the reference itself is JAX, which is not installed on these
@@ -47,7 +51,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-secondary", action="store_true", help="skip the decode / QAT secondary measurements")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["attention", "decode", "qat"], default=None,
+    ap.add_argument("--only", choices=["attention", "decode", "qat", "encoder"], default=None,
                     help="run one workload (profiling); the JSON line then carries only its numbers")
     return ap.parse_args()
 
@@ -70,6 +74,17 @@ class Dist:
 
             dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
             self.pg = dist
+
+    def nccl_group(self):
+        """A NCCL group over all ranks for the gradient allreduce (None on one GPU)."""
+        if not self.pg:
+            return None
+        if getattr(self, "_nccl", None) is None:
+            import torch
+
+            torch.cuda.set_device(self.local)
+            self._nccl = self.pg.new_group(backend="nccl")
+        return self._nccl
 
     def barrier(self):
         if self.pg:
@@ -369,6 +384,69 @@ class QatWorkload:
 # ---------------------------------------------------------------------------
 
 
+class EncoderStepWorkload:
+    """Config 5: one data-parallel QAT encoder training step over this rank's rows."""
+
+    def __init__(self, dist):
+        from minifield_training_b200 import workloads
+        from minifield_training_b200.device import HostBuffer
+        from minifield_training_b200.models import encoder as me
+
+        cfg = workloads.CONFIG5
+        if cfg.global_batch % dist.world:
+            raise ValueError("the global batch must split evenly over the ranks")
+        self.cfg, self.rows = cfg, cfg.global_batch // dist.world
+        self.model = me.EncoderStep(cfg, rows=self.rows, seed=0, group=dist.nccl_group())
+        self.batch = workloads.encoder_batch(cfg, 0, rows=self.rows, row0=dist.rank * self.rows)
+        self.model.set_batch(*self.batch)
+        full_seg = workloads.packed_segments(0, cfg.global_batch, cfg.length)
+        self.global_flops = workloads.encoder_step_flops(cfg, full_seg)
+        self.tokens = cfg.global_batch * cfg.length
+        # Pinned host copies of the step inputs for the end-to-end leg.
+        self.host = [HostBuffer(a.shape, np.int32) for a in self.batch]
+        for h, a in zip(self.host, self.batch):
+            h.array[...] = a
+        self.h2d_bytes = sum(a.nbytes for a in self.batch)
+        self.d2h_bytes = 24  # the commit result: code, committed, loss and three norms
+
+    def step(self):
+        self.model.step()
+
+    def e2e_step(self):
+        from minifield_training_b200.device import h2d
+
+        m = self.model
+        for dst, h in zip((m.ids, m.mask, m.seg, m.pos, m.labels), self.host):
+            h2d(dst, h.ptr, h.array.nbytes)
+        m._build_ids()
+        res = m.step()
+        res.loss  # device -> host read of the step result (synchronizes)
+
+    launches_per_step = None  # counted from the C-ABI calls (see count_launches)
+
+    def count_launches(self):
+        """Kernel launches of one step, counted by wrapping the C-ABI entry points once."""
+        from minifield_training_b200 import _lib
+
+        per_call = {"mfb_fakequant": 1, "mfb_cast_f32_bf16": 1, "mfb_embed_gather": 1, "mfb_rmsnorm_fwd": 1,
+                    "mfb_rmsnorm_bwd": 2, "mfb_gemm_bf16": 1, "mfb_conv_fwd": 1, "mfb_conv_bwd": 2,
+                    "mfb_swiglu_fwd": 1, "mfb_swiglu_bwd": 1, "mfb_qknorm_rope_fwd": 1, "mfb_qknorm_rope_bwd": 3,
+                    "mfb_attn_fwd": 2, "mfb_attn_bwd": 4, "mfb_head_loss": 3, "mfb_step_normalize": 1,
+                    "mfb_adamw_commit": 3}
+        orig, count = _lib.call, [0]
+
+        def counting(name, *a):
+            count[0] += per_call.get(name, 0)
+            return orig(name, *a)
+
+        _lib.call = counting
+        try:
+            self.model.step()
+        finally:
+            _lib.call = orig
+        return count[0]
+
+
 def cpu_attention_sample(rows=2):
     """Time the oracle's FP32 forward+backward on ``rows`` rows of config 2."""
     from minifield_training_b200 import workloads
@@ -511,6 +589,26 @@ def run_ours(args, dist):
             "tflops": qat.flops / (qms * 1e-3) / 1e12, "tensor_frac": qat.flops / (qms * 1e-3) / 1e12 / tf_sus,
             "peak_tflops": tf_sus, "peak_source": f"{peak_kind} bf16 sustained"}
         del qat
+    if only in (None, "encoder") and not (only is None and args.no_secondary):
+        enc = EncoderStepWorkload(dist)
+        esteps = max(3, args.steps // 5)
+        per_step = enc.count_launches()
+        ems, _ = measure(dist, enc.step, esteps, max(3, args.warmup // 2))
+        launches += per_step * esteps
+        e2e_ms, _ = measure(dist, enc.e2e_step, max(3, esteps // 2), 1)
+        res = enc.model.result
+        tflops = enc.global_flops / (ems * 1e-3) / 1e12
+        secondary["encoder_step"] = {
+            "workload": workloads.CONFIG5.name, "tokens_per_s": enc.tokens / (ems * 1e-3), "ms_per_step": ems,
+            "global_batch": workloads.CONFIG5.global_batch, "seq_len": workloads.CONFIG5.length,
+            "rows_per_gpu": enc.rows, "scaling": "strong", "tflops": tflops,
+            "tensor_frac_per_gpu": tflops / n / tf_sus, "peak_tflops": tf_sus,
+            "peak_source": f"{peak_kind} bf16 sustained", "flops_per_step": enc.global_flops,
+            "quant": workloads.CONFIG5.quant, "committed": res.committed, "loss": res.loss,
+            "launches_per_step": per_step,
+            "e2e": {"tokens_per_s": enc.tokens / (e2e_ms * 1e-3), "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": enc.h2d_bytes * n, "d2h_bytes_per_step": enc.d2h_bytes * n}}
+        del enc
     line["clocks"] = clocks.stop()
 
     if dist.rank == 0 and not args.no_cpu_baseline and only in (None, "attention"):

@@ -187,6 +187,10 @@ class EncoderStep:
         inv = inventory(cfg)
         self.layout = adamw.Layout(inv, arena_order(cfg))
         n_grad = self.layout.n_train + 4  # tail: loss sum, count
+        if torch_grads is None and group is not None:
+            # The collective library addresses the gradient buffer as a tensor.
+            import torch
+            torch_grads = torch.zeros(n_grad, dtype=torch.float32, device=f"cuda:{torch.cuda.current_device()}")
         if torch_grads is not None:
             grads = DeviceArray((n_grad,), "float32", ptr=torch_grads.data_ptr(), owner=False)
             grads._base = torch_grads

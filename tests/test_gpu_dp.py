@@ -1,0 +1,98 @@
+"""Data-parallel encoder step on two GPUs against one GPU (needs >= 2 GPUs; skipped otherwise).
+
+Two NCCL ranks each take one row of a two-row batch; after the bucketed
+allreduce their gradient sums, loss sum and count must equal a single GPU's
+over both rows (up to FP32 summation order: rel-L2 1e-4 per leaf), and after
+the AdamW commit both ranks must hold bit-identical masters (replicated state,
+engine/step.py:62 and the data-parallel known answers' replication checks).
+Ranks run as child processes; NCCL's NVLS is off, as for every multi-rank
+test on this pool.
+"""
+
+import dataclasses
+import os
+
+import numpy as np
+import pytest
+
+from tests.gpu_env import require_gpu
+
+pytestmark = pytest.mark.gpu
+
+
+def _cfg():
+    from minifield_training_b200 import workloads
+    return dataclasses.replace(workloads.CONFIG5, global_batch=2, length=128, ffn=256,
+                               layer_types=("conv", "full_attention"), vocab=1000)
+
+
+def _rank(rank, port, out):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    from minifield_training_b200 import device, workloads
+    from minifield_training_b200.models import encoder as me
+    device.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=120))
+    cfg = _cfg()
+    step = me.EncoderStep(cfg, rows=1, seed=0, group=dist.group.WORLD)
+    step.set_batch(*workloads.encoder_batch(cfg, 7, rows=1, row0=rank))
+    step.quantize()
+    step.forward()
+    red = me.BucketReducer(step.grads._base, step._buckets, step.group)
+    step.backward(red.layer_done)
+    red.finish()
+    torch.cuda.synchronize()
+    grads = {n: v.numpy() for n, v in step.gviews.items()}
+    lc = step.loss_count.numpy()
+    step._commit()
+    committed = step.result.committed
+    params = {n: v.numpy() for n, v in step.params.items() if n != "lfm2.embed_tokens.weight"}
+    out[rank] = (grads, lc, committed, params)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_rank_step_matches_one_gpu():
+    require_gpu()
+    from minifield_training_b200 import device
+    if device.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    port = 29600 + os.getpid() % 300
+    procs = [ctx.Process(target=_rank, args=(r, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+        assert p.exitcode == 0
+    # One GPU over both rows.
+    from minifield_training_b200 import workloads
+    from minifield_training_b200.device import sync
+    from minifield_training_b200.models import encoder as me
+    cfg = _cfg()
+    ref = me.EncoderStep(cfg, rows=2, seed=0)
+    ref.set_batch(*workloads.encoder_batch(cfg, 7))
+    ref.quantize()
+    ref.forward()
+    ref.backward()
+    sync()
+    g0, lc0, c0, p0 = out[0]
+    g1, lc1, c1, p1 = out[1]
+    np.testing.assert_allclose(lc0, ref.loss_count.numpy(), rtol=1e-4)
+    np.testing.assert_array_equal(lc0, lc1)
+    for name, v in ref.gviews.items():
+        r = v.numpy().astype(np.float64)
+        np.testing.assert_array_equal(g0[name], g1[name])
+        err = np.linalg.norm(g0[name] - r) / max(np.linalg.norm(r), 1e-30)
+        assert err < 1e-4, (name, err)
+    assert c0 and c1
+    for name in p0:
+        np.testing.assert_array_equal(p0[name], p1[name])
