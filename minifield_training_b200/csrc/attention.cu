@@ -9,19 +9,22 @@
 // Layout in HBM (the reference's "bthd" arrays): q/o/dq [B,T,H,D],
 // k/v/dk/dv [B,S,Hk,D] bf16; lse [B,H,T] f32 (log2 domain).
 //
-// Work decomposition: 64x64 (query x key) tiles. Per-64-block id ranges
-// (min/max of nonzero ids, "uniform" flag) are built once per call so tile
-// pairs without any shared id -- and, when causal, pairs entirely above the
-// diagonal -- are skipped before any load ("splash"-style block sparsity).
-// Tiles whose ids are uniform and equal skip the per-element mask.
+// Work decomposition: per-64-block id ranges (min/max of nonzero ids,
+// "uniform" flag) are built once per call; the tensor-core kernels combine
+// them into 128 x 128 (query x key) tile tests, so tile pairs without any
+// shared id -- and, when causal, pairs entirely above the diagonal -- are
+// skipped before any load ("splash"-style block sparsity), and tiles whose ids
+// are uniform and equal skip the per-element mask.
 //
-// Forward: CTA = (query block, 2 query heads of one KV head, batch); the two
-// heads share each K/V tile (GQA reuse), 8 warps x 16 query rows, online
-// softmax in FP32 with exp2, P rounded to bf16 for the PV product (the
-// reference casts probabilities to the query dtype, attention.py:31).
-// Backward: CTA = (key block, KV head, batch); loops over the group's query
-// heads and live query blocks, keeps dK/dV in registers (no atomics for the
-// GQA reduction), and accumulates dQ in FP32 with atomics into the workspace.
+// Forward (attn_fwd_tc_kernel): CTA = (128 query rows, the two query heads of
+// one KV head, batch row); the heads share every K/V tile (GQA reuse); S, P and
+// O live in TMEM (tcgen05), the softmax is FP32 with exp2 and P is rounded to
+// bf16 for the PV product (the reference casts probabilities to the query
+// dtype, attention.py:31).
+// Backward (attn_bwd_tc_kernel): CTA = (128 key rows, KV head, batch row);
+// loops over the group's query heads and live query tiles, accumulates dK/dV
+// in TMEM (no atomics for the GQA reduction) and dQ in FP32 with vector atomics
+// into the workspace.
 #include <math.h>
 
 #include "common.cuh"
@@ -154,281 +157,6 @@ __global__ void ranges_kernel(const int* __restrict__ qid, const int* __restrict
   }
 }
 
-__device__ __forceinline__ bool tile_live(const Params& p, const Range& qr, const Range& kr, int q0, int s0) {
-  if (p.causal) {
-    const int tmax = min(q0 + BQ - 1, p.T - 1);
-    if (s0 > tmax + p.offset) return false;
-  }
-  return max(qr.lo, kr.lo) <= min(qr.hi, kr.hi);
-}
-
-__device__ __forceinline__ bool tile_full(const Params& p, const Range& qr, const Range& kr, int q0, int s0) {
-  if (!qr.full || !kr.full || qr.lo != kr.lo) return false;
-  if (p.causal && s0 + BK - 1 > q0 + p.offset) return false;
-  return true;
-}
-
-// Loads a 64 x 64 bf16 tile (rows strided by row_stride elements) into a
-// swizzled shared buffer; rows >= nrows are zero-filled.
-template <int NT>
-__device__ __forceinline__ void load_tile(uint32_t sbuf, const __nv_bfloat16* g, long long row_stride, int nrows,
-                                          int tid) {
-#pragma unroll
-  for (int i = 0; i < (64 * 8) / NT; ++i) {
-    const int c = tid + i * NT;
-    const int row = c >> 3, ch = c & 7;
-    const bool ok = row < nrows;
-    const __nv_bfloat16* src = g + (ok ? (long long)row * row_stride : 0) + ch * 8;
-    cp_async_16(sbuf + swz64(row, ch * 8), src, ok);
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Forward.
-// ---------------------------------------------------------------------------
-constexpr int FWD_HPB = 2;  // query heads per CTA (sharing one KV head)
-constexpr int FWD_THREADS = 128 * FWD_HPB;
-constexpr int FWD_SMEM = FWD_HPB * 8192 + 4 * 8192 + 2 * 64 * 4 + 1024;
-
-__global__ void __launch_bounds__(FWD_THREADS) attn_fwd_kernel(Params p) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // Offset from the __shared__ array itself so accesses keep the shared state space.
-  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  const uint32_t sQ = smem_u32(smem);
-  const uint32_t sK = sQ + FWD_HPB * 8192;
-  const uint32_t sV = sK + 2 * 8192;
-  int* sKid = reinterpret_cast<int*>(smem + FWD_HPB * 8192 + 4 * 8192);  // [2][64]
-
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int qb = blockIdx.x, b = blockIdx.z;
-  const int h0 = blockIdx.y * FWD_HPB;
-  const int hk = h0 / p.G;
-  const int q0 = qb * BQ;
-  const int hh = warp >> 2, r0 = (warp & 3) * 16;
-  const int h = h0 + hh;
-  const Range qrange = p.qr[(long long)b * p.nqb + qb];
-
-  // Query tile for both heads.
-  {
-    const int nrows = min(BQ, p.T - q0);
-#pragma unroll
-    for (int i = 0; i < FWD_HPB * 512 / FWD_THREADS; ++i) {
-      const int c = tid + i * FWD_THREADS;
-      const int head = c >> 9, row = (c >> 3) & 63, ch = c & 7;
-      const bool ok = row < nrows;
-      const __nv_bfloat16* src = p.q + (((long long)b * p.T + q0 + (ok ? row : 0)) * p.H + h0 + head) * HD + ch * 8;
-      cp_async_16(sQ + head * 8192 + swz64(row, ch * 8), src, ok);
-    }
-    cp_async_commit();
-  }
-
-  const long long kv_stride = (long long)p.Hk * HD;
-  const __nv_bfloat16* kbase = p.k + ((long long)b * p.S * p.Hk + hk) * HD;
-  const __nv_bfloat16* vbase = p.v + ((long long)b * p.S * p.Hk + hk) * HD;
-  const Range* krs = p.kr + (long long)b * p.nkb;
-
-  auto next_live = [&](int j) {
-    for (; j < p.nkb; ++j) {
-      if (tile_live(p, qrange, krs[j], q0, j * BK)) return j;
-      if (p.causal && j * BK > min(q0 + BQ - 1, p.T - 1) + p.offset) return p.nkb;
-    }
-    return p.nkb;
-  };
-  auto issue_kv = [&](int j, int buf) {
-    const int s0 = j * BK;
-    const int nrows = min(BK, p.S - s0);
-    load_tile<FWD_THREADS>(sK + buf * 8192, kbase + s0 * kv_stride, kv_stride, nrows, tid);
-    load_tile<FWD_THREADS>(sV + buf * 8192, vbase + s0 * kv_stride, kv_stride, nrows, tid);
-    if (tid < 64) sKid[buf * 64 + tid] = (s0 + tid < p.S) ? p.kid[(long long)b * p.S + s0 + tid] : 0;
-    cp_async_commit();
-  };
-
-  int j = next_live(0);
-  if (j < p.nkb) issue_kv(j, 0);
-
-  const int g = lane >> 2, c4 = lane & 3;
-  const int ta = q0 + r0 + g, tb = ta + 8;
-  const int qid_a = ta < p.T ? p.qid[(long long)b * p.T + ta] : 0;
-  const int qid_b = tb < p.T ? p.qid[(long long)b * p.T + tb] : 0;
-
-  // Wait for Q (oldest group), load its fragments into registers.
-  if (j < p.nkb)
-    cp_async_wait<1>();
-  else
-    cp_async_wait<0>();
-  __syncthreads();
-  uint32_t qf[4][4];
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk)
-    ldmatrix_x4(sQ + hh * 8192 + swz64(r0 + (lane & 15), kk * 16 + (lane >> 4) * 8), qf[kk][0], qf[kk][1],
-                qf[kk][2], qf[kk][3]);
-
-  float oacc[8][4];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
-  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
-
-  int buf = 0;
-  while (j < p.nkb) {
-    const int jn = next_live(j + 1);
-    if (jn < p.nkb) {
-      issue_kv(jn, buf ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    const int s0 = j * BK;
-    const uint32_t kt = sK + buf * 8192, vt = sV + buf * 8192;
-
-    float sacc[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) sacc[i][0] = sacc[i][1] = sacc[i][2] = sacc[i][3] = 0.f;
-#pragma unroll
-    for (int nt2 = 0; nt2 < 4; ++nt2) {
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(kt + swz64(nt2 * 16 + (lane & 7) + ((lane >> 4) << 3), kk * 16 + ((lane >> 3) & 1) * 8), b0, b1,
-                    b2, b3);
-        const uint32_t bb0[2] = {b0, b1}, bb1[2] = {b2, b3};
-        mma_bf16_16816(sacc[2 * nt2], qf[kk], bb0);
-        mma_bf16_16816(sacc[2 * nt2 + 1], qf[kk], bb1);
-      }
-    }
-
-    if (!tile_full(p, qrange, krs[j], q0, s0)) {
-      const int* kidt = sKid + buf * 64;
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int sl = nt * 8 + 2 * c4 + (e & 1);
-          const int s = s0 + sl;
-          const int t = e < 2 ? ta : tb;
-          const int qv = e < 2 ? qid_a : qid_b;
-          const bool ok = qv != 0 && qv == kidt[sl] && (!p.causal || s <= t + p.offset);
-          if (!ok) sacc[nt][e] = -INFINITY;
-        }
-      }
-    }
-
-    float mx_a = -INFINITY, mx_b = -INFINITY;
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      mx_a = fmaxf(mx_a, fmaxf(sacc[nt][0], sacc[nt][1]));
-      mx_b = fmaxf(mx_b, fmaxf(sacc[nt][2], sacc[nt][3]));
-    }
-    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
-    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
-    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
-    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
-    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
-    const float mu_a = mn_a == -INFINITY ? 0.f : mn_a * p.scale_log2;
-    const float mu_b = mn_b == -INFINITY ? 0.f : mn_b * p.scale_log2;
-    const float al_a = ex2(m_a * p.scale_log2 - mu_a), al_b = ex2(m_b * p.scale_log2 - mu_b);
-    m_a = mn_a;
-    m_b = mn_b;
-    float rs_a = 0.f, rs_b = 0.f;
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      sacc[nt][0] = ex2(sacc[nt][0] * p.scale_log2 - mu_a);
-      sacc[nt][1] = ex2(sacc[nt][1] * p.scale_log2 - mu_a);
-      sacc[nt][2] = ex2(sacc[nt][2] * p.scale_log2 - mu_b);
-      sacc[nt][3] = ex2(sacc[nt][3] * p.scale_log2 - mu_b);
-      rs_a += sacc[nt][0] + sacc[nt][1];
-      rs_b += sacc[nt][2] + sacc[nt][3];
-    }
-    l_a = l_a * al_a + rs_a;
-    l_b = l_b * al_b + rs_b;
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      oacc[nt][0] *= al_a;
-      oacc[nt][1] *= al_a;
-      oacc[nt][2] *= al_b;
-      oacc[nt][3] *= al_b;
-    }
-
-#pragma unroll
-    for (int kk2 = 0; kk2 < 4; ++kk2) {
-      uint32_t pa[4];
-      pa[0] = pack_bf16(sacc[2 * kk2][0], sacc[2 * kk2][1]);
-      pa[1] = pack_bf16(sacc[2 * kk2][2], sacc[2 * kk2][3]);
-      pa[2] = pack_bf16(sacc[2 * kk2 + 1][0], sacc[2 * kk2 + 1][1]);
-      pa[3] = pack_bf16(sacc[2 * kk2 + 1][2], sacc[2 * kk2 + 1][3]);
-#pragma unroll
-      for (int nd2 = 0; nd2 < 4; ++nd2) {
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4_trans(vt + swz64(kk2 * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, nd2 * 16 + (lane >> 4) * 8), b0,
-                          b1, b2, b3);
-        const uint32_t bb0[2] = {b0, b1}, bb1[2] = {b2, b3};
-        mma_bf16_16816(oacc[2 * nd2], pa, bb0);
-        mma_bf16_16816(oacc[2 * nd2 + 1], pa, bb1);
-      }
-    }
-    __syncthreads();  // buffer `buf` is refilled by the next-next issue
-    buf ^= 1;
-    j = jn;
-  }
-
-  // Epilogue: normalise, handle empty rows, stage through shared memory.
-  l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
-  l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
-  l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
-  l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
-  const bool empty_a = !(l_a > 0.f), empty_b = !(l_b > 0.f);
-  const float inv_a = empty_a ? 0.f : 1.f / l_a, inv_b = empty_b ? 0.f : 1.f / l_b;
-
-  // Rare path: a row with no valid key under the dense finfo.min fill is the
-  // uniform average of all S values of its KV head.
-  float vm0 = 0.f, vm1 = 0.f;
-  const bool need_uniform =
-      p.policy == MFB_EMPTY_UNIFORM && __any_sync(0xffffffffu, (empty_a && ta < p.T) || (empty_b && tb < p.T));
-  if (need_uniform) {
-    for (int s = 0; s < p.S; ++s) {
-      const __nv_bfloat162 x = *reinterpret_cast<const __nv_bfloat162*>(vbase + s * kv_stride + 2 * lane);
-      vm0 += __bfloat162float(x.x);
-      vm1 += __bfloat162float(x.y);
-    }
-    vm0 /= (float)p.S;
-    vm1 /= (float)p.S;
-  }
-
-  const uint32_t so = sQ + hh * 8192;  // Q tile is dead: reuse it for O
-#pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
-    const int d = nt * 8 + 2 * c4;
-    float x0 = oacc[nt][0] * inv_a, x1 = oacc[nt][1] * inv_a;
-    float x2 = oacc[nt][2] * inv_b, x3 = oacc[nt][3] * inv_b;
-    if (need_uniform) {
-      const float u0 = __shfl_sync(0xffffffffu, vm0, d >> 1), u1 = __shfl_sync(0xffffffffu, vm1, d >> 1);
-      if (empty_a) x0 = u0, x1 = u1;
-      if (empty_b) x2 = u0, x3 = u1;
-    }
-    asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(so + swz64(r0 + g, d)), "r"(pack_bf16(x0, x1)));
-    asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(so + swz64(r0 + g + 8, d)), "r"(pack_bf16(x2, x3)));
-  }
-  if (c4 == 0) {
-    float* lrow = p.lse + ((long long)b * p.H + h) * p.T;
-    if (ta < p.T) lrow[ta] = empty_a ? -INFINITY : m_a * p.scale_log2 + __log2f(l_a);
-    if (tb < p.T) lrow[tb] = empty_b ? -INFINITY : m_b * p.scale_log2 + __log2f(l_b);
-  }
-  __syncthreads();
-  const int nrows = min(BQ, p.T - q0);
-#pragma unroll
-  for (int i = 0; i < FWD_HPB * 512 / FWD_THREADS; ++i) {
-    const int c = tid + i * FWD_THREADS;
-    const int head = c >> 9, row = (c >> 3) & 63, ch = c & 7;
-    if (row < nrows) {
-      uint4 val;
-      asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];\n"
-                   : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
-                   : "r"(sQ + head * 8192 + swz64(row, ch * 8)));
-      *reinterpret_cast<uint4*>(p.o + (((long long)b * p.T + q0 + row) * p.H + h0 + head) * HD + ch * 8) = val;
-    }
-  }
-}
-
 // ---------------------------------------------------------------------------
 // Backward.
 // ---------------------------------------------------------------------------
@@ -468,256 +196,6 @@ __global__ void __launch_bounds__(256) attn_bwd_pre_kernel(Params p) {
 #pragma unroll
       for (int i = 0; i < 8; ++i)
         atomicAdd(p.uvec + ((long long)b * p.Hk + hk) * HD + sub * 8 + i, __bfloat162float(a[i]) * inv);
-    }
-  }
-}
-
-constexpr int BWD_THREADS = 128;
-constexpr int BWD_SMEM = 8192 * 7 + 2 * 64 * 4 * 3 + 1024;
-
-__global__ void __launch_bounds__(BWD_THREADS) attn_bwd_main_kernel(Params p) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // Offset from the __shared__ array itself so accesses keep the shared state space.
-  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  const uint32_t sK = smem_u32(smem);
-  const uint32_t sV = sK + 8192;
-  const uint32_t sQ = sK + 2 * 8192;    // [2]
-  const uint32_t sdO = sK + 4 * 8192;   // [2]
-  const uint32_t sdS = sK + 6 * 8192;   // dS^T, [kv][q]
-  float* sLse = reinterpret_cast<float*>(smem + 7 * 8192);  // [2][64]
-  float* sDs = sLse + 128;                                  // [2][64]
-  int* sQid = reinterpret_cast<int*>(sDs + 128);            // [2][64]
-
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int kb = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
-  const int s0 = kb * BK;
-  const long long kv_stride = (long long)p.Hk * HD;
-  const long long q_stride = (long long)p.H * HD;
-  const Range krange = p.kr[(long long)b * p.nkb + kb];
-  const Range* qrs = p.qr + (long long)b * p.nqb;
-  const int g = lane >> 2, c4 = lane & 3;
-
-  {
-    const int nrows = min(BK, p.S - s0);
-    const long long off = ((long long)b * p.S + s0) * kv_stride + (long long)hk * HD;
-    load_tile<BWD_THREADS>(sK, p.k + off, kv_stride, nrows, tid);
-    load_tile<BWD_THREADS>(sV, p.v + off, kv_stride, nrows, tid);
-    cp_async_commit();
-  }
-  // This thread's key rows (C-fragment rows of S^T) and their ids.
-  const int sa = s0 + warp * 16 + g, sb = sa + 8;
-  const int kid_a = sa < p.S ? p.kid[(long long)b * p.S + sa] : 0;
-  const int kid_b = sb < p.S ? p.kid[(long long)b * p.S + sb] : 0;
-
-  const int total = p.G * p.nqb;
-  auto next_live = [&](int it) {
-    for (; it < total; ++it) {
-      const int i = it % p.nqb;
-      if (tile_live(p, qrs[i], krange, i * BQ, s0)) return it;
-    }
-    return total;
-  };
-  auto issue_q = [&](int it, int buf) {
-    const int hh = it / p.nqb, i = it % p.nqb;
-    const int h = hk * p.G + hh;
-    const int q0 = i * BQ;
-    const int nrows = min(BQ, p.T - q0);
-    const long long off = ((long long)b * p.T + q0) * q_stride + (long long)h * HD;
-    load_tile<BWD_THREADS>(sQ + buf * 8192, p.q + off, q_stride, nrows, tid);
-    load_tile<BWD_THREADS>(sdO + buf * 8192, p.d_o + off, q_stride, nrows, tid);
-    if (tid < 64) {
-      const int t = q0 + tid;
-      const long long li = ((long long)b * p.H + h) * p.T + t;
-      const bool ok = t < p.T;
-      sLse[buf * 64 + tid] = ok ? p.lse[li] : -INFINITY;
-      sDs[buf * 64 + tid] = ok ? p.dsum[li] : 0.f;
-      sQid[buf * 64 + tid] = ok ? p.qid[(long long)b * p.T + t] : 0;
-    }
-    cp_async_commit();
-  };
-
-  float dv[8][4], dk[8][4];
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) dv[i][e] = dk[i][e] = 0.f;
-
-  int it = next_live(0);
-  if (it < total) issue_q(it, 0);
-  int buf = 0;
-  while (it < total) {
-    const int itn = next_live(it + 1);
-    if (itn < total) {
-      issue_q(itn, buf ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    const int hh = it / p.nqb, i = it % p.nqb;
-    const int h = hk * p.G + hh;
-    const int q0 = i * BQ;
-    const uint32_t qt = sQ + buf * 8192, dot = sdO + buf * 8192;
-    const float* lse = sLse + buf * 64;
-    const float* dsm = sDs + buf * 64;
-    const int* qidt = sQid + buf * 64;
-    const bool full = tile_full(p, qrs[i], krange, q0, s0);
-
-    // S^T = K Q^T and dP^T = V dO^T (rows: this warp's 16 keys, cols: 64 queries).
-    float st[8][4], dpt[8][4];
-#pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) st[n][e] = dpt[n][e] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      uint32_t ka[4], va[4];
-      ldmatrix_x4(sK + swz64(warp * 16 + (lane & 15), kk * 16 + (lane >> 4) * 8), ka[0], ka[1], ka[2], ka[3]);
-      ldmatrix_x4(sV + swz64(warp * 16 + (lane & 15), kk * 16 + (lane >> 4) * 8), va[0], va[1], va[2], va[3]);
-#pragma unroll
-      for (int nt2 = 0; nt2 < 4; ++nt2) {
-        uint32_t b0, b1, b2, b3;
-        const uint32_t a_off = swz64(nt2 * 16 + (lane & 7) + ((lane >> 4) << 3), kk * 16 + ((lane >> 3) & 1) * 8);
-        ldmatrix_x4(qt + a_off, b0, b1, b2, b3);
-        const uint32_t q0f[2] = {b0, b1}, q1f[2] = {b2, b3};
-        mma_bf16_16816(st[2 * nt2], ka, q0f);
-        mma_bf16_16816(st[2 * nt2 + 1], ka, q1f);
-        ldmatrix_x4(dot + a_off, b0, b1, b2, b3);
-        const uint32_t d0f[2] = {b0, b1}, d1f[2] = {b2, b3};
-        mma_bf16_16816(dpt[2 * nt2], va, d0f);
-        mma_bf16_16816(dpt[2 * nt2 + 1], va, d1f);
-      }
-    }
-
-    // P^T and dS^T.
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int tl = nt * 8 + 2 * c4 + (e & 1);
-        const int t = q0 + tl;
-        const int s = e < 2 ? sa : sb;
-        bool ok = true;
-        if (!full) {
-          const int qv = qidt[tl];
-          ok = qv != 0 && qv == (e < 2 ? kid_a : kid_b) && (!p.causal || s <= t + p.offset);
-        }
-        const float l = lse[tl];
-        const float pv = (ok && l != -INFINITY) ? ex2(st[nt][e] * p.scale_log2 - l) : 0.f;
-        st[nt][e] = pv;
-        dpt[nt][e] = pv * (dpt[nt][e] - dsm[tl]);
-      }
-    }
-
-    // dV += P^T dO ; dK += dS^T Q ; stage dS^T for dQ.
-#pragma unroll
-    for (int kk2 = 0; kk2 < 4; ++kk2) {
-      uint32_t pa[4], da[4];
-      pa[0] = pack_bf16(st[2 * kk2][0], st[2 * kk2][1]);
-      pa[1] = pack_bf16(st[2 * kk2][2], st[2 * kk2][3]);
-      pa[2] = pack_bf16(st[2 * kk2 + 1][0], st[2 * kk2 + 1][1]);
-      pa[3] = pack_bf16(st[2 * kk2 + 1][2], st[2 * kk2 + 1][3]);
-      da[0] = pack_bf16(dpt[2 * kk2][0], dpt[2 * kk2][1]);
-      da[1] = pack_bf16(dpt[2 * kk2][2], dpt[2 * kk2][3]);
-      da[2] = pack_bf16(dpt[2 * kk2 + 1][0], dpt[2 * kk2 + 1][1]);
-      da[3] = pack_bf16(dpt[2 * kk2 + 1][2], dpt[2 * kk2 + 1][3]);
-      asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(sdS + swz64(warp * 16 + g, kk2 * 16 + 2 * c4)), "r"(da[0]));
-      asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(sdS + swz64(warp * 16 + g + 8, kk2 * 16 + 2 * c4)), "r"(da[1]));
-      asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(sdS + swz64(warp * 16 + g, kk2 * 16 + 8 + 2 * c4)), "r"(da[2]));
-      asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(sdS + swz64(warp * 16 + g + 8, kk2 * 16 + 8 + 2 * c4)),
-                   "r"(da[3]));
-#pragma unroll
-      for (int nd2 = 0; nd2 < 4; ++nd2) {
-        uint32_t b0, b1, b2, b3;
-        const uint32_t t_off = swz64(kk2 * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, nd2 * 16 + (lane >> 4) * 8);
-        ldmatrix_x4_trans(dot + t_off, b0, b1, b2, b3);
-        const uint32_t x0[2] = {b0, b1}, x1[2] = {b2, b3};
-        mma_bf16_16816(dv[2 * nd2], pa, x0);
-        mma_bf16_16816(dv[2 * nd2 + 1], pa, x1);
-        ldmatrix_x4_trans(qt + t_off, b0, b1, b2, b3);
-        const uint32_t y0[2] = {b0, b1}, y1[2] = {b2, b3};
-        mma_bf16_16816(dk[2 * nd2], da, y0);
-        mma_bf16_16816(dk[2 * nd2 + 1], da, y1);
-      }
-    }
-    __syncthreads();
-
-    // dQ (this warp: 16 query rows x 64 dims) = dS K.
-    float dq[8][4];
-#pragma unroll
-    for (int n = 0; n < 8; ++n) dq[n][0] = dq[n][1] = dq[n][2] = dq[n][3] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      uint32_t a[4];
-      ldmatrix_x4_trans(sdS + swz64(kk * 16 + (lane & 7) + ((lane >> 4) << 3), warp * 16 + ((lane >> 3) & 1) * 8),
-                        a[0], a[1], a[2], a[3]);
-#pragma unroll
-      for (int nd2 = 0; nd2 < 4; ++nd2) {
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4_trans(sK + swz64(kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, nd2 * 16 + (lane >> 4) * 8), b0,
-                          b1, b2, b3);
-        const uint32_t x0[2] = {b0, b1}, x1[2] = {b2, b3};
-        mma_bf16_16816(dq[2 * nd2], a, x0);
-        mma_bf16_16816(dq[2 * nd2 + 1], a, x1);
-      }
-    }
-    const int ta = q0 + warp * 16 + g, tb = ta + 8;
-    float* dqa = p.dq_acc + (((long long)b * p.T + ta) * p.H + h) * HD;
-    float* dqb = p.dq_acc + (((long long)b * p.T + tb) * p.H + h) * HD;
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      const int d = nt * 8 + 2 * c4;
-      if (ta < p.T) {
-        atomicAdd(dqa + d, dq[nt][0]);
-        atomicAdd(dqa + d + 1, dq[nt][1]);
-      }
-      if (tb < p.T) {
-        atomicAdd(dqb + d, dq[nt][2]);
-        atomicAdd(dqb + d + 1, dq[nt][3]);
-      }
-    }
-    buf ^= 1;
-    it = itn;
-  }
-
-  // Epilogue: dK * scale, dV (+ uniform-row contribution), via shared staging.
-  __syncthreads();
-  float u0[8], u1[8];
-#pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
-    u0[nt] = u1[nt] = 0.f;
-    if (p.policy == MFB_EMPTY_UNIFORM) {
-      const float* uv = p.uvec + ((long long)b * p.Hk + hk) * HD + nt * 8 + 2 * c4;
-      u0[nt] = uv[0];
-      u1[nt] = uv[1];
-    }
-  }
-#pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
-    const int d = nt * 8 + 2 * c4;
-    const int r = warp * 16 + g;
-    asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(sQ + swz64(r, d)),
-                 "r"(pack_bf16(dk[nt][0] * p.scale, dk[nt][1] * p.scale)));
-    asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(sQ + swz64(r + 8, d)),
-                 "r"(pack_bf16(dk[nt][2] * p.scale, dk[nt][3] * p.scale)));
-    asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(sQ + 8192 + swz64(r, d)),
-                 "r"(pack_bf16(dv[nt][0] + u0[nt], dv[nt][1] + u1[nt])));
-    asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(sQ + 8192 + swz64(r + 8, d)),
-                 "r"(pack_bf16(dv[nt][2] + u0[nt], dv[nt][3] + u1[nt])));
-  }
-  __syncthreads();
-  const int nrows = min(BK, p.S - s0);
-#pragma unroll
-  for (int i = 0; i < 2 * 512 / BWD_THREADS; ++i) {
-    const int c = tid + i * BWD_THREADS;
-    const int which = c >> 9, row = (c >> 3) & 63, ch = c & 7;
-    if (row < nrows) {
-      uint4 val;
-      asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];\n"
-                   : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
-                   : "r"(sQ + which * 8192 + swz64(row, ch * 8)));
-      __nv_bfloat16* dst = (which ? p.dv : p.dk) + ((long long)b * p.S + s0 + row) * kv_stride + (long long)hk * HD;
-      *reinterpret_cast<uint4*>(dst + ch * 8) = val;
     }
   }
 }
@@ -764,6 +242,7 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(const float* __restrict
 __device__ int g_tc_status;
 
 constexpr int TQ = 128, TK = 128;
+constexpr int TF_HPB = 2;  // query heads per CTA: the two heads of a GQA pair share K/V
 constexpr int TF_ST = 3;
 constexpr int TF_THREADS = 320;
 constexpr int TF_Q_OFF = 0;
@@ -1644,7 +1123,7 @@ int check_dims(int B, int T, int S, int H, int Hk, int D) {
   MFB_CHECK_ARG(B > 0 && T > 0 && S > 0, "Attention needs nonempty batch/query/key dims (B=%d T=%d S=%d)", B, T, S);
   MFB_CHECK_ARG(H > 0 && Hk > 0 && H % Hk == 0, "Query heads must be divisible by KV heads (H=%d Hk=%d)", H, Hk);
   MFB_CHECK_ARG(D == HD, "head_dim %d unsupported: this build implements D = 64", D);
-  MFB_CHECK_ARG((H / Hk) % FWD_HPB == 0, "GQA group size %d must be a multiple of %d", H / Hk, FWD_HPB);
+  MFB_CHECK_ARG((H / Hk) % TF_HPB == 0, "GQA group size %d must be a multiple of %d", H / Hk, TF_HPB);
   return MFB_OK;
 }
 
