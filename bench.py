@@ -255,7 +255,7 @@ class AttentionWorkload:
         self.fwd()
         self.bwd()
 
-    launches_per_step = 7  # ids, ranges, fwd, ranges, bwd-pre, bwd-main, dq-convert
+    launches_per_step = 9  # ids, ranges, schedule, fwd, ranges, bwd-pre, schedule, bwd-main, dq-convert
 
     def e2e_setup(self):
         from minifield_training_b200.device import HostBuffer
@@ -431,7 +431,7 @@ class EncoderStepWorkload:
         per_call = {"mfb_fakequant": 1, "mfb_cast_f32_bf16": 1, "mfb_embed_gather": 1, "mfb_rmsnorm_fwd": 1,
                     "mfb_rmsnorm_bwd": 2, "mfb_gemm_bf16": 1, "mfb_conv_fwd": 1, "mfb_conv_bwd": 2,
                     "mfb_swiglu_fwd": 1, "mfb_swiglu_bwd": 1, "mfb_qknorm_rope_fwd": 1, "mfb_qknorm_rope_bwd": 3,
-                    "mfb_attn_fwd": 2, "mfb_attn_bwd": 4, "mfb_head_loss": 3, "mfb_step_normalize": 1,
+                    "mfb_attn_fwd": 3, "mfb_attn_bwd": 5, "mfb_head_loss": 3, "mfb_step_normalize": 1,
                     "mfb_adamw_commit": 3}
         orig, count = _lib.call, [0]
 

@@ -61,6 +61,7 @@ struct Params {
   const int* kid;
   const Range* qr;
   const Range* kr;
+  const int* order;  // work items of the tensor-core kernel, longest first
   int B, T, S, H, Hk, G;
   int causal, offset, policy;
   int nqb, nkb;
@@ -310,8 +311,12 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   int* list = reinterpret_cast<int*>(smem + TF_LIST_OFF);  // [0] = count, then tile | full << 30
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x, b = blockIdx.z;
-  const int h0 = blockIdx.y * 2;
+  // Work item (query tile, batch row) from the longest-first order; the head
+  // pairs of one item are adjacent launches (they share K/V tiles in L2).
+  const int hpairs = p.H / TF_HPB;
+  const int item = p.order[blockIdx.x / hpairs];
+  const int qt = item % cdiv(p.T, TQ), b = item / cdiv(p.T, TQ);
+  const int h0 = (blockIdx.x % hpairs) * TF_HPB;
   const int hk = h0 / p.G;
   const int q0 = qt * TQ;
   const int nkt = cdiv(p.S, TK);
@@ -772,7 +777,10 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
   int* list = reinterpret_cast<int*>(smem + TB_LIST_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  // Work item (key tile, batch row) from the longest-first order; the KV heads
+  // of one item are adjacent launches.
+  const int item = p.order[blockIdx.x / p.Hk];
+  const int kt = item % cdiv(p.S, TK), b = item / cdiv(p.S, TK), hk = blockIdx.x % p.Hk;
   const int s0 = kt * TK;
   const int ntq = cdiv(p.T, TQ);
   const Range krange = range128(p.kr + (long long)b * p.nkb, p.nkb, kt);
@@ -1092,6 +1100,7 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
 struct Workspace {
   Range* qr;
   Range* kr;
+  int* order;
   float* dsum;
   float* uvec;
   float* dq_acc;
@@ -1109,6 +1118,8 @@ Workspace carve(void* base, int B, int T, int S, int H, int Hk) {
   off += align256(sizeof(Range) * (size_t)B * nqb);
   w.kr = reinterpret_cast<Range*>(p + off);
   off += align256(sizeof(Range) * (size_t)B * nkb);
+  w.order = reinterpret_cast<int*>(p + off);
+  off += align256(sizeof(int) * (size_t)B * (size_t)max(cdiv(T, TQ), cdiv(S, TK)));
   w.dsum = reinterpret_cast<float*>(p + off);
   off += align256(sizeof(float) * (size_t)B * H * T);
   w.uvec = reinterpret_cast<float*>(p + off);
@@ -1140,6 +1151,7 @@ Params make_params(const Workspace& w, int B, int T, int S, int H, int Hk, int c
   Params p{};
   p.qr = w.qr;
   p.kr = w.kr;
+  p.order = w.order;
   p.dsum = w.dsum;
   p.uvec = w.uvec;
   p.dq_acc = w.dq_acc;
@@ -1157,6 +1169,46 @@ Params make_params(const Workspace& w, int B, int T, int S, int H, int Hk, int c
   p.scale = scale;
   p.scale_log2 = scale * kLog2e;
   return p;
+}
+
+// Longest-first order of the tensor-core kernels' work items (uneven segment
+// lengths make some tiles several times longer than others; launching them
+// first keeps the last wave short). Forward items are (query tile, batch row)
+// weighted by their live key tiles, backward items (key tile, batch row) by
+// their live query tiles -- the same tile test the kernels use. One CTA,
+// counting sort over the tile counts.
+__global__ void __launch_bounds__(1024) schedule_kernel(Params p, int backward, int* order) {
+  __shared__ int hist[TF_MAX_TILES + 1], base[TF_MAX_TILES + 1];
+  const int ntq = cdiv(p.T, TQ), nkt = cdiv(p.S, TK);
+  const int per = backward ? nkt : ntq, other = backward ? ntq : nkt;
+  const int n = p.B * per;
+  for (int i = threadIdx.x; i <= TF_MAX_TILES; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  auto weight = [&](int it) {
+    const int t = it % per, b = it / per;
+    const Range* qrs = p.qr + (long long)b * p.nqb;
+    const Range* krs = p.kr + (long long)b * p.nkb;
+    int c = 0;
+    if (backward) {
+      const Range kr = range128(krs, p.nkb, t);
+      for (int j = 0; j < other; ++j) c += tile_live128(p, range128(qrs, p.nqb, j), kr, j * TQ, t * TK) ? 1 : 0;
+    } else {
+      const Range qr = range128(qrs, p.nqb, t);
+      for (int j = 0; j < other; ++j) c += tile_live128(p, qr, range128(krs, p.nkb, j), t * TQ, j * TK) ? 1 : 0;
+    }
+    return c;
+  };
+  for (int it = threadIdx.x; it < n; it += blockDim.x) atomicAdd(&hist[weight(it)], 1);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int c = TF_MAX_TILES; c >= 0; --c) {
+      base[c] = acc;
+      acc += hist[c];
+    }
+  }
+  __syncthreads();
+  for (int it = threadIdx.x; it < n; it += blockDim.x) order[atomicAdd(&base[weight(it)], 1)] = it;
 }
 
 int launch_ranges(const Params& p, const int* qid, const int* kid, cudaStream_t s) {
@@ -1262,8 +1314,10 @@ extern "C" int mfb_attn_fwd(const uint16_t* q, const uint16_t* k, const uint16_t
   if ((st = tc::make_tmap_bf16(&tv, v, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
   MFB_CHECK_ARG(S <= TF_MAX_TILES * TK, "key length %d above the supported %d", S, TF_MAX_TILES * TK);
   if ((st = set_smem((const void*)attn_fwd_tc_kernel, TF_SMEM))) return st;
-  dim3 grid(cdiv(T, TQ), H / 2, B);
-  attn_fwd_tc_kernel<<<grid, TF_THREADS, TF_SMEM, s>>>(tq, tk, tv, p);
+  schedule_kernel<<<1, 1024, 0, s>>>(p, 0, w.order);
+  MFB_LAUNCH_CHECK("attention forward schedule");
+  const long long fwd_ctas = (long long)B * cdiv(T, TQ) * (H / TF_HPB);
+  attn_fwd_tc_kernel<<<(unsigned)fwd_ctas, TF_THREADS, TF_SMEM, s>>>(tq, tk, tv, p);
   MFB_LAUNCH_CHECK("mfb_attn_fwd");
   return MFB_OK;
 }
@@ -1308,8 +1362,10 @@ extern "C" int mfb_attn_bwd(const uint16_t* q, const uint16_t* k, const uint16_t
   if ((st = tc::make_tmap_bf16(&tk, k, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
   if ((st = tc::make_tmap_bf16(&tv, v, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
   if ((st = set_smem((const void*)attn_bwd_tc_kernel, TB_SMEM))) return st;
-  dim3 grid(cdiv(S, TK), Hk, B);
-  attn_bwd_tc_kernel<<<grid, TB_THREADS, TB_SMEM, s>>>(tq, tk, tv, tdo, p);
+  schedule_kernel<<<1, 1024, 0, s>>>(p, 1, w.order);
+  MFB_LAUNCH_CHECK("attention backward schedule");
+  const long long bwd_ctas = (long long)B * cdiv(S, TK) * Hk;
+  attn_bwd_tc_kernel<<<(unsigned)bwd_ctas, TB_THREADS, TB_SMEM, s>>>(tq, tk, tv, tdo, p);
   MFB_LAUNCH_CHECK("attention backward");
   const long long n4 = (long long)B * T * H * HD / 4;
   dq_convert_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, s>>>(w.dq_acc, reinterpret_cast<__nv_bfloat16*>(dq), n4,
