@@ -388,7 +388,7 @@ class EncoderStepWorkload:
     """Config 5: one data-parallel QAT encoder training step over this rank's rows."""
 
     def __init__(self, dist):
-        from minifield_training_b200 import workloads
+        from minifield_training_b200 import _lib, workloads
         from minifield_training_b200.device import HostBuffer
         from minifield_training_b200.models import encoder as me
 
@@ -396,7 +396,11 @@ class EncoderStepWorkload:
         if cfg.global_batch % dist.world:
             raise ValueError("the global batch must split evenly over the ranks")
         self.cfg, self.rows = cfg, cfg.global_batch // dist.world
-        self.model = me.EncoderStep(cfg, rows=self.rows, seed=0, group=dist.nccl_group())
+        # A created stream, so the step can be captured and replayed as CUDA graphs.
+        s = ctypes.c_void_p()
+        _lib.call("mfb_stream_create", ctypes.byref(s))
+        self.stream = s.value
+        self.model = me.EncoderStep(cfg, rows=self.rows, seed=0, group=dist.nccl_group(), stream=self.stream)
         self.batch = workloads.encoder_batch(cfg, 0, rows=self.rows, row0=dist.rank * self.rows)
         self.model.set_batch(*self.batch)
         full_seg = workloads.packed_segments(0, cfg.global_batch, cfg.length)
@@ -417,7 +421,7 @@ class EncoderStepWorkload:
 
         m = self.model
         for dst, h in zip((m.ids, m.mask, m.seg, m.pos, m.labels), self.host):
-            h2d(dst, h.ptr, h.array.nbytes)
+            h2d(dst, h.ptr, h.array.nbytes, self.stream)
         m._build_ids()
         res = m.step()
         res.loss  # device -> host read of the step result (synchronizes)
@@ -498,7 +502,8 @@ def run_reference(args, dist):
 # ---------------------------------------------------------------------------
 
 
-def measure(dist, fn, steps, warmup, clocks=None):
+def measure(dist, fn, steps, warmup, clocks=None, stream=None):
+    """Max over ranks of the mean step time, CUDA events on the launching stream."""
     from minifield_training_b200.device import Event, sync
 
     for _ in range(warmup):
@@ -509,10 +514,10 @@ def measure(dist, fn, steps, warmup, clocks=None):
     a, b = Event(), Event()
     if clocks:
         clocks.start()
-    a.record()
+    a.record(stream)
     for _ in range(steps):
         fn()
-    b.record()
+    b.record(stream)
     sync()
     clk = clocks.stop() if clocks else None
     dist.barrier()
@@ -592,10 +597,11 @@ def run_ours(args, dist):
     if only in (None, "encoder") and not (only is None and args.no_secondary):
         enc = EncoderStepWorkload(dist)
         esteps = max(3, args.steps // 5)
-        per_step = enc.count_launches()
-        ems, _ = measure(dist, enc.step, esteps, max(3, args.warmup // 2))
+        per_step = enc.count_launches()  # one eager step, counting the kernels each call launches
+        enc.model.capture()  # then the step replays as CUDA graphs
+        ems, _ = measure(dist, enc.step, esteps, max(3, args.warmup // 2), stream=enc.stream)
         launches += per_step * esteps
-        e2e_ms, _ = measure(dist, enc.e2e_step, max(3, esteps // 2), 1)
+        e2e_ms, _ = measure(dist, enc.e2e_step, max(3, esteps // 2), 1, stream=enc.stream)
         res = enc.model.result
         tflops = enc.global_flops / (ems * 1e-3) / 1e12
         secondary["encoder_step"] = {

@@ -58,6 +58,13 @@ int mfb_event_create(void** event);
 int mfb_event_destroy(void* event);
 int mfb_event_record(void* event, void* stream);
 int mfb_event_elapsed_ms(void* start, void* end, float* ms);
+/* CUDA graphs: everything enqueued on `stream` (a created stream) between
+ * mfb_graph_begin and mfb_graph_end is recorded into one executable graph;
+ * mfb_graph_launch replays it. Arguments are fixed at capture. */
+int mfb_graph_begin(void* stream);
+int mfb_graph_end(void* stream, void** graph_exec);
+int mfb_graph_launch(void* graph_exec, void* stream);
+int mfb_graph_destroy(void* graph_exec);
 
 /* ---- fake quantization ----------------------------------------------------
  * Replaces Quantizer.effective (src/minifield_training/kernels/quantization.py:11-22,

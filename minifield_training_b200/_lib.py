@@ -67,6 +67,10 @@ SIGNATURES = {
     "mfb_decode_attn_noalloc": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, F, P]),
     "mfb_gemm_bf16": (I, [P, I, I, P, I, I, P, I, I, I, I, I, F, P, P]),
     "mfb_gemm_status": (I, [IP]),
+    "mfb_graph_begin": (I, [P]),
+    "mfb_graph_end": (I, [P, ctypes.POINTER(ctypes.c_void_p)]),
+    "mfb_graph_launch": (I, [P, P]),
+    "mfb_graph_destroy": (I, [P]),
     "mfb_adamw_workspace_size": (SZ, []),
     "mfb_adamw_commit": (I, [P, P, P, P, LL, LL, LL, P, P, P, P, F, F, F, F, F, F, P, P, SZ, P]),
     "mfb_step_normalize": (I, [P, P, P, P, P, P, P]),

@@ -145,4 +145,38 @@ int mfb_event_elapsed_ms(void* start, void* end, float* ms) {
   return MFB_OK;
 }
 
+// Work recorded on a stream between mfb_graph_begin and mfb_graph_end becomes
+// one executable CUDA graph (relaxed capture: the library's host-side queries
+// during capture, such as tensor-map encoding, are allowed); mfb_graph_launch
+// replays it on a stream. Kernel arguments, buffers and sizes are fixed at
+// capture; the buffers' contents may change between replays.
+int mfb_graph_begin(void* stream) {
+  MFB_CHECK_ARG(stream != nullptr, "graph capture needs a created stream (not the legacy default stream)");
+  MFB_CUDA_TRY(cudaStreamBeginCapture((cudaStream_t)stream, cudaStreamCaptureModeRelaxed));
+  return MFB_OK;
+}
+
+int mfb_graph_end(void* stream, void** graph_exec) {
+  MFB_CHECK_ARG(stream != nullptr && graph_exec != nullptr, "NULL graph argument");
+  cudaGraph_t g = nullptr;
+  MFB_CUDA_TRY(cudaStreamEndCapture((cudaStream_t)stream, &g));
+  cudaGraphExec_t e = nullptr;
+  const cudaError_t err = cudaGraphInstantiate(&e, g, 0);
+  cudaGraphDestroy(g);
+  if (err != cudaSuccess) return mfb::set_error(MFB_ERR_CUDA, "cudaGraphInstantiate: %s", cudaGetErrorString(err));
+  *graph_exec = e;
+  return MFB_OK;
+}
+
+int mfb_graph_launch(void* graph_exec, void* stream) {
+  MFB_CHECK_ARG(graph_exec != nullptr, "NULL graph");
+  MFB_CUDA_TRY(cudaGraphLaunch((cudaGraphExec_t)graph_exec, (cudaStream_t)stream));
+  return MFB_OK;
+}
+
+int mfb_graph_destroy(void* graph_exec) {
+  if (graph_exec) MFB_CUDA_TRY(cudaGraphExecDestroy((cudaGraphExec_t)graph_exec));
+  return MFB_OK;
+}
+
 }  // extern "C"

@@ -228,6 +228,8 @@ class EncoderStep:
         aws = _lib.lib().mfb_attn_workspace_size(rows, self.T, self.T, h, hk, cfg.head_dim)
         self.attn_ws = E((max(aws, 16),), "uint8")
         self.result = None
+        # Normalized loss, gradient divisor and accumulation flag of the commit.
+        self._scalars = (E((1,), f32), E((1,), f32), E((1,), "uint8"))
         self.layers = []
         for kind in cfg.layer_types:
             L = _Layer(kind, x=E((m, c), bf), h=E((m, c), bf), rstd_op=E((m,), f32), mid=E((m, c), bf),
@@ -247,6 +249,9 @@ class EncoderStep:
             self.layers.append(L)
         self.head_eff = E((cfg.classes, c), bf)
         self._buckets = reduction_plan(self.layout, len(self.layers), self.grads.size)
+        # Initialization ran on the default stream; a created (non-blocking)
+        # step stream does not order after it, so finish it here.
+        _lib.call("mfb_device_sync")
 
     # ---- helpers -----------------------------------------------------------------
     def _p(self, name):
@@ -353,76 +358,153 @@ class EncoderStep:
                   P(dy.ptr), P(dres.ptr) if dres is not None else None, P(dx.ptr), P(dw.ptr), 0, self.M,
                   self.cfg.hidden, P(self.ws.ptr), self.ws.nbytes, self.stream)
 
-    def backward(self, on_layer_done=None):
-        cfg, m, c, f, s = self.cfg, self.M, self.cfg.hidden, self.cfg.ffn, self.stream
+    def _grad_bufs(self, i):
+        """Residual-stream gradient buffers (into layer i's output, out of its input).
+
+        Fixed per layer (ping-pong by layer parity), so captured graphs see the
+        same pointers on every replay.
+        """
+        k = len(self.layers) - 1 - i
+        return (self.d_a, self.d_b) if k % 2 == 0 else (self.d_b, self.d_a)
+
+    def _bwd_head(self):
+        """Head + loss (which also starts the backward) and the final norm's backward."""
+        cfg, m, c, s = self.cfg, self.M, self.cfg.hidden, self.stream
         lc = self.loss_count
         _lib.call("mfb_head_loss", P(self.enc.ptr), P(self._p("head.weight").ptr), P(self.labels.ptr),
                   P(self.mask.ptr), P(self.d_h.ptr), P(self._g("head.weight").ptr), P(lc.ptr), m, c, cfg.classes,
                   P(self.ws.ptr), self.ws.nbytes, s)
-        d, spare = self.d_a, self.d_b
+        d, _ = self._grad_bufs(len(self.layers) - 1)
         self._rms_bwd(self.final, self._p("lfm2.embedding_norm.weight"), self.rstd_final, self.mask, self.d_h, None,
                       d, self._g("lfm2.embedding_norm.weight"))
+
+    def _bwd_layer(self, i):
+        """Backward of layer i: d (gradient of its output) -> spare (gradient of its input)."""
+        cfg, m, c, f, s = self.cfg, self.M, self.cfg.hidden, self.cfg.ffn, self.stream
+        L, p = self.layers[i], _prefix(i)
+        d, spare = self._grad_bufs(i)
+        # FFN: x_next = mid + y.
+        _dgrad(d, L.w2, self.d_f, m, c, f, s)
+        _wgrad(d, L.a, self._g(p + "feed_forward.w2.weight").ptr, L.ste2, m, c, f, s)
+        _lib.call("mfb_swiglu_bwd", P(L.gu.ptr), P(self.d_f.ptr), P(self.d_gu.ptr), m, f, s)
+        _dgrad(self.d_gu, L.w13, self.d_h, m, 2 * f, c, s)
+        _wgrad(self.d_gu, L.h2, self._g(p + "feed_forward.w1.weight").ptr, L.ste13, m, 2 * f, c, s)
+        self._rms_bwd(L.mid, self._p(p + "ffn_norm.weight"), L.rstd_ffn, None, self.d_h, d, self.d_mid,
+                      self._g(p + "ffn_norm.weight"))
+        # Operator: mid = x + r.
+        if L.kind == "conv":
+            _dgrad(self.d_mid, L.w_out, self.d_o, m, c, c, s)
+            _wgrad(self.d_mid, L.mixed, self._g(p + "conv.out_proj.weight").ptr, L.ste_out, m, c, c, s)
+            _lib.call("mfb_conv_bwd", P(L.proj.ptr), P(self._p(p + "conv.conv.weight").ptr), P(self.seg.ptr),
+                      P(self.d_o.ptr), P(self.d_proj.ptr), P(self._g(p + "conv.conv.weight").ptr), 0, m, self.T,
+                      c, P(self.ws.ptr), self.ws.nbytes, s)
+            _dgrad(self.d_proj, L.w_in, self.d_h, m, 3 * c, c, s)
+            _wgrad(self.d_proj, L.h, self._g(p + "conv.in_proj.weight").ptr, L.ste_in, m, 3 * c, c, s)
+        else:
+            _dgrad(self.d_mid, L.w_out, self.d_o, m, c, c, s)
+            _wgrad(self.d_mid, L.o, self._g(p + "self_attn.out_proj.weight").ptr, L.ste_out, m, c, c, s)
+            causal, off, pol = self.attn_flags
+            _lib.call("mfb_attn_bwd", P(L.q.ptr), P(L.k.ptr), P(L.v.ptr), P(L.o.ptr), P(L.lse.ptr),
+                      P(self.d_o.ptr), P(self.d_q.ptr), P(self.d_k.ptr), P(self.d_v.ptr), P(self.qid.ptr),
+                      P(self.kid.ptr), self.rows, self.T, self.T, cfg.heads, cfg.kv_heads, cfg.head_dim, causal,
+                      off, pol, ctypes.c_float(cfg.head_dim ** -0.5), P(self.attn_ws.ptr), self.attn_ws.nbytes, s)
+            _lib.call("mfb_qknorm_rope_bwd", P(L.proj.ptr), self.nq,
+                      P(self._p(p + "self_attn.q_layernorm.weight").ptr),
+                      P(self._p(p + "self_attn.k_layernorm.weight").ptr), P(self.pos.ptr), P(self.freqs.ptr),
+                      P(L.rstd_q.ptr), P(L.rstd_k.ptr), P(self.d_q.ptr), P(self.d_k.ptr), P(self.d_v.ptr),
+                      P(self.d_proj.ptr), P(self._g(p + "self_attn.q_layernorm.weight").ptr),
+                      P(self._g(p + "self_attn.k_layernorm.weight").ptr), 0, m, cfg.heads, cfg.kv_heads,
+                      P(self.ws.ptr), self.ws.nbytes, s)
+            _dgrad(self.d_proj, L.w_in, self.d_h, m, self.nq, c, s)
+            _wgrad(self.d_proj, L.h, self._g(p + "self_attn.q_proj.weight").ptr, L.ste_in, m, self.nq, c, s)
+        opmask = self.mask if L.kind == "conv" else None
+        self._rms_bwd(L.x, self._p(p + "operator_norm.weight"), L.rstd_op, opmask, self.d_h, self.d_mid, spare,
+                      self._g(p + "operator_norm.weight"))
+
+    def backward(self, on_layer_done=None):
+        self._bwd_head()
         for i in reversed(range(len(self.layers))):
-            L, p = self.layers[i], _prefix(i)
-            # FFN: x_next = mid + y.
-            _dgrad(d, L.w2, self.d_f, m, c, f, s)
-            _wgrad(d, L.a, self._g(p + "feed_forward.w2.weight").ptr, L.ste2, m, c, f, s)
-            _lib.call("mfb_swiglu_bwd", P(L.gu.ptr), P(self.d_f.ptr), P(self.d_gu.ptr), m, f, s)
-            _dgrad(self.d_gu, L.w13, self.d_h, m, 2 * f, c, s)
-            _wgrad(self.d_gu, L.h2, self._g(p + "feed_forward.w1.weight").ptr, L.ste13, m, 2 * f, c, s)
-            self._rms_bwd(L.mid, self._p(p + "ffn_norm.weight"), L.rstd_ffn, None, self.d_h, d, self.d_mid,
-                          self._g(p + "ffn_norm.weight"))
-            # Operator: mid = x + r.
-            if L.kind == "conv":
-                _dgrad(self.d_mid, L.w_out, self.d_o, m, c, c, s)
-                _wgrad(self.d_mid, L.mixed, self._g(p + "conv.out_proj.weight").ptr, L.ste_out, m, c, c, s)
-                _lib.call("mfb_conv_bwd", P(L.proj.ptr), P(self._p(p + "conv.conv.weight").ptr), P(self.seg.ptr),
-                          P(self.d_o.ptr), P(self.d_proj.ptr), P(self._g(p + "conv.conv.weight").ptr), 0, m, self.T,
-                          c, P(self.ws.ptr), self.ws.nbytes, s)
-                _dgrad(self.d_proj, L.w_in, self.d_h, m, 3 * c, c, s)
-                _wgrad(self.d_proj, L.h, self._g(p + "conv.in_proj.weight").ptr, L.ste_in, m, 3 * c, c, s)
-            else:
-                _dgrad(self.d_mid, L.w_out, self.d_o, m, c, c, s)
-                _wgrad(self.d_mid, L.o, self._g(p + "self_attn.out_proj.weight").ptr, L.ste_out, m, c, c, s)
-                causal, off, pol = self.attn_flags
-                _lib.call("mfb_attn_bwd", P(L.q.ptr), P(L.k.ptr), P(L.v.ptr), P(L.o.ptr), P(L.lse.ptr),
-                          P(self.d_o.ptr), P(self.d_q.ptr), P(self.d_k.ptr), P(self.d_v.ptr), P(self.qid.ptr),
-                          P(self.kid.ptr), self.rows, self.T, self.T, cfg.heads, cfg.kv_heads, cfg.head_dim, causal,
-                          off, pol, ctypes.c_float(cfg.head_dim ** -0.5), P(self.attn_ws.ptr), self.attn_ws.nbytes, s)
-                _lib.call("mfb_qknorm_rope_bwd", P(L.proj.ptr), self.nq,
-                          P(self._p(p + "self_attn.q_layernorm.weight").ptr),
-                          P(self._p(p + "self_attn.k_layernorm.weight").ptr), P(self.pos.ptr), P(self.freqs.ptr),
-                          P(L.rstd_q.ptr), P(L.rstd_k.ptr), P(self.d_q.ptr), P(self.d_k.ptr), P(self.d_v.ptr),
-                          P(self.d_proj.ptr), P(self._g(p + "self_attn.q_layernorm.weight").ptr),
-                          P(self._g(p + "self_attn.k_layernorm.weight").ptr), 0, m, cfg.heads, cfg.kv_heads,
-                          P(self.ws.ptr), self.ws.nbytes, s)
-                _dgrad(self.d_proj, L.w_in, self.d_h, m, self.nq, c, s)
-                _wgrad(self.d_proj, L.h, self._g(p + "self_attn.q_proj.weight").ptr, L.ste_in, m, self.nq, c, s)
-            opmask = self.mask if L.kind == "conv" else None
-            self._rms_bwd(L.x, self._p(p + "operator_norm.weight"), L.rstd_op, opmask, self.d_h, self.d_mid, spare,
-                          self._g(p + "operator_norm.weight"))
-            d, spare = spare, d
+            self._bwd_layer(i)
             if on_layer_done is not None:
                 on_layer_done(i)
-        self.d_x0 = d  # the embeddings are frozen: this gradient is not used
+        self.d_x0 = self._grad_bufs(0)[1]  # the embeddings are frozen: this gradient is not used
 
     # ---- the logical step ------------------------------------------------------------
+    def capture(self):
+        """Record the step as CUDA graphs on this step's stream (a created stream).
+
+        One GPU: one graph (quantize, forward, backward, normalize, commit).
+        With a process group: the forward and the head's backward, one graph per
+        layer's backward (so each layer's bucket allreduce is launched between
+        them), and the commit.
+        """
+        if getattr(self, "graphs", None) is not None:
+            return
+        if self.stream is None:
+            raise ValueError("graph capture needs EncoderStep(stream=...) from mfb_stream_create")
+
+        def rec(fn):
+            _lib.call("mfb_graph_begin", P(self.stream))
+            try:
+                fn()
+            finally:
+                g = ctypes.c_void_p()
+                _lib.call("mfb_graph_end", P(self.stream), ctypes.byref(g))
+            return g
+
+        if self.group is None:
+            self.graphs = {"all": rec(self._eager_local_step)}
+        else:
+            self.graphs = {"pre": rec(lambda: (self.quantize(), self.forward(), self._bwd_head())),
+                           "layers": [rec(lambda i=i: self._bwd_layer(i)) for i in reversed(range(len(self.layers)))],
+                           "post": rec(self._commit)}
+        self._result_dev = self.result._dev
+
+    def _eager_local_step(self):
+        self.quantize()
+        self.forward()
+        self.backward()
+        self._commit()
+
+    def _launch(self, g):
+        _lib.call("mfb_graph_launch", g, P(self.stream))
+
     def step(self):
         """quantize -> forward -> backward (+ bucketed allreduce) -> normalize -> AdamW commit."""
+        graphs = getattr(self, "graphs", None)
+        if graphs is not None:
+            if self.group is None:
+                self._launch(graphs["all"])
+            else:
+                import torch
+                with torch.cuda.stream(torch.cuda.ExternalStream(self.stream)):
+                    self._launch(graphs["pre"])
+                    reducer = BucketReducer(self.grads._base, self._buckets, self.group)
+                    for g, i in zip(graphs["layers"], reversed(range(len(self.layers)))):
+                        self._launch(g)
+                        reducer.layer_done(i)
+                    reducer.finish()
+                    self._launch(graphs["post"])
+            self.result = adamw.CommitResult(self.state, self._result_dev, self.stream)
+            return self.result
         self.quantize()
         self.forward()
         if self.group is not None:
-            reducer = BucketReducer(self.grads._base, self._buckets, self.group)
-            self.backward(reducer.layer_done)
-            reducer.finish()
+            import contextlib
+
+            import torch
+            ctx = (torch.cuda.stream(torch.cuda.ExternalStream(self.stream)) if self.stream is not None
+                   else contextlib.nullcontext())
+            with ctx:  # the collectives are ordered after the kernels on this step's stream
+                reducer = BucketReducer(self.grads._base, self._buckets, self.group)
+                self.backward(reducer.layer_done)
+                reducer.finish()
         else:
             self.backward()
         self._commit()
         return self.result
 
     def _commit(self):
-        if not hasattr(self, "_scalars"):
-            self._scalars = (DeviceArray((1,), "float32"), DeviceArray((1,), "float32"), DeviceArray((1,), "uint8"))
         loss, div, ok = self._scalars
         lc = self.loss_count
         _lib.call("mfb_step_normalize", P(lc.ptr), P(lc.ptr + 4), None, P(loss.ptr), P(div.ptr), P(ok.ptr),

@@ -109,3 +109,36 @@ def test_small_steps_lower_the_loss_on_a_fixed_batch():
         assert res.committed
         losses.append(res.loss)
     assert all(b < a for a, b in zip(losses, losses[1:])), losses
+
+
+def test_graph_replay_matches_eager_steps():
+    """Two steps replayed from one captured CUDA graph equal two eager steps.
+
+    Same kernels in the same order; the attention backward's dQ atomics may
+    sum in another order, so masters are compared at rtol 1e-5.
+    """
+    import ctypes
+
+    from minifield_training_b200 import _lib, workloads
+    from minifield_training_b200.device import sync
+    from minifield_training_b200.models import encoder as me
+    cfg = _cfg()
+    batch = workloads.encoder_batch(cfg, 9)
+    stream = ctypes.c_void_p()
+    _lib.call("mfb_stream_create", ctypes.byref(stream))
+    graph = me.EncoderStep(cfg, rows=2, seed=2, stream=stream.value)
+    eager = me.EncoderStep(cfg, rows=2, seed=2)
+    graph.set_batch(*batch)
+    eager.set_batch(*batch)
+    graph.capture()  # records (does not run) one step
+    sync()
+    assert int(graph.state["step"].numpy()[0]) == 0
+    for _ in range(2):
+        rg, re_ = graph.step(), eager.step()
+        assert rg.committed and re_.committed
+        np.testing.assert_allclose(rg.loss, re_.loss, rtol=1e-5)
+    sync()
+    assert int(graph.state["step"].numpy()[0]) == 2
+    for name in graph.params:
+        np.testing.assert_allclose(graph.params[name].numpy(), eager.params[name].numpy(), rtol=1e-5, atol=1e-7,
+                                   err_msg=name)
