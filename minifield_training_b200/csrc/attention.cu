@@ -74,6 +74,7 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+
 // ---------------------------------------------------------------------------
 // Id encoding from the reference's mask arguments.
 // ---------------------------------------------------------------------------
@@ -605,7 +606,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         for (int i = 0; i < 32; i += 2) {
           const float e0 = ex2(fmaf(__uint_as_float(x[c * 32 + i]), sl2, nmu));
           const float e1 = ex2(fmaf(__uint_as_float(x[c * 32 + i + 1]), sl2, nmu));
-          pk[i >> 1] = pack_bf16_finite(e0, e1);  // P in [0, 2^8]: finite
+          pk[i >> 1] = pack_bf16(e0, e1);
         }
         tc::tmem_st_32x32b_x16(s_t + c * 16, pk);
       }
@@ -1008,10 +1009,8 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
           pv[e] = (vm >> (i + e)) & 1u ? pe : 0.f;
           dv4[e] = pv[e] * (__uint_as_float(dx[i + e]) - dsm[e]);
         }
-        // P in [0, 1] (masked entries zeroed): the integer-pipe packing; dS
-        // may carry a NaN from dO, so it keeps the conversion instruction.
-        pk[i >> 1] = pack_bf16_finite(pv[0], pv[1]);
-        pk[(i >> 1) + 1] = pack_bf16_finite(pv[2], pv[3]);
+        pk[i >> 1] = pack_bf16(pv[0], pv[1]);
+        pk[(i >> 1) + 1] = pack_bf16(pv[2], pv[3]);
         dk4[i >> 1] = pack_bf16(dv4[0], dv4[1]);
         dk4[(i >> 1) + 1] = pack_bf16(dv4[2], dv4[3]);
       }

@@ -83,18 +83,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// The same round-to-nearest-even packing on the integer pipe, for finite
-// inputs only (no NaN handling): adding 0x7FFF plus the kept half's lowest bit
-// carries into the upper half exactly when the dropped half is above one half
-// ulp, or equal to it with an odd kept half; a byte permute then takes both
-// upper halves. Frees the conversion unit, which the softmax exponentials
-// also use.
-__device__ __forceinline__ uint32_t pack_bf16_finite(float lo, float hi) {
-  uint32_t a = __float_as_uint(lo), b = __float_as_uint(hi);
-  a += 0x7FFFu + ((a >> 16) & 1u);
-  b += 0x7FFFu + ((b >> 16) & 1u);
-  return __byte_perm(a, b, 0x7632);
-}
 
 // 64-column bf16 tile rows are 128 bytes = 8 chunks of 16 bytes; chunk index is
 // XOR-swizzled with (row % 8) so ldmatrix row reads hit distinct banks.
