@@ -158,7 +158,9 @@ def test_two_rank_graph_steps_stay_replicated_and_match_eager():
     ref.set_batch(*workloads.encoder_batch(cfg, 7))
     for k in range(2):
         r = ref.step()
-        np.testing.assert_allclose(l0[k][1], r.loss, rtol=1e-4)
+        # Step 0's loss is the same sum in another order; step 1's follows the
+        # first update, where sign flips of near-zero gradients (below) move it.
+        np.testing.assert_allclose(l0[k][1], r.loss, rtol=1e-4 if k == 0 else 2e-3)
     # Adam's first steps move each master by about lr * sign(g): a gradient
     # within summation noise of zero may flip sign between the two reduction
     # orders (a 2 * lr difference), so allow that bound on a tiny fraction.
