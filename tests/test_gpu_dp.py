@@ -167,4 +167,4 @@ def test_two_rank_graph_steps_stay_replicated_and_match_eager():
     for name in p0:
         diff = np.abs(p0[name] - ref.params[name].numpy())
         assert diff.max() <= 4.5 * cfg.learning_rate, name
-        assert np.mean(diff > 1e-6) < 2e-3, name
+        assert np.mean(diff > cfg.learning_rate) < 2e-3, name  # only sign flips move a master by ~lr
