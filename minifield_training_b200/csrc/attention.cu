@@ -684,7 +684,10 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 //               the sub-item's 64 query columns per warp (two warps per lane
 //               quarter).
 //   warps 10-13 dQ flush: add each item's dQ tile into the FP32 accumulator
-//               (vector reductions) while the next item is computed.
+//               while the next item is computed: TMEM -> swizzled shared
+//               staging -> TMA tensor reduce-add (the reductions run in the
+//               TMA unit and L2, off the SM's load/store path that the
+//               mbarrier polls and the shared-memory traffic share).
 // Products (M = 128 keys unless noted), issued in the order
 //   S/dP(j), [P ready j-1] dV/dK(j-1), [dQ tile free] dQ(item of j-1), S/dP(j+1)...
 //   S^T_j  = K Q_j^T        N = 64 -> TMEM buffer j%2 [0,64)
@@ -707,7 +710,11 @@ constexpr int TB_COL_OFF = TB_DS_OFF + 2 * 32768;
 constexpr int TB_COL_STRIDE = 3 * 128 + 32;  // lse[128], dsum[128], qid[128], run table
 constexpr int TB_LIST_OFF = TB_COL_OFF + TB_ST * TB_COL_STRIDE * 4;
 constexpr int TB_BAR_OFF = TB_LIST_OFF + (TF_MAX_TILES + 4) * 4;
-constexpr int TB_SMEM = 1024 + TB_BAR_OFF + 256;
+// dQ staging: one 4 KB box (32 query rows x 32 FP32 columns, 128-byte
+// swizzle) per dQ flush warp, 1024-byte aligned for the TMA reduction.
+constexpr int TB_DQS_OFF = (TB_BAR_OFF + 256 + 1023) / 1024 * 1024;
+constexpr int TB_SMEM = 1024 + TB_DQS_OFF + 4 * 4096;
+static_assert(TB_SMEM <= 227 * 1024, "backward shared memory");
 
 // Run table of equal nonzero ids over a 128-entry tile: rt[0] = count (or -1
 // when an id recurs or there are more than 8 runs), then {id, first, last}.
@@ -759,7 +766,8 @@ __device__ __forceinline__ void warp_run_table(const int* v4, int lane, int* rt)
 
 __global__ void __launch_bounds__(TB_THREADS, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                       const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo, Params p) {
+                       const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                       const __grid_constant__ CUtensorMap tdq, Params p) {
   extern __shared__ uint8_t smem_raw[];
   // Offset from the __shared__ array itself so accesses keep the shared state space.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -1063,29 +1071,46 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       }
     }
   } else {
-    // dQ flush warps: query row = TMEM lane, all 64 columns.
+    // dQ flush warps: query row = TMEM lane (this warp's 32 rows), all 64
+    // columns, reduced into the accumulator as two 32-column boxes.
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
     const uint32_t dq_t = tmem + ((uint32_t)(quarter * 32) << 16) + 384;
+    uint8_t* stage = smem + TB_DQS_OFF + quarter * 4096;
+    const uint32_t stage_u = sb + TB_DQS_OFF + quarter * 4096;
     for (int it = 0; it < nitems; ++it) {
       if (!__all_sync(0xffffffffu, tc::mbar_wait(dq_full, it & 1, status, 40))) break;
       tc::tc_fence_after();
       const int h = hk * p.G + it / nlive;
-      const int q = (list[1 + it % nlive] & 0xFFFF) * TQ + r;
+      const int t0 = (list[1 + it % nlive] & 0xFFFF) * TQ + quarter * 32;
       uint32_t v[64];
       tc::tmem_ld_32x32b_x32(dq_t, v);
       tc::tmem_ld_32x32b_x32(dq_t + 32, v + 32);
       tc::tmem_ld_wait();
       tc::tc_fence_before();
       tc::mbar_arrive(dq_free);
-      if (q < p.T) {
-        float* dst = p.dq_acc + (((long long)b * p.T + q) * p.H + h) * HD;
+      if (t0 < p.T) {  // rows past T inside the box are clipped by the tensor map
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          red_add_v4(dst + 4 * e, __uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
-                     __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
+        for (int half = 0; half < 2; ++half) {
+          // The staging box is free once the previous reduction has read it.
+          if (lane == 0) tc::bulk_wait_group_read0();
+          __syncwarp();
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                make_uint4(v[32 * half + 4 * c], v[32 * half + 4 * c + 1], v[32 * half + 4 * c + 2],
+                           v[32 * half + 4 * c + 3]);
+          tc::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tc::tma_reduce_add_4d(&tdq, stage_u, 32 * half, h, t0, b);
+            tc::bulk_commit_group();
+          }
+        }
       }
     }
+    // The accumulator is read by the next kernel: every reduction complete.
+    if (lane == 0) tc::bulk_wait_group0();
+    __syncwarp();
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -1357,16 +1382,17 @@ extern "C" int mfb_attn_bwd(const uint16_t* q, const uint16_t* k, const uint16_t
   MFB_CHECK_ARG(((uintptr_t)q & 15) == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0 &&
                     ((uintptr_t)d_o & 15) == 0,
                 "q/k/v/d_o must be 16-byte aligned");
-  CUtensorMap tq, tk, tv, tdo;
+  CUtensorMap tq, tk, tv, tdo, tdq;
   if ((st = tc::make_tmap_bf16(&tq, q, (uint64_t)H * HD, (uint64_t)B * T, (uint64_t)H * HD, TQ))) return st;
   if ((st = tc::make_tmap_bf16(&tdo, d_o, (uint64_t)H * HD, (uint64_t)B * T, (uint64_t)H * HD, TQ))) return st;
+  if ((st = tc::make_tmap_f32_rows_heads(&tdq, w.dq_acc, H, (uint64_t)T, (uint64_t)B, 32))) return st;
   if ((st = tc::make_tmap_bf16(&tk, k, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
   if ((st = tc::make_tmap_bf16(&tv, v, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
   if ((st = set_smem((const void*)attn_bwd_tc_kernel, TB_SMEM))) return st;
   schedule_kernel<<<1, 1024, 0, s>>>(p, 1, w.order);
   MFB_LAUNCH_CHECK("attention backward schedule");
   const long long bwd_ctas = (long long)B * cdiv(S, TK) * Hk;
-  attn_bwd_tc_kernel<<<(unsigned)bwd_ctas, TB_THREADS, TB_SMEM, s>>>(tq, tk, tv, tdo, p);
+  attn_bwd_tc_kernel<<<(unsigned)bwd_ctas, TB_THREADS, TB_SMEM, s>>>(tq, tk, tv, tdo, tdq, p);
   MFB_LAUNCH_CHECK("attention backward");
   const long long n4 = (long long)B * T * H * HD / 4;
   dq_convert_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, s>>>(w.dq_acc, reinterpret_cast<__nv_bfloat16*>(dq), n4,

@@ -300,6 +300,21 @@ int make_tmap_bf16_heads(CUtensorMap* map, const void* base, uint64_t rows, int 
   return MFB_OK;
 }
 
+int make_tmap_f32_rows_heads(CUtensorMap* map, const void* base, int heads, uint64_t T, uint64_t batch,
+                             uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(MFB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  cuuint64_t dims[4] = {64, (cuuint64_t)heads, T, batch};
+  cuuint64_t strides[3] = {256, (cuuint64_t)heads * 256, T * (cuuint64_t)heads * 256};
+  cuuint32_t box[4] = {32, 1, box_rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(MFB_ERR_CUDA, "cuTensorMapEncodeTiled (4-D f32) failed (%d)", (int)r);
+  return MFB_OK;
+}
+
 }  // namespace tc
 }  // namespace mfb
 

@@ -174,6 +174,24 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
 }
 
+// ---- TMA reductions (shared -> global, bulk async-group completion) --------
+// Element-wise add of a shared-memory box into a 4-D tensor (type from the
+// map); coordinates innermost first, none negative.
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, uint32_t src, int x, int y, int z, int w) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2, %3, %4}], [%5];\n" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(x), "r"(y), "r"(z), "r"(w), "r"(src)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+// Every committed group has finished reading its shared-memory source.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+}
+// Every committed group is complete (its global writes performed).
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
+
 // ---- host: tensor maps ------------------------------------------------------
 // 2-D bf16 tensor map over a row-major [outer, inner] array with row stride
 // `ld` elements; box = {64 inner (128 bytes), box_outer}; 128-byte swizzle.
@@ -184,6 +202,11 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t 
 // {dim, row, head} so that box {64, box_rows, heads} lands in shared memory as
 // [head][box_rows][64]: one 128-byte-swizzled tile per head.
 int make_tmap_bf16_heads(CUtensorMap* map, const void* base, uint64_t rows, int heads, uint32_t box_rows);
+// 4-D FP32 tensor map over a [batch, T, heads, 64] array, addressed as
+// {dim, head, t, batch}; box {32, 1, box_rows, 1} (128-byte rows, 128-byte
+// swizzle). Boxes that run past T are clipped there, not into the next batch row.
+int make_tmap_f32_rows_heads(CUtensorMap* map, const void* base, int heads, uint64_t T, uint64_t batch,
+                             uint32_t box_rows);
 
 }  // namespace tc
 }  // namespace mfb
