@@ -710,6 +710,9 @@ constexpr int TB_COL_OFF = TB_DS_OFF + 2 * 32768;
 constexpr int TB_COL_STRIDE = 3 * 128 + 32;  // lse[128], dsum[128], qid[128], run table
 constexpr int TB_LIST_OFF = TB_COL_OFF + TB_ST * TB_COL_STRIDE * 4;
 constexpr int TB_BAR_OFF = TB_LIST_OFF + (TF_MAX_TILES + 4) * 4;
+// TMEM columns of the backward: S^T/dP^T double buffer [0,256), dV [256,320),
+// dK [320,384), dQ [384,448), K [448,480) and V [480,512) (bf16 pairs).
+constexpr int TB_KT_COL = 448, TB_VT_COL = 480;
 // dQ staging: one 4 KB box (32 query rows x 32 FP32 columns, 128-byte
 // swizzle) per dQ flush warp, 1024-byte aligned for the TMA reduction.
 constexpr int TB_DQS_OFF = (TB_BAR_OFF + 256 + 1023) / 1024 * 1024;
@@ -781,7 +784,8 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
   const uint32_t dq_full = bars + 8u * (5 + 2 * TB_ST);
   const uint32_t dq_free = bars + 8u * (6 + 2 * TB_ST);
   const uint32_t done_bar = bars + 8u * (7 + 2 * TB_ST);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TB_BAR_OFF + 8 * (8 + 2 * TB_ST));
+  const uint32_t kv_tm = bars + 8u * (8 + 2 * TB_ST);  // K and V copied into TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TB_BAR_OFF + 8 * (9 + 2 * TB_ST));
   int* cols = reinterpret_cast<int*>(smem + TB_COL_OFF);
   int* list = reinterpret_cast<int*>(smem + TB_LIST_OFF);
 
@@ -809,6 +813,7 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
     tc::mbar_init(dq_full, 1);
     tc::mbar_init(dq_free, 128);
     tc::mbar_init(done_bar, 1);
+    tc::mbar_init(kv_tm, 256);
     tc::mbar_fence_init();
   }
   if (warp == 0) {
@@ -886,24 +891,25 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       tc::mbar_arrive(qd_full(st));
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    // The whole warp runs the issue loop (converged); one elected lane issues.
+    {
       const uint32_t idesc_s = tc::idesc_bf16_f32(128, 64, 0, 0);
       const uint32_t idesc_kn = tc::idesc_bf16_f32(128, 64, 0, 1);  // K-major A, MN-major B
       const uint32_t idesc_nn = tc::idesc_bf16_f32(128, 64, 1, 1);  // MN-major A and B
       const uint32_t dv_t = tmem + 256, dk_t = tmem + 320, dq_t = tmem + 384;
-      const uint32_t kb_ = sb + TB_K_OFF, vb_ = sb + TB_V_OFF;
-      // K-major K and V descriptors do not change; the per-step advance is
-      // added to the start-address field (bits 0-13, in 16-byte units).
-      const uint64_t kdesc = tc::smem_desc_sw128(kb_, 16, 1024), vdesc = tc::smem_desc_sw128(vb_, 16, 1024);
-      const uint64_t kdesc_mn = tc::smem_desc_sw128(kb_, 8192, 1024);
-      bool ok = tc::mbar_wait(kv_full, 0, status, 32);
+      const uint32_t k_tm = tmem + TB_KT_COL, v_tm = tmem + TB_VT_COL;
+      // The MN-major K descriptor (dQ's B operand) does not change; the
+      // per-step advance is added to the start-address field (bits 0-13, in
+      // 16-byte units).
+      const uint64_t kdesc_mn = tc::smem_desc_sw128(sb + TB_K_OFF, 8192, 1024);
+      bool ok = tc::mbar_wait_w(kv_tm, 0, status, 32);
       tc::tc_fence_after();
       const int nsub = 2 * nitems;
       // Issues dV/dK of sub-item j (its P^T is ready) and, after the second
       // half of an item, that item's dQ; then frees the item's Q/dO stage.
       auto finish = [&](int j) -> bool {
         const int it = j >> 1, hf = j & 1, u = j & 1, st = it % TB_ST;
-        if (!tc::mbar_wait(p_full(u), (j >> 1) & 1, status, 34)) return false;
+        if (!tc::mbar_wait_w(p_full(u), (j >> 1) & 1, status, 34)) return false;
         tc::tc_fence_after();
         const uint32_t qb_ = sb + TB_QD_OFF + st * 32768 + hf * 8192, dob_ = qb_ + 16384;
         const uint32_t ds_ = sb + TB_DS_OFF + (it & 1) * 32768;
@@ -912,46 +918,47 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
         const uint64_t dsd = tc::smem_desc_sw128(ds_ + hf * 16384, 16, 1024);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          tc::mma_bf16_ts(dv_t, s_t + (k >> 1) * 32 + (k & 1) * 8, dod_mn + (uint64_t)(k * 2048 >> 4), idesc_kn,
+          tc::mma_bf16_ts_w(dv_t, s_t + (k >> 1) * 32 + (k & 1) * 8, dod_mn + (uint64_t)(k * 2048 >> 4), idesc_kn,
                           (j | k) != 0 ? 1u : 0u);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          tc::mma_bf16(dk_t, dsd + (uint64_t)(k * 32 >> 4), qd_mn + (uint64_t)(k * 2048 >> 4), idesc_kn,
+          tc::mma_bf16_w(dk_t, dsd + (uint64_t)(k * 32 >> 4), qd_mn + (uint64_t)(k * 2048 >> 4), idesc_kn,
                        (j | k) != 0 ? 1u : 0u);
         if (hf == 1) {
-          tc::mma_commit(qd_empty(st));
-          if (it > 0 && !tc::mbar_wait(dq_free, (it - 1) & 1, status, 39)) return false;
+          tc::mma_commit_w(qd_empty(st));
+          if (it > 0 && !tc::mbar_wait_w(dq_free, (it - 1) & 1, status, 39)) return false;
           tc::tc_fence_after();
           const uint64_t dsn = tc::smem_desc_sw128(ds_, 16384, 1024);
 #pragma unroll
           for (int k = 0; k < 8; ++k)
-            tc::mma_bf16(dq_t, dsn + (uint64_t)(k * 2048 >> 4), kdesc_mn + (uint64_t)(k * 2048 >> 4), idesc_nn,
+            tc::mma_bf16_w(dq_t, dsn + (uint64_t)(k * 2048 >> 4), kdesc_mn + (uint64_t)(k * 2048 >> 4), idesc_nn,
                          k > 0 ? 1u : 0u);
-          tc::mma_commit(dq_full);
+          tc::mma_commit_w(dq_full);
         }
         return true;
       };
       for (int j = 0; ok && j < nsub; ++j) {
         const int it = j >> 1, hf = j & 1, u = j & 1, st = it % TB_ST;
         if (hf == 0) {
-          if (!(ok = tc::mbar_wait(qd_full(st), (it / TB_ST) & 1, status, 33))) break;
+          if (!(ok = tc::mbar_wait_w(qd_full(st), (it / TB_ST) & 1, status, 33))) break;
           tc::tc_fence_after();
         }
         const uint32_t qb_ = sb + TB_QD_OFF + st * 32768 + hf * 8192, dob_ = qb_ + 16384;
         const uint32_t s_t = tmem + u * 128, dp_t = s_t + 64;
         const uint64_t qd = tc::smem_desc_sw128(qb_, 16, 1024), dod = tc::smem_desc_sw128(dob_, 16, 1024);
+        // A = K / V from TMEM (16 head dims = 8 columns per step), B = Q / dO.
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          tc::mma_bf16(s_t, kdesc + (uint64_t)(k * 32 >> 4), qd + (uint64_t)(k * 32 >> 4), idesc_s, k > 0 ? 1u : 0u);
+          tc::mma_bf16_ts_w(s_t, k_tm + k * 8, qd + (uint64_t)(k * 32 >> 4), idesc_s, k > 0 ? 1u : 0u);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          tc::mma_bf16(dp_t, vdesc + (uint64_t)(k * 32 >> 4), dod + (uint64_t)(k * 32 >> 4), idesc_s, k > 0 ? 1u : 0u);
-        tc::mma_commit(s_full(u));
+          tc::mma_bf16_ts_w(dp_t, v_tm + k * 8, dod + (uint64_t)(k * 32 >> 4), idesc_s, k > 0 ? 1u : 0u);
+        tc::mma_commit_w(s_full(u));
         if (j > 0 && !(ok = finish(j - 1))) break;
       }
       if (ok && nsub > 0) finish(nsub - 1);
-      tc::mma_commit(done_bar);
-      tc::mbar_wait(done_bar, 0, status, 35);
+      tc::mma_commit_w(done_bar);
+      tc::mbar_wait_w(done_bar, 0, status, 35);
     }
   } else if (warp < 10) {
     const int quarter = warp & 3, wh = (warp - 2) >> 2;  // wh: which 32 of the sub-item's 64 columns
@@ -960,43 +967,72 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
     const int kid_row = s < p.S ? p.kid[(long long)b * p.S + s] : 0;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const float sl2 = p.scale_log2;
-    bool ok = true;
+    bool ok;
     const int nsub = 2 * nitems;
-    for (int j = 0; j < nsub; ++j) {
+    {
+      // K (wh 0) or V (wh 1) key row r into TMEM as the A operand of the
+      // score products: un-swizzle the 128-byte shared row, two bf16 per column.
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(kv_full, 0, status, 41));
+      if (ok) {
+        const uint8_t* row = smem + (wh ? TB_V_OFF : TB_K_OFF) + r * 128;
+        uint32_t w[32];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 x = *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) << 4));
+          w[4 * c] = x.x, w[4 * c + 1] = x.y, w[4 * c + 2] = x.z, w[4 * c + 3] = x.w;
+        }
+        const uint32_t dst = tmem + lane_off + (wh ? TB_VT_COL : TB_KT_COL);
+        tc::tmem_st_32x32b_x16(dst, w);
+        tc::tmem_st_32x32b_x16(dst + 16, w + 16);
+        tc::tmem_st_wait();
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(kv_tm);
+    }
+    uint32_t vm_lo = 0xFFFFFFFFu, vm_hi = 0xFFFFFFFFu;  // validity of this warp's columns, both sub-items
+    for (int j = 0; ok && j < nsub; ++j) {
       const int it = j >> 1, hf = j & 1, u = j & 1, st = it % TB_ST;
-      const int entry = list[1 + it % nlive];
-      const int q0 = (entry & 0xFFFF) * TQ;
-      const bool full = (entry >> 30) & 1;
+      const int* cs = cols + st * TB_COL_STRIDE;
       // Warp-uniform wait outcomes: the TMEM accesses below are warp-collective.
-      ok = tc::mbar_wait(s_full(u), (j >> 1) & 1, status, 36);
-      if (!(ok = __all_sync(0xffffffffu, ok))) break;
       if (hf == 0) {
+        // Once per item, before its scores are ready: the item's column data
+        // and this key row's validity masks for both sub-items.
         ok = tc::mbar_wait(qd_full(st), (it / TB_ST) & 1, status, 37);
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        const int entry = list[1 + it % nlive];
+        vm_lo = vm_hi = 0xFFFFFFFFu;
+        if (!((entry >> 30) & 1)) {
+          const int q0 = (entry & 0xFFFF) * TQ;
+          const int* rt = cs + 384;
+          const int nr = rt[0];
+          int lo = 1, hi = 0;
+          if (nr >= 0) {
+            for (int q = 0; q < nr; ++q)
+              if (rt[1 + 3 * q] == kid_row) lo = rt[2 + 3 * q], hi = rt[3 + 3 * q];
+          } else {
+            lo = 0, hi = TQ - 1;
+          }
+          if (p.causal) lo = max(lo, s - p.offset - q0);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int cb = h2 * 64 + wh * 32;
+            const int a0 = max(lo - cb, 0), b0 = min(hi - cb, 31);
+            uint32_t vm = a0 > b0 ? 0u : ((0xFFFFFFFFu >> (31 - b0)) & (0xFFFFFFFFu << a0));
+            if (nr < 0) {
+              uint32_t bits = 0;
+              for (int i = 0; i < 32; ++i) bits |= (kid_row != 0 && cs[256 + cb + i] == kid_row) ? 1u << i : 0u;
+              vm &= bits;
+            }
+            if (h2 == 0) vm_lo = vm;
+            else vm_hi = vm;
+          }
+        }
       }
+      ok = tc::mbar_wait(s_full(u), (j >> 1) & 1, status, 36);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
       tc::tc_fence_after();
-      const int* cs = cols + st * TB_COL_STRIDE;
       const int cbase = hf * 64 + wh * 32;  // this warp's 32 query columns within the item
-      uint32_t vm = 0xFFFFFFFFu;
-      if (!full) {
-        const int* rt = cs + 384;
-        const int nr = rt[0];
-        int lo = 1, hi = 0;
-        if (nr >= 0) {
-          for (int q = 0; q < nr; ++q)
-            if (rt[1 + 3 * q] == kid_row) lo = rt[2 + 3 * q], hi = rt[3 + 3 * q];
-        } else {
-          lo = 0, hi = TQ - 1;
-        }
-        if (p.causal) lo = max(lo, s - p.offset - q0);
-        const int a0 = max(lo - cbase, 0), b0 = min(hi - cbase, 31);
-        vm = a0 > b0 ? 0u : ((0xFFFFFFFFu >> (31 - b0)) & (0xFFFFFFFFu << a0));
-        if (nr < 0) {
-          uint32_t bits = 0;
-          for (int i = 0; i < 32; ++i) bits |= (kid_row != 0 && cs[256 + cbase + i] == kid_row) ? 1u << i : 0u;
-          vm &= bits;
-        }
-      }
+      const uint32_t vm = hf ? vm_hi : vm_lo;
       const uint32_t s_t = tmem + lane_off + u * 128 + wh * 32, dp_t = tmem + lane_off + u * 128 + 64 + wh * 32;
       uint32_t sx[32], dx[32];
       tc::tmem_ld_32x32b_x32(s_t, sx);
