@@ -449,53 +449,54 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       tc::mbar_arrive(kv_full(st));
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    // The whole warp runs the issue loop (converged); one elected lane issues.
+    {
       const uint32_t idesc_s = tc::idesc_bf16_f32(128, 128, 0, 0);
       const uint32_t idesc_o = tc::idesc_bf16_f32(128, TF_ON, 0, 1);
-      bool ok = tc::mbar_wait(q_full, 0, status, 13);
+      bool ok = tc::mbar_wait_w(q_full, 0, status, 13);
       tc::tc_fence_after();
       int it = 0, prev = -1;
       for (; ok && it < ntiles; ++it) {
         const int st = it % TF_ST;
-        if (!(ok = tc::mbar_wait(kv_full(st), (it / TF_ST) & 1, status, 14))) break;
+        if (!(ok = tc::mbar_wait_w(kv_full(st), (it / TF_ST) & 1, status, 14))) break;
         tc::tc_fence_after();
         for (int g = 0; g < 2; ++g) {
           const uint32_t s_t = tmem + g * 256, o_t = tmem + g * 256 + 128;
           if (it > 0) {
-            if (!(ok = tc::mbar_wait(p_full(g), (it - 1) & 1, status, 15))) break;
+            if (!(ok = tc::mbar_wait_w(p_full(g), (it - 1) & 1, status, 15))) break;
             tc::tc_fence_after();
             const uint32_t vb = sb + TF_V_OFF + prev * TF_V_STRIDE;
 #pragma unroll
             for (int k = 0; k < TK / 16; ++k)
-              tc::mma_bf16_ts(o_t, s_t + k * 8, tc::smem_desc_sw128(vb + k * 2048, TF_ONES_OFF - TF_V_OFF - prev * TF_V_STRIDE, 1024), idesc_o,
+              tc::mma_bf16_ts_w(o_t, s_t + k * 8, tc::smem_desc_sw128(vb + k * 2048, TF_ONES_OFF - TF_V_OFF - prev * TF_V_STRIDE, 1024), idesc_o,
                               (it > 1 || k > 0) ? 1u : 0u);
           }
           const uint32_t qb_ = sb + TF_Q_OFF + g * 16384, kb_ = sb + TF_K_OFF + st * 16384;
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            tc::mma_bf16(s_t, tc::smem_desc_sw128(qb_ + k * 32, 16, 1024), tc::smem_desc_sw128(kb_ + k * 32, 16, 1024),
+            tc::mma_bf16_w(s_t, tc::smem_desc_sw128(qb_ + k * 32, 16, 1024), tc::smem_desc_sw128(kb_ + k * 32, 16, 1024),
                          idesc_s, k > 0 ? 1u : 0u);
-          tc::mma_commit(s_full(g));
+          tc::mma_commit_w(s_full(g));
         }
         if (!ok) break;
-        if (it > 0) tc::mma_commit(kv_empty(prev));
+        if (it > 0) tc::mma_commit_w(kv_empty(prev));
         prev = st;
       }
       if (ok && it > 0) {
         for (int g = 0; g < 2; ++g) {
           const uint32_t s_t = tmem + g * 256, o_t = tmem + g * 256 + 128;
-          if (!tc::mbar_wait(p_full(g), (it - 1) & 1, status, 16)) break;
+          if (!tc::mbar_wait_w(p_full(g), (it - 1) & 1, status, 16)) break;
           tc::tc_fence_after();
           const uint32_t vb = sb + TF_V_OFF + prev * TF_V_STRIDE;
 #pragma unroll
           for (int k = 0; k < TK / 16; ++k)
-            tc::mma_bf16_ts(o_t, s_t + k * 8, tc::smem_desc_sw128(vb + k * 2048, TF_ONES_OFF - TF_V_OFF - prev * TF_V_STRIDE, 1024), idesc_o,
+            tc::mma_bf16_ts_w(o_t, s_t + k * 8, tc::smem_desc_sw128(vb + k * 2048, TF_ONES_OFF - TF_V_OFF - prev * TF_V_STRIDE, 1024), idesc_o,
                             (it > 1 || k > 0) ? 1u : 0u);
-          tc::mma_commit(o_full(g));
+          tc::mma_commit_w(o_full(g));
         }
       }
-      tc::mma_commit(done_bar);
-      tc::mbar_wait(done_bar, 0, status, 17);
+      tc::mma_commit_w(done_bar);
+      tc::mbar_wait_w(done_bar, 0, status, 17);
     }
   } else {
     const int g = (warp - 2) >> 2, quarter = warp & 3;

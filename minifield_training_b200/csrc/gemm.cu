@@ -182,17 +182,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    // The whole warp runs the issue loop (converged); one elected lane issues.
+    {
       const uint32_t idesc = tc::idesc_bf16_f32(BM, BN, args.a_mn, args.b_mn);
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        if (!tc::mbar_wait(tempty_bar(acc), acc_phase ^ 1, &g_status, 2)) break;
+        if (!tc::mbar_wait_w(tempty_bar(acc), acc_phase ^ 1, &g_status, 2)) break;
         tc::tc_fence_after();
         const uint32_t d = tmem + acc * BN;
         for (int kb = 0; kb < args.num_k; ++kb) {
-          if (!tc::mbar_wait(full_bar(stage), phase, &g_status, 3)) {
+          if (!tc::mbar_wait_w(full_bar(stage), phase, &g_status, 3)) {
             ok = false;
             break;
           }
@@ -204,23 +205,23 @@ __global__ void __launch_bounds__(THREADS, 1)
                                           : tc::smem_desc_sw128(sa + k * 32, 16, 1024);
             const uint64_t bd = args.b_mn ? tc::smem_desc_sw128(sb + k * 2048, 8192, 1024)
                                           : tc::smem_desc_sw128(sb + k * 32, 16, 1024);
-            tc::mma_bf16(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            tc::mma_bf16_w(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
-          tc::mma_commit(empty_bar(stage));
+          tc::mma_commit_w(empty_bar(stage));
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
-        tc::mma_commit(tfull_bar(acc));
+        tc::mma_commit_w(tfull_bar(acc));
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
         }
       }
       // Drain: every MMA issued above has completed before TMEM is freed.
-      tc::mma_commit(done_bar);
-      tc::mbar_wait(done_bar, 0, &g_status, 4);
+      tc::mma_commit_w(done_bar);
+      tc::mbar_wait_w(done_bar, 0, &g_status, 4);
     }
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may access
