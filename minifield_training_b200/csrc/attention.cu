@@ -708,7 +708,7 @@ constexpr int TB_V_OFF = 16384;
 constexpr int TB_QD_OFF = 32768;  // stage st: Q at +st*32768, dO at +st*32768+16384
 constexpr int TB_DS_OFF = TB_QD_OFF + TB_ST * 32768;  // two 32 KB dS^T buffers (item parity)
 constexpr int TB_COL_OFF = TB_DS_OFF + 2 * 32768;
-constexpr int TB_COL_STRIDE = 3 * 128 + 32;  // lse[128], dsum[128], qid[128], run table
+constexpr int TB_COL_STRIDE = 3 * 128;  // lse[128], dsum[128], qid[128]
 constexpr int TB_LIST_OFF = TB_COL_OFF + TB_ST * TB_COL_STRIDE * 4;
 constexpr int TB_BAR_OFF = TB_LIST_OFF + (TF_MAX_TILES + 4) * 4;
 // TMEM columns of the backward: S^T/dP^T double buffer [0,256), dV [256,320),
@@ -720,52 +720,37 @@ constexpr int TB_DQS_OFF = (TB_BAR_OFF + 256 + 1023) / 1024 * 1024;
 constexpr int TB_SMEM = 1024 + TB_DQS_OFF + 4 * 4096;
 static_assert(TB_SMEM <= 227 * 1024, "backward shared memory");
 
-// Run table of equal nonzero ids over a 128-entry tile: rt[0] = count (or -1
-// when an id recurs or there are more than 8 runs), then {id, first, last}.
-// Called by one full warp with its lane's four consecutive ids.
-__device__ __forceinline__ void warp_run_table(const int* v4, int lane, int* rt) {
-  const int prev = __shfl_up_sync(0xffffffffu, v4[3], 1);
-  const int next = __shfl_down_sync(0xffffffffu, v4[0], 1);
-  unsigned sbits = 0, ebits = 0;
+// P and dS for one key row and 32 query columns: p = 2^(s*scale*log2e - lse)
+// (zero where the query's id differs from the key row's, or before the
+// causal first column), ds = p * (dp - dsum); both packed to bf16 pairs. DENSE skips
+// the mask (the whole tile is valid). A key row with id 0 needs no test of its
+// own: only inactive queries carry id 0, and their lse is +inf (p = 0).
+template <bool DENSE>
+__device__ __forceinline__ void ds_chunk(const uint32_t (&sx)[32], const uint32_t (&dx)[32], const float* lse_s,
+                                         const float* dsum_s, const int* qid_s, int kid_row, int cfirst, float sl2,
+                                         uint32_t (&pk)[16], uint32_t (&dk4)[16]) {
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int before = e == 0 ? (lane == 0 ? 0 : prev) : v4[e - 1];
-    const int after = e == 3 ? (lane == 31 ? 0 : next) : v4[e + 1];
-    if (v4[e] != 0 && (e + lane == 0 || before != v4[e])) sbits |= 1u << e;
-    if (v4[e] != 0 && ((e == 3 && lane == 31) || after != v4[e])) ebits |= 1u << e;
-  }
-  const int ns = __popc(sbits), ne = __popc(ebits);
-  int incl_s = ns, incl_e = ne;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int ys = __shfl_up_sync(0xffffffffu, incl_s, o), ye = __shfl_up_sync(0xffffffffu, incl_e, o);
-    if (lane >= o) incl_s += ys, incl_e += ye;
-  }
-  const int total = __shfl_sync(0xffffffffu, incl_s, 31);
-  if (total <= TF_MAX_RUNS) {
-    int is = incl_s - ns, ie = incl_e - ne;
+  for (int i = 0; i < 32; i += 4) {
+    const float4 l4 = *reinterpret_cast<const float4*>(lse_s + i);
+    const float4 d4 = *reinterpret_cast<const float4*>(dsum_s + i);
+    const float ls[4] = {l4.x, l4.y, l4.z, l4.w}, dsm[4] = {d4.x, d4.y, d4.z, d4.w};
+    int qd[4] = {0, 0, 0, 0};
+    if (!DENSE) {
+      const int4 q4 = *reinterpret_cast<const int4*>(qid_s + i);
+      qd[0] = q4.x, qd[1] = q4.y, qd[2] = q4.z, qd[3] = q4.w;
+    }
+    float pv[4], dv4[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      if (sbits & (1u << e)) {
-        rt[1 + 3 * is] = v4[e];
-        rt[2 + 3 * is] = 4 * lane + e;
-        ++is;
-      }
-      if (ebits & (1u << e)) {
-        rt[3 + 3 * ie] = 4 * lane + e;
-        ++ie;
-      }
+      const float pe = ex2(fmaf(__uint_as_float(sx[i + e]), sl2, -ls[e]));
+      pv[e] = DENSE ? pe : ((qd[e] == kid_row && i + e >= cfirst) ? pe : 0.f);
+      dv4[e] = pv[e] * (__uint_as_float(dx[i + e]) - dsm[e]);
     }
+    pk[i >> 1] = pack_bf16(pv[0], pv[1]);
+    pk[(i >> 1) + 1] = pack_bf16(pv[2], pv[3]);
+    dk4[i >> 1] = pack_bf16(dv4[0], dv4[1]);
+    dk4[(i >> 1) + 1] = pack_bf16(dv4[2], dv4[3]);
   }
-  __syncwarp();
-  if (lane == 0) {
-    int cnt = total <= TF_MAX_RUNS ? total : -1;
-    for (int a = 0; cnt > 0 && a < total; ++a)
-      for (int c = a + 1; c < total; ++c)
-        if (rt[1 + 3 * a] == rt[1 + 3 * c]) cnt = -1;
-    rt[0] = cnt;
-  }
-  __syncwarp();
 }
 
 __global__ void __launch_bounds__(TB_THREADS, 1)
@@ -853,11 +838,32 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       tc::tma_load_2d(sb + TB_K_OFF, &tk, hk * 64, b * p.S + s0, kv_full);
       tc::tma_load_2d(sb + TB_V_OFF, &tv, hk * 64, b * p.S + s0, kv_full);
     }
+    // Column data (lse, dsum, query id) of an item, loaded one item ahead so
+    // that the global-load latency overlaps the wait for a free stage.
+    float cl[4], cd[4];
+    int cq[4];
+    auto load_cols = [&](int it) {
+      const int h = hk * p.G + it / nlive;
+      const int q0 = (list[1 + it % nlive] & 0xFFFF) * TQ;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = q0 + 4 * lane + e;
+        const long long li = ((long long)b * p.H + h) * p.T + t;
+        cl[e] = INFINITY, cd[e] = 0.f, cq[e] = 0;
+        if (t < p.T) {
+          cl[e] = p.lse[li];
+          cd[e] = p.dsum[li];
+          cq[e] = p.qid[(long long)b * p.T + t];
+        }
+      }
+    };
+    if (nitems > 0) load_cols(0);
     for (int it = 0; it < nitems; ++it) {
       const int st = it % TB_ST;
       const uint32_t ph = (it / TB_ST) & 1;
       const int h = hk * p.G + it / nlive;
-      const int q0 = (list[1 + it % nlive] & 0xFFFF) * TQ;
+      const int entry = list[1 + it % nlive];
+      const int q0 = (entry & 0xFFFF) * TQ;
       if (!tc::mbar_wait(qd_empty(st), ph ^ 1, status, 31)) break;
       if (lane == 0) {
         const uint32_t qb_ = sb + TB_QD_OFF + st * 32768;
@@ -869,27 +875,15 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       float* lse_s = reinterpret_cast<float*>(cs);
       float* dsum_s = reinterpret_cast<float*>(cs + 128);
       int* qid_s = cs + 256;
-      int v4[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int c = 4 * lane + e;
-        const int t = q0 + c;
-        const long long li = ((long long)b * p.H + h) * p.T + t;
-        float l = INFINITY, d = 0.f;
-        int q = 0;
-        if (t < p.T) {
-          l = p.lse[li];
-          d = p.dsum[li];
-          q = p.qid[(long long)b * p.T + t];
-          if (l == -INFINITY) l = INFINITY;  // a row without valid keys contributes no P
-        }
-        lse_s[c] = l;
-        dsum_s[c] = d;
-        qid_s[c] = q;
-        v4[e] = q;
+        lse_s[c] = cl[e] == -INFINITY ? INFINITY : cl[e];  // a row without valid keys contributes no P
+        dsum_s[c] = cd[e];
+        qid_s[c] = cq[e];
       }
-      warp_run_table(v4, lane, cs + 384);
       tc::mbar_arrive(qd_full(st));
+      if (it + 1 < nitems) load_cols(it + 1);
     }
   } else if (warp == 1) {
     // The whole warp runs the issue loop (converged); one elected lane issues.
@@ -990,50 +984,26 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       tc::tc_fence_before();
       tc::mbar_arrive(kv_tm);
     }
-    uint32_t vm_lo = 0xFFFFFFFFu, vm_hi = 0xFFFFFFFFu;  // validity of this warp's columns, both sub-items
+    bool full = true;  // the current item's tile is valid everywhere
+    int cfirst = -TQ;  // first causally valid query column of this key row in the current item
     for (int j = 0; ok && j < nsub; ++j) {
       const int it = j >> 1, hf = j & 1, u = j & 1, st = it % TB_ST;
       const int* cs = cols + st * TB_COL_STRIDE;
       // Warp-uniform wait outcomes: the TMEM accesses below are warp-collective.
       if (hf == 0) {
-        // Once per item, before its scores are ready: the item's column data
-        // and this key row's validity masks for both sub-items.
+        // Once per item, before its scores are ready: the item's column data,
+        // whether the whole tile is valid, and this key row's first causally
+        // valid column (key s sees queries t >= s - offset).
         ok = tc::mbar_wait(qd_full(st), (it / TB_ST) & 1, status, 37);
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
         const int entry = list[1 + it % nlive];
-        vm_lo = vm_hi = 0xFFFFFFFFu;
-        if (!((entry >> 30) & 1)) {
-          const int q0 = (entry & 0xFFFF) * TQ;
-          const int* rt = cs + 384;
-          const int nr = rt[0];
-          int lo = 1, hi = 0;
-          if (nr >= 0) {
-            for (int q = 0; q < nr; ++q)
-              if (rt[1 + 3 * q] == kid_row) lo = rt[2 + 3 * q], hi = rt[3 + 3 * q];
-          } else {
-            lo = 0, hi = TQ - 1;
-          }
-          if (p.causal) lo = max(lo, s - p.offset - q0);
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            const int cb = h2 * 64 + wh * 32;
-            const int a0 = max(lo - cb, 0), b0 = min(hi - cb, 31);
-            uint32_t vm = a0 > b0 ? 0u : ((0xFFFFFFFFu >> (31 - b0)) & (0xFFFFFFFFu << a0));
-            if (nr < 0) {
-              uint32_t bits = 0;
-              for (int i = 0; i < 32; ++i) bits |= (kid_row != 0 && cs[256 + cb + i] == kid_row) ? 1u << i : 0u;
-              vm &= bits;
-            }
-            if (h2 == 0) vm_lo = vm;
-            else vm_hi = vm;
-          }
-        }
+        full = (entry >> 30) & 1;
+        cfirst = p.causal ? s - p.offset - (entry & 0xFFFF) * TQ : -TQ;
       }
       ok = tc::mbar_wait(s_full(u), (j >> 1) & 1, status, 36);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;
       tc::tc_fence_after();
       const int cbase = hf * 64 + wh * 32;  // this warp's 32 query columns within the item
-      const uint32_t vm = hf ? vm_hi : vm_lo;
       const uint32_t s_t = tmem + lane_off + u * 128 + wh * 32, dp_t = tmem + lane_off + u * 128 + 64 + wh * 32;
       uint32_t sx[32], dx[32];
       tc::tmem_ld_32x32b_x32(s_t, sx);
@@ -1042,23 +1012,10 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       const float* lse_s = reinterpret_cast<const float*>(cs) + cbase;
       const float* dsum_s = reinterpret_cast<const float*>(cs + 128) + cbase;
       uint32_t pk[16], dk4[16];
-#pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const float4 l4 = *reinterpret_cast<const float4*>(lse_s + i);
-        const float4 d4 = *reinterpret_cast<const float4*>(dsum_s + i);
-        const float ls[4] = {l4.x, l4.y, l4.z, l4.w}, dsm[4] = {d4.x, d4.y, d4.z, d4.w};
-        float pv[4], dv4[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float pe = ex2(fmaf(__uint_as_float(sx[i + e]), sl2, -ls[e]));
-          pv[e] = (vm >> (i + e)) & 1u ? pe : 0.f;
-          dv4[e] = pv[e] * (__uint_as_float(dx[i + e]) - dsm[e]);
-        }
-        pk[i >> 1] = pack_bf16(pv[0], pv[1]);
-        pk[(i >> 1) + 1] = pack_bf16(pv[2], pv[3]);
-        dk4[i >> 1] = pack_bf16(dv4[0], dv4[1]);
-        dk4[(i >> 1) + 1] = pack_bf16(dv4[2], dv4[3]);
-      }
+      if (full)
+        ds_chunk<true>(sx, dx, lse_s, dsum_s, nullptr, kid_row, 0, sl2, pk, dk4);
+      else
+        ds_chunk<false>(sx, dx, lse_s, dsum_s, cs + 256 + cbase, kid_row, cfirst - cbase, sl2, pk, dk4);
       // P^T into the first 16 of this warp's own 32 consumed S^T columns.
       tc::tmem_st_32x32b_x16(s_t, pk);
       uint8_t* ds_row = smem + TB_DS_OFF + (it & 1) * 32768 + hf * 16384 + r * 128;
