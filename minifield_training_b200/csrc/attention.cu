@@ -702,7 +702,13 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 //                           queries), after both sub-items -> TMEM [384,448)
 // ---------------------------------------------------------------------------
 constexpr int TB_ST = 3;
-constexpr int TB_THREADS = 448;
+// Softmax-gradient warps per TMEM lane quarter and the query columns each
+// handles per 64-query sub-item; then the warp roles: producer, MMA issuer,
+// 4 * TB_SMW softmax-gradient warps, 4 dQ flush warps.
+constexpr int TB_SMW = 4;
+constexpr int TB_CW = 64 / TB_SMW;
+constexpr int TB_SM_WARPS = 4 * TB_SMW;
+constexpr int TB_THREADS = (2 + TB_SM_WARPS + 4) * 32;
 constexpr int TB_K_OFF = 0;
 constexpr int TB_V_OFF = 16384;
 constexpr int TB_QD_OFF = 32768;  // stage st: Q at +st*32768, dO at +st*32768+16384
@@ -720,17 +726,17 @@ constexpr int TB_DQS_OFF = (TB_BAR_OFF + 256 + 1023) / 1024 * 1024;
 constexpr int TB_SMEM = 1024 + TB_DQS_OFF + 4 * 4096;
 static_assert(TB_SMEM <= 227 * 1024, "backward shared memory");
 
-// P and dS for one key row and 32 query columns: p = 2^(s*scale*log2e - lse)
+// P and dS for one key row and N query columns: p = 2^(s*scale*log2e - lse)
 // (zero where the query's id differs from the key row's, or before the
 // causal first column), ds = p * (dp - dsum); both packed to bf16 pairs. DENSE skips
 // the mask (the whole tile is valid). A key row with id 0 needs no test of its
 // own: only inactive queries carry id 0, and their lse is +inf (p = 0).
-template <bool DENSE>
-__device__ __forceinline__ void ds_chunk(const uint32_t (&sx)[32], const uint32_t (&dx)[32], const float* lse_s,
+template <bool DENSE, int N>
+__device__ __forceinline__ void ds_chunk(const uint32_t (&sx)[N], const uint32_t (&dx)[N], const float* lse_s,
                                          const float* dsum_s, const int* qid_s, int kid_row, int cfirst, float sl2,
-                                         uint32_t (&pk)[16], uint32_t (&dk4)[16]) {
+                                         uint32_t (&pk)[N / 2], uint32_t (&dk4)[N / 2]) {
 #pragma unroll
-  for (int i = 0; i < 32; i += 4) {
+  for (int i = 0; i < N; i += 4) {
     const float4 l4 = *reinterpret_cast<const float4*>(lse_s + i);
     const float4 d4 = *reinterpret_cast<const float4*>(dsum_s + i);
     const float ls[4] = {l4.x, l4.y, l4.z, l4.w}, dsm[4] = {d4.x, d4.y, d4.z, d4.w};
@@ -794,12 +800,12 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
     }
     for (int u = 0; u < 2; ++u) {
       tc::mbar_init(s_full(u), 1);
-      tc::mbar_init(p_full(u), 256);
+      tc::mbar_init(p_full(u), 32 * TB_SM_WARPS);
     }
     tc::mbar_init(dq_full, 1);
     tc::mbar_init(dq_free, 128);
     tc::mbar_init(done_bar, 1);
-    tc::mbar_init(kv_tm, 256);
+    tc::mbar_init(kv_tm, 32 * TB_SM_WARPS);
     tc::mbar_fence_init();
   }
   if (warp == 0) {
@@ -913,7 +919,8 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
         const uint64_t dsd = tc::smem_desc_sw128(ds_ + hf * 16384, 16, 1024);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          tc::mma_bf16_ts_w(dv_t, s_t + (k >> 1) * 32 + (k & 1) * 8, dod_mn + (uint64_t)(k * 2048 >> 4), idesc_kn,
+          tc::mma_bf16_ts_w(dv_t, s_t + (16 * k / TB_CW) * TB_CW + (16 * k % TB_CW) / 2,
+                            dod_mn + (uint64_t)(k * 2048 >> 4), idesc_kn,
                           (j | k) != 0 ? 1u : 0u);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
@@ -955,8 +962,8 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       tc::mma_commit_w(done_bar);
       tc::mbar_wait_w(done_bar, 0, status, 35);
     }
-  } else if (warp < 10) {
-    const int quarter = warp & 3, wh = (warp - 2) >> 2;  // wh: which 32 of the sub-item's 64 columns
+  } else if (warp < 2 + TB_SM_WARPS) {
+    const int quarter = warp & 3, wq = (warp - 2) >> 2;  // wq: which TB_CW of the sub-item's 64 columns
     const int r = quarter * 32 + lane;
     const int s = s0 + r;
     const int kid_row = s < p.S ? p.kid[(long long)b * p.S + s] : 0;
@@ -965,20 +972,24 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
     bool ok;
     const int nsub = 2 * nitems;
     {
-      // K (wh 0) or V (wh 1) key row r into TMEM as the A operand of the
-      // score products: un-swizzle the 128-byte shared row, two bf16 per column.
+      // Key row r of K and V into TMEM as the A operand of the score
+      // products (K in columns [0,32), V in [32,64) of the K/V block; two
+      // bf16 per column): this warp copies TB_CW of those 64 columns,
+      // un-swizzling the 128-byte shared rows.
       ok = __all_sync(0xffffffffu, tc::mbar_wait(kv_full, 0, status, 41));
       if (ok) {
-        const uint8_t* row = smem + (wh ? TB_V_OFF : TB_K_OFF) + r * 128;
-        uint32_t w[32];
+        const int c0 = wq * TB_CW;  // first column of the K/V block
+        const uint8_t* row = smem + (c0 >= 32 ? TB_V_OFF : TB_K_OFF) + r * 128;
+        uint32_t w[TB_CW];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint4 x = *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) << 4));
+        for (int c = 0; c < TB_CW / 4; ++c) {
+          const int chunk = (c0 % 32) / 4 + c;
+          const uint4 x = *reinterpret_cast<const uint4*>(row + ((chunk ^ (r & 7)) << 4));
           w[4 * c] = x.x, w[4 * c + 1] = x.y, w[4 * c + 2] = x.z, w[4 * c + 3] = x.w;
         }
-        const uint32_t dst = tmem + lane_off + (wh ? TB_VT_COL : TB_KT_COL);
-        tc::tmem_st_32x32b_x16(dst, w);
-        tc::tmem_st_32x32b_x16(dst + 16, w + 16);
+        const uint32_t dst = tmem + lane_off + TB_KT_COL + c0;
+#pragma unroll
+        for (int c = 0; c < TB_CW; c += 16) tc::tmem_st_32x32b_x16(dst + c, w + c);
         tc::tmem_st_wait();
       }
       tc::tc_fence_before();
@@ -1003,25 +1014,31 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       ok = tc::mbar_wait(s_full(u), (j >> 1) & 1, status, 36);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;
       tc::tc_fence_after();
-      const int cbase = hf * 64 + wh * 32;  // this warp's 32 query columns within the item
-      const uint32_t s_t = tmem + lane_off + u * 128 + wh * 32, dp_t = tmem + lane_off + u * 128 + 64 + wh * 32;
-      uint32_t sx[32], dx[32];
-      tc::tmem_ld_32x32b_x32(s_t, sx);
-      tc::tmem_ld_32x32b_x32(dp_t, dx);
+      const int cbase = hf * 64 + wq * TB_CW;  // this warp's query columns within the item
+      const uint32_t s_t = tmem + lane_off + u * 128 + wq * TB_CW, dp_t = s_t + 64;
+      uint32_t sx[TB_CW], dx[TB_CW];
+#pragma unroll
+      for (int c = 0; c < TB_CW; c += 16) {
+        tc::tmem_ld_32x32b_x16(s_t + c, sx + c);
+        tc::tmem_ld_32x32b_x16(dp_t + c, dx + c);
+      }
       tc::tmem_ld_wait();
       const float* lse_s = reinterpret_cast<const float*>(cs) + cbase;
       const float* dsum_s = reinterpret_cast<const float*>(cs + 128) + cbase;
-      uint32_t pk[16], dk4[16];
+      uint32_t pk[TB_CW / 2], dk4[TB_CW / 2];
       if (full)
-        ds_chunk<true>(sx, dx, lse_s, dsum_s, nullptr, kid_row, 0, sl2, pk, dk4);
+        ds_chunk<true, TB_CW>(sx, dx, lse_s, dsum_s, nullptr, kid_row, 0, sl2, pk, dk4);
       else
-        ds_chunk<false>(sx, dx, lse_s, dsum_s, cs + 256 + cbase, kid_row, cfirst - cbase, sl2, pk, dk4);
-      // P^T into the first 16 of this warp's own 32 consumed S^T columns.
-      tc::tmem_st_32x32b_x16(s_t, pk);
+        ds_chunk<false, TB_CW>(sx, dx, lse_s, dsum_s, cs + 256 + cbase, kid_row, cfirst - cbase, sl2, pk, dk4);
+      // P^T (bf16 pairs) into the first TB_CW / 2 of this warp's own consumed
+      // S^T columns; dS^T into the item's shared buffer (128-byte swizzle,
+      // 64-query atom rows).
+#pragma unroll
+      for (int c = 0; c < TB_CW / 2; c += 8) tc::tmem_st_32x32b_x8(s_t + c, pk + c);
       uint8_t* ds_row = smem + TB_DS_OFF + (it & 1) * 32768 + hf * 16384 + r * 128;
 #pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const int c16 = wh * 4 + jj;  // 16-byte chunk of the 64-query atom row
+      for (int jj = 0; jj < TB_CW / 8; ++jj) {
+        const int c16 = wq * (TB_CW / 8) + jj;  // 16-byte chunk of the atom row
         *reinterpret_cast<uint4*>(ds_row + ((c16 ^ (r & 7)) << 4)) =
             make_uint4(dk4[4 * jj], dk4[4 * jj + 1], dk4[4 * jj + 2], dk4[4 * jj + 3]);
       }
@@ -1031,20 +1048,23 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       tc::mbar_arrive(p_full(u));
     }
     // Epilogue: after the last products, dK (times the logit scale) and dV
-    // (plus the uniform-row term) for this key row, this warp's 32 columns.
+    // (plus the uniform-row term) for this key row, this warp's TB_CW dims.
     const bool done_ok = ok && tc::mbar_wait(done_bar, 0, status, 38);
     if (__all_sync(0xffffffffu, done_ok)) {
       tc::tc_fence_after();
-      uint32_t kv[32], vv[32];
-      tc::tmem_ld_32x32b_x32(tmem + lane_off + 320 + wh * 32, kv);
-      tc::tmem_ld_32x32b_x32(tmem + lane_off + 256 + wh * 32, vv);
+      uint32_t kv[TB_CW], vv[TB_CW];
+#pragma unroll
+      for (int c = 0; c < TB_CW; c += 16) {
+        tc::tmem_ld_32x32b_x16(tmem + lane_off + 320 + wq * TB_CW + c, kv + c);
+        tc::tmem_ld_32x32b_x16(tmem + lane_off + 256 + wq * TB_CW + c, vv + c);
+      }
       tc::tmem_ld_wait();
       if (s < p.S) {
-        const long long off = (((long long)b * p.S + s) * p.Hk + hk) * HD + wh * 32;
-        const float* uv = p.uvec + ((long long)b * p.Hk + hk) * HD + wh * 32;
+        const long long off = (((long long)b * p.S + s) * p.Hk + hk) * HD + wq * TB_CW;
+        const float* uv = p.uvec + ((long long)b * p.Hk + hk) * HD + wq * TB_CW;
         const bool uni = p.policy == MFB_EMPTY_UNIFORM;
 #pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8) {
+        for (int c8 = 0; c8 < TB_CW / 8; ++c8) {
           uint4 a, c;
           uint32_t* aw = reinterpret_cast<uint32_t*>(&a);
           uint32_t* cw = reinterpret_cast<uint32_t*>(&c);
@@ -1076,23 +1096,23 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       tc::tc_fence_after();
       const int h = hk * p.G + it / nlive;
       const int t0 = (list[1 + it % nlive] & 0xFFFF) * TQ + quarter * 32;
-      uint32_t v[64];
-      tc::tmem_ld_32x32b_x32(dq_t, v);
-      tc::tmem_ld_32x32b_x32(dq_t + 32, v + 32);
-      tc::tmem_ld_wait();
-      tc::tc_fence_before();
-      tc::mbar_arrive(dq_free);
-      if (t0 < p.T) {  // rows past T inside the box are clipped by the tensor map
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
+      for (int half = 0; half < 2; ++half) {
+        uint32_t v[32];
+        tc::tmem_ld_32x32b_x32(dq_t + 32 * half, v);
+        tc::tmem_ld_wait();
+        if (half == 1) {  // the dQ columns are free for the next item's product
+          tc::tc_fence_before();
+          tc::mbar_arrive(dq_free);
+        }
+        if (t0 < p.T) {  // rows past T inside the box are clipped by the tensor map
           // The staging box is free once the previous reduction has read it.
           if (lane == 0) tc::bulk_wait_group_read0();
           __syncwarp();
 #pragma unroll
           for (int c = 0; c < 8; ++c)
             *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
-                make_uint4(v[32 * half + 4 * c], v[32 * half + 4 * c + 1], v[32 * half + 4 * c + 2],
-                           v[32 * half + 4 * c + 3]);
+                make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
           tc::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
