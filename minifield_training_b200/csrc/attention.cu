@@ -702,10 +702,15 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 //                           queries), after both sub-items -> TMEM [384,448)
 // ---------------------------------------------------------------------------
 constexpr int TB_ST = 3;
-// Softmax-gradient warps per TMEM lane quarter and the query columns each
-// handles per 64-query sub-item; then the warp roles: producer, MMA issuer,
-// 4 * TB_SMW softmax-gradient warps, 4 dQ flush warps.
+// Softmax-gradient warps per TMEM lane quarter (TB_SMW), in two groups that
+// take alternate sub-items (group g the sub-items of half g of every item, so
+// one group computes while the other waits for its scores); each warp handles
+// TB_PW query columns of its sub-items. TB_CW = the head dims (and K/V
+// columns) each of a quarter's warps covers in the prologue and epilogue.
+// Warp roles: producer, MMA issuer, 4 * TB_SMW softmax-gradient warps, 4 dQ
+// flush warps.
 constexpr int TB_SMW = 4;
+constexpr int TB_PW = 128 / TB_SMW;
 constexpr int TB_CW = 64 / TB_SMW;
 constexpr int TB_SM_WARPS = 4 * TB_SMW;
 constexpr int TB_THREADS = (2 + TB_SM_WARPS + 4) * 32;
@@ -800,7 +805,7 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
     }
     for (int u = 0; u < 2; ++u) {
       tc::mbar_init(s_full(u), 1);
-      tc::mbar_init(p_full(u), 32 * TB_SM_WARPS);
+      tc::mbar_init(p_full(u), 32 * TB_SM_WARPS / 2);
     }
     tc::mbar_init(dq_full, 1);
     tc::mbar_init(dq_free, 128);
@@ -906,8 +911,8 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       bool ok = tc::mbar_wait_w(kv_tm, 0, status, 32);
       tc::tc_fence_after();
       const int nsub = 2 * nitems;
-      // Issues dV/dK of sub-item j (its P^T is ready) and, after the second
-      // half of an item, that item's dQ; then frees the item's Q/dO stage.
+      // dV/dK of sub-item j (its P^T is ready); after the second half of an
+      // item, frees the item's Q/dO stage.
       auto finish = [&](int j) -> bool {
         const int it = j >> 1, hf = j & 1, u = j & 1, st = it % TB_ST;
         if (!tc::mbar_wait_w(p_full(u), (j >> 1) & 1, status, 34)) return false;
@@ -919,26 +924,34 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
         const uint64_t dsd = tc::smem_desc_sw128(ds_ + hf * 16384, 16, 1024);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          tc::mma_bf16_ts_w(dv_t, s_t + (16 * k / TB_CW) * TB_CW + (16 * k % TB_CW) / 2,
-                            dod_mn + (uint64_t)(k * 2048 >> 4), idesc_kn,
-                          (j | k) != 0 ? 1u : 0u);
+          tc::mma_bf16_ts_w(dv_t, s_t + (16 * k / TB_PW) * TB_PW + (16 * k % TB_PW) / 2,
+                            dod_mn + (uint64_t)(k * 2048 >> 4), idesc_kn, (j | k) != 0 ? 1u : 0u);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           tc::mma_bf16_w(dk_t, dsd + (uint64_t)(k * 32 >> 4), qd_mn + (uint64_t)(k * 2048 >> 4), idesc_kn,
-                       (j | k) != 0 ? 1u : 0u);
-        if (hf == 1) {
-          tc::mma_commit_w(qd_empty(st));
-          if (it > 0 && !tc::mbar_wait_w(dq_free, (it - 1) & 1, status, 39)) return false;
-          tc::tc_fence_after();
-          const uint64_t dsn = tc::smem_desc_sw128(ds_, 16384, 1024);
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            tc::mma_bf16_w(dq_t, dsn + (uint64_t)(k * 2048 >> 4), kdesc_mn + (uint64_t)(k * 2048 >> 4), idesc_nn,
-                         k > 0 ? 1u : 0u);
-          tc::mma_commit_w(dq_full);
-        }
+                         (j | k) != 0 ? 1u : 0u);
+        if (hf == 1) tc::mma_commit_w(qd_empty(st));
         return true;
       };
+      // dQ of item `it` from its dS^T (both halves written) once the flush
+      // warps have emptied the dQ columns.
+      auto issue_dq = [&](int it) -> bool {
+        if (it > 0 && !tc::mbar_wait_w(dq_free, (it - 1) & 1, status, 39)) return false;
+        tc::tc_fence_after();
+        const uint64_t dsn = tc::smem_desc_sw128(sb + TB_DS_OFF + (it & 1) * 32768, 16384, 1024);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          tc::mma_bf16_w(dq_t, dsn + (uint64_t)(k * 2048 >> 4), kdesc_mn + (uint64_t)(k * 2048 >> 4), idesc_nn,
+                         k > 0 ? 1u : 0u);
+        tc::mma_commit_w(dq_full);
+        return true;
+      };
+      // Order: S/dP(j), then the dQ an item left pending, then dV/dK(j-1).
+      // The next scores (which the softmax-gradient warps wait for) follow
+      // dV/dK directly; an item's dQ goes after the next sub-item's scores.
+      // dS^T buffer reuse stays safe: dQ(it) precedes S/dP of item it+2,
+      // whose completion the writers of dS^T(it+2) wait for.
+      int pend = -1;
       for (int j = 0; ok && j < nsub; ++j) {
         const int it = j >> 1, hf = j & 1, u = j & 1, st = it % TB_ST;
         if (hf == 0) {
@@ -956,9 +969,19 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
         for (int k = 0; k < 4; ++k)
           tc::mma_bf16_ts_w(dp_t, v_tm + k * 8, dod + (uint64_t)(k * 32 >> 4), idesc_s, k > 0 ? 1u : 0u);
         tc::mma_commit_w(s_full(u));
-        if (j > 0 && !(ok = finish(j - 1))) break;
+        if (pend >= 0) {
+          if (!(ok = issue_dq(pend))) break;
+          pend = -1;
+        }
+        if (j > 0) {
+          if (!(ok = finish(j - 1))) break;
+          if ((j - 1) & 1) pend = (j - 1) >> 1;
+        }
       }
-      if (ok && nsub > 0) finish(nsub - 1);
+      if (ok && nsub > 0) {
+        ok = finish(nsub - 1);
+        if (ok) ok = issue_dq(nitems - 1);
+      }
       tc::mma_commit_w(done_bar);
       tc::mbar_wait_w(done_bar, 0, status, 35);
     }
@@ -995,52 +1018,47 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       tc::tc_fence_before();
       tc::mbar_arrive(kv_tm);
     }
-    bool full = true;  // the current item's tile is valid everywhere
-    int cfirst = -TQ;  // first causally valid query column of this key row in the current item
-    for (int j = 0; ok && j < nsub; ++j) {
-      const int it = j >> 1, hf = j & 1, u = j & 1, st = it % TB_ST;
+    const int g = wq >> 1, wh = wq & 1;  // group (= sub-item half), which TB_PW of its 64 columns
+    for (int j = g; ok && j < nsub; j += 2) {
+      const int it = j >> 1, u = g, st = it % TB_ST;
       const int* cs = cols + st * TB_COL_STRIDE;
       // Warp-uniform wait outcomes: the TMEM accesses below are warp-collective.
-      if (hf == 0) {
-        // Once per item, before its scores are ready: the item's column data,
-        // whether the whole tile is valid, and this key row's first causally
-        // valid column (key s sees queries t >= s - offset).
-        ok = tc::mbar_wait(qd_full(st), (it / TB_ST) & 1, status, 37);
-        if (!(ok = __all_sync(0xffffffffu, ok))) break;
-        const int entry = list[1 + it % nlive];
-        full = (entry >> 30) & 1;
-        cfirst = p.causal ? s - p.offset - (entry & 0xFFFF) * TQ : -TQ;
-      }
-      ok = tc::mbar_wait(s_full(u), (j >> 1) & 1, status, 36);
+      // The item's column data, whether its whole tile is valid, and this key
+      // row's first causally valid column (key s sees queries t >= s - offset).
+      ok = tc::mbar_wait(qd_full(st), (it / TB_ST) & 1, status, 37);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      const int entry = list[1 + it % nlive];
+      const bool full = (entry >> 30) & 1;
+      const int cfirst = p.causal ? s - p.offset - (entry & 0xFFFF) * TQ : -TQ;
+      ok = tc::mbar_wait(s_full(u), it & 1, status, 36);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;
       tc::tc_fence_after();
-      const int cbase = hf * 64 + wq * TB_CW;  // this warp's query columns within the item
-      const uint32_t s_t = tmem + lane_off + u * 128 + wq * TB_CW, dp_t = s_t + 64;
-      uint32_t sx[TB_CW], dx[TB_CW];
+      const uint32_t s_t = tmem + lane_off + u * 128 + wh * TB_PW, dp_t = s_t + 64;
+      uint8_t* ds_row = smem + TB_DS_OFF + (it & 1) * 32768 + g * 16384 + r * 128;
+      // 16 columns at a time: P^T (bf16 pairs) into the first TB_PW / 2 of this
+      // warp's own consumed S^T columns; dS^T into the item's shared buffer
+      // (128-byte swizzle, 64-query atom rows).
 #pragma unroll
-      for (int c = 0; c < TB_CW; c += 16) {
-        tc::tmem_ld_32x32b_x16(s_t + c, sx + c);
-        tc::tmem_ld_32x32b_x16(dp_t + c, dx + c);
-      }
-      tc::tmem_ld_wait();
-      const float* lse_s = reinterpret_cast<const float*>(cs) + cbase;
-      const float* dsum_s = reinterpret_cast<const float*>(cs + 128) + cbase;
-      uint32_t pk[TB_CW / 2], dk4[TB_CW / 2];
-      if (full)
-        ds_chunk<true, TB_CW>(sx, dx, lse_s, dsum_s, nullptr, kid_row, 0, sl2, pk, dk4);
-      else
-        ds_chunk<false, TB_CW>(sx, dx, lse_s, dsum_s, cs + 256 + cbase, kid_row, cfirst - cbase, sl2, pk, dk4);
-      // P^T (bf16 pairs) into the first TB_CW / 2 of this warp's own consumed
-      // S^T columns; dS^T into the item's shared buffer (128-byte swizzle,
-      // 64-query atom rows).
+      for (int c = 0; c < TB_PW; c += 16) {
+        const int cbase = g * 64 + wh * TB_PW + c;  // query columns within the item
+        uint32_t sx[16], dx[16];
+        tc::tmem_ld_32x32b_x16(s_t + c, sx);
+        tc::tmem_ld_32x32b_x16(dp_t + c, dx);
+        tc::tmem_ld_wait();
+        const float* lse_s = reinterpret_cast<const float*>(cs) + cbase;
+        const float* dsum_s = reinterpret_cast<const float*>(cs + 128) + cbase;
+        uint32_t pk[8], dk4[8];
+        if (full)
+          ds_chunk<true, 16>(sx, dx, lse_s, dsum_s, nullptr, kid_row, 0, sl2, pk, dk4);
+        else
+          ds_chunk<false, 16>(sx, dx, lse_s, dsum_s, cs + 256 + cbase, kid_row, cfirst - cbase, sl2, pk, dk4);
+        tc::tmem_st_32x32b_x8(s_t + c / 2, pk);
 #pragma unroll
-      for (int c = 0; c < TB_CW / 2; c += 8) tc::tmem_st_32x32b_x8(s_t + c, pk + c);
-      uint8_t* ds_row = smem + TB_DS_OFF + (it & 1) * 32768 + hf * 16384 + r * 128;
-#pragma unroll
-      for (int jj = 0; jj < TB_CW / 8; ++jj) {
-        const int c16 = wq * (TB_CW / 8) + jj;  // 16-byte chunk of the atom row
-        *reinterpret_cast<uint4*>(ds_row + ((c16 ^ (r & 7)) << 4)) =
-            make_uint4(dk4[4 * jj], dk4[4 * jj + 1], dk4[4 * jj + 2], dk4[4 * jj + 3]);
+        for (int jj = 0; jj < 2; ++jj) {
+          const int c16 = (wh * TB_PW + c) / 8 + jj;  // 16-byte chunk of the atom row
+          *reinterpret_cast<uint4*>(ds_row + ((c16 ^ (r & 7)) << 4)) =
+              make_uint4(dk4[4 * jj], dk4[4 * jj + 1], dk4[4 * jj + 2], dk4[4 * jj + 3]);
+        }
       }
       tc::tmem_st_wait();
       tc::fence_proxy_async_smem();
