@@ -23,8 +23,8 @@
 // dtype, attention.py:31).
 // Backward (attn_bwd_tc_kernel): CTA = (128 key rows, KV head, batch row);
 // loops over the group's query heads and live query tiles, accumulates dK/dV
-// in TMEM (no atomics for the GQA reduction) and dQ in FP32 with vector atomics
-// into the workspace.
+// in TMEM (no atomics for the GQA reduction) and dQ in FP32 with TMA tensor
+// reduce-adds into the workspace.
 #include <math.h>
 
 #include "common.cuh"
@@ -163,7 +163,8 @@ __global__ void ranges_kernel(const int* __restrict__ qid, const int* __restrict
 // Backward.
 // ---------------------------------------------------------------------------
 
-// dsum[b,h,t] = sum_d dO * O; uniform-policy empty rows add dO/S to uvec[b,hk].
+// dsum[b,h,t] = sum_d dO * O; uniform-policy empty rows add dO/S to uvec[b,hk];
+// and the row's FP32 dQ accumulator is zeroed for the main kernel's reductions.
 __global__ void __launch_bounds__(256) attn_bwd_pre_kernel(Params p) {
   const long long row = (long long)blockIdx.x * 32 + (threadIdx.x >> 3);  // (b, t, h) flattened as bthd rows
   const int sub = threadIdx.x & 7;
@@ -172,6 +173,9 @@ __global__ void __launch_bounds__(256) attn_bwd_pre_kernel(Params p) {
   float acc = 0.f;
   uint4 dov = make_uint4(0, 0, 0, 0);
   if (ok) {
+    float4* z = reinterpret_cast<float4*>(p.dq_acc + row * HD + sub * 8);
+    z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
     dov = *reinterpret_cast<const uint4*>(p.d_o + row * HD + sub * 8);
     const uint4 ov = *reinterpret_cast<const uint4*>(p.o + row * HD + sub * 8);
     const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(&dov);
@@ -221,7 +225,7 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(const float* __restrict
 //   warp 0      TMA producer (lane 0): both Q tiles once, then K/V tiles
 //               through a 3-stage ring (128 keys x 64 dims, 128-byte swizzle);
 //               all lanes stage each key tile's ids and run table.
-//   warp 1      TMEM owner and single-thread tcgen05.mma issuer.
+//   warp 1      TMEM owner and MMA issuer (whole warp, one elected lane).
 //   warps 2-5   softmax for query head h0, warps 6-9 for h0 + 1: one thread
 //               per query row (TMEM lane quarter = warp % 4), reading its S row
 //               with tcgen05.ld.
@@ -677,22 +681,25 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 // CTA = (128 keys, one KV head, batch row); it loops over the group's query
 // heads x live 128-row query tiles ("items"), each split into two 64-query
 // sub-items so the tensor core works on one sub-item while the
-// softmax-gradient warps work on the other. Warp roles (448 threads):
+// softmax-gradient warps work on the other. Warp roles (704 threads):
 //   warp 0      producer: K and V once; per item the Q and dO tiles (TMA, three
-//               stages) and the per-query lse, dsum, qid and run table.
-//   warp 1      TMEM owner, single-thread tcgen05.mma issuer.
-//   warps 2-9   softmax-gradient: one key row (TMEM lane) per thread, 32 of
-//               the sub-item's 64 query columns per warp (two warps per lane
-//               quarter).
-//   warps 10-13 dQ flush: add each item's dQ tile into the FP32 accumulator
+//               stages) and the per-query lse, dsum and query id (loaded one
+//               item ahead).
+//   warp 1      TMEM owner and MMA issuer (whole warp, one elected lane).
+//   warps 2-17  softmax-gradient, two groups of eight taking alternate
+//               sub-items (half 0 / half 1 of every item): one key row (TMEM
+//               lane) per thread, 32 of the sub-item's 64 query columns per
+//               warp, two warps of a group per TMEM lane quarter. Prologue: K
+//               and V rows into TMEM; epilogue: dK/dV rows out.
+//   warps 18-21 dQ flush: add each item's dQ tile into the FP32 accumulator
 //               while the next item is computed: TMEM -> swizzled shared
 //               staging -> TMA tensor reduce-add (the reductions run in the
 //               TMA unit and L2, off the SM's load/store path that the
 //               mbarrier polls and the shared-memory traffic share).
 // Products (M = 128 keys unless noted), issued in the order
-//   S/dP(j), [P ready j-1] dV/dK(j-1), [dQ tile free] dQ(item of j-1), S/dP(j+1)...
-//   S^T_j  = K Q_j^T        N = 64 -> TMEM buffer j%2 [0,64)
-//   dP^T_j = V dO_j^T       N = 64 -> TMEM buffer j%2 [64,128)
+//   S/dP(j), [dQ tile free] dQ(item pending), [P ready j-1] dV/dK(j-1), S/dP(j+1)...
+//   S^T_j  = K Q_j^T        TS (K from TMEM), N = 64 -> TMEM buffer j%2 [0,64)
+//   dP^T_j = V dO_j^T       TS (V from TMEM), N = 64 -> TMEM buffer j%2 [64,128)
 //   P^T_j (bf16) goes back into its warp's own consumed S^T columns; dS^T_j
 //   (bf16) into shared memory (128-byte swizzle, item parity buffer, 64-query
 //   atom per sub-item).
@@ -1240,7 +1247,7 @@ __global__ void __launch_bounds__(1024) schedule_kernel(Params p, int backward, 
   const int ntq = cdiv(p.T, TQ), nkt = cdiv(p.S, TK);
   const int per = backward ? nkt : ntq, other = backward ? ntq : nkt;
   const int n = p.B * per;
-  for (int i = threadIdx.x; i <= TF_MAX_TILES; i += blockDim.x) hist[i] = 0;
+  for (int i = threadIdx.x; i <= other; i += blockDim.x) hist[i] = 0;
   __syncthreads();
   auto weight = [&](int it) {
     const int t = it % per, b = it / per;
@@ -1258,9 +1265,9 @@ __global__ void __launch_bounds__(1024) schedule_kernel(Params p, int backward, 
   };
   for (int it = threadIdx.x; it < n; it += blockDim.x) atomicAdd(&hist[weight(it)], 1);
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0) {  // weights are tile counts, at most `other`
     int acc = 0;
-    for (int c = TF_MAX_TILES; c >= 0; --c) {
+    for (int c = other; c >= 0; --c) {
       base[c] = acc;
       acc += hist[c];
     }
@@ -1405,7 +1412,6 @@ extern "C" int mfb_attn_bwd(const uint16_t* q, const uint16_t* k, const uint16_t
   p.kid = kid;
   cudaStream_t s = (cudaStream_t)stream;
   if ((st = launch_ranges(p, qid, kid, s))) return st;
-  MFB_CUDA_TRY(cudaMemsetAsync(w.dq_acc, 0, sizeof(float) * (size_t)B * T * H * HD, s));
   MFB_CUDA_TRY(cudaMemsetAsync(w.uvec, 0, sizeof(float) * (size_t)B * Hk * HD, s));
   const long long rows = (long long)B * T * H;
   attn_bwd_pre_kernel<<<(unsigned)((rows + 31) / 32), 256, 0, s>>>(p);

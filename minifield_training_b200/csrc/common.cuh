@@ -103,11 +103,4 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Fire-and-forget vector reduction into global memory (no returned value, so
-// the issuing thread does not wait for the L2 atomic unit).
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
-
 }  // namespace mfb
