@@ -726,7 +726,10 @@ constexpr int TB_V_OFF = 16384;
 constexpr int TB_QD_OFF = 32768;  // stage st: Q at +st*32768, dO at +st*32768+16384
 constexpr int TB_DS_OFF = TB_QD_OFF + TB_ST * 32768;  // two 32 KB dS^T buffers (item parity)
 constexpr int TB_COL_OFF = TB_DS_OFF + 2 * 32768;
-constexpr int TB_COL_STRIDE = 3 * 128;  // lse[128], dsum[128], qid[128]
+// Per stage: lse[128], dsum[128], qid[128], then per 16-query chunk its id
+// (valid when the chunk's bit in the mask word that follows is set: all 16
+// queries share it).
+constexpr int TB_COL_STRIDE = 3 * 128 + 8 + 8;
 constexpr int TB_LIST_OFF = TB_COL_OFF + TB_ST * TB_COL_STRIDE * 4;
 constexpr int TB_BAR_OFF = TB_LIST_OFF + (TF_MAX_TILES + 4) * 4;
 // TMEM columns of the backward: S^T/dP^T double buffer [0,256), dV [256,320),
@@ -900,6 +903,18 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
         dsum_s[c] = cd[e];
         qid_s[c] = cq[e];
       }
+      {  // 16-query chunks whose queries all carry one id (lanes 4c..4c+3 hold chunk c)
+        const int first = __shfl_sync(0xffffffffu, cq[0], lane & ~3);
+        const bool same = cq[0] == first && cq[1] == first && cq[2] == first && cq[3] == first;
+        const unsigned bal = __ballot_sync(0xffffffffu, same);
+        if ((lane & 3) == 0) qid_s[128 + (lane >> 2)] = first;
+        if (lane == 0) {
+          unsigned m = 0;
+          for (int c = 0; c < 8; ++c) m |= ((bal >> (4 * c)) & 0xFu) == 0xFu ? 1u << c : 0u;
+          qid_s[136] = (int)m;
+        }
+      }
+      __syncwarp();
       tc::mbar_arrive(qd_full(st));
       if (it + 1 < nitems) load_cols(it + 1);
     }
@@ -1048,17 +1063,31 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
 #pragma unroll
       for (int c = 0; c < TB_PW; c += 16) {
         const int cbase = g * 64 + wh * TB_PW + c;  // query columns within the item
-        uint32_t sx[16], dx[16];
-        tc::tmem_ld_32x32b_x16(s_t + c, sx);
-        tc::tmem_ld_32x32b_x16(dp_t + c, dx);
-        tc::tmem_ld_wait();
-        const float* lse_s = reinterpret_cast<const float*>(cs) + cbase;
-        const float* dsum_s = reinterpret_cast<const float*>(cs + 128) + cbase;
+        // Chunk class for the warp's 32 key rows: dense (every pair valid),
+        // zero (none valid: P = dS = 0 without touching the scores) or mixed.
+        bool dense = full, zero = false;
+        if (!full) {
+          const bool uni = (cs[256 + 136] >> (cbase >> 4)) & 1;
+          const int uid = cs[256 + 128 + (cbase >> 4)];
+          dense = __all_sync(0xffffffffu, uni && uid == kid_row && cfirst <= cbase);
+          zero = !dense && __all_sync(0xffffffffu, (uni && uid != kid_row) || cfirst > cbase + 15);
+        }
         uint32_t pk[8], dk4[8];
-        if (full)
-          ds_chunk<true, 16>(sx, dx, lse_s, dsum_s, nullptr, kid_row, 0, sl2, pk, dk4);
-        else
-          ds_chunk<false, 16>(sx, dx, lse_s, dsum_s, cs + 256 + cbase, kid_row, cfirst - cbase, sl2, pk, dk4);
+        if (zero) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) pk[e] = 0u, dk4[e] = 0u;
+        } else {
+          uint32_t sx[16], dx[16];
+          tc::tmem_ld_32x32b_x16(s_t + c, sx);
+          tc::tmem_ld_32x32b_x16(dp_t + c, dx);
+          tc::tmem_ld_wait();
+          const float* lse_s = reinterpret_cast<const float*>(cs) + cbase;
+          const float* dsum_s = reinterpret_cast<const float*>(cs + 128) + cbase;
+          if (dense)
+            ds_chunk<true, 16>(sx, dx, lse_s, dsum_s, nullptr, kid_row, 0, sl2, pk, dk4);
+          else
+            ds_chunk<false, 16>(sx, dx, lse_s, dsum_s, cs + 256 + cbase, kid_row, cfirst - cbase, sl2, pk, dk4);
+        }
         tc::tmem_st_32x32b_x8(s_t + c / 2, pk);
 #pragma unroll
         for (int jj = 0; jj < 2; ++jj) {
