@@ -217,6 +217,27 @@ int mfb_adamw_commit(float* params, float* m, float* v, const float* grads, long
                      const float* grad_divisor, float learning_rate, float beta1, float beta2, float epsilon,
                      float weight_decay, float clip_norm, void* result, void* workspace, size_t workspace_bytes,
                      void* stream);
+/* One pass of the same transaction over this rank's slice, for an AdamW state
+ * sharded across data-parallel ranks (the reference keeps the state
+ * replicated: adamw.py:384-571 applied to every rank's copy after the psum of
+ * engine/step.py:62; slicing the elementwise update leaves the arithmetic per
+ * element unchanged). Order per step: CHECK on [lo, hi) of [0, n_total) ->
+ * SUM-allreduce red[0..2] -> CHECK_FINALIZE -> CANDIDATE on [lo, hi) of the
+ * trainable range -> SUM-allreduce red[0..1] -> CANDIDATE_FINALIZE -> COMMIT
+ * on that slice -> all-gather of the masters. `red` is a caller-owned device
+ * buffer of 3 doubles. Slices start at multiples of 4 elements. */
+enum {
+  MFB_ADAMW_CHECK = 0,
+  MFB_ADAMW_CHECK_FINALIZE = 1,
+  MFB_ADAMW_CANDIDATE = 2,
+  MFB_ADAMW_CANDIDATE_FINALIZE = 3,
+  MFB_ADAMW_COMMIT = 4
+};
+int mfb_adamw_shard_pass(int pass, float* params, float* m, float* v, const float* grads, long long lo, long long hi,
+                         long long n_train, long long n_decayed, long long n_total, int32_t* step, const float* loss,
+                         const uint8_t* accumulation_valid, const float* grad_divisor, float learning_rate,
+                         float beta1, float beta2, float epsilon, float weight_decay, float clip_norm, double* red,
+                         void* result, void* workspace, size_t workspace_bytes, void* stream);
 /* Logical-step normalization (src/minifield_training/engine/step.py:384-389):
  * accumulation_valid = counts_valid && isfinite(count_sum) && count_sum > 0;
  * divisor = count_sum if valid else 1; loss = loss_sum / divisor. All device

@@ -73,6 +73,7 @@ SIGNATURES = {
     "mfb_graph_destroy": (I, [P]),
     "mfb_adamw_workspace_size": (SZ, []),
     "mfb_adamw_commit": (I, [P, P, P, P, LL, LL, LL, P, P, P, P, F, F, F, F, F, F, P, P, SZ, P]),
+    "mfb_adamw_shard_pass": (I, [I, P, P, P, P, LL, LL, LL, LL, LL, P, P, P, P, F, F, F, F, F, F, P, P, P, SZ, P]),
     "mfb_step_normalize": (I, [P, P, P, P, P, P, P]),
     "mfb_norm_workspace_size": (SZ, [I, I]),
     "mfb_rmsnorm_fwd": (I, [P, P, P, P, P, P, P, I, I, F, P]),

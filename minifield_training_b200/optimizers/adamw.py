@@ -181,17 +181,24 @@ class State(dict):
         return self.layout.views(self.arenas["grads"], self.layout.trainable)
 
 
-def initialize_state(parameters, inventory: Inventory, *, order=None, grads=None) -> State:
+def initialize_state(parameters, inventory: Inventory, *, order=None, grads=None, params=None) -> State:
     """Zero-moment FP32 state (adamw.py:300-322); rejects non-finite masters.
 
-    ``order`` sets the arena order (see Layout); ``grads`` optionally supplies
-    the gradient arena (FP32, at least n_train elements, 16-byte aligned), e.g.
-    a buffer that a collective library also addresses.
+    ``order`` sets the arena order (see Layout); ``grads`` / ``params``
+    optionally supply the gradient arena (FP32, at least n_train elements) and
+    the master arena (FP32, zeroed, at least n_total elements), both 16-byte
+    aligned, e.g. buffers that a collective library also addresses.
     """
     layout = Layout(inventory, order)
     if set(parameters) != set(layout.specs):
         raise ValueError("Full-weight parameter tree mismatch")
-    arenas = {k: DeviceArray.zeros((max(layout.n_total, 4),), "float32") for k in ("params", "m", "v")}
+    arenas = {k: DeviceArray.zeros((max(layout.n_total, 4),), "float32") for k in ("m", "v")}
+    if params is not None:
+        if params.dtype != "float32" or params.size < layout.n_total or params.ptr % 16:
+            raise ValueError("master arena must be 16-byte aligned float32 with n_total elements")
+        arenas["params"] = params
+    else:
+        arenas["params"] = DeviceArray.zeros((max(layout.n_total, 4),), "float32")
     if grads is not None:
         if grads.dtype != "float32" or grads.size < layout.n_train or grads.ptr % 16:
             raise ValueError("gradient arena must be 16-byte aligned float32 with n_train elements")
@@ -301,6 +308,88 @@ def make_transaction(inventory: Inventory, config: AdamWConfig):
                   P(divisor.ptr) if divisor is not None else None, config.learning_rate, config.beta1, config.beta2,
                   config.epsilon, config.weight_decay, config.clip_norm, P(result_dev.ptr), P(workspace.ptr),
                   workspace.nbytes, stream)
+        return CommitResult(state, result_dev, stream)
+
+    return transition
+
+
+# Passes of mfb_adamw_shard_pass (include/mfb200.h).
+_CHECK, _CHECK_FINALIZE, _CANDIDATE, _CANDIDATE_FINALIZE, _COMMIT = range(5)
+
+
+def shard_slices(n: int, world: int, rank: int):
+    """(lo, hi, per) of ``rank``'s slice of [0, n): ``world`` slices of ``per``
+    elements (a multiple of 4, per * world >= n), the last ones clipped at n."""
+    per = -(-n // (4 * world)) * 4
+    lo = min(rank * per, n)
+    return lo, min(lo + per, n), per
+
+
+def sharded_master_elements(layout, world: int) -> int:
+    """Master arena size for a sharded transaction: the all-gather covers
+    ``world`` equal trainable slices, which may run past n_total."""
+    return max(layout.n_total, shard_slices(layout.n_train, world, 0)[2] * world, 4)
+
+
+def make_sharded_transaction(inventory: Inventory, config: AdamWConfig, group):
+    """The transaction of ``make_transaction`` with the elementwise passes split
+    across the data-parallel ranks of ``group`` (a torch.distributed process
+    group over NCCL): ``transition(state, active_loss, accumulation_valid, *,
+    divisor=None, stream=None)`` on the reduced gradients already in
+    ``state.arenas["grads"]``.
+
+    Each rank checks its slice of the state, runs the candidate and the commit
+    on its slice of the trainable masters and moments, and the ranks
+    all-gather the masters; the global decisions (gradient norm and flags,
+    update norm and candidate flags) are SUM-allreduces of three doubles, so
+    every rank reaches the same code. The moments outside a rank's slice are
+    never read or written on that rank. ``state.arenas["params"]`` must be a
+    torch-backed DeviceArray (``._base``) of ``sharded_master_elements``.
+    """
+    import torch
+    import torch.distributed as dist
+
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    workspace = DeviceArray((_lib.lib().mfb_adamw_workspace_size(),), "uint8")
+    result_dev = DeviceArray((6,), "int32")
+    red = torch.zeros(3, dtype=torch.float64, device=f"cuda:{torch.cuda.current_device()}")
+    scalars = {}
+    names = set(inventory.names)
+
+    def transition(state: State, active_loss, accumulation_valid, *, divisor=None, stream=None):
+        if not isinstance(state, State) or set(state.layout.specs) != names:
+            raise ValueError("Full-weight state does not match the inventory")
+        layout, a = state.layout, state.arenas
+        base = a["params"]._base
+        if base is None or base.numel() < sharded_master_elements(layout, world):
+            raise ValueError("sharded AdamW needs a torch-backed master arena of sharded_master_elements")
+        loss = _device_scalar(active_loss, "float32", scalars, "loss")
+        valid = _device_scalar(bool(accumulation_valid) if not isinstance(accumulation_valid, DeviceArray)
+                               else accumulation_valid, "uint8", scalars, "valid")
+        P = ctypes.c_void_p
+        c_lo, c_hi, _ = shard_slices(layout.n_total, world, rank)
+        t_lo, t_hi, per = shard_slices(layout.n_train, world, rank)
+
+        def run(pass_id, lo, hi):
+            _lib.call("mfb_adamw_shard_pass", pass_id, P(a["params"].ptr), P(a["m"].ptr), P(a["v"].ptr),
+                      P(a["grads"].ptr), lo, hi, layout.n_train, layout.n_decayed, layout.n_total,
+                      P(a["step"].ptr), P(loss.ptr), P(valid.ptr), P(divisor.ptr) if divisor is not None else None,
+                      config.learning_rate, config.beta1, config.beta2, config.epsilon, config.weight_decay,
+                      config.clip_norm, P(red.data_ptr()), P(result_dev.ptr), P(workspace.ptr), workspace.nbytes,
+                      stream)
+
+        import contextlib
+        ctx = (torch.cuda.stream(torch.cuda.ExternalStream(stream)) if stream is not None
+               else contextlib.nullcontext())
+        with ctx:  # the collectives order after this stream's kernels, and it after them
+            run(_CHECK, c_lo, c_hi)
+            dist.all_reduce(red, group=group)
+            run(_CHECK_FINALIZE, 0, 0)
+            run(_CANDIDATE, t_lo, t_hi)
+            dist.all_reduce(red[:2], group=group)
+            run(_CANDIDATE_FINALIZE, 0, 0)
+            run(_COMMIT, t_lo, t_hi)
+            dist.all_gather_into_tensor(base[:per * world], base[rank * per:(rank + 1) * per], group=group)
         return CommitResult(state, result_dev, stream)
 
     return transition

@@ -170,3 +170,79 @@ def test_normalized_step_divides_gradients_and_loss():
     for g in ("params", "m", "v"):
         for n in shapes:
             np.testing.assert_array_equal(after[g][n], ref[0][g][n], err_msg=f"{g}/{n}")
+
+
+def _sharded_vs_full(out, port):
+    """Child process: one-rank NCCL group; the sharded transaction against the full one on equal states."""
+    import datetime
+    import os
+
+    import torch
+    import torch.distributed as dist
+
+    from minifield_training_b200 import device
+    from minifield_training_b200.device import DeviceArray
+    from minifield_training_b200.optimizers import adamw
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(0)
+    device.set_device(0)
+    dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=60))
+    rng = np.random.default_rng(3)
+    shapes = {"a.matrix": (37, 53), "b.matrix": (64, 16), "c.vector": (61,), "d.frozen": (9, 7)}
+    inv = adamw.build_inventory(shapes, decayed_names=frozenset({"a.matrix", "b.matrix"}),
+                                frozen_names=frozenset({"d.frozen"}))
+    params = {n: rng.standard_normal(s).astype(F) for n, s in shapes.items()}
+    m = {n: (rng.standard_normal(s) * 0.1).astype(F) for n, s in shapes.items()}
+    v = {n: (rng.random(s) * 0.01).astype(F) for n, s in shapes.items()}
+    cfg = adamw.AdamWConfig(**_cfg(clip_norm=0.5))
+    results = {}
+    for bad in (False, True):
+        grads = {n: rng.standard_normal(shapes[n]).astype(F) for n in shapes if n != "d.frozen"}
+        if bad:
+            grads["b.matrix"][3, 5] = np.inf
+        layout = adamw.Layout(inv)
+        n_master = adamw.sharded_master_elements(layout, 1)
+        tp = torch.zeros(n_master, dtype=torch.float32, device="cuda:0")
+        masters = DeviceArray((n_master,), "float32", ptr=tp.data_ptr(), owner=False)
+        masters._base = tp
+        states = {}
+        for kind in ("full", "sharded"):
+            st = adamw.initialize_state(params, inv, params=masters if kind == "sharded" else None)
+            for name in shapes:
+                _upload(st["m"][name], m[name])
+                _upload(st["v"][name], v[name])
+            for name, g in grads.items():
+                _upload(st.arenas["grads"].view(st.layout.offsets[name], g.shape), g)
+            states[kind] = st
+        r_full = adamw.make_transaction(inv, cfg)(states["full"], states["full"].gradient_tree(), F(0.7), True)
+        r_sh = adamw.make_sharded_transaction(inv, cfg, dist.group.WORLD)(states["sharded"], F(0.7), True)
+        torch.cuda.synchronize()
+        results[bad] = ([(r.code, r.committed, r.loss, r.gradient_norm, r.update_norm) for r in (r_full, r_sh)],
+                        [_read(states[k]) for k in ("full", "sharded")])
+    out["results"] = results
+    dist.destroy_process_group()
+
+
+def test_sharded_transaction_on_one_rank_matches_the_full_one():
+    """The sharded passes over a one-rank group reproduce mfb_adamw_commit bit for bit (commit and rejection)."""
+    import os
+
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    p = ctx.Process(target=_sharded_vs_full, args=(out, 29400 + os.getpid() % 300))
+    p.start()
+    p.join(240)
+    assert p.exitcode == 0
+    for bad, (res, arenas) in out["results"].items():
+        full, sharded = res
+        assert full[0] == sharded[0] and full[1] == sharded[1], (bad, full, sharded)
+        assert full[1] == (not bad)
+        np.testing.assert_array_equal(np.array(full[2:], np.float64), np.array(sharded[2:], np.float64))
+        (fa, fs), (sa, ss) = arenas
+        assert fs == ss
+        for g in ("params", "m", "v"):
+            for n in fa[g]:
+                np.testing.assert_array_equal(fa[g][n], sa[g][n], err_msg=f"{bad} {g}/{n}")

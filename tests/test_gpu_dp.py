@@ -4,7 +4,9 @@ Two NCCL ranks each take one row of a two-row batch; after the bucketed
 allreduce their gradient sums, loss sum and count must equal a single GPU's
 over both rows (up to FP32 summation order: rel-L2 1e-4 per leaf), and after
 the AdamW commit both ranks must hold bit-identical masters (replicated state,
-engine/step.py:62 and the data-parallel known answers' replication checks).
+engine/step.py:62 and the data-parallel known answers' replication checks),
+with the replicated transaction and with the optimizer sharded across the
+ranks (its masters all-gathered).
 Ranks run as child processes; NCCL's NVLS is off, as for every multi-rank
 test on this pool.
 """
@@ -57,7 +59,7 @@ def _rank_graph(rank, port, out):
     dist.destroy_process_group()
 
 
-def _rank(rank, port, out):
+def _rank(rank, port, out, shard=False):
     import datetime
 
     import torch
@@ -70,7 +72,7 @@ def _rank(rank, port, out):
     device.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=120))
     cfg = _cfg()
-    step = me.EncoderStep(cfg, rows=1, seed=0, group=dist.group.WORLD)
+    step = me.EncoderStep(cfg, rows=1, seed=0, group=dist.group.WORLD, shard_optimizer=shard)
     step.set_batch(*workloads.encoder_batch(cfg, 7, rows=1, row0=rank))
     step.quantize()
     step.forward()
@@ -88,7 +90,8 @@ def _rank(rank, port, out):
     dist.destroy_process_group()
 
 
-def test_two_rank_step_matches_one_gpu():
+@pytest.mark.parametrize("shard", [False, True], ids=["replicated", "sharded_optimizer"])
+def test_two_rank_step_matches_one_gpu(shard):
     require_gpu()
     from minifield_training_b200 import device
     if device.device_count() < 2:
@@ -98,7 +101,7 @@ def test_two_rank_step_matches_one_gpu():
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
     port = 29600 + os.getpid() % 300
-    procs = [ctx.Process(target=_rank, args=(r, port, out)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, port, out, shard)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
