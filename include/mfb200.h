@@ -225,7 +225,7 @@ int mfb_adamw_commit(float* params, float* m, float* v, const float* grads, long
  * SUM-allreduce red[0..2] -> CHECK_FINALIZE -> CANDIDATE on [lo, hi) of the
  * trainable range -> SUM-allreduce red[0..1] -> CANDIDATE_FINALIZE -> COMMIT
  * on that slice -> all-gather of the masters. `red` is a caller-owned device
- * buffer of 3 doubles. Slices start at multiples of 4 elements. */
+ * buffer of 3 doubles. Nonempty slices start at multiples of 4 elements. */
 enum {
   MFB_ADAMW_CHECK = 0,
   MFB_ADAMW_CHECK_FINALIZE = 1,

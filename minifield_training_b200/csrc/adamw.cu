@@ -187,7 +187,8 @@ __global__ void __launch_bounds__(THREADS) check_kernel(const float* __restrict_
   // Scalar tails (fewer than four elements each) inside the range.
   if (blockIdx.x == 0) {
     const long long e = nv * 4 + threadIdx.x;
-    if (e < min(hi, n_total) && (!finite(params[e]) || !finite(m[e]) || !finite(v[e]) || v[e] < 0.f)) bad |= 1;
+    if (e >= lo && e < min(hi, n_total) && (!finite(params[e]) || !finite(m[e]) || !finite(v[e]) || v[e] < 0.f))
+      bad |= 1;
     const long long f = nt4 * 4 + threadIdx.x;
     if (f >= lo && f < min(hi, n_train)) {
       const float g = __fdiv_rn(grads[f], div);
@@ -368,7 +369,8 @@ extern "C" int mfb_adamw_commit(float* params, float* m, float* v, const float* 
 // trainable range -> SUM-allreduce red[0..1] -> CANDIDATE_FINALIZE -> COMMIT
 // over the same trainable slice; then the ranks all-gather the updated
 // masters. The finalize passes see the same reduced values on every rank, so
-// every rank reaches the same code. Slices start at multiples of 4 elements.
+// every rank reaches the same code. Nonempty slices start at multiples of 4
+// elements.
 extern "C" int mfb_adamw_shard_pass(int pass, float* params, float* m, float* v, const float* grads, long long lo,
                                     long long hi, long long n_train, long long n_decayed, long long n_total,
                                     int32_t* step, const float* loss, const uint8_t* accumulation_valid,
@@ -380,7 +382,7 @@ extern "C" int mfb_adamw_shard_pass(int pass, float* params, float* m, float* v,
                 "AdamW needs 0 <= n_decayed <= n_train <= n_total and a trainable leaf (%lld, %lld, %lld)", n_decayed,
                 n_train, n_total);
   const long long lim = (pass == MFB_ADAMW_CHECK) ? n_total : n_train;
-  MFB_CHECK_ARG(lo >= 0 && lo <= hi && hi <= lim && lo % 4 == 0 && (hi % 4 == 0 || hi == lim),
+  MFB_CHECK_ARG(lo >= 0 && lo <= hi && hi <= lim && (lo % 4 == 0 || lo == hi) && (hi % 4 == 0 || hi == lim),
                 "AdamW slice [%lld, %lld) must start at a multiple of 4 inside [0, %lld)", lo, hi, lim);
   MFB_CHECK_ARG(params && m && v && grads && step && loss && accumulation_valid && result && red,
                 "NULL AdamW argument");

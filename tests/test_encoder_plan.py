@@ -78,3 +78,25 @@ def test_bucketed_allreduce_equals_full_allreduce_on_two_gloo_ranks():
         p.join(120)
         assert p.exitcode == 0
     assert out[0] == 0.0 and out[1] == 0.0
+
+
+@pytest.mark.parametrize("n", [1, 3, 4, 17, 1000, 388_000_001])
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_optimizer_slices_partition_the_range(n, world):
+    """The sharded AdamW slices: equal 4-aligned slices covering [0, n) once (empty ones past n)."""
+    slices = [adamw.shard_slices(n, world, r) for r in range(world)]
+    per = slices[0][2]
+    assert per % 4 == 0 and per * world >= n and all(s[2] == per for s in slices)
+    covered = 0
+    for r, (lo, hi, _) in enumerate(slices):
+        assert (lo % 4 == 0 or lo == hi) and lo <= hi and lo == min(r * per, n)
+        assert hi == min(lo + per, n)
+        covered += hi - lo
+    assert covered == n
+
+
+def test_sharded_master_arena_holds_the_all_gather():
+    layout = adamw.Layout(me.inventory(TINY), me.arena_order(TINY))
+    for world in (1, 2, 8):
+        per = adamw.shard_slices(layout.n_train, world, 0)[2]
+        assert adamw.sharded_master_elements(layout, world) >= max(layout.n_total, per * world)
