@@ -226,6 +226,7 @@ class AttentionWorkload:
         self.causal = ctypes.c_int()
         self.offset = ctypes.c_int()
         self.policy = ctypes.c_int()
+        self.stream = None  # CUDA stream of the three calls (None: the default stream)
         self.ids()
 
     def ids(self):
@@ -233,14 +234,14 @@ class AttentionWorkload:
         b, t, s = self.dims[:3]
         self.L.call("mfb_attn_ids", self.mode, P(self.mask.ptr), P(self.seg.ptr) if self.seg else None, None,
                     P(self.qid.ptr), P(self.kid.ptr), b, t, s, 0, ctypes.byref(self.causal),
-                    ctypes.byref(self.offset), ctypes.byref(self.policy), None)
+                    ctypes.byref(self.offset), ctypes.byref(self.policy), self.stream)
 
     def fwd(self):
         P = ctypes.c_void_p
         b, t, s, h, hk, d = self.dims
         self.L.call("mfb_attn_fwd", P(self.q.ptr), P(self.k.ptr), P(self.v.ptr), P(self.o.ptr), P(self.lse.ptr),
                     P(self.qid.ptr), P(self.kid.ptr), b, t, s, h, hk, d, self.causal.value, self.offset.value,
-                    self.policy.value, ctypes.c_float(d ** -0.5), P(self.ws.ptr), self.ws.nbytes, None)
+                    self.policy.value, ctypes.c_float(d ** -0.5), P(self.ws.ptr), self.ws.nbytes, self.stream)
 
     def bwd(self):
         P = ctypes.c_void_p
@@ -248,7 +249,7 @@ class AttentionWorkload:
         self.L.call("mfb_attn_bwd", P(self.q.ptr), P(self.k.ptr), P(self.v.ptr), P(self.o.ptr), P(self.lse.ptr),
                     P(self.do.ptr), P(self.dq.ptr), P(self.dk.ptr), P(self.dv.ptr), P(self.qid.ptr),
                     P(self.kid.ptr), b, t, s, h, hk, d, self.causal.value, self.offset.value, self.policy.value,
-                    ctypes.c_float(d ** -0.5), P(self.ws.ptr), self.ws.nbytes, None)
+                    ctypes.c_float(d ** -0.5), P(self.ws.ptr), self.ws.nbytes, self.stream)
 
     def step(self):
         self.ids()
@@ -258,7 +259,16 @@ class AttentionWorkload:
     launches_per_step = 9  # ids, ranges, schedule, fwd, ranges, bwd-pre, schedule, bwd-main, dq-convert
 
     def e2e_setup(self):
-        from minifield_training_b200.device import HostBuffer
+        """Pinned host buffers, a second device buffer set and three streams.
+
+        The end-to-end loop pipelines consecutive steps the way a serving or
+        training input pipeline would: step i uploads into buffer set i % 2 on
+        one stream, computes on a second and downloads on a third, so step
+        i + 1's upload and step i - 1's download (opposite PCIe directions)
+        overlap step i's kernels. Every step still moves its whole input up
+        and its whole output down inside the timed region.
+        """
+        from minifield_training_b200.device import Event, HostBuffer
 
         self.pin = {}
         for name in ("q", "k", "v", "do"):
@@ -273,16 +283,37 @@ class AttentionWorkload:
         self.pin_out = {n: HostBuffer(getattr(self, n).shape, np.uint16) for n in ("o", "dq", "dk", "dv")}
         self.h2d_bytes = sum(hb.array.nbytes for hb in self.pin.values())
         self.d2h_bytes = sum(hb.array.nbytes for hb in self.pin_out.values())
+        self.twin = AttentionWorkload(self.cfg, seed=0)
+        streams = []
+        for _ in range(3):
+            sp = ctypes.c_void_p()
+            self.L.call("mfb_stream_create", ctypes.byref(sp))
+            streams.append(sp.value)
+        self.s_in, self.s_comp, self.s_out = streams
+        self.e2e_sets = []
+        for w in (self, self.twin):
+            w.stream = self.s_comp
+            self.e2e_sets.append((w, Event(), Event(), Event()))  # uploaded, computed, downloaded
+        self.e2e_i = 0
 
     def e2e_step(self):
         from minifield_training_b200.device import d2h, h2d
 
-        dev = {"q": self.q, "k": self.k, "v": self.v, "do": self.do, "mask": self.mask, "seg": self.seg}
+        w, up, comp, down = self.e2e_sets[self.e2e_i % 2]
+        self.e2e_i += 1
+        dev = {"q": w.q, "k": w.k, "v": w.v, "do": w.do, "mask": w.mask, "seg": w.seg}
+        comp.wait_on(self.s_in)  # the set's inputs were read by its previous step
         for name, hb in self.pin.items():
-            h2d(dev[name], hb.ptr, hb.array.nbytes)
-        self.step()
+            h2d(dev[name], hb.ptr, hb.array.nbytes, self.s_in)
+        up.record(self.s_in)
+        up.wait_on(self.s_comp)
+        down.wait_on(self.s_comp)  # the set's outputs of its previous step are downloaded
+        w.step()
+        comp.record(self.s_comp)
+        comp.wait_on(self.s_out)
         for name, hb in self.pin_out.items():
-            d2h(hb.ptr, getattr(self, name), hb.array.nbytes)
+            d2h(hb.ptr, getattr(w, name), hb.array.nbytes, self.s_out)
+        down.record(self.s_out)
 
 
 class DecodeWorkload:
@@ -502,8 +533,12 @@ def run_reference(args, dist):
 # ---------------------------------------------------------------------------
 
 
-def measure(dist, fn, steps, warmup, clocks=None, stream=None):
-    """Max over ranks of the mean step time, CUDA events on the launching stream."""
+def measure(dist, fn, steps, warmup, clocks=None, stream=None, end_stream=None):
+    """Max over ranks of the mean step time, CUDA events on the launching stream.
+
+    ``end_stream`` (default ``stream``) is the stream that finishes each step
+    last when a step spans several streams.
+    """
     from minifield_training_b200.device import Event, sync
 
     for _ in range(warmup):
@@ -517,7 +552,7 @@ def measure(dist, fn, steps, warmup, clocks=None, stream=None):
     a.record(stream)
     for _ in range(steps):
         fn()
-    b.record(stream)
+    b.record(end_stream if end_stream is not None else stream)
     sync()
     clk = clocks.stop() if clocks else None
     dist.barrier()
@@ -561,7 +596,7 @@ def run_ours(args, dist):
                     "bwd_tflops": 2.5 * att.fwd_flops / (bwd_ms * 1e-3) / 1e12}
         # End to end through the C ABI with pinned host buffers.
         att.e2e_setup()
-        e2e_ms, _ = measure(dist, att.e2e_step, max(3, args.steps // 4), 2)
+        e2e_ms, _ = measure(dist, att.e2e_step, max(3, args.steps // 4), 2, stream=att.s_in, end_stream=att.s_out)
         e2e = {"value": n * att.total_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
                "h2d_bytes_per_step": att.h2d_bytes, "d2h_bytes_per_step": att.d2h_bytes, "ms_per_step": e2e_ms}
         line.update(value=value, ms_per_step=ms, tensor_peak_frac=value / n / tf_burst, roofline=roofline, e2e=e2e)

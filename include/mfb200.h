@@ -57,6 +57,7 @@ int mfb_device_sync(void);
 int mfb_event_create(void** event);
 int mfb_event_destroy(void* event);
 int mfb_event_record(void* event, void* stream);
+int mfb_stream_wait_event(void* stream, void* event);
 int mfb_event_elapsed_ms(void* start, void* end, float* ms);
 /* CUDA graphs: everything enqueued on `stream` (a created stream) between
  * mfb_graph_begin and mfb_graph_end is recorded into one executable graph;

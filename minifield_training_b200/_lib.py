@@ -55,6 +55,7 @@ SIGNATURES = {
     "mfb_event_create": (I, [ctypes.POINTER(P)]),
     "mfb_event_destroy": (I, [P]),
     "mfb_event_record": (I, [P, P]),
+    "mfb_stream_wait_event": (I, [P, P]),
     "mfb_event_elapsed_ms": (I, [P, P, ctypes.POINTER(F)]),
     "mfb_fakequant": (I, [P, I, I, I, P, P, P, P, P, P]),
     "mfb_attn_ids": (I, [I, P, P, P, P, P, I, I, I, I, IP, IP, IP, P]),

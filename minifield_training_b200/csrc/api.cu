@@ -139,6 +139,13 @@ int mfb_event_record(void* event, void* stream) {
   return MFB_OK;
 }
 
+// Later work on `stream` waits for `event`'s most recent record (no-op if never recorded).
+int mfb_stream_wait_event(void* stream, void* event) {
+  MFB_CHECK_ARG(event != nullptr, "event is NULL");
+  MFB_CUDA_TRY(cudaStreamWaitEvent((cudaStream_t)stream, (cudaEvent_t)event, 0));
+  return MFB_OK;
+}
+
 int mfb_event_elapsed_ms(void* start, void* end, float* ms) {
   MFB_CHECK_ARG(ms != nullptr, "ms is NULL");
   MFB_CUDA_TRY(cudaEventElapsedTime(ms, (cudaEvent_t)start, (cudaEvent_t)end));

@@ -208,6 +208,10 @@ class Event:
     def record(self, stream=None):
         _lib.call("mfb_event_record", self.ptr, stream)
 
+    def wait_on(self, stream):
+        """Make later work on ``stream`` wait for this event's most recent record."""
+        _lib.call("mfb_stream_wait_event", stream, self.ptr)
+
     def elapsed_ms(self, end: "Event") -> float:
         ms = ctypes.c_float()
         _lib.call("mfb_event_elapsed_ms", self.ptr, end.ptr, ctypes.byref(ms))
