@@ -256,7 +256,7 @@ class AttentionWorkload:
         self.fwd()
         self.bwd()
 
-    launches_per_step = 9  # ids, ranges, schedule, fwd, ranges, bwd-pre, schedule, bwd-main, dq-convert
+    launches_per_step = 9  # ids, ranges, schedule, fwd, ranges, schedule, bwd-pre, bwd-main, dq-convert
 
     def e2e_setup(self):
         """Pinned host buffers, a second device buffer set and three streams.

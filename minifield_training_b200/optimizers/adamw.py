@@ -19,6 +19,8 @@ transaction, adamw.py:574-591); a rejected update leaves them untouched, so
 import ctypes
 import dataclasses
 import enum
+import hashlib
+import json
 import math
 
 import numpy as np
@@ -85,19 +87,33 @@ class AdamWConfig:
 
 @dataclasses.dataclass(frozen=True)
 class ParameterSpec:
-    """One stored leaf (core/parameters.py:12-22)."""
+    """One stored leaf (core/parameters.py:11-21)."""
 
     name: str
     shape: tuple
     trainable: bool
     decayed: bool
+    source_dtype: str = "bfloat16"
+    master_dtype: str = "float32"
+    quantized: bool = False
 
 
 @dataclasses.dataclass(frozen=True)
 class Inventory:
-    """Leaf metadata with the derived membership views (core/parameters.py:25-57)."""
+    """Leaf metadata with the derived membership views (core/parameters.py:24-55).
+
+    ``sha256`` identifies the inventory the way the reference does: SHA-256 of
+    the canonical JSON of (format, dtypes, quantization profile, specs), so a
+    checkpoint manifest written here names the same inventory hash as one
+    written by the reference for the same build_inventory arguments.
+    """
 
     specs: tuple
+    parameter_count: int = 0
+    source_dtype: str = "bfloat16"
+    master_dtype: str = "float32"
+    quantization_profile: object = None
+    sha256: str = ""
 
     @property
     def names(self):
@@ -112,19 +128,50 @@ class Inventory:
         return tuple(s.name for s in self.specs if not s.trainable)
 
 
-def build_inventory(shapes, *, decayed_names=frozenset(), frozen_names=frozenset()) -> Inventory:
-    """Inventory over ``shapes`` (name -> shape); frozen leaves cannot decay (core/parameters.py:58-125)."""
-    unknown = (set(decayed_names) | set(frozen_names)) - set(shapes)
+def canonical_json(value) -> str:
+    """Deterministic JSON text, non-finite numbers rejected (core/json_io.py:18-26)."""
+    return json.dumps(value, ensure_ascii=False, sort_keys=True, separators=(",", ":"), allow_nan=False)
+
+
+def build_inventory(shapes, *, decayed_names=frozenset(), frozen_names=frozenset(),
+                    format_id="minifield_training_b200/1", source_dtype="bfloat16", master_dtype="float32",
+                    quantization_profile=None, quantized_names=frozenset()) -> Inventory:
+    """Inventory over ``shapes`` (name -> shape) (core/parameters.py:58-152).
+
+    Frozen leaves cannot decay; a quantized leaf needs a named quantization
+    profile. Leaves are ordered by name.
+    """
+    if source_dtype not in {"bfloat16", "float16", "float32"}:
+        raise ValueError("Unsupported checkpoint source dtype")
+    if master_dtype != "float32":
+        raise ValueError("Full-weight masters must be float32")
+    if quantization_profile is None and quantized_names:
+        raise ValueError("Quantized leaves require a declared QAT profile")
+    if quantization_profile is not None and not quantization_profile:
+        raise ValueError("Quantization profile cannot be empty")
+    unknown = (set(decayed_names) | set(frozen_names) | set(quantized_names)) - set(shapes)
     if unknown:
         raise ValueError(f"Inventory names are not parameters: {sorted(unknown)}")
     if set(decayed_names) & set(frozen_names):
         raise ValueError("Frozen parameters cannot be decayed")
     specs = tuple(
-        ParameterSpec(name, tuple(int(x) for x in shapes[name]), name not in frozen_names, name in decayed_names)
+        ParameterSpec(name, tuple(int(x) for x in shapes[name]), name not in frozen_names, name in decayed_names,
+                      source_dtype, master_dtype, name in quantized_names)
         for name in sorted(shapes))
     if not specs:
         raise ValueError("Full-weight inventory must not be empty")
-    return Inventory(specs)
+    payload = {
+        "format": format_id,
+        "source_dtype": source_dtype,
+        "master_dtype": master_dtype,
+        "quantization_profile": quantization_profile,
+        "specs": [{"name": sp.name, "shape": list(sp.shape), "source_dtype": sp.source_dtype,
+                   "master_dtype": sp.master_dtype, "trainable": sp.trainable, "decayed": sp.decayed,
+                   "quantized": sp.quantized} for sp in specs],
+    }
+    return Inventory(specs, parameter_count=sum(int(np.prod(sp.shape)) for sp in specs), source_dtype=source_dtype,
+                     master_dtype=master_dtype, quantization_profile=quantization_profile,
+                     sha256=hashlib.sha256(canonical_json(payload).encode("utf-8")).hexdigest())
 
 
 class Layout:

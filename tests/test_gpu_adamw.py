@@ -246,3 +246,32 @@ def test_sharded_transaction_on_one_rank_matches_the_full_one():
         for g in ("params", "m", "v"):
             for n in fa[g]:
                 np.testing.assert_array_equal(fa[g][n], sa[g][n], err_msg=f"{bad} {g}/{n}")
+
+
+def test_checkpoint_resumes_the_device_state_exactly(tmp_path):
+    """save -> verify_roundtrip -> load into fresh arenas -> the next commit matches the uninterrupted state."""
+    from minifield_training_b200.checkpoints import training_state as ts
+    from minifield_training_b200.optimizers import adamw
+
+    shapes, s, grads = _fixture()
+    decayed, frozen = {"w.matrix"}, {"w.frozen_matrix", "w.frozen_vector"}
+    inv, st = _make(shapes, decayed, frozen, s["params"], s["m"], s["v"], s["step"])
+    tr = adamw.make_transaction(inv, adamw.AdamWConfig(**_cfg(clip_norm=10.0)))
+    assert tr(st, grads, F(1.0), True).committed
+    cursor = ts.Cursor("run", "data", "source", 1)
+    ts.save(tmp_path / "ck", st, inv, optimizer_id="adamw", cursor=cursor)
+    ts.verify_roundtrip(tmp_path / "ck", st, cursor, inv, "adamw")
+    st2, cur2 = ts.load(tmp_path / "ck", inv, optimizer_id="adamw", run_id="run", data_sha256="data",
+                        source_id="source")
+    assert cur2 == cursor
+    (a1, s1), (a2, s2) = _read(st), _read(st2)
+    assert s1 == s2
+    for g in ("params", "m", "v"):
+        for n in shapes:
+            np.testing.assert_array_equal(a1[g][n], a2[g][n], err_msg=f"{g}/{n}")
+    assert tr(st, grads, F(1.0), True).committed and tr(st2, grads, F(1.0), True).committed
+    (a1, s1), (a2, s2) = _read(st), _read(st2)
+    assert s1 == s2
+    for g in ("params", "m", "v"):
+        for n in shapes:
+            np.testing.assert_array_equal(a1[g][n], a2[g][n], err_msg=f"after resume {g}/{n}")
