@@ -296,6 +296,13 @@ class AttentionWorkload:
             self.e2e_sets.append((w, Event(), Event(), Event()))  # uploaded, computed, downloaded
         self.e2e_i = 0
 
+    def e2e_close(self):
+        """Finish the pipelined steps and release their streams."""
+        self.L.call("mfb_device_sync")
+        for s in (self.s_in, self.s_comp, self.s_out):
+            self.L.call("mfb_stream_destroy", s)
+        self.stream = self.twin.stream = None
+
     def e2e_step(self):
         from minifield_training_b200.device import d2h, h2d
 
@@ -597,6 +604,7 @@ def run_ours(args, dist):
         # End to end through the C ABI with pinned host buffers.
         att.e2e_setup()
         e2e_ms, _ = measure(dist, att.e2e_step, max(3, args.steps // 4), 2, stream=att.s_in, end_stream=att.s_out)
+        att.e2e_close()
         e2e = {"value": n * att.total_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
                "h2d_bytes_per_step": att.h2d_bytes, "d2h_bytes_per_step": att.d2h_bytes, "ms_per_step": e2e_ms}
         line.update(value=value, ms_per_step=ms, tensor_peak_frac=value / n / tf_burst, roofline=roofline, e2e=e2e)
