@@ -603,7 +603,7 @@ def run_ours(args, dist):
                     "bwd_tflops": 2.5 * att.fwd_flops / (bwd_ms * 1e-3) / 1e12}
         # End to end through the C ABI with pinned host buffers.
         att.e2e_setup()
-        e2e_ms, _ = measure(dist, att.e2e_step, max(3, args.steps // 4), 2, stream=att.s_in, end_stream=att.s_out)
+        e2e_ms, _ = measure(dist, att.e2e_step, max(8, args.steps // 2), 2, stream=att.s_in, end_stream=att.s_out)
         att.e2e_close()
         e2e = {"value": n * att.total_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
                "h2d_bytes_per_step": att.h2d_bytes, "d2h_bytes_per_step": att.d2h_bytes, "ms_per_step": e2e_ms}
