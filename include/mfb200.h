@@ -286,6 +286,13 @@ int mfb_embed_gather(const float* table, const int32_t* ids, uint16_t* out, long
 int mfb_conv_fwd(const uint16_t* bcx, const float* taps, const int32_t* segment_ids, uint16_t* mixed, long long M,
                  int T, int C, void* stream);
 size_t mfb_encoder_workspace_size(int C, int classes);
+/* One decode step of the causal gated short convolution
+ * (src/minifield_training/layers/convolution.py:153-178,
+ * kernels/convolution.py:82-111): bcx [B, 3C] = [b | c | values] of one token
+ * per row, taps [C, 3] FP32, history [B, 2, C] bf16 (the two preceding gated
+ * inputs, oldest first; shifted in place) -> mixed [B, C]. */
+int mfb_conv_step(const uint16_t* bcx, const float* taps, uint16_t* history, uint16_t* mixed, int B, int C,
+                  void* stream);
 int mfb_conv_bwd(const uint16_t* bcx, const float* taps, const int32_t* segment_ids, const uint16_t* dmixed,
                  uint16_t* dbcx, float* dtaps, int accumulate, long long M, int T, int C, void* workspace,
                  size_t workspace_bytes, void* stream);
@@ -307,6 +314,9 @@ int mfb_swiglu_bwd(const uint16_t* gu, const uint16_t* dh, uint16_t* dgu, int M,
 /* FP32 -> bf16 round-to-nearest-even cast of n elements: the master cast of
  * full_linear (src/minifield_training/kernels/linear.py:11). */
 int mfb_cast_f32_bf16(const float* x, uint16_t* y, long long n, void* stream);
+/* bf16 -> FP32 widening of n elements (the logits' .astype(float32),
+ * src/minifield_training/models/lfm2_5/model.py:829). */
+int mfb_cast_bf16_f32(const uint16_t* x, float* y, long long n, void* stream);
 
 #ifdef __cplusplus
 }

@@ -89,6 +89,31 @@ __device__ __forceinline__ void conv_at(const float* gm, const float* g0, const 
   }
 }
 
+// One decode step of the causal gated short convolution
+// (kernels/convolution.py:82-111 via layers/convolution.py:153-178): window =
+// [history oldest .. newest, b * values] of one token per row, mixed = c *
+// sum_k window_k * tap_k (taps rounded to bf16, each product and partial sum
+// rounded as in conv_at), and the history shifts by one with this step's
+// gated input. In place on the history: every element is read before it is
+// written by the same thread.
+__global__ void conv_step_kernel(const uint16_t* __restrict__ bcx, const float* __restrict__ taps,
+                                 uint16_t* __restrict__ hist, uint16_t* __restrict__ mixed, int B, int C) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)B * C) return;
+  const int b = (int)(i / C), ch = (int)(i % C);
+  auto ld = [](const uint16_t* p) { return __bfloat162float(__ushort_as_bfloat16(*p)); };
+  const uint16_t* row = bcx + (long long)b * 3 * C;
+  const float g = bf(ld(row + ch) * ld(row + 2 * C + ch));
+  uint16_t* h = hist + (long long)b * 2 * C + ch;
+  const float h0 = ld(h), h1 = ld(h + C);
+  const float t0 = bf(h0 * bf(taps[ch * 3 + 0])), t1 = bf(h1 * bf(taps[ch * 3 + 1]));
+  const float t2 = bf(g * bf(taps[ch * 3 + 2]));
+  const float acc = bf(bf(t0 + t1) + t2);
+  mixed[i] = __bfloat16_as_ushort(__float2bfloat16_rn(ld(row + C + ch) * acc));
+  h[0] = h[C];
+  h[C] = __bfloat16_as_ushort(__float2bfloat16_rn(g));
+}
+
 __global__ void __launch_bounds__(128) conv_fwd_kernel(const uint16_t* __restrict__ bcx, const float* __restrict__ taps,
                                                        const int32_t* __restrict__ seg, uint16_t* __restrict__ mixed,
                                                        long long M, int T, int C) {
@@ -387,6 +412,17 @@ extern "C" int mfb_conv_fwd(const uint16_t* bcx, const float* taps, const int32_
   const int grid = (int)std::min<long long>((work + 127) / 128, 16LL * enc::sm_count());
   enc::conv_fwd_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(bcx, taps, segment_ids, mixed, M, T, C);
   MFB_LAUNCH_CHECK("gated conv fwd");
+  return MFB_OK;
+}
+
+extern "C" int mfb_conv_step(const uint16_t* bcx, const float* taps, uint16_t* history, uint16_t* mixed, int B,
+                             int C, void* stream) {
+  MFB_CHECK_ARG(B > 0 && C > 0, "conv step: bad shape (B=%d C=%d)", B, C);
+  MFB_CHECK_ARG(bcx && taps && history && mixed, "NULL conv step argument");
+  const long long n = (long long)B * C;
+  enc::conv_step_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(bcx, taps, history, mixed, B,
+                                                                                        C);
+  MFB_LAUNCH_CHECK("conv step");
   return MFB_OK;
 }
 

@@ -94,6 +94,10 @@ __global__ void cast_f32_bf16_kernel(const float* __restrict__ x, __nv_bfloat16*
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) y[i] = __float2bfloat16_rn(x[i]);
 }
+__global__ void cast_bf16_f32_kernel(const __nv_bfloat16* __restrict__ x, float* __restrict__ y, long long n) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = __bfloat162float(x[i]);
+}
 }  // namespace
 }  // namespace mfb
 
@@ -105,5 +109,16 @@ extern "C" int mfb_cast_f32_bf16(const float* x, uint16_t* y, long long n, void*
   cast_f32_bf16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
       x, reinterpret_cast<__nv_bfloat16*>(y), n);
   MFB_LAUNCH_CHECK("mfb_cast_f32_bf16");
+  return MFB_OK;
+}
+
+// bf16 -> FP32 widening (exact): the `.astype(float32)` of the logits
+// (src/minifield_training/models/lfm2_5/model.py:829).
+extern "C" int mfb_cast_bf16_f32(const uint16_t* x, float* y, long long n, void* stream) {
+  MFB_CHECK_ARG(n >= 0 && (n == 0 || (x && y)), "bad cast arguments");
+  if (n == 0) return MFB_OK;
+  cast_bf16_f32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), y, n);
+  MFB_LAUNCH_CHECK("mfb_cast_bf16_f32");
   return MFB_OK;
 }

@@ -1,0 +1,237 @@
+"""Fixed-capacity cached decoding of the LFM2.5 causal decoder on the B200 kernels.
+
+Mirrors src/minifield_training/models/lfm2_5/decode.py: ``new_state`` (:75-134)
+allocates zeroed per-layer caches (attention K/V [B, capacity, Hk, 64] bf16,
+conv history [B, 2, C] bf16) and ``Decoder.decode_one`` (:419-466) runs one
+token per row through every block (:225-262) and returns FP32 logits of the
+tied head (model.py:818-829), advancing the state's valid length. Per block:
+
+  conv       RMSNorm -> in_proj GEMM -> mfb_conv_step (gated causal conv over
+             the history, history shifted in place) -> out_proj GEMM
+  attention  RMSNorm -> fused q|k|v GEMM -> q/k RMSNorm + RoPE at the position
+             -> mfb_decode_attn (cache append at the position, split-K
+             attention over the valid length) -> out_proj GEMM
+  then       residual + RMSNorm (one kernel) -> fused w1|w3 GEMM -> SwiGLU ->
+             w2 GEMM, the residual folded into the next block's norm.
+
+The masters are cast to bf16 once at construction (full_linear's cast,
+kernels/linear.py:11); the q|k|v and w1|w3 products are single GEMMs over
+concatenated rows.
+"""
+
+import ctypes
+
+import numpy as np
+
+from .. import _lib
+from ..device import DeviceArray
+from .encoder import _fwd, rope_freqs
+
+P = ctypes.c_void_p
+
+
+class DecodeOverflow(ValueError):
+    """A token would be written past the fixed cache capacity (decode.py:22-23)."""
+
+
+def parameter_shapes(cfg) -> dict:
+    """Reference decoder parameter names and shapes (models/lfm2_5/model.py:127-166)."""
+    c, f, kv = cfg.hidden, cfg.ffn, cfg.kv_heads * cfg.head_dim
+    shapes = {"model.embed_tokens.weight": (cfg.vocab, c), "model.embedding_norm.weight": (c,)}
+    for i, kind in enumerate(cfg.layer_types):
+        p = f"model.layers.{i}."
+        shapes.update({p + "operator_norm.weight": (c,), p + "ffn_norm.weight": (c,),
+                       p + "feed_forward.w1.weight": (f, c), p + "feed_forward.w3.weight": (f, c),
+                       p + "feed_forward.w2.weight": (c, f)})
+        if kind == "conv":
+            shapes.update({p + "conv.in_proj.weight": (3 * c, c), p + "conv.out_proj.weight": (c, c),
+                           p + "conv.conv.weight": (c, 1, cfg.conv_kernel)})
+        else:
+            shapes.update({p + "self_attn.q_proj.weight": (cfg.heads * cfg.head_dim, c),
+                           p + "self_attn.k_proj.weight": (kv, c), p + "self_attn.v_proj.weight": (kv, c),
+                           p + "self_attn.out_proj.weight": (c, cfg.heads * cfg.head_dim),
+                           p + "self_attn.q_layernorm.weight": (cfg.head_dim,),
+                           p + "self_attn.k_layernorm.weight": (cfg.head_dim,)})
+    return shapes
+
+
+def init_parameters(cfg, seed: int = 0) -> dict:
+    """Random init: N(0, 0.02) for matrices, taps and the embedding table; ones for norm gains."""
+    rng = np.random.default_rng(seed)
+    out = {}
+    for name, shape in parameter_shapes(cfg).items():
+        if name.endswith("norm.weight") or name.endswith("layernorm.weight"):
+            out[name] = np.ones(shape, np.float32)
+        else:
+            out[name] = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
+    return out
+
+
+class DecodeState:
+    """Device caches of one prompt batch plus its logical position (decode.py:34-41).
+
+    ``keys`` / ``values`` / ``history`` are per-layer lists (None where the
+    layer has no such cache); ``valid_length`` is the number of written
+    positions, which is also the position the next token takes.
+    """
+
+    def __init__(self, cfg, batch_size: int, capacity: int):
+        if isinstance(capacity, bool) or not isinstance(capacity, int) or capacity <= 0 or capacity & (capacity - 1):
+            raise ValueError("Cache capacity must be a positive power of two")
+        if isinstance(batch_size, bool) or not isinstance(batch_size, int) or batch_size <= 0:
+            raise ValueError("batch_size must be a positive integer")
+        self.cfg, self.batch, self.capacity, self.valid_length = cfg, batch_size, capacity, 0
+        self.keys, self.values, self.history = [], [], []
+        for kind in cfg.layer_types:
+            if kind == "full_attention":
+                shape = (batch_size, capacity, cfg.kv_heads, cfg.head_dim)
+                self.keys.append(DeviceArray.zeros(shape, "bfloat16"))
+                self.values.append(DeviceArray.zeros(shape, "bfloat16"))
+                self.history.append(None)
+            else:
+                self.keys.append(None)
+                self.values.append(None)
+                self.history.append(DeviceArray.zeros((batch_size, cfg.conv_kernel - 1, cfg.hidden), "bfloat16"))
+
+
+def new_state(cfg, batch_size: int, capacity: int) -> DecodeState:
+    """Zeroed fixed-capacity state (decode.py:75-134)."""
+    return DecodeState(cfg, batch_size, capacity)
+
+
+class Decoder:
+    """Device weights of the decoder and the single-token step over a DecodeState."""
+
+    def __init__(self, cfg, parameters: dict, *, stream=None):
+        if cfg.head_dim != 64 or cfg.conv_kernel != 3:
+            raise ValueError("this build decodes head_dim 64 with a 3-tap convolution")
+        shapes = parameter_shapes(cfg)
+        if set(parameters) != set(shapes):
+            raise ValueError("Decoder parameter tree mismatch")
+        for name, shape in shapes.items():
+            if tuple(np.shape(parameters[name])) != shape:
+                raise ValueError(f"Decoder parameter shape mismatch: {name}")
+        self.cfg, self.stream = cfg, stream
+        f32 = lambda a: DeviceArray.from_numpy(np.ascontiguousarray(a, np.float32), "float32")  # noqa: E731
+
+        def bf16(*names):  # rows of the named matrices, concatenated, cast to bf16 on the device
+            host = np.ascontiguousarray(np.concatenate([np.asarray(parameters[n], np.float32) for n in names]))
+            src = f32(host)
+            out = DeviceArray(host.shape, "bfloat16")
+            _lib.call("mfb_cast_f32_bf16", P(src.ptr), P(out.ptr), host.size, None)
+            return out
+
+        self.embed = f32(parameters["model.embed_tokens.weight"])
+        self.head = bf16("model.embed_tokens.weight")
+        self.final_norm = f32(parameters["model.embedding_norm.weight"])
+        self.freqs = DeviceArray.from_numpy(rope_freqs(cfg.rope_theta, cfg.head_dim), "float32")
+        self.layers = []
+        for i, kind in enumerate(cfg.layer_types):
+            p = f"model.layers.{i}."
+            L = {"kind": kind, "op_norm": f32(parameters[p + "operator_norm.weight"]),
+                 "ffn_norm": f32(parameters[p + "ffn_norm.weight"]),
+                 "w13": bf16(p + "feed_forward.w1.weight", p + "feed_forward.w3.weight"),
+                 "w2": bf16(p + "feed_forward.w2.weight")}
+            if kind == "conv":
+                L["w_in"] = bf16(p + "conv.in_proj.weight")
+                L["w_out"] = bf16(p + "conv.out_proj.weight")
+                L["taps"] = f32(np.asarray(parameters[p + "conv.conv.weight"], np.float32)[:, 0, :])
+            else:
+                L["w_in"] = bf16(p + "self_attn.q_proj.weight", p + "self_attn.k_proj.weight",
+                                 p + "self_attn.v_proj.weight")
+                L["w_out"] = bf16(p + "self_attn.out_proj.weight")
+                L["qn"] = f32(parameters[p + "self_attn.q_layernorm.weight"])
+                L["kn"] = f32(parameters[p + "self_attn.k_layernorm.weight"])
+            self.layers.append(L)
+        _lib.call("mfb_device_sync")
+        self._scratch = {}
+
+    def _buffers(self, batch: int, capacity: int):
+        key = (batch, capacity)
+        if key not in self._scratch:
+            cfg, E = self.cfg, DeviceArray
+            c, f, h, hk = cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads
+            nq = (h + 2 * hk) * cfg.head_dim
+            ws = _lib.lib().mfb_decode_workspace_size(batch, capacity, h, cfg.head_dim)
+            self._scratch[key] = dict(
+                ids=E((batch,), "int32"), pos=E((batch,), "int32"), lens=E((batch,), "int32"),
+                x=E((batch, c), "bfloat16"), xb=E((batch, c), "bfloat16"), hn=E((batch, c), "bfloat16"),
+                proj=E((batch, max(3 * c, nq)), "bfloat16"), mixed=E((batch, c), "bfloat16"),
+                r=E((batch, c), "bfloat16"), mid=E((batch, c), "bfloat16"), h2=E((batch, c), "bfloat16"),
+                gu=E((batch, 2 * f), "bfloat16"), a=E((batch, f), "bfloat16"), y=E((batch, c), "bfloat16"),
+                q=E((batch, h, 64), "bfloat16"), k=E((batch, hk, 64), "bfloat16"), v=E((batch, hk, 64), "bfloat16"),
+                o=E((batch, h * 64), "bfloat16"), rq=E((batch, h), "float32"), rk=E((batch, hk), "float32"),
+                rstd=E((batch,), "float32"), enc=E((batch, c), "bfloat16"),
+                logits16=E((batch, cfg.vocab), "bfloat16"), ws=E((max(ws, 16),), "uint8"))
+        return self._scratch[key]
+
+    def _rms(self, x, res, w, sum_out, y, rstd, m):
+        _lib.call("mfb_rmsnorm_fwd", P(x.ptr), P(res.ptr) if res is not None else None, P(w.ptr), None,
+                  P(sum_out.ptr) if sum_out is not None else None, P(y.ptr), P(rstd.ptr), m, self.cfg.hidden,
+                  ctypes.c_float(self.cfg.norm_eps), self.stream)
+
+    def decode_one(self, input_ids, state: DecodeState):
+        """FP32 logits [B, vocab] of the next token for each row; writes the caches and advances the state."""
+        cfg, s = self.cfg, self.stream
+        if state.cfg != cfg:
+            raise ValueError("Decode state does not match the decoder config")
+        if state.valid_length >= cfg.max_position_embeddings:
+            raise ValueError("Decode position exceeds model max_position_embeddings")
+        if state.valid_length >= state.capacity:
+            raise DecodeOverflow(f"Cannot decode at position {state.valid_length}; capacity is {state.capacity}")
+        ids = np.asarray(input_ids, np.int32)
+        if ids.ndim == 2 and ids.shape[1] == 1:
+            ids = ids[:, 0]
+        if ids.ndim != 1 or ids.shape[0] != state.batch:
+            raise ValueError("decode_one input_ids must have shape [batch] or [batch, 1] matching the state")
+        b, c, f, h, hk = state.batch, cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads
+        nq = (h + 2 * hk) * cfg.head_dim
+        B = self._buffers(b, state.capacity)
+        pos = state.valid_length
+        for name, host in (("ids", ids), ("pos", np.full(b, pos, np.int32)), ("lens", np.full(b, pos + 1, np.int32))):
+            host = np.ascontiguousarray(host)
+            _lib.call("mfb_memcpy_h2d", P(B[name].ptr), host.ctypes.data_as(P), host.nbytes, s)
+        _lib.call("mfb_embed_gather", P(self.embed.ptr), P(B["ids"].ptr), P(B["x"].ptr), b, c, cfg.vocab, s)
+        x, prev_mid, prev_y = B["x"], None, None
+        for i, L in enumerate(self.layers):
+            # Block input (the previous block's mid + FFN output) and its operator norm.
+            if prev_mid is None:
+                self._rms(x, None, L["op_norm"], None, B["hn"], B["rstd"], b)
+            else:
+                self._rms(prev_mid, prev_y, L["op_norm"], x, B["hn"], B["rstd"], b)
+            if L["kind"] == "conv":
+                _fwd(B["hn"], L["w_in"], B["proj"], b, 3 * c, c, s)
+                _lib.call("mfb_conv_step", P(B["proj"].ptr), P(L["taps"].ptr), P(state.history[i].ptr),
+                          P(B["mixed"].ptr), b, c, s)
+                _fwd(B["mixed"], L["w_out"], B["r"], b, c, c, s)
+            else:
+                _fwd(B["hn"], L["w_in"], B["proj"], b, nq, c, s)
+                _lib.call("mfb_qknorm_rope_fwd", P(B["proj"].ptr), nq, P(L["qn"].ptr), P(L["kn"].ptr),
+                          P(B["pos"].ptr), P(self.freqs.ptr), P(B["q"].ptr), P(B["k"].ptr), P(B["v"].ptr),
+                          P(B["rq"].ptr), P(B["rk"].ptr), b, h, hk, ctypes.c_float(cfg.norm_eps), s)
+                _lib.call("mfb_decode_attn", P(B["q"].ptr), P(state.keys[i].ptr), P(state.values[i].ptr),
+                          P(B["k"].ptr), P(B["v"].ptr), P(B["pos"].ptr), P(B["lens"].ptr), P(B["o"].ptr), b,
+                          state.capacity, h, hk, cfg.head_dim, ctypes.c_float(cfg.head_dim ** -0.5),
+                          P(B["ws"].ptr), B["ws"].nbytes, s)
+                _fwd(B["o"], L["w_out"], B["r"], b, c, h * cfg.head_dim, s)
+            self._rms(x, B["r"], L["ffn_norm"], B["mid"], B["h2"], B["rstd"], b)
+            _fwd(B["h2"], L["w13"], B["gu"], b, 2 * f, c, s)
+            _lib.call("mfb_swiglu_fwd", P(B["gu"].ptr), P(B["a"].ptr), b, f, s)
+            _fwd(B["a"], L["w2"], B["y"], b, c, f, s)
+            prev_mid, prev_y = B["mid"], B["y"]
+            x = B["xb"] if x is B["x"] else B["x"]  # the next block's input buffer (ping-pong)
+        self._rms(prev_mid, prev_y, self.final_norm, x, B["enc"], B["rstd"], b)
+        _fwd(B["enc"], self.head, B["logits16"], b, cfg.vocab, c, s)
+        logits = DeviceArray((b, cfg.vocab), "float32")
+        _lib.call("mfb_cast_bf16_f32", P(B["logits16"].ptr), P(logits.ptr), b * cfg.vocab, s)
+        state.valid_length = pos + 1
+        return logits
+
+
+def decode_one(decoder: Decoder, input_ids, state: DecodeState):
+    """``(logits, state)`` like models/lfm2_5/decode.py:419 (the state's device caches are updated in place)."""
+    return decoder.decode_one(input_ids, state), state
+
+
+__all__ = ["DecodeOverflow", "DecodeState", "Decoder", "decode_one", "init_parameters", "new_state",
+           "parameter_shapes"]

@@ -243,3 +243,26 @@ def encoder_step_flops(cfg: EncoderStepConfig, segment_ids) -> float:
     attn = sum(1 for k in cfg.layer_types if k != "conv") * 3.5 * 4 * cfg.heads * cfg.head_dim * \
         segment_square_sum(segment_ids)
     return 6.0 * encoder_matmul_params(cfg) * tokens + attn
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    """The LFM2.5 causal decoder's dimensions for cached decoding
+    (src/minifield_training/models/lfm2_5/model.py:28-47; the 350M layout: 16
+    layers, attention at 2, 5, 8, 10, 12, 14, tied embeddings)."""
+
+    name: str = "lfm2.5-350m-decode-one"
+    hidden: int = 1024
+    ffn: int = 6656
+    heads: int = 16
+    kv_heads: int = 8
+    head_dim: int = 64
+    vocab: int = 65536
+    layer_types: tuple = ENCODER_LAYERS
+    conv_kernel: int = 3
+    norm_eps: float = 1e-5
+    rope_theta: float = 1000000.0
+    max_position_embeddings: int = 128000
+
+
+DECODER = DecoderConfig()
