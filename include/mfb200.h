@@ -49,6 +49,11 @@ int mfb_host_free(void* ptr);
 int mfb_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
 int mfb_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
 int mfb_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream);
+/* Strided device copy of `height` rows of `width` bytes (pitches in bytes):
+ * writes prompt keys/values into the fixed-capacity cache rows, the
+ * jnp.pad(key * keep) of layers/attention.py:269-278. */
+int mfb_memcpy2d_d2d(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t width, size_t height,
+                     void* stream);
 int mfb_memset(void* dst, int value, size_t bytes, void* stream);
 int mfb_stream_create(void** stream);
 int mfb_stream_destroy(void* stream);
@@ -293,6 +298,15 @@ size_t mfb_encoder_workspace_size(int C, int classes);
  * inputs, oldest first; shifted in place) -> mixed [B, C]. */
 int mfb_conv_step(const uint16_t* bcx, const float* taps, uint16_t* history, uint16_t* mixed, int B, int C,
                   void* stream);
+/* The causal gated short convolution over T tokens per row
+ * (kernels/convolution.py:7-22, and :82-111 when history_in is given): bcx
+ * [B*T, 3C], taps [C, 3] FP32, history_in [B, 2, C] bf16 or NULL (zeros, the
+ * prompt prefix of layers/convolution.py:77-101) -> mixed [B*T, C] and, when
+ * history_out is non-NULL, the continuation history [B, 2, C] (state_tail,
+ * kernels/convolution.py:56-79, at length T). history_out must not alias
+ * history_in. */
+int mfb_conv_causal(const uint16_t* bcx, const float* taps, const uint16_t* history_in, uint16_t* history_out,
+                    uint16_t* mixed, int B, int T, int C, void* stream);
 int mfb_conv_bwd(const uint16_t* bcx, const float* taps, const int32_t* segment_ids, const uint16_t* dmixed,
                  uint16_t* dbcx, float* dtaps, int accumulate, long long M, int T, int C, void* workspace,
                  size_t workspace_bytes, void* stream);

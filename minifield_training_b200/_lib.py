@@ -47,6 +47,7 @@ SIGNATURES = {
     "mfb_memcpy_h2d": (I, [P, P, SZ, P]),
     "mfb_memcpy_d2h": (I, [P, P, SZ, P]),
     "mfb_memcpy_d2d": (I, [P, P, SZ, P]),
+    "mfb_memcpy2d_d2d": (I, [P, SZ, P, SZ, SZ, SZ, P]),
     "mfb_memset": (I, [P, I, SZ, P]),
     "mfb_stream_create": (I, [ctypes.POINTER(P)]),
     "mfb_stream_destroy": (I, [P]),
@@ -91,6 +92,7 @@ SIGNATURES = {
     "mfb_cast_f32_bf16": (I, [P, P, ctypes.c_longlong, P]),
     "mfb_cast_bf16_f32": (I, [P, P, LL, P]),
     "mfb_conv_step": (I, [P, P, P, P, I, I, P]),
+    "mfb_conv_causal": (I, [P, P, P, P, P, I, I, I, P]),
 }
 
 _lib = None

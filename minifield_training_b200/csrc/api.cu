@@ -92,6 +92,15 @@ int mfb_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream) {
   return MFB_OK;
 }
 
+int mfb_memcpy2d_d2d(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t width, size_t height,
+                     void* stream) {
+  if (width == 0 || height == 0) return MFB_OK;
+  MFB_CHECK_ARG(dst && src && width <= dst_pitch && width <= src_pitch, "bad strided copy (width %zu)", width);
+  MFB_CUDA_TRY(cudaMemcpy2DAsync(dst, dst_pitch, src, src_pitch, width, height, cudaMemcpyDeviceToDevice,
+                                 (cudaStream_t)stream));
+  return MFB_OK;
+}
+
 int mfb_memset(void* dst, int value, size_t bytes, void* stream) {
   if (bytes == 0) return MFB_OK;
   MFB_CUDA_TRY(cudaMemsetAsync(dst, value, bytes, (cudaStream_t)stream));

@@ -114,6 +114,48 @@ __global__ void conv_step_kernel(const uint16_t* __restrict__ bcx, const float* 
   h[C] = __bfloat16_as_ushort(__float2bfloat16_rn(g));
 }
 
+// Causal gated short convolution over a whole prompt of T tokens per row
+// (kernels/convolution.py:7-22 for a zero history, :82-111 with one), plus the
+// continuation history of layers/convolution.py:77-101 (state_tail at the row's
+// full length: the last two gated inputs, zeros or the incoming history where
+// the row is shorter). One thread per (row, chunk of CAUSAL_TOK tokens,
+// channel): channels are the fastest index, so a warp reads 64 contiguous bytes
+// of each of b, c and values per token. Rounding as conv_step_kernel.
+constexpr int CAUSAL_TOK = 32;
+
+__global__ void conv_causal_kernel(const uint16_t* __restrict__ bcx, const float* __restrict__ taps,
+                                   const uint16_t* __restrict__ hist_in, uint16_t* __restrict__ hist_out,
+                                   uint16_t* __restrict__ mixed, int B, int T, int C) {
+  const int chunks = (T + CAUSAL_TOK - 1) / CAUSAL_TOK;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)B * chunks * C) return;
+  const int ch = (int)(i % C);
+  const long long bk = i / C;
+  const int k = (int)(bk % chunks), b = (int)(bk / chunks);
+  auto ld = [](const uint16_t* p) { return __bfloat162float(__ushort_as_bfloat16(*p)); };
+  const uint16_t* rows = bcx + (long long)b * T * 3 * C;
+  // Gated input at token t of this row; t in {-2, -1} reads the incoming history.
+  auto gated = [&](int t) -> float {
+    if (t >= 0) return bf(ld(rows + (long long)t * 3 * C + ch) * ld(rows + (long long)t * 3 * C + 2 * C + ch));
+    return hist_in ? ld(hist_in + ((long long)b * 2 + 2 + t) * C + ch) : 0.f;
+  };
+  const float w0 = bf(taps[ch * 3 + 0]), w1 = bf(taps[ch * 3 + 1]), w2 = bf(taps[ch * 3 + 2]);
+  const int t0 = k * CAUSAL_TOK, t1 = min(T, t0 + CAUSAL_TOK);
+  float h0 = gated(t0 - 2), h1 = gated(t0 - 1);
+  for (int t = t0; t < t1; ++t) {
+    const float g = gated(t);
+    const float acc = bf(bf(bf(h0 * w0) + bf(h1 * w1)) + bf(g * w2));
+    mixed[((long long)b * T + t) * C + ch] =
+        __bfloat16_as_ushort(__float2bfloat16_rn(ld(rows + (long long)t * 3 * C + C + ch) * acc));
+    h0 = h1;
+    h1 = g;
+  }
+  if (hist_out && t1 == T) {
+    hist_out[(long long)b * 2 * C + ch] = __bfloat16_as_ushort(__float2bfloat16_rn(h0));
+    hist_out[((long long)b * 2 + 1) * C + ch] = __bfloat16_as_ushort(__float2bfloat16_rn(h1));
+  }
+}
+
 __global__ void __launch_bounds__(128) conv_fwd_kernel(const uint16_t* __restrict__ bcx, const float* __restrict__ taps,
                                                        const int32_t* __restrict__ seg, uint16_t* __restrict__ mixed,
                                                        long long M, int T, int C) {
@@ -423,6 +465,19 @@ extern "C" int mfb_conv_step(const uint16_t* bcx, const float* taps, uint16_t* h
   enc::conv_step_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(bcx, taps, history, mixed, B,
                                                                                         C);
   MFB_LAUNCH_CHECK("conv step");
+  return MFB_OK;
+}
+
+extern "C" int mfb_conv_causal(const uint16_t* bcx, const float* taps, const uint16_t* history_in,
+                               uint16_t* history_out, uint16_t* mixed, int B, int T, int C, void* stream) {
+  MFB_CHECK_ARG(B > 0 && T > 0 && C > 0, "causal conv: bad shape (B=%d T=%d C=%d)", B, T, C);
+  MFB_CHECK_ARG(bcx && taps && mixed, "NULL causal conv argument");
+  MFB_CHECK_ARG(history_out == nullptr || history_out != history_in,
+                "causal conv: history_out must not alias history_in");
+  const long long n = (long long)B * ((T + enc::CAUSAL_TOK - 1) / enc::CAUSAL_TOK) * C;
+  enc::conv_causal_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      bcx, taps, history_in, history_out, mixed, B, T, C);
+  MFB_LAUNCH_CHECK("causal conv");
   return MFB_OK;
 }
 

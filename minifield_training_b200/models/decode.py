@@ -2,9 +2,24 @@
 
 Mirrors src/minifield_training/models/lfm2_5/decode.py: ``new_state`` (:75-134)
 allocates zeroed per-layer caches (attention K/V [B, capacity, Hk, 64] bf16,
-conv history [B, 2, C] bf16) and ``Decoder.decode_one`` (:419-466) runs one
-token per row through every block (:225-262) and returns FP32 logits of the
-tied head (model.py:818-829), advancing the state's valid length. Per block:
+conv history [B, 2, C] bf16); ``Decoder.prefill`` (:373-416) runs a prompt of
+T tokens per row through every block (:183-222), fills the caches and returns
+the FP32 logits of the last prompt token; ``Decoder.decode_one`` (:419-466)
+runs one token per row through every block (:225-262) and returns FP32 logits
+of the tied head (model.py:818-829), advancing the state's valid length.
+
+Prefill, per block over the B*T prompt tokens:
+
+  conv       RMSNorm -> in_proj GEMM -> mfb_conv_causal (zero history in, the
+             continuation history out) -> out_proj GEMM
+  attention  RMSNorm -> fused q|k|v GEMM -> q/k RMSNorm + RoPE at 0..T-1 ->
+             causal mfb_attn_fwd -> K/V rows copied into the cache
+             (mfb_memcpy2d_d2d) -> out_proj GEMM
+
+The reference pads the prompt to a power-of-two bucket (decode.py:63-67);
+the padded tokens sit after every valid one and are masked, so causal
+attention and the causal convolution never read them and the prompt runs
+at its own length here. Decode, per block:
 
   conv       RMSNorm -> in_proj GEMM -> mfb_conv_step (gated causal conv over
              the history, history shifted in place) -> out_proj GEMM
@@ -170,6 +185,90 @@ class Decoder:
                   P(sum_out.ptr) if sum_out is not None else None, P(y.ptr), P(rstd.ptr), m, self.cfg.hidden,
                   ctypes.c_float(self.cfg.norm_eps), self.stream)
 
+    def prefill(self, input_ids, state: DecodeState):
+        """FP32 logits [B, vocab] of the token after the prompt; fills the caches of a fresh state.
+
+        ``input_ids`` [B, T] int32; raises the reference's ValueErrors
+        (decode.py:382-396) before any kernel runs.
+        """
+        cfg, s = self.cfg, self.stream
+        if state.cfg != cfg:
+            raise ValueError("Decode state does not match the decoder config")
+        if state.valid_length != 0:
+            raise ValueError("Prefill requires a fresh state")
+        ids = np.asarray(input_ids)
+        if ids.ndim != 2:
+            raise ValueError("Prefill input_ids must have shape [batch, tokens]")
+        b, t = ids.shape
+        if t > cfg.max_position_embeddings:
+            raise ValueError("Logical length exceeds model max_position_embeddings")
+        if b != state.batch:
+            raise ValueError("Prompt batch does not match cache batch")
+        if t <= 0 or t > state.capacity:
+            raise ValueError("Prompt length must fit the cache capacity")
+        ids = np.ascontiguousarray(ids, np.int32)
+        c, f, h, hk, hd = cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads, cfg.head_dim
+        m, nq, E = b * t, (h + 2 * hk) * hd, DeviceArray
+        B = dict(ids=E((m,), "int32"), pos=E((m,), "int32"), mask=E((b, t), "int32"),
+                 qid=E((b, t), "int32"), kid=E((b, t), "int32"),
+                 x=E((m, c), "bfloat16"), xb=E((m, c), "bfloat16"), hn=E((m, c), "bfloat16"),
+                 proj=E((m, max(3 * c, nq)), "bfloat16"), mixed=E((m, c), "bfloat16"), r=E((m, c), "bfloat16"),
+                 mid=E((m, c), "bfloat16"), h2=E((m, c), "bfloat16"), gu=E((m, 2 * f), "bfloat16"),
+                 a=E((m, f), "bfloat16"), y=E((m, c), "bfloat16"), q=E((m, h, hd), "bfloat16"),
+                 k=E((m, hk, hd), "bfloat16"), v=E((m, hk, hd), "bfloat16"), o=E((m, h * hd), "bfloat16"),
+                 lse=E((b, h, t), "float32"), rq=E((m, h), "float32"), rk=E((m, hk), "float32"),
+                 rstd=E((m,), "float32"), enc=E((m, c), "bfloat16"), last=E((b, c), "bfloat16"),
+                 logits16=E((b, cfg.vocab), "bfloat16"))
+        ws_bytes = max(int(_lib.lib().mfb_attn_workspace_size(b, t, t, h, hk, hd)), 16)
+        ws = E((ws_bytes,), "uint8")
+        for name, host in (("ids", ids.reshape(-1)), ("pos", np.tile(np.arange(t, dtype=np.int32), b)),
+                           ("mask", np.ones((b, t), np.int32))):
+            host = np.ascontiguousarray(host)
+            _lib.call("mfb_memcpy_h2d", P(B[name].ptr), host.ctypes.data_as(P), host.nbytes, s)
+        causal, off, pol = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        _lib.call("mfb_attn_ids", _lib.MASK_CAUSAL, P(B["mask"].ptr), None, None, P(B["qid"].ptr),
+                  P(B["kid"].ptr), b, t, t, 0, ctypes.byref(causal), ctypes.byref(off), ctypes.byref(pol), s)
+        _lib.call("mfb_embed_gather", P(self.embed.ptr), P(B["ids"].ptr), P(B["x"].ptr), m, c, cfg.vocab, s)
+        row_kv = hk * hd * 2  # bytes of one token's K (or V) row
+        x, prev_mid, prev_y = B["x"], None, None
+        for i, L in enumerate(self.layers):
+            if prev_mid is None:
+                self._rms(x, None, L["op_norm"], None, B["hn"], B["rstd"], m)
+            else:
+                self._rms(prev_mid, prev_y, L["op_norm"], x, B["hn"], B["rstd"], m)
+            if L["kind"] == "conv":
+                _fwd(B["hn"], L["w_in"], B["proj"], m, 3 * c, c, s)
+                _lib.call("mfb_conv_causal", P(B["proj"].ptr), P(L["taps"].ptr), None, P(state.history[i].ptr),
+                          P(B["mixed"].ptr), b, t, c, s)
+                _fwd(B["mixed"], L["w_out"], B["r"], m, c, c, s)
+            else:
+                _fwd(B["hn"], L["w_in"], B["proj"], m, nq, c, s)
+                _lib.call("mfb_qknorm_rope_fwd", P(B["proj"].ptr), nq, P(L["qn"].ptr), P(L["kn"].ptr),
+                          P(B["pos"].ptr), P(self.freqs.ptr), P(B["q"].ptr), P(B["k"].ptr), P(B["v"].ptr),
+                          P(B["rq"].ptr), P(B["rk"].ptr), m, h, hk, ctypes.c_float(cfg.norm_eps), s)
+                _lib.call("mfb_attn_fwd", P(B["q"].ptr), P(B["k"].ptr), P(B["v"].ptr), P(B["o"].ptr),
+                          P(B["lse"].ptr), P(B["qid"].ptr), P(B["kid"].ptr), b, t, t, h, hk, hd, causal.value,
+                          off.value, pol.value, ctypes.c_float(hd ** -0.5), P(ws.ptr), ws.nbytes, s)
+                for cache, src in ((state.keys[i], B["k"]), (state.values[i], B["v"])):
+                    _lib.call("mfb_memcpy2d_d2d", P(cache.ptr), state.capacity * row_kv, P(src.ptr), t * row_kv,
+                              t * row_kv, b, s)
+                _fwd(B["o"], L["w_out"], B["r"], m, c, h * hd, s)
+            self._rms(x, B["r"], L["ffn_norm"], B["mid"], B["h2"], B["rstd"], m)
+            _fwd(B["h2"], L["w13"], B["gu"], m, 2 * f, c, s)
+            _lib.call("mfb_swiglu_fwd", P(B["gu"].ptr), P(B["a"].ptr), m, f, s)
+            _fwd(B["a"], L["w2"], B["y"], m, c, f, s)
+            prev_mid, prev_y = B["mid"], B["y"]
+            x = B["xb"] if x is B["x"] else B["x"]
+        self._rms(prev_mid, prev_y, self.final_norm, x, B["enc"], B["rstd"], m)
+        _lib.call("mfb_memcpy2d_d2d", P(B["last"].ptr), c * 2, P(B["enc"].ptr + (t - 1) * c * 2), t * c * 2, c * 2,
+                  b, s)  # the last prompt token of every row
+        _fwd(B["last"], self.head, B["logits16"], b, cfg.vocab, c, s)
+        logits = DeviceArray((b, cfg.vocab), "float32")
+        _lib.call("mfb_cast_bf16_f32", P(B["logits16"].ptr), P(logits.ptr), b * cfg.vocab, s)
+        _lib.call("mfb_stream_sync", s)  # the prompt buffers are released on return
+        state.valid_length = t
+        return logits
+
     def decode_one(self, input_ids, state: DecodeState):
         """FP32 logits [B, vocab] of the next token for each row; writes the caches and advances the state."""
         cfg, s = self.cfg, self.stream
@@ -228,10 +327,15 @@ class Decoder:
         return logits
 
 
+def prefill(decoder: Decoder, input_ids, state: DecodeState):
+    """``(logits, state)`` like models/lfm2_5/decode.py:373 (the state's device caches are filled in place)."""
+    return decoder.prefill(input_ids, state), state
+
+
 def decode_one(decoder: Decoder, input_ids, state: DecodeState):
     """``(logits, state)`` like models/lfm2_5/decode.py:419 (the state's device caches are updated in place)."""
     return decoder.decode_one(input_ids, state), state
 
 
-__all__ = ["DecodeOverflow", "DecodeState", "Decoder", "decode_one", "init_parameters", "new_state",
+__all__ = ["DecodeOverflow", "DecodeState", "Decoder", "decode_one", "init_parameters", "new_state", "prefill",
            "parameter_shapes"]

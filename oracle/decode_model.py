@@ -4,6 +4,12 @@ Restates (paths inside src/minifield_training/):
 
   decode_one / _decode_one_impl  models/lfm2_5/decode.py:325-364, 419-466
   _decode_block                  models/lfm2_5/decode.py:225-262
+  prefill / _prefill_impl        models/lfm2_5/decode.py:265-312, 373-416
+  _prefill_block                 models/lfm2_5/decode.py:183-222
+  conv_block_prefix              layers/convolution.py:77-101, state_tail
+                                 kernels/convolution.py:56-79
+  attention_block_prefill        layers/attention.py:246-278 (causal attention,
+                                 kernels/attention.py:206-222)
   conv_block_step                layers/convolution.py:153-178, 40-48
   gated conv with history        kernels/convolution.py:82-111
   attention_block_step           layers/attention.py:281-322, 61-108
@@ -65,6 +71,75 @@ def _w(t):
     return rb(t)
 
 
+def _ffn_tail(P, p, x, r, eps):
+    """x + r, then the residual SwiGLU (layers/feed_forward.py:24-35)."""
+    x = rb(x + r)
+    h2 = _rms(x, P[p + "ffn_norm.weight"], eps)
+    gg = _linear(h2, _w(P[p + "feed_forward.w1.weight"]))
+    uu = _linear(h2, _w(P[p + "feed_forward.w3.weight"]))
+    a = rb(gg * torch.sigmoid(gg) * uu)
+    return rb(x + _linear(a, _w(P[p + "feed_forward.w2.weight"])))
+
+
+def prefill(cfg, params: dict, ids, capacity: int):
+    """(logits [B, V] of the last prompt token, state after the prompt) for a fresh state.
+
+    Every row holds the same T valid tokens (the reference's scalar
+    valid_length); its power-of-two padding bucket only adds masked tokens
+    after them, which causal attention and the causal convolution never read,
+    so the oracle runs on the T tokens themselves.
+    """
+    with torch.no_grad():
+        P = {n: torch.tensor(np.asarray(v, np.float64), dtype=D) for n, v in params.items()}
+        ids = np.asarray(ids)
+        b, t = ids.shape
+        if t <= 0 or t > capacity:
+            raise ValueError("Prompt length must fit the cache capacity")
+        eps, hd, c = cfg.norm_eps, cfg.head_dim, cfg.hidden
+        x = rb(P["model.embed_tokens.weight"][torch.from_numpy(np.clip(ids, 0, cfg.vocab - 1)).long()])  # [B,T,C]
+        x = x.reshape(b * t, c)
+        positions = np.tile(np.arange(t, dtype=np.int32), b)
+        state = new_state(cfg, b, capacity)
+        state["pos"] = t
+        for i, kind in enumerate(cfg.layer_types):
+            p = f"model.layers.{i}."
+            h = _rms(x, P[p + "operator_norm.weight"], eps)
+            if kind == "conv":
+                bcx = _linear(h, _w(P[p + "conv.in_proj.weight"])).reshape(b, t, 3 * c)
+                gate_b, gate_c, vals = bcx[..., :c], bcx[..., c:2 * c], bcx[..., 2 * c:]
+                g = rb(gate_b * vals)
+                taps = rb(P[p + "conv.conv.weight"][:, 0, :])
+                gp = torch.cat((torch.zeros(b, 2, c, dtype=D), g), dim=1)  # two zero columns before token 0
+                acc = rb(rb(rb(gp[:, :t] * taps[:, 0]) + rb(gp[:, 1:t + 1] * taps[:, 1])) + rb(g * taps[:, 2]))
+                mixed = rb(gate_c * acc).reshape(b * t, c)
+                state["hist"][i] = gp[:, t:t + 2].numpy().copy()  # state_tail at length t (zeros when t == 1)
+                r = _linear(mixed, _w(P[p + "conv.out_proj.weight"]))
+            else:
+                q = _linear(h, _w(P[p + "self_attn.q_proj.weight"])).reshape(b * t, cfg.heads, hd)
+                k = _linear(h, _w(P[p + "self_attn.k_proj.weight"])).reshape(b * t, cfg.kv_heads, hd)
+                v = _linear(h, _w(P[p + "self_attn.v_proj.weight"])).reshape(b * t, cfg.kv_heads, hd)
+                q = _rope(_rms(q, P[p + "self_attn.q_layernorm.weight"], eps), positions, cfg.rope_theta, hd)
+                k = _rope(_rms(k, P[p + "self_attn.k_layernorm.weight"], eps), positions, cfg.rope_theta, hd)
+                group = cfg.heads // cfg.kv_heads
+                q4 = q.reshape(b, t, cfg.heads, hd)
+                k4 = k.reshape(b, t, cfg.kv_heads, hd)
+                v4 = v.reshape(b, t, cfg.kv_heads, hd)
+                kk = torch.repeat_interleave(k4, group, dim=2)
+                vv = torch.repeat_interleave(v4, group, dim=2)
+                s = torch.einsum("bthd,bshd->bhts", q4, kk) * hd ** -0.5
+                causal = torch.tril(torch.ones(t, t, dtype=torch.bool))
+                s = torch.where(causal, s, torch.full_like(s, -1e300))
+                prob = rb(torch.softmax(s, dim=-1))
+                o = rb(torch.einsum("bhts,bshd->bthd", prob, vv))
+                state["k"][i][:, :t] = k4.numpy()
+                state["v"][i][:, :t] = v4.numpy()
+                r = _linear(o.reshape(b * t, cfg.heads * hd), _w(P[p + "self_attn.out_proj.weight"]))
+            x = _ffn_tail(P, p, x, r, eps)
+        last = x.reshape(b, t, c)[:, t - 1]
+        enc = _rms(last, P["model.embedding_norm.weight"], eps)
+        return _linear(enc, _w(P["model.embed_tokens.weight"])).numpy(), state
+
+
 def decode_one(cfg, params: dict, ids, state: dict):
     """(logits [B, V] float64 (bf16-exact values), new state) for one token per row."""
     with torch.no_grad():
@@ -111,12 +186,7 @@ def decode_one(cfg, params: dict, ids, state: dict):
                 new["v"].append(vc.numpy())
                 new["hist"].append(None)
                 r = _linear(o.reshape(b, cfg.heads * hd), _w(P[p + "self_attn.out_proj.weight"]))
-            x = rb(x + r)
-            h2 = _rms(x, P[p + "ffn_norm.weight"], eps)
-            gg = _linear(h2, _w(P[p + "feed_forward.w1.weight"]))
-            uu = _linear(h2, _w(P[p + "feed_forward.w3.weight"]))
-            a = rb(gg * torch.sigmoid(gg) * uu)
-            x = rb(x + _linear(a, _w(P[p + "feed_forward.w2.weight"])))
+            x = _ffn_tail(P, p, x, r, eps)
         enc = _rms(x, P["model.embedding_norm.weight"], eps)
         logits = _linear(enc, _w(P["model.embed_tokens.weight"]))
         return logits.numpy(), new

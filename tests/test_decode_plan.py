@@ -2,6 +2,7 @@
 
 import dataclasses
 
+import numpy as np
 import pytest
 
 from minifield_training_b200.models import decode
@@ -39,3 +40,47 @@ def test_state_rejects_a_bad_batch_size(batch):
 
 def test_overflow_is_a_value_error():
     assert issubclass(decode.DecodeOverflow, ValueError)
+
+
+def _tiny():
+    return dataclasses.replace(DECODER, hidden=128, ffn=256, heads=4, kv_heads=2, vocab=512,
+                               layer_types=("conv", "full_attention", "conv"))
+
+
+def _rel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def test_oracle_prefill_then_cached_steps_equal_the_uninterrupted_prompt():
+    """The reference's prefix/cached-step property (tests/layers/test_blocks.py:223-340) at model level."""
+    cfg = _tiny()
+    params = decode.init_parameters(cfg, 3)
+    ids = np.random.default_rng(4).integers(0, cfg.vocab, (2, 6)).astype(np.int32)
+    logits, state = decode_model.prefill(cfg, params, ids[:, :3], 8)
+    assert state["pos"] == 3
+    for t in range(3, 6):
+        full, full_state = decode_model.prefill(cfg, params, ids[:, :t], 8)
+        assert _rel(logits, full) < 1e-2, t
+        for i, kind in enumerate(cfg.layer_types):
+            if kind == "conv":
+                assert _rel(state["hist"][i], full_state["hist"][i]) < 1e-2
+            else:
+                assert _rel(state["k"][i], full_state["k"][i]) < 1e-2
+                assert not full_state["k"][i][:, t:].any() and not full_state["v"][i][:, t:].any()
+        logits, state = decode_model.decode_one(cfg, params, ids[:, t], state)
+
+
+def test_oracle_one_token_prefill_history_starts_with_zeros():
+    cfg = _tiny()
+    params = decode.init_parameters(cfg, 5)
+    _, state = decode_model.prefill(cfg, params, np.array([[7], [9]], np.int32), 4)
+    for i, kind in enumerate(cfg.layer_types):
+        if kind == "conv":
+            assert not state["hist"][i][:, 0].any() and state["hist"][i][:, 1].any()
+
+
+def test_oracle_prefill_rejects_a_prompt_longer_than_the_capacity():
+    cfg = _tiny()
+    with pytest.raises(ValueError):
+        decode_model.prefill(cfg, decode.init_parameters(cfg, 0), np.zeros((1, 5), np.int32), 4)

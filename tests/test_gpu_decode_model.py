@@ -7,6 +7,11 @@ output scale, rel-L2 1e-2), and the caches must hold the same K/V rows and
 conv history (rel-L2 1e-2; max-abs 5e-2, as they sit several bf16 layers
 deep). Writing past the capacity raises DecodeOverflow before any
 kernel runs (decode.py:447-451).
+
+Prefill (decode.py:373-416) of ragged prompt lengths (one token, a length
+inside the first 128-token tile, one that crosses it, the full capacity)
+must give the oracle's last-token logits, K/V cache rows (zero past the
+prompt) and conv history, and decode_one must continue from that state.
 """
 
 import dataclasses
@@ -78,3 +83,59 @@ def test_decode_past_capacity_is_rejected():
         dm.new_state(cfg, 2, 3)
     with pytest.raises(ValueError):
         dec.decode_one(np.array([1, 2, 3], np.int32), dm.new_state(cfg, 2, 4))
+
+
+@pytest.mark.parametrize("t", [1, 37, 130, 256])
+def test_prefill_then_decode_matches_the_oracle(t):
+    require_gpu()
+    from minifield_training_b200.models import decode as dm
+    from oracle import decode_model as odm
+
+    cfg, b, cap = _cfg(), 3, 256
+    params = dm.init_parameters(cfg, 2)
+    dec = dm.Decoder(cfg, params)
+    rng = np.random.default_rng(t)
+    prompt = rng.integers(0, cfg.vocab, (b, t)).astype(np.int32)
+    state = dm.new_state(cfg, b, cap)
+    logits, same = dm.prefill(dec, prompt, state)
+    ref, ref_state = odm.prefill(cfg, params, prompt, cap)
+    assert same is state and state.valid_length == t
+    assert logits.shape == (b, cfg.vocab) and logits.dtype == "float32"
+    _close(logits.numpy(), ref, f"prefill logits T={t}")
+    for i, kind in enumerate(cfg.layer_types):
+        if kind == "full_attention":
+            for got, want in ((state.keys[i], ref_state["k"][i]), (state.values[i], ref_state["v"][i])):
+                g = got.numpy()
+                _close(g[:, :t].astype(np.float32), want[:, :t], f"prefill cache layer {i}", tol=5e-2)
+                assert not g[:, t:].any()
+        else:
+            h = state.history[i].numpy().astype(np.float32)
+            _close(h, ref_state["hist"][i], f"prefill conv history layer {i}", tol=5e-2)
+            if t == 1:
+                assert not h[:, 0].any()
+    for step in range(3 if t < cap else 0):
+        ids = rng.integers(0, cfg.vocab, b).astype(np.int32)
+        got = dec.decode_one(ids, state).numpy()
+        ref, ref_state = odm.decode_one(cfg, params, ids, ref_state)
+        _close(got, ref, f"decode after prefill T={t} step {step}")
+    if t == cap:
+        with pytest.raises(dm.DecodeOverflow):
+            dec.decode_one(np.zeros(b, np.int32), state)
+
+
+def test_prefill_rejects_what_the_reference_rejects():
+    require_gpu()
+    from minifield_training_b200.models import decode as dm
+
+    cfg = _cfg()
+    dec = dm.Decoder(cfg, dm.init_parameters(cfg, 0))
+    with pytest.raises(ValueError):  # longer than the capacity
+        dec.prefill(np.zeros((2, 9), np.int32), dm.new_state(cfg, 2, 8))
+    with pytest.raises(ValueError):  # batch mismatch
+        dec.prefill(np.zeros((3, 4), np.int32), dm.new_state(cfg, 2, 8))
+    with pytest.raises(ValueError):  # not [batch, tokens]
+        dec.prefill(np.zeros(4, np.int32), dm.new_state(cfg, 2, 8))
+    state = dm.new_state(cfg, 2, 8)
+    dec.prefill(np.ones((2, 3), np.int32), state)
+    with pytest.raises(ValueError):  # not a fresh state
+        dec.prefill(np.ones((2, 3), np.int32), state)
