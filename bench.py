@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-secondary", action="store_true", help="skip the decode / QAT secondary measurements")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["attention", "decode", "qat", "encoder"], default=None,
+    ap.add_argument("--only", choices=["attention", "decode", "decode_one", "qat", "encoder"], default=None,
                     help="run one workload (profiling); the JSON line then carries only its numbers")
     return ap.parse_args()
 
@@ -362,6 +362,62 @@ class DecodeWorkload:
     launches_per_step = 6
 
 
+class DecodeOneWorkload:
+    """The LFM2.5 decoder's cached generation (decode.py:373-466): prefill of a
+    1024-token prompt for 64 rows into 4096-slot caches, then single-token
+    decode_one steps replayed as one CUDA graph each."""
+
+    batch, capacity, prompt = 64, 4096, 1024
+
+    def __init__(self, seed):
+        from minifield_training_b200 import _lib, workloads
+        from minifield_training_b200.device import DeviceArray
+        from minifield_training_b200.models import decode
+
+        self.L, self.dm, cfg = _lib, decode, workloads.DECODER
+        self.cfg = cfg
+        s = ctypes.c_void_p()
+        _lib.call("mfb_stream_create", ctypes.byref(s))
+        self.stream = s.value
+        self.dec = decode.Decoder(cfg, decode.init_parameters(cfg, seed), stream=self.stream)
+        rng = np.random.default_rng(seed)
+        self.prompt = rng.integers(0, cfg.vocab, (self.batch, self.prompt)).astype(np.int32)
+        self.tokens = rng.integers(0, cfg.vocab, (self.capacity, self.batch)).astype(np.int32)
+        self.out = DeviceArray((self.batch, cfg.vocab), "float32")
+        self.state = None
+
+    def prefill(self):
+        self.state = self.dm.new_state(self.cfg, self.batch, self.capacity)
+        self.dec.prefill(self.prompt, self.state)
+
+    def step(self):
+        st = self.state
+        self.dec.decode_one(self.tokens[st.valid_length], st, out=self.out, graph=True)
+
+    def bytes_per_step(self, first_length, steps):
+        """HBM bytes one step must move, averaged over steps that start at first_length valid keys:
+        the bf16 weights of every projection and the tied head, the valid K/V cache rows of the
+        attention layers (plus the appended row), the gathered FP32 embedding rows and the logits
+        (bf16 product written and read, FP32 written)."""
+        cfg, b = self.cfg, self.batch
+        c, f, kv, q = cfg.hidden, cfg.ffn, cfg.kv_heads * cfg.head_dim, cfg.heads * cfg.head_dim
+        weights = 0
+        for kind in cfg.layer_types:
+            weights += 3 * f * c + (4 * c * c if kind == "conv" else (q + 2 * kv) * c + c * q)
+        weights = 2 * (weights + cfg.vocab * c)
+        n_attn = sum(1 for k in cfg.layer_types if k == "full_attention")
+        mean_len = first_length + (steps + 1) / 2.0
+        cache = n_attn * b * mean_len * kv * 2 * 2
+        return weights + cache + b * c * 4 + b * cfg.vocab * (2 + 2 + 4)
+
+    def close(self):
+        self.dec.close()
+        self.L.call("mfb_stream_sync", self.stream)
+        self.L.call("mfb_stream_destroy", self.stream)
+
+    launches_per_step = 1  # one graph replay (plus the logits copy)
+
+
 class QatWorkload:
     """Config 4: int8 fake-quant + SwiGLU FFN GEMM chain forward + backward."""
 
@@ -626,6 +682,31 @@ def run_ours(args, dist):
             "ms_per_step": dms, "hbm_gbs": gbs, "hbm_frac": gbs / hbm, "peak_gbs": hbm,
             "bytes_per_step": dec.bytes, "traffic": traffic.get("decode")}
         del dec
+    if only in (None, "decode_one") and not (only is None and args.no_secondary):
+        d1 = DecodeOneWorkload(seed=dist.rank)
+        d1.prefill()  # warm-up prompt (allocates the prompt buffers, loads the kernels)
+        d1.state = d1.dm.new_state(d1.cfg, d1.batch, d1.capacity)
+        device.sync()
+        dist.barrier()
+        ev0, ev1 = device.Event(), device.Event()
+        ev0.record(d1.stream)
+        d1.dec.prefill(d1.prompt, d1.state)
+        ev1.record(d1.stream)
+        device.sync()
+        pre_ms = dist.max(ev0.elapsed_ms(ev1))
+        first = d1.state.valid_length + args.warmup
+        dms1, _ = measure(dist, d1.step, args.steps, args.warmup, stream=d1.stream)
+        nbytes = d1.bytes_per_step(first, args.steps)
+        gbs = nbytes / (dms1 * 1e-3) / 1e9
+        launches += DecodeOneWorkload.launches_per_step * args.steps
+        secondary["decode_one"] = {
+            "workload": "lfm2.5-350m-decode-one-b64-cap4096", "layers": len(d1.cfg.layer_types),
+            "prompt_tokens": d1.prompt.shape[1], "tokens_per_s": n * d1.batch / (dms1 * 1e-3), "ms_per_step": dms1,
+            "hbm_gbs": gbs, "hbm_frac": gbs / hbm, "peak_gbs": hbm, "bytes_per_step": nbytes,
+            "prefill_ms": pre_ms, "prefill_tokens_per_s": n * d1.prompt.size / (pre_ms * 1e-3),
+            "graph": True}
+        d1.close()
+        del d1
     if only in (None, "qat") and not (only is None and args.no_secondary):
         qat = QatWorkload(seed=dist.rank)
         qsteps = max(3, args.steps // 2)

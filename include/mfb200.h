@@ -193,6 +193,17 @@ enum mfb_major { MFB_MAJOR_K = 0, MFB_MAJOR_MN = 1 };
 enum mfb_dtype { MFB_DTYPE_BF16 = 0, MFB_DTYPE_F32 = 1 };
 int mfb_gemm_bf16(const uint16_t* A, int a_major, int lda, const uint16_t* B, int b_major, int ldb, void* C,
                   int ldc, int out_dtype, int M, int N, int K, float alpha, const uint8_t* mask, void* stream);
+/* The same product with a caller-owned workspace that enables split-K for
+ * small M (the decode step's [batch, C] x W^T projections and logits,
+ * models/lfm2_5/decode.py:356-361, layers/attention.py:281-322): when the
+ * output tiles fill fewer than half the SMs and mask is NULL, K is cut into
+ * slices whose FP32 partials are summed in slice order (deterministic). The
+ * workspace (16-byte aligned) needs mfb_gemm_workspace_size(M, N, K) bytes for
+ * the full split; a smaller one gets fewer slices, NULL or 0 none. */
+size_t mfb_gemm_workspace_size(int M, int N, int K);
+int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const uint16_t* B, int b_major, int ldb, void* C,
+                     int ldc, int out_dtype, int M, int N, int K, float alpha, const uint8_t* mask, void* workspace,
+                     size_t workspace_bytes, void* stream);
 /* Reads (and clears) the tensor-core kernels' device status word of the
  * current device: 0 = ok, otherwise the id of a bounded pipeline wait that gave
  * up (the kernel then unwound instead of hanging). Synchronous. */

@@ -68,6 +68,8 @@ SIGNATURES = {
     "mfb_decode_attn": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, F, P, SZ, P]),
     "mfb_decode_attn_noalloc": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, F, P]),
     "mfb_gemm_bf16": (I, [P, I, I, P, I, I, P, I, I, I, I, I, F, P, P]),
+    "mfb_gemm_workspace_size": (SZ, [I, I, I]),
+    "mfb_gemm_bf16_ws": (I, [P, I, I, P, I, I, P, I, I, I, I, I, F, P, P, SZ, P]),
     "mfb_gemm_status": (I, [IP]),
     "mfb_graph_begin": (I, [P]),
     "mfb_graph_end": (I, [P, ctypes.POINTER(ctypes.c_void_p)]),

@@ -23,7 +23,17 @@
 // Two TMEM accumulators (2 x 256 columns) let the epilogue of one tile overlap
 // the main loop of the next. Every mbarrier wait is bounded; a timeout writes a
 // device status word that the host reads back (no trap, no endless spin).
+//
+// Split-K for small M (the decode step's projections: 64 rows, a handful of
+// 128x256 tiles): when a caller-owned workspace is given and the output tiles
+// fill fewer than half the SMs, the K range is cut into up to 16 slices of at
+// least 256. Each (tile, slice) is a work item that writes its FP32 partial
+// [M, N] to the workspace; splitk_reduce_kernel sums the slices in slice order
+// (deterministic), scales and converts. The weights then stream through many
+// SMs instead of a few.
 #include <cudaTypedefs.h>
+
+#include <algorithm>
 
 #include "tc.cuh"
 
@@ -52,7 +62,72 @@ struct Args {
   int num_m, num_n, num_k;
   int vec_ok;  // C rows 16-byte aligned: vector stores
   float alpha;
+  int k_split, kb_per;  // K slices and k-blocks per slice (1, num_k without split-K)
+  float* partial;       // [k_split, M, N] FP32 partials when k_split > 1
 };
+
+// Work item -> (m block, n block, first and end k-block).
+struct Item {
+  int mb, nb, kb0, kb1;
+};
+__device__ __forceinline__ Item item_of(const Args& a, int tile) {
+  const int mn = tile % (a.num_m * a.num_n), ks = tile / (a.num_m * a.num_n);
+  Item it;
+  it.mb = mn % a.num_m;
+  it.nb = mn / a.num_m;
+  it.kb0 = ks * a.kb_per;
+  it.kb1 = min(a.num_k, it.kb0 + a.kb_per);
+  return it;
+}
+
+// Raw FP32 partial of 32 columns of one row for split-K.
+__device__ __forceinline__ void store_partial(const Args& a, int ks, int row, int col0, const uint32_t* r) {
+  float* c = a.partial + ((long long)ks * a.M + row) * a.N + col0;
+  if (col0 + 32 <= a.N && (a.N & 3) == 0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      reinterpret_cast<float4*>(c)[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                                    __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+  } else {
+    for (int i = 0; i < 32; ++i)
+      if (col0 + i < a.N) c[i] = __uint_as_float(r[i]);
+  }
+}
+
+// C = alpha * sum over slices of the partials, slice 0 first. One thread per
+// 4 consecutive columns when N % 4 == 0 (float4 partial loads, issued ahead of
+// the in-order adds), else one per element.
+template <bool VEC4>
+__global__ void splitk_reduce_kernel(const float* __restrict__ partial, int k_split, int M, int N, void* C,
+                                     long long ldc, int out_f32, float alpha) {
+  const int per = VEC4 ? 4 : 1, cols = N / per;
+  const long long total = (long long)M * cols, slice = (long long)M * N;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(i / cols), col = (int)(i - (long long)row * cols) * per;
+    const float* p = partial + (long long)row * N + col;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+    for (int ks = 0; ks < k_split; ++ks) {
+      if (VEC4) {
+        const float4 v = *reinterpret_cast<const float4*>(p + ks * slice);
+        acc[0] += v.x;
+        acc[1] += v.y;
+        acc[2] += v.z;
+        acc[3] += v.w;
+      } else {
+        acc[0] += p[ks * slice];
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < per; ++e) {
+      if (out_f32)
+        reinterpret_cast<float*>(C)[row * ldc + col + e] = acc[e] * alpha;
+      else
+        reinterpret_cast<__nv_bfloat16*>(C)[row * ldc + col + e] = __float2bfloat16_rn(acc[e] * alpha);
+    }
+  }
+}
 
 __device__ __forceinline__ void store_chunk(const Args& a, int row, int col0, const uint32_t* r) {
   float v[32];
@@ -146,7 +221,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int num_tiles = args.num_m * args.num_n;
+  const int num_tiles = args.num_m * args.num_n * args.k_split;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -154,8 +229,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        const int mb = tile % args.num_m, nb = tile / args.num_m;
-        for (int kb = 0; kb < args.num_k; ++kb) {
+        const Item it = item_of(args, tile);
+        const int mb = it.mb, nb = it.nb;
+        for (int kb = it.kb0; kb < it.kb1; ++kb) {
           if (!tc::mbar_wait(empty_bar(stage), phase ^ 1, &g_status, 1)) {
             ok = false;
             break;
@@ -192,7 +268,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!tc::mbar_wait_w(tempty_bar(acc), acc_phase ^ 1, &g_status, 2)) break;
         tc::tc_fence_after();
         const uint32_t d = tmem + acc * BN;
-        for (int kb = 0; kb < args.num_k; ++kb) {
+        const Item it = item_of(args, tile);
+        for (int kb = it.kb0; kb < it.kb1; ++kb) {
           if (!tc::mbar_wait_w(full_bar(stage), phase, &g_status, 3)) {
             ok = false;
             break;
@@ -205,7 +282,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                                           : tc::smem_desc_sw128(sa + k * 32, 16, 1024);
             const uint64_t bd = args.b_mn ? tc::smem_desc_sw128(sb + k * 2048, 8192, 1024)
                                           : tc::smem_desc_sw128(sb + k * 32, 16, 1024);
-            tc::mma_bf16_w(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            tc::mma_bf16_w(d, ad, bd, idesc, (kb != it.kb0 || k != 0) ? 1u : 0u);
           }
           tc::mma_commit_w(empty_bar(stage));
           if (++stage == STAGES) {
@@ -228,7 +305,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int mb = tile % args.num_m, nb = tile / args.num_m;
+      const Item it = item_of(args, tile);
+      const int mb = it.mb, nb = it.nb, ks = tile / (args.num_m * args.num_n);
       if (!tc::mbar_wait(tfull_bar(acc), acc_phase, &g_status, 5)) break;
       tc::tc_fence_after();
       const int row = mb * BM + q * 32 + lane;
@@ -238,7 +316,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + acc * BN + ch * 32, r);
         tc::tmem_ld_wait();
         const int col0 = nb * BN + ch * 32;
-        if (row < args.M && col0 < args.N) store_chunk(args, row, col0, r);
+        if (row < args.M && col0 < args.N) {
+          if (args.k_split > 1)
+            store_partial(args, ks, row, col0, r);
+          else
+            store_chunk(args, row, col0, r);
+        }
       }
       tc::tc_fence_before();
       tc::mbar_arrive(tempty_bar(acc));
@@ -330,9 +413,40 @@ int sm_count(int dev) {
 }
 }  // namespace
 
+namespace {
+// K slices for an (M, N, K) product: > 1 only when the output tiles fill fewer
+// than half the SMs. A slice keeps at least SPLIT_MIN_KB 64-deep k-blocks and
+// there are at most SPLIT_MAX slices, so the FP32 partials (M x N x 4 bytes a
+// slice) stay well below the bf16 operand bytes a slice streams.
+constexpr int SPLIT_MIN_KB = 4, SPLIT_MAX = 16;
+int choose_split(int M, int N, int K, int sms, int* kb_per) {
+  const int tiles = cdiv(M, gemm::BM) * cdiv(N, gemm::BN), num_k = cdiv(K, gemm::BK);
+  *kb_per = num_k;
+  if (2 * tiles > sms || num_k < 2 * SPLIT_MIN_KB) return 1;
+  int split = std::min(std::min(num_k / SPLIT_MIN_KB, sms / tiles), SPLIT_MAX);
+  *kb_per = cdiv(num_k, split);
+  return cdiv(num_k, *kb_per);
+}
+}  // namespace
+
+extern "C" size_t mfb_gemm_workspace_size(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  int dev = 0, kb_per = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  const int split = choose_split(M, N, K, sm_count(dev), &kb_per);
+  return split > 1 ? sizeof(float) * (size_t)split * M * N : 0;
+}
+
 extern "C" int mfb_gemm_bf16(const uint16_t* A, int a_major, int lda, const uint16_t* B, int b_major, int ldb,
                              void* C, int ldc, int out_dtype, int M, int N, int K, float alpha, const uint8_t* mask,
                              void* stream) {
+  return mfb_gemm_bf16_ws(A, a_major, lda, B, b_major, ldb, C, ldc, out_dtype, M, N, K, alpha, mask, nullptr, 0,
+                          stream);
+}
+
+extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const uint16_t* B, int b_major, int ldb,
+                                void* C, int ldc, int out_dtype, int M, int N, int K, float alpha,
+                                const uint8_t* mask, void* workspace, size_t workspace_bytes, void* stream) {
   MFB_CHECK_ARG(M > 0 && N > 0 && K > 0, "GEMM needs nonempty M/N/K (%d, %d, %d)", M, N, K);
   MFB_CHECK_ARG(A && B && C, "NULL operand");
   MFB_CHECK_ARG(a_major == MFB_MAJOR_K || a_major == MFB_MAJOR_MN, "bad a_major");
@@ -374,11 +488,42 @@ extern "C" int mfb_gemm_bf16(const uint16_t* A, int a_major, int lda, const uint
     const long long esize = out_dtype == MFB_DTYPE_F32 ? 4 : 2;
     a.vec_ok = ((uintptr_t)C % 16 == 0) && ((long long)ldc * esize) % 16 == 0;
   }
+  a.k_split = 1;
+  a.kb_per = a.num_k;
+  a.partial = nullptr;
+  if (workspace && !mask) {
+    int kb_per = 0;
+    int split = choose_split(M, N, K, sm_count(dev), &kb_per);
+    const size_t slice = sizeof(float) * (size_t)M * N;
+    if (split > 1 && workspace_bytes < slice * split) {  // a smaller workspace gets fewer slices
+      split = (int)std::min<size_t>(split, workspace_bytes / slice);
+      if (split > 1) {
+        kb_per = cdiv(a.num_k, split);
+        split = cdiv(a.num_k, kb_per);
+      }
+    }
+    if (split > 1 && ((uintptr_t)workspace & 15) == 0) {
+      a.k_split = split;
+      a.kb_per = kb_per;
+      a.partial = static_cast<float*>(workspace);
+    }
+  }
   MFB_CUDA_TRY(cudaFuncSetAttribute(gemm::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM));
-  const int tiles = a.num_m * a.num_n;
+  const int tiles = a.num_m * a.num_n * a.k_split;
   const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
   gemm::gemm_kernel<<<grid, gemm::THREADS, gemm::SMEM, (cudaStream_t)stream>>>(ta, tb, a);
   MFB_LAUNCH_CHECK("mfb_gemm_bf16");
+  if (a.k_split > 1) {
+    const long long total = (long long)M * N / (N % 4 == 0 ? 4 : 1);
+    const int blocks = (int)std::min<long long>((total + 255) / 256, 8LL * sm_count(dev));
+    if (N % 4 == 0)
+      gemm::splitk_reduce_kernel<true><<<blocks, 256, 0, (cudaStream_t)stream>>>(a.partial, a.k_split, M, N, C,
+                                                                                ldc, a.out_f32, alpha);
+    else
+      gemm::splitk_reduce_kernel<false><<<blocks, 256, 0, (cudaStream_t)stream>>>(a.partial, a.k_split, M, N, C,
+                                                                                 ldc, a.out_f32, alpha);
+    MFB_LAUNCH_CHECK("GEMM split-K reduce");
+  }
   return MFB_OK;
 }
 

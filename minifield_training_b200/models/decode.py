@@ -159,7 +159,7 @@ class Decoder:
                 L["kn"] = f32(parameters[p + "self_attn.k_layernorm.weight"])
             self.layers.append(L)
         _lib.call("mfb_device_sync")
-        self._scratch = {}
+        self._scratch, self._graphs, self._prefill_scratch = {}, {}, {}
 
     def _buffers(self, batch: int, capacity: int):
         key = (batch, capacity)
@@ -168,8 +168,13 @@ class Decoder:
             c, f, h, hk = cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads
             nq = (h + 2 * hk) * cfg.head_dim
             ws = _lib.lib().mfb_decode_workspace_size(batch, capacity, h, cfg.head_dim)
+            gemm_ws = max(int(_lib.lib().mfb_gemm_workspace_size(batch, n, k))
+                          for n, k in ((3 * c, c), (c, c), (nq, c), (c, h * cfg.head_dim), (2 * f, c), (c, f),
+                                       (cfg.vocab, c)))
+            meta = E((3, batch), "int32")  # ids, positions, lengths: one upload per step
             self._scratch[key] = dict(
-                ids=E((batch,), "int32"), pos=E((batch,), "int32"), lens=E((batch,), "int32"),
+                meta=meta, ids=meta.view(0, (batch,)), pos=meta.view(batch, (batch,)),
+                lens=meta.view(2 * batch, (batch,)),
                 x=E((batch, c), "bfloat16"), xb=E((batch, c), "bfloat16"), hn=E((batch, c), "bfloat16"),
                 proj=E((batch, max(3 * c, nq)), "bfloat16"), mixed=E((batch, c), "bfloat16"),
                 r=E((batch, c), "bfloat16"), mid=E((batch, c), "bfloat16"), h2=E((batch, c), "bfloat16"),
@@ -177,8 +182,15 @@ class Decoder:
                 q=E((batch, h, 64), "bfloat16"), k=E((batch, hk, 64), "bfloat16"), v=E((batch, hk, 64), "bfloat16"),
                 o=E((batch, h * 64), "bfloat16"), rq=E((batch, h), "float32"), rk=E((batch, hk), "float32"),
                 rstd=E((batch,), "float32"), enc=E((batch, c), "bfloat16"),
-                logits16=E((batch, cfg.vocab), "bfloat16"), ws=E((max(ws, 16),), "uint8"))
+                logits16=E((batch, cfg.vocab), "bfloat16"), logits=E((batch, cfg.vocab), "float32"),
+                ws=E((max(ws, 16),), "uint8"), gemm_ws=E((max(gemm_ws, 16),), "uint8"))
         return self._scratch[key]
+
+    def _proj(self, x, w, out, m, n, k, B):
+        """out[m, n] = x[m, k] . w[n, k]^T (bf16); split-K through the step's workspace when m is small."""
+        _lib.call("mfb_gemm_bf16_ws", P(x.ptr), _lib.MAJOR_K, k, P(w.ptr), _lib.MAJOR_K, k, P(out.ptr), n,
+                  _lib.DTYPE_BF16, m, n, k, ctypes.c_float(1.0), None, P(B["gemm_ws"].ptr), B["gemm_ws"].nbytes,
+                  self.stream)
 
     def _rms(self, x, res, w, sum_out, y, rstd, m):
         _lib.call("mfb_rmsnorm_fwd", P(x.ptr), P(res.ptr) if res is not None else None, P(w.ptr), None,
@@ -209,18 +221,22 @@ class Decoder:
         ids = np.ascontiguousarray(ids, np.int32)
         c, f, h, hk, hd = cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads, cfg.head_dim
         m, nq, E = b * t, (h + 2 * hk) * hd, DeviceArray
-        B = dict(ids=E((m,), "int32"), pos=E((m,), "int32"), mask=E((b, t), "int32"),
-                 qid=E((b, t), "int32"), kid=E((b, t), "int32"),
-                 x=E((m, c), "bfloat16"), xb=E((m, c), "bfloat16"), hn=E((m, c), "bfloat16"),
-                 proj=E((m, max(3 * c, nq)), "bfloat16"), mixed=E((m, c), "bfloat16"), r=E((m, c), "bfloat16"),
-                 mid=E((m, c), "bfloat16"), h2=E((m, c), "bfloat16"), gu=E((m, 2 * f), "bfloat16"),
-                 a=E((m, f), "bfloat16"), y=E((m, c), "bfloat16"), q=E((m, h, hd), "bfloat16"),
-                 k=E((m, hk, hd), "bfloat16"), v=E((m, hk, hd), "bfloat16"), o=E((m, h * hd), "bfloat16"),
-                 lse=E((b, h, t), "float32"), rq=E((m, h), "float32"), rk=E((m, hk), "float32"),
-                 rstd=E((m,), "float32"), enc=E((m, c), "bfloat16"), last=E((b, c), "bfloat16"),
-                 logits16=E((b, cfg.vocab), "bfloat16"))
-        ws_bytes = max(int(_lib.lib().mfb_attn_workspace_size(b, t, t, h, hk, hd)), 16)
-        ws = E((ws_bytes,), "uint8")
+        B = self._prefill_scratch.get((b, t))
+        if B is None:  # kept for the next prompt of the same shape
+            B = dict(ids=E((m,), "int32"), pos=E((m,), "int32"), mask=E((b, t), "int32"),
+                     qid=E((b, t), "int32"), kid=E((b, t), "int32"),
+                     x=E((m, c), "bfloat16"), xb=E((m, c), "bfloat16"), hn=E((m, c), "bfloat16"),
+                     proj=E((m, max(3 * c, nq)), "bfloat16"), mixed=E((m, c), "bfloat16"), r=E((m, c), "bfloat16"),
+                     mid=E((m, c), "bfloat16"), h2=E((m, c), "bfloat16"), gu=E((m, 2 * f), "bfloat16"),
+                     a=E((m, f), "bfloat16"), y=E((m, c), "bfloat16"), q=E((m, h, hd), "bfloat16"),
+                     k=E((m, hk, hd), "bfloat16"), v=E((m, hk, hd), "bfloat16"), o=E((m, h * hd), "bfloat16"),
+                     lse=E((b, h, t), "float32"), rq=E((m, h), "float32"), rk=E((m, hk), "float32"),
+                     rstd=E((m,), "float32"), enc=E((m, c), "bfloat16"), last=E((b, c), "bfloat16"),
+                     logits16=E((b, cfg.vocab), "bfloat16"))
+            ws_bytes = max(int(_lib.lib().mfb_attn_workspace_size(b, t, t, h, hk, hd)), 16)
+            B["ws"] = E((ws_bytes,), "uint8")
+            self._prefill_scratch[(b, t)] = B
+        ws = B["ws"]
         for name, host in (("ids", ids.reshape(-1)), ("pos", np.tile(np.arange(t, dtype=np.int32), b)),
                            ("mask", np.ones((b, t), np.int32))):
             host = np.ascontiguousarray(host)
@@ -265,12 +281,19 @@ class Decoder:
         _fwd(B["last"], self.head, B["logits16"], b, cfg.vocab, c, s)
         logits = DeviceArray((b, cfg.vocab), "float32")
         _lib.call("mfb_cast_bf16_f32", P(B["logits16"].ptr), P(logits.ptr), b * cfg.vocab, s)
-        _lib.call("mfb_stream_sync", s)  # the prompt buffers are released on return
         state.valid_length = t
         return logits
 
-    def decode_one(self, input_ids, state: DecodeState):
-        """FP32 logits [B, vocab] of the next token for each row; writes the caches and advances the state."""
+    def decode_one(self, input_ids, state: DecodeState, *, out=None, graph: bool = False):
+        """FP32 logits [B, vocab] of the next token for each row; writes the caches and advances the state.
+
+        ``out`` (a float32 [B, vocab] DeviceArray) receives the logits instead
+        of a new array. ``graph=True`` replays the step as one CUDA graph,
+        captured on the first call for this state's caches (needs a created
+        stream); the step reads its token ids, positions and lengths from
+        device buffers uploaded before each replay, so one graph serves every
+        step.
+        """
         cfg, s = self.cfg, self.stream
         if state.cfg != cfg:
             raise ValueError("Decode state does not match the decoder config")
@@ -283,13 +306,40 @@ class Decoder:
             ids = ids[:, 0]
         if ids.ndim != 1 or ids.shape[0] != state.batch:
             raise ValueError("decode_one input_ids must have shape [batch] or [batch, 1] matching the state")
-        b, c, f, h, hk = state.batch, cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads
-        nq = (h + 2 * hk) * cfg.head_dim
+        b = state.batch
+        if out is not None and (tuple(out.shape) != (b, cfg.vocab) or out.dtype != "float32"):
+            raise ValueError("out must be a float32 [batch, vocab] device array")
+        if graph and not s:
+            raise ValueError("graph replay needs Decoder(stream=...) from mfb_stream_create")
         B = self._buffers(b, state.capacity)
         pos = state.valid_length
-        for name, host in (("ids", ids), ("pos", np.full(b, pos, np.int32)), ("lens", np.full(b, pos + 1, np.int32))):
-            host = np.ascontiguousarray(host)
-            _lib.call("mfb_memcpy_h2d", P(B[name].ptr), host.ctypes.data_as(P), host.nbytes, s)
+        meta = np.ascontiguousarray(np.stack([ids, np.full(b, pos, np.int32), np.full(b, pos + 1, np.int32)]))
+        _lib.call("mfb_memcpy_h2d", P(B["meta"].ptr), meta.ctypes.data_as(P), meta.nbytes, s)
+        logits = out if out is not None else DeviceArray((b, cfg.vocab), "float32")
+        if graph:
+            key = (b, state.capacity) + tuple(a.ptr for a in (*state.keys, *state.values, *state.history)
+                                               if a is not None)
+            g = self._graphs.get(key)
+            if g is None:
+                _lib.call("mfb_graph_begin", P(s))
+                try:
+                    self._step(B, state, B["logits"])
+                finally:
+                    g_ = P()
+                    _lib.call("mfb_graph_end", P(s), ctypes.byref(g_))
+                g = self._graphs[key] = g_.value
+            _lib.call("mfb_graph_launch", P(g), P(s))
+            _lib.call("mfb_memcpy_d2d", P(logits.ptr), P(B["logits"].ptr), logits.nbytes, s)
+        else:
+            self._step(B, state, logits)
+        state.valid_length = pos + 1
+        return logits
+
+    def _step(self, B, state: DecodeState, logits):
+        """The device work of one decode step (token ids, positions, lengths already in B)."""
+        cfg, s = self.cfg, self.stream
+        b, c, f, h, hk = state.batch, cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads
+        nq = (h + 2 * hk) * cfg.head_dim
         _lib.call("mfb_embed_gather", P(self.embed.ptr), P(B["ids"].ptr), P(B["x"].ptr), b, c, cfg.vocab, s)
         x, prev_mid, prev_y = B["x"], None, None
         for i, L in enumerate(self.layers):
@@ -299,12 +349,12 @@ class Decoder:
             else:
                 self._rms(prev_mid, prev_y, L["op_norm"], x, B["hn"], B["rstd"], b)
             if L["kind"] == "conv":
-                _fwd(B["hn"], L["w_in"], B["proj"], b, 3 * c, c, s)
+                self._proj(B["hn"], L["w_in"], B["proj"], b, 3 * c, c, B)
                 _lib.call("mfb_conv_step", P(B["proj"].ptr), P(L["taps"].ptr), P(state.history[i].ptr),
                           P(B["mixed"].ptr), b, c, s)
-                _fwd(B["mixed"], L["w_out"], B["r"], b, c, c, s)
+                self._proj(B["mixed"], L["w_out"], B["r"], b, c, c, B)
             else:
-                _fwd(B["hn"], L["w_in"], B["proj"], b, nq, c, s)
+                self._proj(B["hn"], L["w_in"], B["proj"], b, nq, c, B)
                 _lib.call("mfb_qknorm_rope_fwd", P(B["proj"].ptr), nq, P(L["qn"].ptr), P(L["kn"].ptr),
                           P(B["pos"].ptr), P(self.freqs.ptr), P(B["q"].ptr), P(B["k"].ptr), P(B["v"].ptr),
                           P(B["rq"].ptr), P(B["rk"].ptr), b, h, hk, ctypes.c_float(cfg.norm_eps), s)
@@ -312,19 +362,29 @@ class Decoder:
                           P(B["k"].ptr), P(B["v"].ptr), P(B["pos"].ptr), P(B["lens"].ptr), P(B["o"].ptr), b,
                           state.capacity, h, hk, cfg.head_dim, ctypes.c_float(cfg.head_dim ** -0.5),
                           P(B["ws"].ptr), B["ws"].nbytes, s)
-                _fwd(B["o"], L["w_out"], B["r"], b, c, h * cfg.head_dim, s)
+                self._proj(B["o"], L["w_out"], B["r"], b, c, h * cfg.head_dim, B)
             self._rms(x, B["r"], L["ffn_norm"], B["mid"], B["h2"], B["rstd"], b)
-            _fwd(B["h2"], L["w13"], B["gu"], b, 2 * f, c, s)
+            self._proj(B["h2"], L["w13"], B["gu"], b, 2 * f, c, B)
             _lib.call("mfb_swiglu_fwd", P(B["gu"].ptr), P(B["a"].ptr), b, f, s)
-            _fwd(B["a"], L["w2"], B["y"], b, c, f, s)
+            self._proj(B["a"], L["w2"], B["y"], b, c, f, B)
             prev_mid, prev_y = B["mid"], B["y"]
             x = B["xb"] if x is B["x"] else B["x"]  # the next block's input buffer (ping-pong)
         self._rms(prev_mid, prev_y, self.final_norm, x, B["enc"], B["rstd"], b)
-        _fwd(B["enc"], self.head, B["logits16"], b, cfg.vocab, c, s)
-        logits = DeviceArray((b, cfg.vocab), "float32")
+        self._proj(B["enc"], self.head, B["logits16"], b, cfg.vocab, c, B)
         _lib.call("mfb_cast_bf16_f32", P(B["logits16"].ptr), P(logits.ptr), b * cfg.vocab, s)
-        state.valid_length = pos + 1
-        return logits
+
+    def close(self):
+        """Release the captured decode graphs."""
+        graphs, self._graphs = getattr(self, "_graphs", {}), {}
+        for g in graphs.values():
+            if _lib._lib is not None:
+                _lib.lib().mfb_graph_destroy(P(g))
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
 
 
 def prefill(decoder: Decoder, input_ids, state: DecodeState):

@@ -139,3 +139,37 @@ def test_prefill_rejects_what_the_reference_rejects():
     dec.prefill(np.ones((2, 3), np.int32), state)
     with pytest.raises(ValueError):  # not a fresh state
         dec.prefill(np.ones((2, 3), np.int32), state)
+
+
+def test_graph_replayed_decode_equals_the_eager_step():
+    """decode_one(graph=True) replays one captured step for every position; logits match the eager path."""
+    require_gpu()
+    from minifield_training_b200 import _lib
+    from minifield_training_b200.device import DeviceArray
+    from minifield_training_b200.models import decode as dm
+    import ctypes
+
+    cfg = _cfg()
+    params = dm.init_parameters(cfg, 4)
+    stream = ctypes.c_void_p()
+    _lib.call("mfb_stream_create", ctypes.byref(stream))
+    try:
+        eager, graphed = dm.Decoder(cfg, params), dm.Decoder(cfg, params, stream=stream.value)
+        se, sg = dm.new_state(cfg, 4, 16), dm.new_state(cfg, 4, 16)
+        prompt = np.random.default_rng(5).integers(0, cfg.vocab, (4, 5)).astype(np.int32)
+        eager.prefill(prompt, se)
+        graphed.prefill(prompt, sg)
+        out = DeviceArray((4, cfg.vocab), "float32")
+        rng = np.random.default_rng(6)
+        for _ in range(4):
+            ids = rng.integers(0, cfg.vocab, 4).astype(np.int32)
+            want = eager.decode_one(ids, se).numpy()
+            got = graphed.decode_one(ids, sg, out=out, graph=True)
+            assert got is out
+            _lib.call("mfb_stream_sync", stream)
+            np.testing.assert_array_equal(got.numpy(), want)
+        assert len(graphed._graphs) == 1
+        graphed.close()
+    finally:
+        _lib.call("mfb_stream_sync", stream)
+        _lib.call("mfb_stream_destroy", stream)

@@ -147,3 +147,46 @@ def test_swiglu_qat_config4_full_size():
     dgu = np.concatenate((dg, du), axis=1)[:, sub]
     ref_dwgu = round_bf16(dgu).T @ xb
     assert_close(dwgu.float32()[sub], ref_dwgu, scaled=True, what="cfg4 dW_gate_up rows")
+
+
+@pytest.mark.parametrize("m,n,k", [(64, 1024, 6656), (64, 3072, 1024), (1, 1024, 1024), (100, 520, 200),
+                                   (64, 13312, 1024)])
+@pytest.mark.parametrize("ws_fraction", [1.0, 0.3])
+def test_split_k_gemm_for_small_m(m, n, k, ws_fraction):
+    """mfb_gemm_bf16_ws: K-sliced partials summed in slice order (deterministic), any workspace size."""
+    import ctypes
+
+    from minifield_training_b200 import _lib as L
+    from minifield_training_b200.device import DeviceArray
+
+    rng = np.random.default_rng(m + n + k)
+    a = round_bf16(rng.standard_normal((m, k), dtype=np.float32))
+    b = round_bf16(rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.05))
+    ad, bd = _dev(a), _dev(b)
+    need = int(L.lib().mfb_gemm_workspace_size(m, n, k))
+    ws = DeviceArray((max(16, int(need * ws_fraction) // 16 * 16),), "uint8")
+    ref = a.astype(np.float64) @ b.astype(np.float64).T
+    for out_dtype, code in (("float32", L.DTYPE_F32), ("bfloat16", L.DTYPE_BF16)):
+        outs = []
+        for _ in range(2):
+            c = DeviceArray((m, n), out_dtype)
+            L.call("mfb_gemm_bf16_ws", ctypes.c_void_p(ad.ptr), L.MAJOR_K, k, ctypes.c_void_p(bd.ptr), L.MAJOR_K, k,
+                   ctypes.c_void_p(c.ptr), n, code, m, n, k, ctypes.c_float(0.5), None, ctypes.c_void_p(ws.ptr),
+                   ws.nbytes, None)
+            outs.append(c.float32())
+        np.testing.assert_array_equal(outs[0], outs[1])  # deterministic slice order
+        if out_dtype == "float32":
+            np.testing.assert_allclose(outs[0], 0.5 * ref, rtol=1e-5, atol=1e-4 * np.sqrt(k))
+        else:
+            assert_close(outs[0], 0.5 * ref, scaled=True, what="split-K bf16 gemm")
+    st = ctypes.c_int()
+    L.call("mfb_gemm_status", ctypes.byref(st))
+    assert st.value == 0
+
+
+def test_split_k_workspace_is_needed_only_for_few_tiles():
+    from minifield_training_b200 import _lib as L
+
+    assert L.lib().mfb_gemm_workspace_size(64, 1024, 6656) > 0
+    assert L.lib().mfb_gemm_workspace_size(16384, 13312, 1024) == 0  # enough tiles: no split
+    assert L.lib().mfb_gemm_workspace_size(64, 1024, 64) == 0  # one k-block: nothing to split
