@@ -199,11 +199,16 @@ int mfb_gemm_bf16(const uint16_t* A, int a_major, int lda, const uint16_t* B, in
  * output tiles fill fewer than half the SMs and mask is NULL, K is cut into
  * slices whose FP32 partials are summed in slice order (deterministic). The
  * workspace (16-byte aligned) needs mfb_gemm_workspace_size(M, N, K) bytes for
- * the full split; a smaller one gets fewer slices, NULL or 0 none. */
+ * the full split; a smaller one gets fewer slices, NULL or 0 none.
+ * flags: MFB_GEMM_PDL launches the GEMM as a programmatic dependent of the
+ * previous kernel on the stream: its first B tiles load while that kernel
+ * finishes, A and the output wait for its completion. The caller asserts that
+ * no kernel still running on the stream writes B (true of weights). */
+enum mfb_gemm_flags { MFB_GEMM_PDL = 1 };
 size_t mfb_gemm_workspace_size(int M, int N, int K);
 int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const uint16_t* B, int b_major, int ldb, void* C,
-                     int ldc, int out_dtype, int M, int N, int K, float alpha, const uint8_t* mask, void* workspace,
-                     size_t workspace_bytes, void* stream);
+                     int ldc, int out_dtype, int M, int N, int K, float alpha, const uint8_t* mask, int flags,
+                     void* workspace, size_t workspace_bytes, void* stream);
 /* Reads (and clears) the tensor-core kernels' device status word of the
  * current device: 0 = ok, otherwise the id of a bounded pipeline wait that gave
  * up (the kernel then unwound instead of hanging). Synchronous. */

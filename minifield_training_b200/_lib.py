@@ -25,6 +25,7 @@ MASK_CAUSAL, MASK_PREFIX, MASK_PACKED, MASK_BIDIR, MASK_CACHED = range(5)
 EMPTY_UNIFORM, EMPTY_ZERO = 0, 1
 MAJOR_K, MAJOR_MN = 0, 1
 DTYPE_BF16, DTYPE_F32 = 0, 1
+GEMM_PDL = 1
 
 P = ctypes.c_void_p
 I = ctypes.c_int
@@ -69,7 +70,7 @@ SIGNATURES = {
     "mfb_decode_attn_noalloc": (I, [P, P, P, P, P, P, P, P, I, I, I, I, I, F, P]),
     "mfb_gemm_bf16": (I, [P, I, I, P, I, I, P, I, I, I, I, I, F, P, P]),
     "mfb_gemm_workspace_size": (SZ, [I, I, I]),
-    "mfb_gemm_bf16_ws": (I, [P, I, I, P, I, I, P, I, I, I, I, I, F, P, P, SZ, P]),
+    "mfb_gemm_bf16_ws": (I, [P, I, I, P, I, I, P, I, I, I, I, I, F, P, I, P, SZ, P]),
     "mfb_gemm_status": (I, [IP]),
     "mfb_graph_begin": (I, [P]),
     "mfb_graph_end": (I, [P, ctypes.POINTER(ctypes.c_void_p)]),

@@ -43,6 +43,14 @@ __host__ __device__ inline int cdiv(int a, int b) { return (a + b - 1) / b; }
 // Device helpers (legacy-path PTX used by the warp-level kernels).
 // ---------------------------------------------------------------------------
 
+// Programmatic dependent launch. allow_dependents lets the next kernel on the
+// stream start now if it was launched as a programmatic dependent (a decode
+// GEMM streaming its weights); that kernel still runs wait_prerequisites, which
+// returns once this grid has completed and its writes are visible, before it
+// reads anything this grid produces. Both are no-ops without such a launch.
+__device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void wait_prerequisites() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

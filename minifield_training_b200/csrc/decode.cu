@@ -164,6 +164,7 @@ __device__ __forceinline__ void combine_row(const Params& p, int b, int c0, int 
 template <int G>
 __global__ void __launch_bounds__(THREADS, 2)
     decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, Params p) {
+  allow_dependents();
   extern __shared__ uint8_t smem_raw[];
   // Offset from the __shared__ array itself so accesses keep the shared state space.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);

@@ -98,6 +98,7 @@ __device__ __forceinline__ void conv_at(const float* gm, const float* g0, const 
 // written by the same thread.
 __global__ void conv_step_kernel(const uint16_t* __restrict__ bcx, const float* __restrict__ taps,
                                  uint16_t* __restrict__ hist, uint16_t* __restrict__ mixed, int B, int C) {
+  allow_dependents();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)B * C) return;
   const int b = (int)(i / C), ch = (int)(i % C);

@@ -32,6 +32,7 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float* f) {
 __device__ __forceinline__ float sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
 
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ h, int M, int F) {
+  allow_dependents();
   const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (i >= (long long)M * F) return;
   const long long m = i / F, f = i % F;

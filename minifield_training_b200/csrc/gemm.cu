@@ -228,27 +228,54 @@ __global__ void __launch_bounds__(THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      // B (the weights in a decode projection) of the first tile's first
+      // stages loads before the dependency wait: a GEMM launched as a
+      // programmatic dependent streams it while the previous kernel finishes.
+      // A, and everything this grid writes, come after the wait.
+      int pre = 0;
+      if ((int)blockIdx.x < num_tiles) {
+        const Item it = item_of(args, blockIdx.x);
+        pre = min(STAGES, it.kb1 - it.kb0);
+        for (int i = 0; i < pre; ++i) {
+          const uint32_t sb = sbase + i * STAGE_BYTES + A_BYTES;
+          const int kb = it.kb0 + i;
+          tc::mbar_expect_tx(full_bar(i), STAGE_BYTES);
+          if (!args.b_mn) {
+            tc::tma_load_2d(sb, &tb, kb * BK, it.nb * BN, full_bar(i));
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tc::tma_load_2d(sb + j * 8192, &tb, it.nb * BN + 64 * j, kb * BK, full_bar(i));
+          }
+        }
+      }
+      wait_prerequisites();
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         const Item it = item_of(args, tile);
         const int mb = it.mb, nb = it.nb;
         for (int kb = it.kb0; kb < it.kb1; ++kb) {
-          if (!tc::mbar_wait(empty_bar(stage), phase ^ 1, &g_status, 1)) {
-            ok = false;
-            break;
+          const bool early = tile == (int)blockIdx.x && kb - it.kb0 < pre;  // B already in flight
+          if (!early) {
+            if (!tc::mbar_wait(empty_bar(stage), phase ^ 1, &g_status, 1)) {
+              ok = false;
+              break;
+            }
+            tc::mbar_expect_tx(full_bar(stage), STAGE_BYTES);
           }
           const uint32_t sa = sbase + stage * STAGE_BYTES, sb = sa + A_BYTES;
-          tc::mbar_expect_tx(full_bar(stage), STAGE_BYTES);
           if (!args.a_mn) {
             tc::tma_load_2d(sa, &ta, kb * BK, mb * BM, full_bar(stage));
           } else {
 #pragma unroll
             for (int i = 0; i < BM / 64; ++i) tc::tma_load_2d(sa + i * 8192, &ta, mb * BM + 64 * i, kb * BK, full_bar(stage));
           }
-          if (!args.b_mn) {
-            tc::tma_load_2d(sb, &tb, kb * BK, nb * BN, full_bar(stage));
-          } else {
+          if (!early) {
+            if (!args.b_mn) {
+              tc::tma_load_2d(sb, &tb, kb * BK, nb * BN, full_bar(stage));
+            } else {
 #pragma unroll
-            for (int i = 0; i < BN / 64; ++i) tc::tma_load_2d(sb + i * 8192, &tb, nb * BN + 64 * i, kb * BK, full_bar(stage));
+              for (int i = 0; i < BN / 64; ++i) tc::tma_load_2d(sb + i * 8192, &tb, nb * BN + 64 * i, kb * BK, full_bar(stage));
+            }
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -440,13 +467,15 @@ extern "C" size_t mfb_gemm_workspace_size(int M, int N, int K) {
 extern "C" int mfb_gemm_bf16(const uint16_t* A, int a_major, int lda, const uint16_t* B, int b_major, int ldb,
                              void* C, int ldc, int out_dtype, int M, int N, int K, float alpha, const uint8_t* mask,
                              void* stream) {
-  return mfb_gemm_bf16_ws(A, a_major, lda, B, b_major, ldb, C, ldc, out_dtype, M, N, K, alpha, mask, nullptr, 0,
+  return mfb_gemm_bf16_ws(A, a_major, lda, B, b_major, ldb, C, ldc, out_dtype, M, N, K, alpha, mask, 0, nullptr, 0,
                           stream);
 }
 
 extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const uint16_t* B, int b_major, int ldb,
                                 void* C, int ldc, int out_dtype, int M, int N, int K, float alpha,
-                                const uint8_t* mask, void* workspace, size_t workspace_bytes, void* stream) {
+                                const uint8_t* mask, int flags, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  MFB_CHECK_ARG((flags & ~MFB_GEMM_PDL) == 0, "unknown GEMM flags %d", flags);
   MFB_CHECK_ARG(M > 0 && N > 0 && K > 0, "GEMM needs nonempty M/N/K (%d, %d, %d)", M, N, K);
   MFB_CHECK_ARG(A && B && C, "NULL operand");
   MFB_CHECK_ARG(a_major == MFB_MAJOR_K || a_major == MFB_MAJOR_MN, "bad a_major");
@@ -511,7 +540,21 @@ extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const u
   MFB_CUDA_TRY(cudaFuncSetAttribute(gemm::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM));
   const int tiles = a.num_m * a.num_n * a.k_split;
   const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
-  gemm::gemm_kernel<<<grid, gemm::THREADS, gemm::SMEM, (cudaStream_t)stream>>>(ta, tb, a);
+  if (flags & MFB_GEMM_PDL) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(gemm::THREADS);
+    cfg.dynamicSmemBytes = gemm::SMEM;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    MFB_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm::gemm_kernel, ta, tb, a));
+  } else {
+    gemm::gemm_kernel<<<grid, gemm::THREADS, gemm::SMEM, (cudaStream_t)stream>>>(ta, tb, a);
+  }
   MFB_LAUNCH_CHECK("mfb_gemm_bf16");
   if (a.k_split > 1) {
     const long long total = (long long)M * N / (N % 4 == 0 ? 4 : 1);

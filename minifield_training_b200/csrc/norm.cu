@@ -65,6 +65,7 @@ __global__ void __launch_bounds__(32 * WARPS) rms_fwd_kernel(const uint16_t* __r
                                                              const int32_t* __restrict__ row_mask,
                                                              uint16_t* __restrict__ sum_out, uint16_t* __restrict__ y,
                                                              float* __restrict__ rstd, int M, float eps) {
+  allow_dependents();
   constexpr int C = 256 * V;
   const int lane = threadIdx.x & 31;
   const int warp = blockIdx.x * WARPS + (threadIdx.x >> 5), nwarps = gridDim.x * WARPS;

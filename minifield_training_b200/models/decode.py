@@ -187,10 +187,16 @@ class Decoder:
         return self._scratch[key]
 
     def _proj(self, x, w, out, m, n, k, B):
-        """out[m, n] = x[m, k] . w[n, k]^T (bf16); split-K through the step's workspace when m is small."""
+        """out[m, n] = x[m, k] . w[n, k]^T (bf16); split-K through the step's workspace when m is small.
+
+        On a created stream it launches as a programmatic dependent: the
+        weight tiles stream in while the previous kernel (norm, SwiGLU, conv
+        step or attention) finishes.
+        """
         _lib.call("mfb_gemm_bf16_ws", P(x.ptr), _lib.MAJOR_K, k, P(w.ptr), _lib.MAJOR_K, k, P(out.ptr), n,
-                  _lib.DTYPE_BF16, m, n, k, ctypes.c_float(1.0), None, P(B["gemm_ws"].ptr), B["gemm_ws"].nbytes,
-                  self.stream)
+                  _lib.DTYPE_BF16, m, n, k, ctypes.c_float(1.0), None, _lib.GEMM_PDL if self.stream else 0,
+                  P(B["gemm_ws"].ptr),
+                  B["gemm_ws"].nbytes, self.stream)
 
     def _rms(self, x, res, w, sum_out, y, rstd, m):
         _lib.call("mfb_rmsnorm_fwd", P(x.ptr), P(res.ptr) if res is not None else None, P(w.ptr), None,

@@ -153,7 +153,8 @@ def test_swiglu_qat_config4_full_size():
                                    (64, 13312, 1024)])
 @pytest.mark.parametrize("ws_fraction", [1.0, 0.3])
 def test_split_k_gemm_for_small_m(m, n, k, ws_fraction):
-    """mfb_gemm_bf16_ws: K-sliced partials summed in slice order (deterministic), any workspace size."""
+    """mfb_gemm_bf16_ws: K-sliced partials summed in slice order (deterministic), any workspace size,
+    launched plainly and as a programmatic dependent (MFB_GEMM_PDL) with the same result."""
     import ctypes
 
     from minifield_training_b200 import _lib as L
@@ -166,19 +167,23 @@ def test_split_k_gemm_for_small_m(m, n, k, ws_fraction):
     need = int(L.lib().mfb_gemm_workspace_size(m, n, k))
     ws = DeviceArray((max(16, int(need * ws_fraction) // 16 * 16),), "uint8")
     ref = a.astype(np.float64) @ b.astype(np.float64).T
+    stream = ctypes.c_void_p()
+    L.call("mfb_stream_create", ctypes.byref(stream))
     for out_dtype, code in (("float32", L.DTYPE_F32), ("bfloat16", L.DTYPE_BF16)):
         outs = []
-        for _ in range(2):
+        for flags, s in ((0, None), (L.GEMM_PDL, stream)):  # plain, then as a programmatic dependent
             c = DeviceArray((m, n), out_dtype)
             L.call("mfb_gemm_bf16_ws", ctypes.c_void_p(ad.ptr), L.MAJOR_K, k, ctypes.c_void_p(bd.ptr), L.MAJOR_K, k,
-                   ctypes.c_void_p(c.ptr), n, code, m, n, k, ctypes.c_float(0.5), None, ctypes.c_void_p(ws.ptr),
-                   ws.nbytes, None)
+                   ctypes.c_void_p(c.ptr), n, code, m, n, k, ctypes.c_float(0.5), None, flags,
+                   ctypes.c_void_p(ws.ptr), ws.nbytes, s)
+            L.call("mfb_stream_sync", s)
             outs.append(c.float32())
         np.testing.assert_array_equal(outs[0], outs[1])  # deterministic slice order
         if out_dtype == "float32":
             np.testing.assert_allclose(outs[0], 0.5 * ref, rtol=1e-5, atol=1e-4 * np.sqrt(k))
         else:
             assert_close(outs[0], 0.5 * ref, scaled=True, what="split-K bf16 gemm")
+    L.call("mfb_stream_destroy", stream)
     st = ctypes.c_int()
     L.call("mfb_gemm_status", ctypes.byref(st))
     assert st.value == 0
