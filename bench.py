@@ -415,7 +415,22 @@ class DecodeOneWorkload:
         self.L.call("mfb_stream_sync", self.stream)
         self.L.call("mfb_stream_destroy", self.stream)
 
-    launches_per_step = 1  # one graph replay (plus the logits copy)
+    def kernels_per_step(self):
+        """Kernels one graph replay runs: a split-K GEMM is the GEMM and its reduce."""
+        cfg, b = self.cfg, self.batch
+        c, f, nq = cfg.hidden, cfg.ffn, (cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim
+
+        def gemm(n, k):
+            return 2 if self.L.lib().mfb_gemm_workspace_size(b, n, k) > 0 else 1
+
+        n = 1 + 1 + gemm(cfg.vocab, c) + 1  # embedding gather, final norm, tied head, FP32 cast
+        for kind in cfg.layer_types:
+            n += 2 + gemm(2 * f, c) + 1 + gemm(c, f)  # two norms, w1|w3, SwiGLU, w2
+            if kind == "conv":
+                n += gemm(3 * c, c) + 1 + gemm(c, c)  # in-proj, conv step, out-proj
+            else:
+                n += gemm(nq, c) + 2 + gemm(c, cfg.heads * cfg.head_dim)  # q|k|v, qk-norm+RoPE, attention, out
+        return n
 
 
 class QatWorkload:
@@ -698,13 +713,13 @@ def run_ours(args, dist):
         dms1, _ = measure(dist, d1.step, args.steps, args.warmup, stream=d1.stream)
         nbytes = d1.bytes_per_step(first, args.steps)
         gbs = nbytes / (dms1 * 1e-3) / 1e9
-        launches += DecodeOneWorkload.launches_per_step * args.steps
+        launches += d1.kernels_per_step() * args.steps
         secondary["decode_one"] = {
             "workload": "lfm2.5-350m-decode-one-b64-cap4096", "layers": len(d1.cfg.layer_types),
             "prompt_tokens": d1.prompt.shape[1], "tokens_per_s": n * d1.batch / (dms1 * 1e-3), "ms_per_step": dms1,
             "hbm_gbs": gbs, "hbm_frac": gbs / hbm, "peak_gbs": hbm, "bytes_per_step": nbytes,
             "prefill_ms": pre_ms, "prefill_tokens_per_s": n * d1.prompt.size / (pre_ms * 1e-3),
-            "graph": True}
+            "graph": True, "kernels_per_step": d1.kernels_per_step()}
         d1.close()
         del d1
     if only in (None, "qat") and not (only is None and args.no_secondary):

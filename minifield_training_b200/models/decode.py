@@ -227,21 +227,28 @@ class Decoder:
         ids = np.ascontiguousarray(ids, np.int32)
         c, f, h, hk, hd = cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads, cfg.head_dim
         m, nq, E = b * t, (h + 2 * hk) * hd, DeviceArray
-        B = self._prefill_scratch.get((b, t))
-        if B is None:  # kept for the next prompt of the same shape
-            B = dict(ids=E((m,), "int32"), pos=E((m,), "int32"), mask=E((b, t), "int32"),
-                     qid=E((b, t), "int32"), kid=E((b, t), "int32"),
-                     x=E((m, c), "bfloat16"), xb=E((m, c), "bfloat16"), hn=E((m, c), "bfloat16"),
-                     proj=E((m, max(3 * c, nq)), "bfloat16"), mixed=E((m, c), "bfloat16"), r=E((m, c), "bfloat16"),
-                     mid=E((m, c), "bfloat16"), h2=E((m, c), "bfloat16"), gu=E((m, 2 * f), "bfloat16"),
-                     a=E((m, f), "bfloat16"), y=E((m, c), "bfloat16"), q=E((m, h, hd), "bfloat16"),
-                     k=E((m, hk, hd), "bfloat16"), v=E((m, hk, hd), "bfloat16"), o=E((m, h * hd), "bfloat16"),
-                     lse=E((b, h, t), "float32"), rq=E((m, h), "float32"), rk=E((m, hk), "float32"),
-                     rstd=E((m,), "float32"), enc=E((m, c), "bfloat16"), last=E((b, c), "bfloat16"),
-                     logits16=E((b, cfg.vocab), "bfloat16"))
-            ws_bytes = max(int(_lib.lib().mfb_attn_workspace_size(b, t, t, h, hk, hd)), 16)
-            B["ws"] = E((ws_bytes,), "uint8")
-            self._prefill_scratch[(b, t)] = B
+        # Scratch sized for the reference's power-of-two prompt bucket
+        # (decode.py:63-67) and kept per (batch, bucket): at most log2(capacity)
+        # buffer sets per batch size, whatever the prompt lengths. A prompt uses
+        # the leading b*t rows ([b, t] arrays stay contiguous with row stride t).
+        bucket = 1 << (t - 1).bit_length()
+        B = self._prefill_scratch.get((b, bucket))
+        if B is None:
+            mb = b * bucket
+            B = dict(ids=E((mb,), "int32"), pos=E((mb,), "int32"), mask=E((mb,), "int32"),
+                     qid=E((mb,), "int32"), kid=E((mb,), "int32"),
+                     x=E((mb, c), "bfloat16"), xb=E((mb, c), "bfloat16"), hn=E((mb, c), "bfloat16"),
+                     proj=E((mb, max(3 * c, nq)), "bfloat16"), mixed=E((mb, c), "bfloat16"),
+                     r=E((mb, c), "bfloat16"), mid=E((mb, c), "bfloat16"), h2=E((mb, c), "bfloat16"),
+                     gu=E((mb, 2 * f), "bfloat16"), a=E((mb, f), "bfloat16"), y=E((mb, c), "bfloat16"),
+                     q=E((mb, h, hd), "bfloat16"), k=E((mb, hk, hd), "bfloat16"), v=E((mb, hk, hd), "bfloat16"),
+                     o=E((mb, h * hd), "bfloat16"), lse=E((mb * h,), "float32"), rq=E((mb, h), "float32"),
+                     rk=E((mb, hk), "float32"), rstd=E((mb,), "float32"), enc=E((mb, c), "bfloat16"),
+                     last=E((b, c), "bfloat16"), logits16=E((b, cfg.vocab), "bfloat16"), ws=E((16,), "uint8"))
+            self._prefill_scratch[(b, bucket)] = B
+        need = int(_lib.lib().mfb_attn_workspace_size(b, t, t, h, hk, hd))
+        if B["ws"].nbytes < need:
+            B["ws"] = E((need,), "uint8")
         ws = B["ws"]
         for name, host in (("ids", ids.reshape(-1)), ("pos", np.tile(np.arange(t, dtype=np.int32), b)),
                            ("mask", np.ones((b, t), np.int32))):
