@@ -201,9 +201,10 @@ int mfb_gemm_bf16(const uint16_t* A, int a_major, int lda, const uint16_t* B, in
  * workspace (16-byte aligned) needs mfb_gemm_workspace_size(M, N, K) bytes for
  * the full split; a smaller one gets fewer slices, NULL or 0 none.
  * flags: MFB_GEMM_PDL launches the GEMM as a programmatic dependent of the
- * previous kernel on the stream: its first B tiles load while that kernel
- * finishes, A and the output wait for its completion. The caller asserts that
- * no kernel still running on the stream writes B (true of weights). */
+ * previous kernel on the stream (a created stream, not the legacy default
+ * one): its first B tiles load while that kernel finishes, A and the output
+ * wait for its completion. The caller asserts that no kernel still running on
+ * the stream writes B (true of weights). */
 enum mfb_gemm_flags { MFB_GEMM_PDL = 1 };
 size_t mfb_gemm_workspace_size(int M, int N, int K);
 int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const uint16_t* B, int b_major, int ldb, void* C,

@@ -476,6 +476,8 @@ extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const u
                                 const uint8_t* mask, int flags, void* workspace, size_t workspace_bytes,
                                 void* stream) {
   MFB_CHECK_ARG((flags & ~MFB_GEMM_PDL) == 0, "unknown GEMM flags %d", flags);
+  MFB_CHECK_ARG(!(flags & MFB_GEMM_PDL) || stream != nullptr,
+                "MFB_GEMM_PDL needs a created stream, not the legacy default stream");
   MFB_CHECK_ARG(M > 0 && N > 0 && K > 0, "GEMM needs nonempty M/N/K (%d, %d, %d)", M, N, K);
   MFB_CHECK_ARG(A && B && C, "NULL operand");
   MFB_CHECK_ARG(a_major == MFB_MAJOR_K || a_major == MFB_MAJOR_MN, "bad a_major");

@@ -60,6 +60,15 @@ def test_invalid_arguments_raise_before_launch(built_lib):
                                 ctypes.c_float(1.0), None, 0, None),
             "decode",
         )
+    a = ctypes.c_void_p(16)  # never dereferenced: the checks fail first
+    with pytest.raises(ValueError, match="created stream"):
+        _lib.check(lib.mfb_gemm_bf16_ws(a, 0, 64, a, 0, 64, a, 64, 0, 64, 64, 64, ctypes.c_float(1.0), None,
+                                        _lib.GEMM_PDL, None, 0, None), "gemm")
+    with pytest.raises(ValueError, match="unknown GEMM flags"):
+        _lib.check(lib.mfb_gemm_bf16_ws(a, 0, 64, a, 0, 64, a, 64, 0, 64, 64, 64, ctypes.c_float(1.0), None,
+                                        6, None, 0, None), "gemm")
+    with pytest.raises(ValueError, match="alias"):
+        _lib.check(lib.mfb_conv_causal(a, a, a, a, a, 2, 4, 8, None), "conv")
 
 
 def test_missing_library_fails_loudly(monkeypatch):
