@@ -115,9 +115,13 @@ class Clocks:
               "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
+        """Samples go to MFB_CLOCKS_DIR when set (to keep the CSV), else to a temporary directory."""
+        import tempfile
+
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv")
+        folder = os.environ.get("MFB_CLOCKS_DIR") or tempfile.mkdtemp(prefix="mfb_clocks_")
+        self.path = os.path.join(folder, f"clocks_rank{index}.csv")
 
     def start(self):
         try:

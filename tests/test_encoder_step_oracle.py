@@ -1,4 +1,4 @@
-"""Model-level properties of oracle/encoder_step.py, the FP64 step the GPU encoder is judged against.
+"""Model-level properties of oracle/encoder_step.py, the FP64 step the GPU encoder is compared with.
 
 The reference pins its encoder with two properties
 (tests/models/lfm2_5/test_encoder.py): segments packed into one row encode

@@ -4,7 +4,7 @@ A two-layer encoder (conv + attention, hidden 1024, FFN 256, packed segments)
 runs the QAT forward and backward through the kernels. For a composed bf16
 model the per-op gate (rel-L2 1e-2) is the wrong ruler: two bf16 runs that
 round at different points already differ by about that much. So every
-trainable leaf's gradient G is judged against the exact FP64 path X of the same
+trainable leaf's gradient G is compared with the exact FP64 path X of the same
 (fake-quantized) model, next to the oracle R that rounds at the reference's
 bf16 cast points: rel-L2(G, X) must stay within 1.5x rel-L2(R, X) + 2e-3, and
 G and R must agree within rel-L2 2e-2. The loss sum must match R within 2e-3
