@@ -564,22 +564,26 @@ class EncoderStepWorkload:
         return count[0]
 
 
-def cpu_attention_sample(rows=2):
-    """Time the oracle's FP32 forward+backward on ``rows`` rows of config 2."""
+def cpu_attention_sample(rows=2, chunk=2):
+    """Time the oracle's FP32 forward+backward on ``rows`` rows of config 2, ``chunk`` rows at a time
+    (a chunk's score grids take about 2.5 GB)."""
     from minifield_training_b200 import workloads
     from oracle import attention as oatt
 
     cfg = workloads.CONFIG2
-    q, k, v, do, mask, seg = workloads.attention_inputs(cfg, 0)
-    q, k, v, do, mask, seg = (x[:rows] for x in (q, k, v, do, mask, seg))
-    ids = oatt.bidirectional_ids(mask, seg)
-    valid = oatt.valid_from_ids(*ids[:4])
-    t0 = time.perf_counter()
-    oatt.attention_forward(q, k, v, valid, ids[4], np.float32)
-    oatt.attention_backward(q, k, v, valid, ids[4], do, np.float32)
-    dt = time.perf_counter() - t0
-    flops = 3.5 * 4.0 * cfg.heads * cfg.head_dim * workloads.segment_square_sum(seg)
-    return flops / dt / 1e12, dt, f"config-2 rows 0..{rows - 1} (B={rows} of 8, T=2048, 16/8 heads), FP32 NumPy"
+    inputs = workloads.attention_inputs(cfg, 0)
+    dt, flops = 0.0, 0.0
+    for lo in range(0, rows, chunk):
+        q, k, v, do, mask, seg = (x[lo:min(rows, lo + chunk)] for x in inputs)
+        ids = oatt.bidirectional_ids(mask, seg)
+        valid = oatt.valid_from_ids(*ids[:4])
+        t0 = time.perf_counter()
+        oatt.attention_forward(q, k, v, valid, ids[4], np.float32)
+        oatt.attention_backward(q, k, v, valid, ids[4], do, np.float32)
+        dt += time.perf_counter() - t0
+        flops += 3.5 * 4.0 * cfg.heads * cfg.head_dim * workloads.segment_square_sum(seg)
+    what = "the whole batch" if rows == cfg.batch else f"rows 0..{rows - 1}"
+    return flops / dt / 1e12, dt, f"config-2 {what} (B={rows} of {cfg.batch}, T=2048, 16/8 heads), FP32 NumPy"
 
 
 def run_reference(args, dist):
@@ -760,8 +764,8 @@ def run_ours(args, dist):
         del enc
     line["clocks"] = clocks.stop()
 
-    if dist.rank == 0 and not args.no_cpu_baseline and only in (None, "attention"):
-        v, dt, sample = cpu_attention_sample(2)
+    if dist.world == 1 and not args.no_cpu_baseline and only in (None, "attention"):
+        v, dt, sample = cpu_attention_sample(workloads.CONFIG2.batch)
         line["cpu_baseline"] = {"value": v, "unit": UNIT,
                                 "cores": int(os.environ.get("OPENBLAS_NUM_THREADS", os.cpu_count() or 1)),
                                 "kind": "port", "sample": sample + f" ({dt:.1f} s)"}
