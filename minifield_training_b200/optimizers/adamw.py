@@ -43,9 +43,45 @@ class CommitCode(enum.IntEnum):
     CANDIDATE_INVALID = 6
 
 
+_F32_MAX = float(np.finfo(np.float32).max)
+_F32_TINY = float(np.finfo(np.float32).tiny)
+
+# Admission of one setting as a float32 scalar: (test on the Python value,
+# what the value must be). The first failing test names the error, so the
+# order is the precedence of the messages (adamw.py:53-93 of the reference).
+_SCALAR_RULES = (
+    (lambda x: not isinstance(x, bool) and isinstance(x, (int, float)), "a non-boolean finite number"),
+    (lambda x: math.isfinite(float(x)) and abs(float(x)) <= _F32_MAX, "a finite float32 scalar"),
+    (lambda x: not float(x) or float(np.float32(x)) != 0, "representable in float32"),
+    (lambda x: not float(np.float32(x)) or abs(float(np.float32(x))) >= _F32_TINY,
+     "zero or a normal float32 scalar"),
+)
+
+# Range of each setting once rounded to float32, checked only after every
+# setting passed the scalar rules; fields in declaration order.
+_RANGE_RULES = {
+    "learning_rate": (lambda x: x > 0, "positive"),
+    "beta1": (lambda x: 0 <= x < 1, "in [0, 1)"),
+    "beta2": (lambda x: 0 <= x < 1, "in [0, 1)"),
+    "epsilon": (lambda x: x > 0, "positive"),
+    "weight_decay": (lambda x: x >= 0, "nonnegative"),
+    "clip_norm": (lambda x: x > 0, "positive"),
+}
+
+
+def _first_broken(rules, value):
+    """The requirement text of the first rule ``value`` fails, or None."""
+    return next((what for test, what in rules if not test(value)), None)
+
+
 @dataclasses.dataclass(frozen=True)
 class AdamWConfig:
-    """Validated float32 settings (adamw.py:42-92)."""
+    """Validated float32 settings (adamw.py:42-92).
+
+    Every setting is stored as the float32 value the update uses. A bad
+    setting raises the reference's ``ValueError`` text ("<name> must be ...");
+    scalar problems of any field are reported before range problems.
+    """
 
     learning_rate: float
     beta1: float = 0.9
@@ -55,33 +91,17 @@ class AdamWConfig:
     clip_norm: float = 1.0
 
     def __post_init__(self):
-        converted = {}
-        for name in ("learning_rate", "beta1", "beta2", "epsilon", "weight_decay", "clip_norm"):
-            value = getattr(self, name)
-            if isinstance(value, bool) or not isinstance(value, (int, float)):
-                raise ValueError(f"{name} must be a non-boolean finite number")
-            number = float(value)
-            if not math.isfinite(number) or abs(number) > float(np.finfo(np.float32).max):
-                raise ValueError(f"{name} must be a finite float32 scalar")
-            effective = float(np.float32(number))
-            if number and effective == 0:
-                raise ValueError(f"{name} must be representable in float32")
-            if effective and abs(effective) < float(np.finfo(np.float32).tiny):
-                raise ValueError(f"{name} must be zero or a normal float32 scalar")
-            converted[name] = effective
-        if converted["learning_rate"] <= 0:
-            raise ValueError("learning_rate must be positive")
-        if not 0 <= converted["beta1"] < 1:
-            raise ValueError("beta1 must be in [0, 1)")
-        if not 0 <= converted["beta2"] < 1:
-            raise ValueError("beta2 must be in [0, 1)")
-        if converted["epsilon"] <= 0:
-            raise ValueError("epsilon must be positive")
-        if converted["weight_decay"] < 0:
-            raise ValueError("weight_decay must be nonnegative")
-        if converted["clip_norm"] <= 0:
-            raise ValueError("clip_norm must be positive")
-        for name, value in converted.items():
+        raw = {name: getattr(self, name) for name in _RANGE_RULES}
+        problems = ((name, _first_broken(_SCALAR_RULES, value)) for name, value in raw.items())
+        problems = [(name, what) for name, what in problems if what is not None]
+        if problems:
+            name, what = problems[0]
+            raise ValueError(f"{name} must be {what}")
+        rounded = {name: float(np.float32(value)) for name, value in raw.items()}
+        for name, (test, what) in _RANGE_RULES.items():
+            if not test(rounded[name]):
+                raise ValueError(f"{name} must be {what}")
+        for name, value in rounded.items():
             object.__setattr__(self, name, value)
 
 

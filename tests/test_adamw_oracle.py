@@ -174,3 +174,48 @@ def test_eight_replica_data_parallel_step():
     np.testing.assert_allclose(new["v"]["weight"], 61.25, rtol=1e-6)
     np.testing.assert_allclose(new["params"]["weight"], 1.9, rtol=1e-6)
     assert new["params"]["bias"] == 1 and new["m"]["bias"] == 0 and new["v"]["bias"] == 0
+
+
+_CONFIG_REJECTIONS = [
+    # The reference's own cases (tests/optimizers/test_adamw.py:481-496) ...
+    ({"learning_rate": 0.0}, "learning_rate must be positive"),
+    ({"learning_rate": 0.1, "beta1": 1.0}, "beta1 must be in [0, 1)"),
+    ({"learning_rate": 0.1, "epsilon": 0.0}, "epsilon must be positive"),
+    ({"learning_rate": 0.1, "weight_decay": -0.1}, "weight_decay must be nonnegative"),
+    ({"learning_rate": 0.1, "clip_norm": 0.0}, "clip_norm must be positive"),
+    ({"learning_rate": float("nan")}, "learning_rate must be a finite float32 scalar"),
+    ({"learning_rate": True}, "learning_rate must be a non-boolean finite number"),
+    # ... and the remaining branches of its validation (optimizers/adamw.py:53-93).
+    ({"learning_rate": "0.1"}, "learning_rate must be a non-boolean finite number"),
+    ({"learning_rate": 1e39}, "learning_rate must be a finite float32 scalar"),
+    ({"learning_rate": float("inf")}, "learning_rate must be a finite float32 scalar"),
+    ({"learning_rate": 1e-50}, "learning_rate must be representable in float32"),
+    ({"learning_rate": 1e-40}, "learning_rate must be zero or a normal float32 scalar"),
+    ({"learning_rate": 0.1, "beta2": -0.5}, "beta2 must be in [0, 1)"),
+    ({"learning_rate": 0.1, "beta2": 1.0}, "beta2 must be in [0, 1)"),
+    ({"learning_rate": -1.0, "clip_norm": False}, "clip_norm must be a non-boolean finite number"),
+    ({"learning_rate": 0.1, "beta1": 1.5, "epsilon": float("nan")}, "epsilon must be a finite float32 scalar"),
+    ({"learning_rate": -1.0, "beta1": 2.0}, "learning_rate must be positive"),
+    ({"learning_rate": 0.1, "beta1": 0.99999999999}, "beta1 must be in [0, 1)"),
+]
+
+
+@pytest.mark.parametrize("kwargs,message", _CONFIG_REJECTIONS)
+def test_adamw_config_rejects_with_the_reference_messages(kwargs, message):
+    """Each bad setting raises the reference's exact ValueError text; scalar problems of any
+    field come before range problems, and fields are checked in declaration order."""
+    from minifield_training_b200.optimizers.adamw import AdamWConfig
+
+    with pytest.raises(ValueError) as err:
+        AdamWConfig(**kwargs)
+    assert str(err.value) == message
+
+
+def test_adamw_config_stores_float32_values():
+    from minifield_training_b200.optimizers.adamw import AdamWConfig
+
+    c = AdamWConfig(learning_rate=3e-4, beta2=0.95, weight_decay=0, epsilon=1e-8, clip_norm=1)
+    for name in ("learning_rate", "beta1", "beta2", "epsilon", "weight_decay", "clip_norm"):
+        value = getattr(c, name)
+        assert isinstance(value, float) and value == float(np.float32(value)), name
+    assert c.learning_rate == float(np.float32(3e-4)) and c.weight_decay == 0.0
