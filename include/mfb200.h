@@ -59,6 +59,10 @@ int mfb_stream_create(void** stream);
 int mfb_stream_destroy(void* stream);
 int mfb_stream_sync(void* stream);
 int mfb_device_sync(void);
+/* Ends this process's context on the current device (cudaDeviceReset): every
+ * device pointer, stream, event and graph of it becomes invalid. Other
+ * processes on the GPU are not affected. */
+int mfb_device_reset(void);
 int mfb_event_create(void** event);
 int mfb_event_destroy(void* event);
 int mfb_event_record(void* event, void* stream);
@@ -169,9 +173,12 @@ int mfb_decode_attn(const uint16_t* q, uint16_t* k_cache, uint16_t* v_cache, con
  * (every GPU that loads the library holds it until the process exits);
  * shapes needing more (mfb_decode_workspace_size > the maximum; B=64 rows
  * of 16 query heads need about 4.6 MB at any capacity) are rejected with
- * MFB_ERR_INVALID. The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress) with that device current; make that first
- * call before any stream capture. Every call on a device shares the one array
+ * MFB_ERR_INVALID. The first call in each CUDA context of a device looks up
+ * the array's device address (cudaGetSymbolAddress) with that device
+ * current, and caches it under the context's unique ID; a context destroyed
+ * and re-created (cudaDeviceReset, mfb_device_reset) gets a new ID, so the
+ * first call after it looks the address up again. Make the first call of each
+ * context before any stream capture. Every call on a device shares the one array
  * and leaves its contents behind (each call clears the parts that must start
  * at zero), so calls that overlap on the GPU -- concurrent streams, or host
  * threads on one device -- race and must be serialised by the caller. No

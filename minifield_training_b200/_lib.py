@@ -54,6 +54,7 @@ SIGNATURES = {
     "mfb_stream_destroy": (I, [P]),
     "mfb_stream_sync": (I, [P]),
     "mfb_device_sync": (I, []),
+    "mfb_device_reset": (I, []),
     "mfb_event_create": (I, [ctypes.POINTER(P)]),
     "mfb_event_destroy": (I, [P]),
     "mfb_event_record": (I, [P, P]),

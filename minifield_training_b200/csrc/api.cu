@@ -130,6 +130,11 @@ int mfb_device_sync(void) {
   return MFB_OK;
 }
 
+int mfb_device_reset(void) {
+  MFB_CUDA_TRY(cudaDeviceReset());
+  return MFB_OK;
+}
+
 int mfb_event_create(void** event) {
   MFB_CHECK_ARG(event != nullptr, "event is NULL");
   cudaEvent_t e;

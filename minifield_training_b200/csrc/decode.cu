@@ -30,6 +30,9 @@
 #include <math.h>
 
 #include <algorithm>
+#include <mutex>
+
+#include <cudaTypedefs.h>
 
 #include "common.cuh"
 #include "tc.cuh"
@@ -588,10 +591,61 @@ namespace dec {
 // device that loads the library, held until the process exits.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[MFB_DECODE_NOALLOC_SCRATCH_BYTES];
 
-// Device address of g_noalloc_scratch per device ordinal, resolved once per
-// device with that device current (the host-side symbol is only a stand-in).
+// Device address of g_noalloc_scratch per device ordinal, with the unique ID
+// of the CUDA context it was resolved in (the host-side symbol is only a
+// stand-in). A context that is destroyed and re-created -- cudaDeviceReset,
+// or the primary context released and retained again -- loads the library's
+// module again at another address, so the cached address is only used while
+// the calling thread's current context has the same ID; otherwise it is
+// looked up again. Slots are read and written under g_noalloc_mutex.
 constexpr int kMaxDevices = 64;
-static void* g_noalloc_ptr[kMaxDevices] = {nullptr};
+struct NoallocSlot {
+  unsigned long long context_id;
+  void* ptr;
+};
+static NoallocSlot g_noalloc_slot[kMaxDevices] = {};
+static std::mutex g_noalloc_mutex;
+
+// Unique ID of the calling thread's current context (cuCtxGetId never reuses
+// an ID within a process), or 0 when there is none or the driver cannot say.
+static unsigned long long current_context_id() {
+  static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+  static PFN_cuCtxGetId_v12000 get_id = nullptr;
+  static std::once_flag resolved;
+  std::call_once(resolved, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// The scratch array's device address in the current context of device dev.
+static int noalloc_scratch(int dev, void** out) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  NoallocSlot& slot = g_noalloc_slot[dev];
+  unsigned long long id = current_context_id();
+  if (slot.ptr == nullptr || id == 0 || slot.context_id != id) {
+    void* ptr = nullptr;
+    MFB_CUDA_TRY(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+    // The lookup makes the device's primary context current if none was, so
+    // read the ID again for the record.
+    slot.context_id = id ? id : current_context_id();
+    slot.ptr = ptr;
+  }
+  *out = slot.ptr;
+  return MFB_OK;
+}
 
 }  // namespace dec
 }  // namespace mfb
@@ -610,14 +664,11 @@ extern "C" int mfb_decode_attn_noalloc(const uint16_t* q, uint16_t* k_cache, uin
   int dev = 0;
   MFB_CUDA_TRY(cudaGetDevice(&dev));
   MFB_CHECK_ARG(dev >= 0 && dev < dec::kMaxDevices, "device ordinal %d out of range", dev);
-  if (dec::g_noalloc_ptr[dev] == nullptr) {
-    void* ptr = nullptr;
-    MFB_CUDA_TRY(cudaGetSymbolAddress(&ptr, dec::g_noalloc_scratch));
-    dec::g_noalloc_ptr[dev] = ptr;
-  }
+  void* scratch = nullptr;
+  if ((st = dec::noalloc_scratch(dev, &scratch))) return st;
   // The array keeps the previous call's contents; the run clears the per-row
   // tickets, which must start at zero, before the launch.
-  const dec::Workspace w = dec::carve(dec::g_noalloc_ptr[dev], B, H);
+  const dec::Workspace w = dec::carve(scratch, B, H);
   return dec::run(q, k_cache, v_cache, new_k, new_v, positions, valid_length, o, B, capacity, H, Hk, scale, w,
                   (cudaStream_t)stream);
 }

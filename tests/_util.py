@@ -41,3 +41,30 @@ def header_functions():
             text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
             names += re.findall(r"\b(mfb_\w+)\s*\(", text)
     return sorted(set(names))
+
+
+def run_ranks(ctx, target, args_per_rank, timeout_s):
+    """Run one child process per rank and wait for all of them, bounded.
+
+    Every rank shares one deadline. A rank still alive at the deadline is
+    killed (and reaped), so a stalled rank fails this test instead of keeping
+    its GPU context and blocking the interpreter's exit; the assertion names
+    the ranks that timed out or exited nonzero.
+    """
+    import time
+
+    procs = [ctx.Process(target=target, args=args) for args in args_per_rank]
+    for p in procs:
+        p.start()
+    deadline = time.monotonic() + timeout_s
+    try:
+        for p in procs:
+            p.join(max(0.0, deadline - time.monotonic()))
+    finally:
+        hung = [r for r, p in enumerate(procs) if p.is_alive()]
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+                p.join(5)
+    failed = [(r, p.exitcode) for r, p in enumerate(procs) if p.exitcode != 0 and r not in hung]
+    assert not hung and not failed, f"ranks timed out after {timeout_s} s: {hung}; ranks failed (exit code): {failed}"

@@ -18,6 +18,7 @@ import torch.multiprocessing as mp
 from minifield_training_b200 import workloads
 from minifield_training_b200.models import encoder as me
 from minifield_training_b200.optimizers import adamw
+from tests._util import run_ranks
 
 TINY = dataclasses.replace(workloads.CONFIG5, global_batch=2, length=128, ffn=256,
                            layer_types=("conv", "full_attention", "conv"), vocab=1000)
@@ -71,12 +72,7 @@ def test_bucketed_allreduce_equals_full_allreduce_on_two_gloo_ranks():
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
     port = 29400 + os.getpid() % 500
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, out)) for r in range(2)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(120)
-        assert p.exitcode == 0
+    run_ranks(ctx, _worker, [(r, 2, port, out) for r in range(2)], 120)
     assert out[0] == 0.0 and out[1] == 0.0
 
 

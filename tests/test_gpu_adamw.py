@@ -12,6 +12,7 @@ import numpy as np
 import pytest
 
 from oracle import adamw as oa
+from tests._util import run_ranks
 from tests.gpu_env import require_gpu
 
 pytestmark = pytest.mark.gpu
@@ -232,10 +233,7 @@ def test_sharded_transaction_on_one_rank_matches_the_full_one():
 
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
-    p = ctx.Process(target=_sharded_vs_full, args=(out, 29400 + os.getpid() % 300))
-    p.start()
-    p.join(240)
-    assert p.exitcode == 0
+    run_ranks(ctx, _sharded_vs_full, [(out, 29400 + os.getpid() % 300)], 240)
     for bad, (res, arenas) in out["results"].items():
         full, sharded = res
         assert full[0] == sharded[0] and full[1] == sharded[1], (bad, full, sharded)

@@ -17,6 +17,7 @@ import os
 import numpy as np
 import pytest
 
+from tests._util import run_ranks
 from tests.gpu_env import require_gpu
 
 pytestmark = pytest.mark.gpu
@@ -101,12 +102,7 @@ def test_two_rank_step_matches_one_gpu(shard):
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
     port = 29600 + os.getpid() % 300
-    procs = [ctx.Process(target=_rank, args=(r, port, out, shard)) for r in range(2)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(300)
-        assert p.exitcode == 0
+    run_ranks(ctx, _rank, [(r, port, out, shard) for r in range(2)], 300)
     # One GPU over both rows.
     from minifield_training_b200 import workloads
     from minifield_training_b200.device import sync
@@ -143,12 +139,7 @@ def test_two_rank_graph_steps_stay_replicated_and_match_eager():
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
     port = 29900 + os.getpid() % 50
-    procs = [ctx.Process(target=_rank_graph, args=(r, port, out)) for r in range(2)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(300)
-        assert p.exitcode == 0
+    run_ranks(ctx, _rank_graph, [(r, port, out) for r in range(2)], 300)
     (l0, p0), (l1, p1) = out[0], out[1]
     assert all(c for c, _ in l0) and l0 == l1
     for name in p0:

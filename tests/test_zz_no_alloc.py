@@ -86,3 +86,43 @@ def test_noalloc_rejects_shapes_beyond_the_fixed_scratch():
     ptrs = [ctypes.c_void_p(dummy.ptr)] * 8
     with pytest.raises(ValueError, match="scratch bytes"):
         _lib.call("mfb_decode_attn_noalloc", *ptrs, b, cap, h, 8, 64, ctypes.c_float(0.125), None)
+
+
+_RESET_CHILD = r"""
+import sys
+import numpy as np
+sys.path.insert(0, {root!r})
+from minifield_training_b200 import _lib, device
+from tests import test_zz_no_alloc as t
+from tests._util import assert_close
+
+device.set_device(0)
+b, cap = 8, 512
+rng = np.random.default_rng(5)
+for round_ in range(2):
+    q, kc, vc, nk, nv = t._inputs(10 + round_, b, cap)
+    lens = rng.integers(1, cap + 1, size=b).astype(np.int32)
+    pos = (lens - 1).astype(np.int32)
+    ref = t._decode("mfb_decode_attn", q, kc, vc, nk, nv, pos, lens)
+    got = t._decode("mfb_decode_attn_noalloc", q, kc, vc, nk, nv, pos, lens)
+    assert_close(got[0], ref[0], what=f"no-alloc context {{round_}}")
+    np.testing.assert_array_equal(got[1], ref[1])
+    np.testing.assert_array_equal(got[2], ref[2])
+    if round_ == 0:
+        _lib.call("mfb_device_reset")  # every device buffer above is already freed
+print("ok")
+"""
+
+
+def test_noalloc_after_a_device_reset_uses_the_new_context():
+    """A reset destroys the context the scratch address was looked up in; the next call must
+    look it up again in the new context. Runs in a child process, so the reset touches no
+    buffer of the other tests."""
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", _RESET_CHILD.format(root=root)], cwd=root, capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-2000:]
