@@ -51,7 +51,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-secondary", action="store_true", help="skip the decode / QAT secondary measurements")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["attention", "decode", "decode_one", "qat", "encoder"], default=None,
+    ap.add_argument("--only", choices=["attention", "attention_cfg1", "decode", "decode_one", "qat", "encoder"],
+                    default=None,
                     help="run one workload (profiling); the JSON line then carries only its numbers")
     return ap.parse_args()
 
@@ -262,6 +263,31 @@ class AttentionWorkload:
 
     launches_per_step = 9  # ids, ranges, schedule, fwd, ranges, schedule, bwd-pre, bwd-main, dq-convert
 
+    def capture_graphs(self):
+        """Capture the step, the forward alone and the backward alone as CUDA graphs on a created
+        stream (config 1 is launch-latency bound: 9 small launches per step)."""
+        sp = ctypes.c_void_p()
+        self.L.call("mfb_stream_create", ctypes.byref(sp))
+        self.stream = sp.value
+        self.ids()  # host outputs (causal, offset, policy) set before capture
+        self.graphs = {}
+        for name, fn in (("step", self.step), ("fwd", self.fwd), ("bwd", self.bwd)):
+            self.L.call("mfb_graph_begin", self.stream)
+            fn()
+            g = ctypes.c_void_p()
+            self.L.call("mfb_graph_end", self.stream, ctypes.byref(g))
+            self.graphs[name] = g.value
+
+    def replay(self, name):
+        self.L.call("mfb_graph_launch", self.graphs[name], self.stream)
+
+    def release_graphs(self):
+        self.L.call("mfb_stream_sync", self.stream)
+        for g in self.graphs.values():
+            self.L.call("mfb_graph_destroy", g)
+        self.L.call("mfb_stream_destroy", self.stream)
+        self.graphs, self.stream = {}, None
+
     def e2e_setup(self):
         """Pinned host buffers, a second device buffer set and three streams.
 
@@ -440,13 +466,14 @@ class DecodeOneWorkload:
 class QatWorkload:
     """Config 4: int8 fake-quant + SwiGLU FFN GEMM chain forward + backward."""
 
-    def __init__(self, seed):
+    def __init__(self, seed, kind=None):
         from minifield_training_b200 import _lib, workloads
         from minifield_training_b200.device import DeviceArray
 
         self.L = _lib
         cfg = workloads.CONFIG4
         self.cfg = cfg
+        self.kind_name = kind or cfg.kind
         x, w_gu, w_d, dy = workloads.qat_inputs(cfg, seed)
         dev = DeviceArray.from_numpy
         m, c, f = cfg.tokens, cfg.hidden, cfg.ffn
@@ -463,7 +490,7 @@ class QatWorkload:
         self.dx = DeviceArray((m, c), "bfloat16")
         self.dw_gu = DeviceArray((2 * f, c), "float32")
         self.dw_d = DeviceArray((c, f), "float32")
-        self.kind = _lib.QUANT_KINDS[cfg.kind]
+        self.kind = _lib.QUANT_KINDS[self.kind_name]
         self.flops = 3.0 * (2.0 * m * c * 2 * f + 2.0 * m * f * c)
 
     def gemm(self, a, am, lda, b, bm, ldb, c, ldc, dt, m, n, k, mask=None):
@@ -564,50 +591,137 @@ class EncoderStepWorkload:
         return count[0]
 
 
-def cpu_attention_sample(rows=2, chunk=2):
-    """Time the oracle's FP32 forward+backward on ``rows`` rows of config 2, ``chunk`` rows at a time
-    (a chunk's score grids take about 2.5 GB)."""
+def _cores():
+    return int(os.environ.get("OPENBLAS_NUM_THREADS", os.cpu_count() or 1))
+
+
+def _cpu_line(value, unit, sample, seconds):
+    return {"value": value, "unit": unit, "cores": _cores(), "kind": "port",
+            "sample": f"{sample} ({seconds:.1f} s of CPU work)"}
+
+
+def cpu_attention_sample(cfg=None, rows=None, chunk=2):
+    """Time the oracle's FP32 forward+backward over ``rows`` rows of an attention config (default:
+    config 2, the whole batch), ``chunk`` rows at a time (a config-2 chunk's score grids take
+    about 2.5 GB). Returns (TFLOP/s, seconds, sample text)."""
     from minifield_training_b200 import workloads
     from oracle import attention as oatt
 
-    cfg = workloads.CONFIG2
+    cfg = cfg or workloads.CONFIG2
+    rows = cfg.batch if rows is None else rows
     inputs = workloads.attention_inputs(cfg, 0)
     dt, flops = 0.0, 0.0
     for lo in range(0, rows, chunk):
-        q, k, v, do, mask, seg = (x[lo:min(rows, lo + chunk)] for x in inputs)
-        ids = oatt.bidirectional_ids(mask, seg)
+        q, k, v, do, mask = (x[lo:min(rows, lo + chunk)] for x in inputs[:5])
+        seg = inputs[5][lo:min(rows, lo + chunk)] if inputs[5] is not None else None
+        ids = oatt.bidirectional_ids(mask, seg) if cfg.packed else oatt.causal_ids(mask)
         valid = oatt.valid_from_ids(*ids[:4])
         t0 = time.perf_counter()
         oatt.attention_forward(q, k, v, valid, ids[4], np.float32)
         oatt.attention_backward(q, k, v, valid, ids[4], do, np.float32)
         dt += time.perf_counter() - t0
-        flops += 3.5 * 4.0 * cfg.heads * cfg.head_dim * workloads.segment_square_sum(seg)
+        flops += 3.5 * 4.0 * cfg.heads * cfg.head_dim * oatt.valid_pair_count(*ids[:4])
     what = "the whole batch" if rows == cfg.batch else f"rows 0..{rows - 1}"
-    return flops / dt / 1e12, dt, f"config-2 {what} (B={rows} of {cfg.batch}, T=2048, 16/8 heads), FP32 NumPy"
+    return flops / dt / 1e12, dt, (f"{cfg.name} {what} (B={rows} of {cfg.batch}, T={cfg.length}, "
+                                   f"{cfg.heads}/{cfg.kv_heads} heads), FP32 NumPy, {chunk} rows at a time")
+
+
+def cpu_decode_sample(layers=2):
+    """Config 3 on the oracle in FP32: the append + cached attention of ``layers`` of the 6 layers over
+    all 64 rows, scaled to the 6-layer step. Returns (tokens/s, GB/s, seconds, sample text)."""
+    from minifield_training_b200 import workloads
+    from oracle import decode as odec
+
+    cfg = workloads.CONFIG3
+    lens = workloads.decode_lengths(cfg, 0)
+    dt = 0.0
+    for layer in range(layers):
+        q, kc, vc, nk, nv = workloads.decode_layer_inputs(cfg, 0, layer)
+        t0 = time.perf_counter()
+        odec.decode_attention(q, kc, vc, lens, nk, nv, lens - 1, np.float32)
+        dt += time.perf_counter() - t0
+    step = dt * cfg.layers / layers
+    nbytes = cfg.layers * workloads.decode_layer_bytes(lens, cfg)
+    return cfg.batch / step, nbytes / step / 1e9, dt, (
+        f"{cfg.name}: {layers} of {cfg.layers} layers over all {cfg.batch} rows, scaled to the 6-layer step; "
+        "FP32 NumPy (the reference's dense cached attention reads every cache slot, then masks)")
+
+
+def cpu_qat_sample(kind, tokens=256):
+    """Config 4 on the oracle in FP32: fake-quant of both weights once, then the GEMM chain forward +
+    backward on ``tokens`` of the 16384 rows, scaled by rows. Returns (TFLOP/s, tokens/s, seconds, text)."""
+    from minifield_training_b200 import workloads
+    from oracle import linear as olin
+
+    cfg = workloads.CONFIG4
+    x, w_gu, w_d, dy = workloads.qat_inputs(cfg, 0, tokens=tokens)
+    t0 = time.perf_counter()
+    olin.qat_weights(w_gu, w_d, kind)
+    t_quant = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    olin.swiglu_qat_step(x, w_gu, w_d, kind, dy, np.float32)  # quantizes again, then the chain
+    t_chain = max(time.perf_counter() - t0 - t_quant, 1e-9)
+    step = t_quant + t_chain * cfg.tokens / tokens
+    flops = 3.0 * olin.ffn_flops(cfg.tokens, cfg.hidden, cfg.ffn)
+    return flops / step / 1e12, cfg.tokens / step, t_quant * 2 + t_chain, (
+        f"{cfg.name} {kind}: both weights fake-quantized once + the chain on {tokens} of {cfg.tokens} "
+        "tokens, scaled by rows; FP32 NumPy")
+
+
+def cpu_encoder_sample():
+    """Config 5 on the oracle (torch autograd on the CPU, FP32): loss and gradients of one 2048-token
+    row through a conv layer and an attention layer at the full hidden/FFN widths, with int8 fake-quant,
+    scaled by FLOPs to the 16-layer step over the 32-row global batch. Returns (tokens/s, TFLOP/s,
+    seconds, text)."""
+    import dataclasses
+
+    import torch
+
+    from minifield_training_b200 import workloads
+    from minifield_training_b200.models import encoder as me
+    from oracle import encoder_step as oes
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    full = workloads.CONFIG5
+    sub = dataclasses.replace(full, global_batch=1, layer_types=("conv", "full_attention"))
+    params = me.init_parameters(sub, 0)
+    batch = workloads.encoder_batch(sub, 0, rows=1)
+    t0 = time.perf_counter()
+    oes.loss_and_grads(sub, params, *batch, rows=1, compute_dtype=torch.float32)
+    dt = time.perf_counter() - t0
+    sub_flops = workloads.encoder_step_flops(sub, batch[2])
+    full_flops = workloads.encoder_step_flops(full, workloads.packed_segments(0, full.global_batch, full.length))
+    step = dt * full_flops / sub_flops
+    tokens = full.global_batch * full.length
+    return tokens / step, full_flops / step / 1e12, dt, (
+        f"{full.name}: 1 row x {full.length} tokens through 2 of the 16 layers (conv + attention; hidden "
+        f"{full.hidden}, FFN {full.ffn}, int8 fake-quant) forward + backward, torch autograd FP32 on the CPU, "
+        "scaled by FLOPs to the 16-layer 32 x 2048 step")
 
 
 def run_reference(args, dist):
+    """The reference algorithm's CPU restatement on the headline config: each step is the whole
+    config-2 batch (8 rows, two at a time), as the GPU arm's step."""
     if dist.rank != 0:
         return 0
-    cores = int(os.environ.get("OPENBLAS_NUM_THREADS", os.cpu_count() or 1))
     for _ in range(max(0, min(args.warmup, 1))):
-        cpu_attention_sample(1)
-    vals = []
-    t0 = time.perf_counter()
+        cpu_attention_sample(rows=2)
+    vals, walls = [], []
     for _ in range(args.steps):
-        v, _, sample = cpu_attention_sample(1)
+        t0 = time.perf_counter()
+        v, _, sample = cpu_attention_sample()
+        walls.append(time.perf_counter() - t0)
         vals.append(v)
-    wall = time.perf_counter() - t0
     value = float(np.median(vals))
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall / args.steps * 1e3,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": float(np.mean(walls)) * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "cfg2-segment-bidirectional-gqa-fwd-bwd", "batch": 8, "seq_len": 2048, "heads": 16,
-                   "kv_heads": 8, "head_dim": 64, "sample": "1 row per step"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": sample.replace("rows 0..0", "row 0") + "; reference is JAX (not installed): "
-                                   "NumPy restatement of its algorithm"},
+                   "kv_heads": 8, "head_dim": 64, "sample": "the whole batch per step"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": _cores(), "kind": "port",
+                         "sample": sample + "; the reference is JAX (not installed): NumPy restatement of its "
+                                            "algorithm"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -646,6 +760,28 @@ def measure(dist, fn, steps, warmup, clocks=None, stream=None, end_stream=None):
     return dist.max(ms), clk
 
 
+def attention_roofline(att, fwd_ms, bwd_ms, tf_burst, peak_kind, traffic):
+    """Roofline entry of the slower attention kernel (forward or backward), each timed alone."""
+    if bwd_ms >= fwd_ms:
+        dom, dom_ms, dom_flops = "attn_bwd", bwd_ms, 2.5 * att.fwd_flops
+    else:
+        dom, dom_ms, dom_flops = "attn_fwd", fwd_ms, att.fwd_flops
+    achieved = dom_flops / (dom_ms * 1e-3) / 1e12
+    return {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s",
+            "frac": achieved / tf_burst, "peak_source": f"{peak_kind} bf16 burst", "traffic": traffic.get(dom),
+            "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "fwd_tflops": att.fwd_flops / (fwd_ms * 1e-3) / 1e12,
+            "bwd_tflops": 2.5 * att.fwd_flops / (bwd_ms * 1e-3) / 1e12}
+
+
+def attention_e2e(att, dist, steps, n):
+    """Pipelined end-to-end leg through the C ABI with pinned host buffers (see e2e_setup)."""
+    att.e2e_setup()
+    e2e_ms, _ = measure(dist, att.e2e_step, max(8, steps // 2), 2, stream=att.s_in, end_stream=att.s_out)
+    att.e2e_close()
+    return {"value": n * att.total_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
+            "h2d_bytes_per_step": att.h2d_bytes, "d2h_bytes_per_step": att.d2h_bytes, "ms_per_step": e2e_ms}
+
+
 def run_ours(args, dist):
     from minifield_training_b200 import device, workloads
 
@@ -657,6 +793,7 @@ def run_ours(args, dist):
     only = args.only
     clocks = Clocks(dist.local)
     clocks.start()  # sampled across every timed phase below
+    cpu_legs = dist.world == 1 and not args.no_cpu_baseline
 
     line = {"metric": METRIC, "unit": UNIT, "n_gpus": n, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic"}
@@ -670,22 +807,9 @@ def run_ours(args, dist):
         timer = Timer()
         fwd_ms = dist.max(timer.time(att.fwd, args.steps))
         bwd_ms = dist.max(timer.time(att.bwd, args.steps))
-        if bwd_ms >= fwd_ms:
-            dom, dom_ms, dom_flops = "attn_bwd", bwd_ms, 2.5 * att.fwd_flops
-        else:
-            dom, dom_ms, dom_flops = "attn_fwd", fwd_ms, att.fwd_flops
-        achieved = dom_flops / (dom_ms * 1e-3) / 1e12
-        roofline = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s",
-                    "frac": achieved / tf_burst, "peak_source": f"{peak_kind} bf16 burst",
-                    "traffic": traffic.get(dom), "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
-                    "fwd_tflops": att.fwd_flops / (fwd_ms * 1e-3) / 1e12,
-                    "bwd_tflops": 2.5 * att.fwd_flops / (bwd_ms * 1e-3) / 1e12}
-        # End to end through the C ABI with pinned host buffers.
-        att.e2e_setup()
-        e2e_ms, _ = measure(dist, att.e2e_step, max(8, args.steps // 2), 2, stream=att.s_in, end_stream=att.s_out)
-        att.e2e_close()
-        e2e = {"value": n * att.total_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
-               "h2d_bytes_per_step": att.h2d_bytes, "d2h_bytes_per_step": att.d2h_bytes, "ms_per_step": e2e_ms}
+        launches += 3 * args.steps + 5 * args.steps
+        roofline = attention_roofline(att, fwd_ms, bwd_ms, tf_burst, peak_kind, traffic)
+        e2e = attention_e2e(att, dist, args.steps, n)
         line.update(value=value, ms_per_step=ms, tensor_peak_frac=value / n / tf_burst, roofline=roofline, e2e=e2e)
         line["config"] = {
             "workload": workloads.CONFIG2.name, "batch": 8, "seq_len": 2048, "heads": 16, "kv_heads": 8,
@@ -695,7 +819,25 @@ def run_ours(args, dist):
         del att
 
     secondary = {}
-    if only in (None, "decode") and not (only is None and args.no_secondary):
+    run_secondary = only is None and not args.no_secondary
+    if only == "attention_cfg1" or run_secondary:
+        # Config 1: dense causal B=4, T=512; tiny (7.5 GFLOP), so every timing replays CUDA graphs.
+        a1 = AttentionWorkload(workloads.CONFIG1, seed=dist.rank)
+        a1.capture_graphs()
+        ms1, _ = measure(dist, lambda: a1.replay("step"), args.steps, args.warmup, stream=a1.stream)
+        f1, _ = measure(dist, lambda: a1.replay("fwd"), args.steps, 2, stream=a1.stream)
+        b1, _ = measure(dist, lambda: a1.replay("bwd"), args.steps, 2, stream=a1.stream)
+        launches += (9 + 3 + 5) * args.steps
+        a1.release_graphs()
+        e2e1 = attention_e2e(a1, dist, args.steps, n)
+        tflops1 = n * a1.total_flops / (ms1 * 1e-3) / 1e12
+        secondary["attention_cfg1"] = {
+            "workload": workloads.CONFIG1.name, "batch": 4, "seq_len": 512, "heads": 16, "kv_heads": 8,
+            "head_dim": 64, "flops_per_step": a1.total_flops, "ms_per_step": ms1, "tflops": tflops1,
+            "tensor_frac": tflops1 / n / tf_burst, "graph": True,
+            "roofline": attention_roofline(a1, f1, b1, tf_burst, peak_kind, {}), "e2e": e2e1}
+        del a1
+    if only == "decode" or run_secondary:
         dec = DecodeWorkload(seed=dist.rank)
         dms, _ = measure(dist, dec.step, args.steps, args.warmup)
         gbs = dec.bytes / (dms * 1e-3) / 1e9
@@ -705,7 +847,7 @@ def run_ours(args, dist):
             "ms_per_step": dms, "hbm_gbs": gbs, "hbm_frac": gbs / hbm, "peak_gbs": hbm,
             "bytes_per_step": dec.bytes, "traffic": traffic.get("decode")}
         del dec
-    if only in (None, "decode_one") and not (only is None and args.no_secondary):
+    if only == "decode_one" or run_secondary:
         d1 = DecodeOneWorkload(seed=dist.rank)
         d1.prefill()  # warm-up prompt (allocates the prompt buffers, loads the kernels)
         d1.state = d1.dm.new_state(d1.cfg, d1.batch, d1.capacity)
@@ -730,18 +872,20 @@ def run_ours(args, dist):
             "graph": True, "kernels_per_step": d1.kernels_per_step()}
         d1.close()
         del d1
-    if only in (None, "qat") and not (only is None and args.no_secondary):
-        qat = QatWorkload(seed=dist.rank)
+    for kind, key in ((workloads.CONFIG4.kind, "qat"), ("int4-g128-absmax-v1", "qat_int4")):
+        if not (only == "qat" or run_secondary):
+            break
+        qat = QatWorkload(seed=dist.rank, kind=kind)
         qsteps = max(3, args.steps // 2)
         qms, _ = measure(dist, qat.step, qsteps, max(3, args.warmup // 2))
         launches += QatWorkload.launches_per_step * qsteps
-        secondary["qat"] = {
-            "workload": workloads.CONFIG4.name, "kind": workloads.CONFIG4.kind,
+        secondary[key] = {
+            "workload": workloads.CONFIG4.name, "kind": kind,
             "tokens_per_s": n * workloads.CONFIG4.tokens / (qms * 1e-3), "ms_per_step": qms,
             "tflops": qat.flops / (qms * 1e-3) / 1e12, "tensor_frac": qat.flops / (qms * 1e-3) / 1e12 / tf_sus,
             "peak_tflops": tf_sus, "peak_source": f"{peak_kind} bf16 sustained"}
         del qat
-    if only in (None, "encoder") and not (only is None and args.no_secondary):
+    if only == "encoder" or run_secondary:
         enc = EncoderStepWorkload(dist)
         esteps = max(3, args.steps // 5)
         per_step = enc.count_launches()  # one eager step, counting the kernels each call launches
@@ -764,11 +908,25 @@ def run_ours(args, dist):
         del enc
     line["clocks"] = clocks.stop()
 
-    if dist.world == 1 and not args.no_cpu_baseline and only in (None, "attention"):
-        v, dt, sample = cpu_attention_sample(workloads.CONFIG2.batch)
-        line["cpu_baseline"] = {"value": v, "unit": UNIT,
-                                "cores": int(os.environ.get("OPENBLAS_NUM_THREADS", os.cpu_count() or 1)),
-                                "kind": "port", "sample": sample + f" ({dt:.1f} s)"}
+    # CPU baselines: the oracle's restatement of the reference algorithm on this host's cores, rank 0 at
+    # N=1 only, each on a bounded sample of its config (after every GPU leg, outside their timing).
+    if cpu_legs:
+        if only in (None, "attention"):
+            v, dt, sample = cpu_attention_sample()
+            line["cpu_baseline"] = _cpu_line(v, UNIT, sample, dt)
+        if "attention_cfg1" in secondary:
+            v, dt, sample = cpu_attention_sample(workloads.CONFIG1)
+            secondary["attention_cfg1"]["cpu_baseline"] = _cpu_line(v, UNIT, sample, dt)
+        if "decode" in secondary:
+            tps, gbs, dt, sample = cpu_decode_sample()
+            secondary["decode"]["cpu_baseline"] = dict(_cpu_line(tps, "tokens/s", sample, dt), hbm_gbs=gbs)
+        for key in ("qat", "qat_int4"):
+            if key in secondary:
+                tf, tps, dt, sample = cpu_qat_sample(secondary[key]["kind"])
+                secondary[key]["cpu_baseline"] = dict(_cpu_line(tf, "TFLOP/s", sample, dt), tokens_per_s=tps)
+        if "encoder_step" in secondary:
+            tps, tf, dt, sample = cpu_encoder_sample()
+            secondary["encoder_step"]["cpu_baseline"] = dict(_cpu_line(tps, "tokens/s", sample, dt), tflops=tf)
     line["gpu_launches"] = launches
     line["secondary"] = secondary
     if dist.rank == 0:

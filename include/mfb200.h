@@ -355,6 +355,11 @@ int mfb_cast_f32_bf16(const float* x, uint16_t* y, long long n, void* stream);
 /* bf16 -> FP32 widening of n elements (the logits' .astype(float32),
  * src/minifield_training/models/lfm2_5/model.py:829). */
 int mfb_cast_bf16_f32(const uint16_t* x, float* y, long long n, void* stream);
+/* out = a + b over n bf16 elements, each sum rounded to nearest even: the
+ * residual adds of the attention block and the SwiGLU block
+ * (src/minifield_training/layers/attention.py:100-108,
+ * layers/feed_forward.py:35). n a multiple of 8; 16-byte aligned buffers. */
+int mfb_add_bf16(const uint16_t* a, const uint16_t* b, uint16_t* out, long long n, void* stream);
 
 #ifdef __cplusplus
 }

@@ -95,6 +95,7 @@ SIGNATURES = {
     "mfb_swiglu_bwd": (I, [P, P, P, I, I, P]),
     "mfb_cast_f32_bf16": (I, [P, P, ctypes.c_longlong, P]),
     "mfb_cast_bf16_f32": (I, [P, P, LL, P]),
+    "mfb_add_bf16": (I, [P, P, P, LL, P]),
     "mfb_conv_step": (I, [P, P, P, P, I, I, P]),
     "mfb_conv_causal": (I, [P, P, P, P, P, I, I, I, P]),
 }

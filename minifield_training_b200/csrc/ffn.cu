@@ -95,6 +95,17 @@ __global__ void cast_f32_bf16_kernel(const float* __restrict__ x, __nv_bfloat16*
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) y[i] = __float2bfloat16_rn(x[i]);
 }
+__global__ void add_bf16_kernel(const __nv_bfloat16* __restrict__ a, const __nv_bfloat16* __restrict__ b,
+                                __nv_bfloat16* __restrict__ out, long long n8) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  float x[8], y[8];
+  load8(a + 8 * i, x);
+  load8(b + 8 * i, y);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) x[e] += y[e];
+  store8(out + 8 * i, x);
+}
 __global__ void cast_bf16_f32_kernel(const __nv_bfloat16* __restrict__ x, float* __restrict__ y, long long n) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) y[i] = __bfloat162float(x[i]);
@@ -121,5 +132,20 @@ extern "C" int mfb_cast_bf16_f32(const uint16_t* x, float* y, long long n, void*
   cast_bf16_f32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(x), y, n);
   MFB_LAUNCH_CHECK("mfb_cast_bf16_f32");
+  return MFB_OK;
+}
+
+// bf16 residual add, each sum rounded to nearest even: the `x + hidden` and
+// `x + down(...)` of layers/attention.py:100-108 and layers/feed_forward.py:35.
+extern "C" int mfb_add_bf16(const uint16_t* a, const uint16_t* b, uint16_t* out, long long n, void* stream) {
+  MFB_CHECK_ARG(n >= 0 && n % 8 == 0, "bf16 add needs n a multiple of 8 (n=%lld)", n);
+  MFB_CHECK_ARG(n == 0 || (a && b && out), "NULL add argument");
+  MFB_CHECK_ARG(((uintptr_t)a | (uintptr_t)b | (uintptr_t)out) % 16 == 0, "bf16 add needs 16-byte aligned buffers");
+  if (n == 0) return MFB_OK;
+  const long long n8 = n / 8;
+  add_bf16_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(a), reinterpret_cast<const __nv_bfloat16*>(b),
+      reinterpret_cast<__nv_bfloat16*>(out), n8);
+  MFB_LAUNCH_CHECK("mfb_add_bf16");
   return MFB_OK;
 }

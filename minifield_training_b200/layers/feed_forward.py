@@ -10,11 +10,24 @@ epilogue. ``w_gate_up`` is [2F, C] (gate rows, then up rows), ``w_down`` is
 
 import ctypes
 from dataclasses import dataclass
+from typing import NamedTuple
 
 from .. import _lib
 from ..device import DeviceArray, as_device
 from ..kernels.linear import gemm_nn, gemm_nt, gemm_tn
 from ..kernels.quantization import effective_bf16
+
+
+class FeedForwardWeights(NamedTuple):
+    """Pre-norm gain and the three SwiGLU projection masters (feed_forward.py:11-21).
+
+    FP32 masters (host or device) or bf16 device arrays: gate and up [F, C], down [C, F].
+    """
+
+    norm: object
+    gate: object
+    up: object
+    down: object
 
 
 @dataclass

@@ -81,6 +81,49 @@ def _ffn_tail(P, p, x, r, eps):
     return rb(x + _linear(a, _w(P[p + "feed_forward.w2.weight"])))
 
 
+def _attention_block_rows(cfg, P, p, x, b, t):
+    """The causal attention block (layers/attention.py:111-138) over T tokens per row at positions 0..T-1:
+    (block output rows [B*T, C], RoPE'd keys [B, T, Hk, D], values [B, T, Hk, D])."""
+    eps, hd = cfg.norm_eps, cfg.head_dim
+    positions = np.tile(np.arange(t, dtype=np.int32), b)
+    h = _rms(x, P[p + "operator_norm.weight"], eps)
+    q = _linear(h, _w(P[p + "self_attn.q_proj.weight"])).reshape(b * t, cfg.heads, hd)
+    k = _linear(h, _w(P[p + "self_attn.k_proj.weight"])).reshape(b * t, cfg.kv_heads, hd)
+    v = _linear(h, _w(P[p + "self_attn.v_proj.weight"])).reshape(b * t, cfg.kv_heads, hd)
+    q = _rope(_rms(q, P[p + "self_attn.q_layernorm.weight"], eps), positions, cfg.rope_theta, hd)
+    k = _rope(_rms(k, P[p + "self_attn.k_layernorm.weight"], eps), positions, cfg.rope_theta, hd)
+    group = cfg.heads // cfg.kv_heads
+    q4 = q.reshape(b, t, cfg.heads, hd)
+    k4 = k.reshape(b, t, cfg.kv_heads, hd)
+    v4 = v.reshape(b, t, cfg.kv_heads, hd)
+    kk = torch.repeat_interleave(k4, group, dim=2)
+    vv = torch.repeat_interleave(v4, group, dim=2)
+    s = torch.einsum("bthd,bshd->bhts", q4, kk) * hd ** -0.5
+    causal = torch.tril(torch.ones(t, t, dtype=torch.bool))
+    s = torch.where(causal, s, torch.full_like(s, -1e300))
+    prob = rb(torch.softmax(s, dim=-1))
+    o = rb(torch.einsum("bhts,bshd->bthd", prob, vv))
+    r = _linear(o.reshape(b * t, cfg.heads * hd), _w(P[p + "self_attn.out_proj.weight"]))
+    return _ffn_tail(P, p, x, r, eps), k4, v4
+
+
+def attention_block(cfg, weights: dict, x):
+    """One causal attention block over x [B, T, C] (bf16-exact values), every token valid, positions 0..T-1:
+    (y [B, T, C], keys [B, T, Hk, D], values [B, T, Hk, D]) in float64 holding bf16-exact values.
+
+    ``weights`` uses the decoder's per-layer names without the layer prefix
+    ("operator_norm.weight", "self_attn.q_proj.weight", ..., "ffn_norm.weight",
+    "feed_forward.w1.weight" (gate), "feed_forward.w3.weight" (up),
+    "feed_forward.w2.weight" (down)).
+    """
+    with torch.no_grad():
+        P = {n: torch.tensor(np.asarray(v, np.float64), dtype=D) for n, v in weights.items()}
+        x = np.asarray(x, np.float64)
+        b, t, c = x.shape
+        y, k4, v4 = _attention_block_rows(cfg, P, "", rb(torch.from_numpy(x.reshape(b * t, c))), b, t)
+        return y.reshape(b, t, c).numpy(), k4.numpy(), v4.numpy()
+
+
 def prefill(cfg, params: dict, ids, capacity: int):
     """(logits [B, V] of the last prompt token, state after the prompt) for a fresh state.
 
@@ -95,16 +138,15 @@ def prefill(cfg, params: dict, ids, capacity: int):
         b, t = ids.shape
         if t <= 0 or t > capacity:
             raise ValueError("Prompt length must fit the cache capacity")
-        eps, hd, c = cfg.norm_eps, cfg.head_dim, cfg.hidden
+        eps, c = cfg.norm_eps, cfg.hidden
         x = rb(P["model.embed_tokens.weight"][torch.from_numpy(np.clip(ids, 0, cfg.vocab - 1)).long()])  # [B,T,C]
         x = x.reshape(b * t, c)
-        positions = np.tile(np.arange(t, dtype=np.int32), b)
         state = new_state(cfg, b, capacity)
         state["pos"] = t
         for i, kind in enumerate(cfg.layer_types):
             p = f"model.layers.{i}."
-            h = _rms(x, P[p + "operator_norm.weight"], eps)
             if kind == "conv":
+                h = _rms(x, P[p + "operator_norm.weight"], eps)
                 bcx = _linear(h, _w(P[p + "conv.in_proj.weight"])).reshape(b, t, 3 * c)
                 gate_b, gate_c, vals = bcx[..., :c], bcx[..., c:2 * c], bcx[..., 2 * c:]
                 g = rb(gate_b * vals)
@@ -115,25 +157,11 @@ def prefill(cfg, params: dict, ids, capacity: int):
                 state["hist"][i] = gp[:, t:t + 2].numpy().copy()  # state_tail at length t (zeros when t == 1)
                 r = _linear(mixed, _w(P[p + "conv.out_proj.weight"]))
             else:
-                q = _linear(h, _w(P[p + "self_attn.q_proj.weight"])).reshape(b * t, cfg.heads, hd)
-                k = _linear(h, _w(P[p + "self_attn.k_proj.weight"])).reshape(b * t, cfg.kv_heads, hd)
-                v = _linear(h, _w(P[p + "self_attn.v_proj.weight"])).reshape(b * t, cfg.kv_heads, hd)
-                q = _rope(_rms(q, P[p + "self_attn.q_layernorm.weight"], eps), positions, cfg.rope_theta, hd)
-                k = _rope(_rms(k, P[p + "self_attn.k_layernorm.weight"], eps), positions, cfg.rope_theta, hd)
-                group = cfg.heads // cfg.kv_heads
-                q4 = q.reshape(b, t, cfg.heads, hd)
-                k4 = k.reshape(b, t, cfg.kv_heads, hd)
-                v4 = v.reshape(b, t, cfg.kv_heads, hd)
-                kk = torch.repeat_interleave(k4, group, dim=2)
-                vv = torch.repeat_interleave(v4, group, dim=2)
-                s = torch.einsum("bthd,bshd->bhts", q4, kk) * hd ** -0.5
-                causal = torch.tril(torch.ones(t, t, dtype=torch.bool))
-                s = torch.where(causal, s, torch.full_like(s, -1e300))
-                prob = rb(torch.softmax(s, dim=-1))
-                o = rb(torch.einsum("bhts,bshd->bthd", prob, vv))
+                y, k4, v4 = _attention_block_rows(cfg, P, p, x, b, t)
                 state["k"][i][:, :t] = k4.numpy()
                 state["v"][i][:, :t] = v4.numpy()
-                r = _linear(o.reshape(b * t, cfg.heads * hd), _w(P[p + "self_attn.out_proj.weight"]))
+                x = y
+                continue
             x = _ffn_tail(P, p, x, r, eps)
         last = x.reshape(b, t, c)[:, t - 1]
         enc = _rms(last, P["model.embedding_norm.weight"], eps)

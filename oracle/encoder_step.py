@@ -28,7 +28,14 @@ import torch
 
 from . import quant
 
+# Arithmetic type of the restatement: FP64 for parity (the default); the
+# bench's CPU baseline times the same graph in FP32.
 D = torch.float64
+_DTYPE = [D]
+
+
+def _dt():
+    return _DTYPE[0]
 
 
 class _RoundBf16(torch.autograd.Function):
@@ -36,7 +43,7 @@ class _RoundBf16(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, t):
-        return t.to(torch.bfloat16).to(D)
+        return t.to(torch.bfloat16).to(_dt())
 
     @staticmethod
     def backward(ctx, g):
@@ -64,8 +71,8 @@ def _qat(w, kind):
     """Effective weight with the straight-through gradient masked by STE."""
     wn = w.detach().numpy().astype(np.float32)
     _, _, ste, dec = quant.fake_quant(wn, kind)
-    dec = torch.from_numpy(np.asarray(dec, np.float64))
-    ste = torch.from_numpy(np.asarray(ste, np.float64))
+    dec = torch.from_numpy(np.asarray(dec, np.float64)).to(_dt())
+    ste = torch.from_numpy(np.asarray(ste, np.float64)).to(_dt())
     return rb(dec) + (w - w.detach()) * ste
 
 
@@ -74,7 +81,7 @@ def _rope(x, positions, theta, head_dim):
                                                     np.float32(head_dim))).astype(np.float32))
     ang = (torch.from_numpy(np.asarray(positions, np.float32))[:, None] * freqs[None, :]).to(torch.float32)
     ang = torch.cat((ang, ang), dim=-1)
-    cos, sin = rb(torch.cos(ang).to(D)), rb(torch.sin(ang).to(D))
+    cos, sin = rb(torch.cos(ang).to(_dt())), rb(torch.sin(ang).to(_dt()))
     rot = torch.cat((-x[..., head_dim // 2:], x[..., :head_dim // 2]), dim=-1)
     return rb(rb(x * cos[:, None, :]) + rb(rot * sin[:, None, :]))
 
@@ -98,7 +105,7 @@ def _conv(bcx, taps, seg, t_len):
             nb[:, :-1] = seg2[:, 1:]
         else:
             sh, nb = g3, seg2
-        same = ((nb == seg2) & (seg2 != 0)).to(D)[..., None]
+        same = ((nb == seg2) & (seg2 != 0)).to(_dt())[..., None]
         tap = rb(rb(sh * tb[:, i]) * same)
         result = rb(result + tap)
     return rb(cg * result.reshape(-1, c))
@@ -113,7 +120,7 @@ def _attention(q, k, v, seg, rows, t_len, heads, kv_heads):
     seg2 = torch.from_numpy(np.asarray(seg)).reshape(rows, t_len)
     active = seg2 != 0
     valid = (seg2[:, :, None] == seg2[:, None, :]) & active[:, :, None] & active[:, None, :]
-    s = torch.where(valid[:, None], s, torch.full_like(s, -1e300))
+    s = torch.where(valid[:, None], s, torch.full_like(s, torch.finfo(s.dtype).min))
     p = torch.softmax(s, dim=-1)
     p = torch.where(active[:, None, :, None], p, torch.zeros_like(p))
     o = rb(torch.einsum("bhts,bshd->bthd", rb(p), v4))
@@ -121,25 +128,29 @@ def _attention(q, k, v, seg, rows, t_len, heads, kv_heads):
     return o.reshape(rows * t_len, heads * hd)
 
 
-def loss_and_grads(cfg, params: dict, ids, mask, seg, pos, labels, rows, bf16=True):
+def loss_and_grads(cfg, params: dict, ids, mask, seg, pos, labels, rows, bf16=True, compute_dtype=torch.float64):
     """(loss_sum, count, {trainable name: FP64 gradient}) for one local batch.
 
     ``bf16=False`` drops every bf16 cast (the FP64 version of the same model,
     fake-quantized weights included): the exact path a bf16 run is compared to.
+    ``compute_dtype=torch.float32`` runs the same graph in FP32 (CPU timing
+    only; parity uses FP64).
     """
     _ROUND[0] = bool(bf16)
+    _DTYPE[0] = compute_dtype
     try:
         return _loss_and_grads(cfg, params, ids, mask, seg, pos, labels, rows)
     finally:
         _ROUND[0] = True
+        _DTYPE[0] = torch.float64
 
 
 def _loss_and_grads(cfg, params, ids, mask, seg, pos, labels, rows):
     t_len = cfg.length
     ids, mask, seg, pos, labels = (np.asarray(a).reshape(-1) for a in (ids, mask, seg, pos, labels))
-    leaves = {n: torch.tensor(np.asarray(v, np.float64), requires_grad=n != "lfm2.embed_tokens.weight")
+    leaves = {n: torch.tensor(np.asarray(v), dtype=_dt(), requires_grad=n != "lfm2.embed_tokens.weight")
               for n, v in params.items()}
-    maskt = torch.from_numpy(mask.astype(np.float64))
+    maskt = torch.from_numpy(mask.astype(np.float64)).to(_dt())
     table = leaves["lfm2.embed_tokens.weight"]
     x = rb(table[torch.from_numpy(np.clip(ids, 0, cfg.vocab - 1)).long()])
     c, eps = cfg.hidden, cfg.norm_eps

@@ -87,6 +87,52 @@ def swiglu_qat_backward(x, w_gate_up, w_down, kind, d_y, dtype=np.float64, bf16_
     return dx, dw_gate_up, dw_down
 
 
+def swiglu_qat_step(x, w_gate_up, w_down, kind, d_y, dtype=np.float64, bf16_casts=True):
+    """One forward + backward of the chain with each product computed once.
+
+    Returns (y, gu, h, dx, dw_gate_up, dw_down): the values of
+    ``swiglu_qat_forward`` and ``swiglu_qat_backward`` without the backward's
+    recomputation of the forward products (what a training step runs).
+    """
+    eff_gu, ste_gu, eff_d, ste_d = qat_weights(w_gate_up, w_down, kind)
+    f = w_down.shape[1]
+    xb = round_bf16(x).astype(dtype)
+    gu = _cast(xb @ eff_gu.astype(dtype).T, bf16_casts, dtype)
+    g, u = gu[:, :f], gu[:, f:]
+    h = round_bf16(silu(g) * u).astype(dtype)
+    y = h @ eff_d.astype(dtype).T
+    dy = round_bf16(d_y).astype(dtype)
+    dh = _cast(dy @ eff_d.astype(dtype), bf16_casts, dtype)
+    dw_down = (dy.T @ h) * ste_d
+    dgu = _cast(np.concatenate((dh * u * silu_grad(g), dh * silu(g)), axis=1), bf16_casts, dtype)
+    dx = dgu @ eff_gu.astype(dtype)
+    dw_gate_up = (dgu.T @ xb) * ste_gu
+    return y, gu, h, dx, dw_gate_up, dw_down
+
+
+def swiglu_qat_weight_grad_columns(x, w_gate_up, w_down, kind, d_y, ffn_cols, dtype=np.float64):
+    """Selected columns of the two weight gradients, from the oracle's own forward.
+
+    For the FFN columns ``ffn_cols`` (indices into F) returns
+    (dw_down[:, ffn_cols], dw_gate_up[ffn_cols], dw_gate_up[F + ffn_cols]) --
+    exactly those entries of ``swiglu_qat_backward`` -- computing only the
+    gate/up/h/dh columns they need, so a full-size batch stays cheap.
+    """
+    eff_gu, ste_gu, eff_d, ste_d = qat_weights(w_gate_up, w_down, kind)
+    f = w_down.shape[1]
+    cols = np.asarray(ffn_cols)
+    xb = round_bf16(x).astype(dtype)
+    dy = round_bf16(d_y).astype(dtype)
+    g = round_bf16(xb @ eff_gu[cols].astype(dtype).T).astype(dtype)
+    u = round_bf16(xb @ eff_gu[f + cols].astype(dtype).T).astype(dtype)
+    h = round_bf16(silu(g) * u).astype(dtype)
+    dh = round_bf16(dy @ eff_d[:, cols].astype(dtype)).astype(dtype)
+    dw_down = (dy.T @ h) * ste_d[:, cols]
+    dg = round_bf16(dh * u * silu_grad(g)).astype(dtype)
+    du = round_bf16(dh * silu(g)).astype(dtype)
+    return dw_down, (dg.T @ xb) * ste_gu[cols], (du.T @ xb) * ste_gu[f + cols]
+
+
 def qat_linear_forward(x, weight, kind, dtype=np.float64):
     """``full_linear(x, effective(weight))`` for one QAT projection."""
     _, _, _, eff = quant.fake_quant(weight, kind)

@@ -31,6 +31,29 @@ def assert_close(actual, expected, max_abs=MAX_ABS, rel_l2=REL_L2, scaled=False,
     return err, rl2
 
 
+def report_errors(what, actual, expected):
+    """Append the unscaled max-abs, the per-element-scaled max-abs and the rel-L2 of one comparison to
+    the JSON-lines file named by MFB_PARITY_REPORT (no-op when unset), so the raw errors behind the
+    scaled gradient gate can be read off a test run."""
+    path = os.environ.get("MFB_PARITY_REPORT")
+    if not path:
+        return
+    import json
+
+    a = np.asarray(actual, np.float64)
+    e = np.asarray(expected, np.float64)
+    unit = np.maximum(max(1.0, float(np.sqrt(np.mean(e * e)))), np.abs(e))
+    norm = float(np.linalg.norm(e))
+    rec = {"what": what, "max_abs": float(np.max(np.abs(a - e))) if a.size else 0.0,
+           "max_abs_scaled": float(np.max(np.abs(a - e) / unit)) if a.size else 0.0,
+           "rel_l2": float(np.linalg.norm(a - e)) / norm if norm > 0 else 0.0,
+           "ref_max_abs": float(np.max(np.abs(e))) if e.size else 0.0,
+           "ref_rms": float(np.sqrt(np.mean(e * e))) if e.size else 0.0}
+    os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
+    with open(path, "a") as fh:
+        fh.write(json.dumps(rec) + "\n")
+
+
 def header_functions():
     """Names of every function declared in include/*.h."""
     names = []

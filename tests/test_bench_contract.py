@@ -2,8 +2,8 @@
 
 The reference arm times the NumPy restatement of the config-2 attention on the
 host cores (the reference is JAX, which is not installed). Two ranks over gloo:
-rank 1 exits 0 without work, rank 0 prints the line. One sampled row per step
-keeps the run to about 20 s.
+rank 1 exits 0 without work, rank 0 prints the line. Each step is the whole
+8-row config-2 batch, the GPU arm's step (about 30 s on 8 cores).
 """
 
 import json
@@ -37,3 +37,21 @@ def test_reference_arm_prints_one_contract_line_from_rank_zero():
     assert line["value"] > 0 and line["unit"] == line["e2e"]["unit"] == line["cpu_baseline"]["unit"]
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
     assert line["cpu_baseline"]["kind"] == "port"
+    assert line["config"]["batch"] == 8 and "whole batch" in line["cpu_baseline"]["sample"]
+
+
+def test_cpu_baseline_legs_return_positive_rates():
+    """The per-config CPU legs bench.py attaches at N=1 (bounded samples of configs 1, 3, 4, 5)."""
+    sys.path.insert(0, ROOT)
+    import bench
+    from minifield_training_b200 import workloads
+
+    tf, dt, sample = bench.cpu_attention_sample(workloads.CONFIG1)
+    assert tf > 0 and dt > 0 and "cfg1" in sample
+    tps, gbs, dt, sample = bench.cpu_decode_sample(layers=1)
+    assert tps > 0 and gbs > 0 and "1 of 6 layers" in sample
+    for kind in ("int8-channel-absmax-v1", "int4-g128-absmax-v1"):
+        tf, tps, dt, sample = bench.cpu_qat_sample(kind, tokens=64)
+        assert tf > 0 and tps > 0 and kind in sample
+    tps, tf, dt, sample = bench.cpu_encoder_sample()
+    assert tps > 0 and tf > 0

@@ -87,3 +87,16 @@ def test_unknown_backend_names_raise_like_the_reference():
         attention.packed_causal_attention(None, None, None, None, None, backend="splash")
     with pytest.raises(ValueError, match="Unsupported cached attention backend"):
         attention.cached_attention(None, None, None, None, backend="cudnn")
+
+
+def test_attention_block_functions_reject_unknown_backends_before_any_launch():
+    from minifield_training_b200.layers import attention as la
+
+    with pytest.raises(ValueError, match="Unsupported causal attention backend: dense"):
+        la.attention_block(None, None, None, None, head_dim=64, rope_theta=1e6, eps=1e-5, backend="dense")
+    with pytest.raises(ValueError, match="Unsupported causal attention backend: cudnn"):
+        la.attention_block_prefill(None, None, None, None, capacity=8, head_dim=64, rope_theta=1e6, eps=1e-5,
+                                   backend="cudnn")
+    with pytest.raises(ValueError, match="Unsupported cached attention backend: dense"):
+        la.attention_block_step(None, None, None, None, None, 0, 1, head_dim=64, rope_theta=1e6, eps=1e-5,
+                                backend="dense")

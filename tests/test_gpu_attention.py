@@ -10,7 +10,7 @@ import pytest
 
 from oracle import attention as oatt
 from oracle.bf16 import round_bf16
-from tests._util import assert_close
+from tests._util import assert_close, report_errors
 from tests.gpu_env import require_gpu
 
 pytestmark = pytest.mark.gpu
@@ -68,9 +68,11 @@ def oracle_attention(q, k, v, ids, dout=None, dtype=np.float64):
 
 def _check(res, ref_out, ref_grads, what):
     assert_close(res["out"], ref_out, what=f"{what} O")
+    report_errors(f"{what} O", res["out"], ref_out)
     if ref_grads is not None:
         for name, r in zip(("dq", "dk", "dv"), ref_grads):
             assert_close(res[name], r, scaled=True, what=f"{what} {name}")
+            report_errors(f"{what} {name}", res[name], r)
 
 
 # --- reference known answers -------------------------------------------------
@@ -231,7 +233,9 @@ def test_config1_dense_causal_full_size():
     _check(r, out, grads, "config1")
 
 
-def test_config2_segment_bidirectional_full_batch_rows_checked():
+def test_config2_segment_bidirectional_full_batch_all_rows():
+    """The headline batch (8 rows, each with its own segment layout) against the oracle, every row;
+    the oracle runs two rows at a time (a chunk's FP32 score grids take about 2.5 GB)."""
     from minifield_training_b200 import workloads
 
     q, k, v, do, mask, seg = workloads.attention_inputs(workloads.CONFIG2, seed=0)
@@ -239,11 +243,12 @@ def test_config2_segment_bidirectional_full_batch_rows_checked():
     ids = oatt.bidirectional_ids(mask, seg)
     np.testing.assert_array_equal(r["qid"], ids[0])
     np.testing.assert_array_equal(r["kid"], ids[1])
-    rows = [0, 5]  # the oracle checks two full rows (B rows are independent)
-    sub = tuple(x[rows] for x in ids[:2]) + ids[2:]
-    out, grads = oracle_attention(q[rows], k[rows], v[rows], sub, do[rows], dtype=np.float32)
-    got = {key: r[key][rows] for key in ("out", "dq", "dk", "dv")}
-    _check(got, out, grads, "config2")
+    for lo in range(0, q.shape[0], 2):
+        rows = slice(lo, lo + 2)
+        sub = tuple(x[rows] for x in ids[:2]) + ids[2:]
+        out, grads = oracle_attention(q[rows], k[rows], v[rows], sub, do[rows], dtype=np.float32)
+        got = {key: r[key][rows] for key in ("out", "dq", "dk", "dv")}
+        _check(got, out, grads, f"config2 rows {lo}-{lo + 1}")
 
 
 def test_rows_of_one_warp_that_rescale_differently():

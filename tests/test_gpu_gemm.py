@@ -6,7 +6,7 @@ import pytest
 from oracle import linear as olin
 from oracle import quant as oq
 from oracle.bf16 import round_bf16
-from tests._util import assert_close
+from tests._util import assert_close, report_errors
 from tests.gpu_env import require_gpu
 
 pytestmark = pytest.mark.gpu
@@ -113,40 +113,33 @@ def test_swiglu_qat_small(kind):
     assert_close(dwd.float32(), rdwd, scaled=True, what="dW_down")
 
 
-def test_swiglu_qat_config4_full_size():
-    """Full config-4 shapes: forward rows and weight-gradient columns checked exactly
-    against FP64 products of the GPU's own bf16 intermediates (GEMM parity at size)."""
+@pytest.mark.parametrize("kind", ["int8-channel-absmax-v1", "int4-g128-absmax-v1"])
+def test_swiglu_qat_config4_full_size(kind):
+    """Full config-4 shapes, both quantizer kinds, every checked value from the oracle: forward and
+    dX rows, and dW_down / dW_gate_up columns from the oracle's own gate/up and SwiGLU intermediates
+    over all 16384 tokens."""
     from minifield_training_b200 import workloads
     from minifield_training_b200.layers.feed_forward import swiglu_qat_bwd, swiglu_qat_fwd
 
     cfg = workloads.CONFIG4
     x, w_gu, w_d, dy = workloads.qat_inputs(cfg, seed=0)
-    y, res = swiglu_qat_fwd(x, w_gu, w_d, cfg.kind)
+    y, res = swiglu_qat_fwd(x, w_gu, w_d, kind)
     dx, dwgu, dwd = swiglu_qat_bwd(res, dy)
-    eff_gu, _, eff_d, _ = olin.qat_weights(w_gu, w_d, cfg.kind)
     rows = np.arange(0, cfg.tokens, 997)
-    ry, _, _ = olin.swiglu_qat_forward(x[rows], w_gu, w_d, cfg.kind, dtype=np.float32)
-    assert_close(y.float32()[rows], ry, scaled=True, what="cfg4 y rows")
-    rdx, _, _ = olin.swiglu_qat_backward(x[rows], w_gu, w_d, cfg.kind, dy[rows], dtype=np.float32)
-    assert_close(dx.float32()[rows], rdx, scaled=True, what="cfg4 dx rows")
-    h = res.h.float32()
+    ry, _, _ = olin.swiglu_qat_forward(x[rows], w_gu, w_d, kind, dtype=np.float32)
+    assert_close(y.float32()[rows], ry, scaled=True, what=f"cfg4 {kind} y rows")
+    rdx, _, _ = olin.swiglu_qat_backward(x[rows], w_gu, w_d, kind, dy[rows], dtype=np.float32)
+    assert_close(dx.float32()[rows], rdx, scaled=True, what=f"cfg4 {kind} dx rows")
     cols = np.arange(0, cfg.ffn, 331)
-    ref_dwd = round_bf16(dy).astype(np.float64).T @ h[:, cols].astype(np.float64)
-    assert_close(dwd.float32()[:, cols], ref_dwd, scaled=True, what="cfg4 dW_down cols")
-    from minifield_training_b200.device import DeviceArray  # noqa: F401
-
-    xb = round_bf16(x).astype(np.float64)
-    gu = res.gu.float32()
-    # dGU from the GPU's own gate/up output (exact SwiGLU derivative in FP64).
-    dh = round_bf16(dy).astype(np.float64) @ eff_d.astype(np.float64)
-    sub = np.arange(0, 2 * cfg.ffn, 1013)
-    g = gu[:, :cfg.ffn].astype(np.float64)
-    u = gu[:, cfg.ffn:].astype(np.float64)
-    dg = dh * u * olin.silu_grad(g)
-    du = dh * olin.silu(g)
-    dgu = np.concatenate((dg, du), axis=1)[:, sub]
-    ref_dwgu = round_bf16(dgu).T @ xb
-    assert_close(dwgu.float32()[sub], ref_dwgu, scaled=True, what="cfg4 dW_gate_up rows")
+    rdwd, rdg, rdu = olin.swiglu_qat_weight_grad_columns(x, w_gu, w_d, kind, dy, cols, dtype=np.float32)
+    dwd_h, dwgu_h = dwd.float32(), dwgu.float32()
+    assert_close(dwd_h[:, cols], rdwd, scaled=True, what=f"cfg4 {kind} dW_down cols")
+    assert_close(dwgu_h[cols], rdg, scaled=True, what=f"cfg4 {kind} dW_gate rows")
+    assert_close(dwgu_h[cfg.ffn + cols], rdu, scaled=True, what=f"cfg4 {kind} dW_up rows")
+    for what, a, e in (("dW_down", dwd_h[:, cols], rdwd), ("dW_gate", dwgu_h[cols], rdg),
+                       ("dW_up", dwgu_h[cfg.ffn + cols], rdu), ("y", y.float32()[rows], ry),
+                       ("dx", dx.float32()[rows], rdx)):
+        report_errors(f"cfg4 {kind} {what}", a, e)
 
 
 @pytest.mark.parametrize("m,n,k", [(64, 1024, 6656), (64, 3072, 1024), (1, 1024, 1024), (100, 520, 200),

@@ -292,3 +292,37 @@ def test_config2_segments_match_stated_square_sum():
     seg = workloads.packed_segments(0, 8, 2048)
     assert workloads.segment_square_sum(seg) == 11_171_716
     assert seg.dtype == np.int32 and seg.shape == (8, 2048)
+
+
+@pytest.mark.parametrize("kind", ["int8-channel-absmax-v1", "int4-g128-absmax-v1"])
+def test_swiglu_step_equals_forward_and_backward(kind):
+    """The one-pass chain (CPU baseline, full-size parity) returns exactly the values of the
+    separate forward and backward restatements."""
+    from oracle import linear as ol
+
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((64, 256)).astype(np.float32)
+    wgu = (rng.standard_normal((256, 256)) * 0.02).astype(np.float32)
+    wd = (rng.standard_normal((256, 128)) * 0.02).astype(np.float32)
+    dy = rng.standard_normal((64, 256)).astype(np.float32)
+    fwd = ol.swiglu_qat_forward(x, wgu, wd, kind)
+    bwd = ol.swiglu_qat_backward(x, wgu, wd, kind, dy)
+    for a, b in zip(fwd + bwd, ol.swiglu_qat_step(x, wgu, wd, kind, dy)):
+        np.testing.assert_array_equal(a, b)
+
+
+@pytest.mark.parametrize("kind", ["int8-channel-absmax-v1", "int4-g128-absmax-v1"])
+def test_swiglu_weight_grad_columns_equal_the_full_backward(kind):
+    from oracle import linear as ol
+
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((48, 256)).astype(np.float32)
+    wgu = (rng.standard_normal((2 * 128, 256)) * 0.02).astype(np.float32)
+    wd = (rng.standard_normal((256, 128)) * 0.02).astype(np.float32)
+    dy = rng.standard_normal((48, 256)).astype(np.float32)
+    _, dwgu, dwd = ol.swiglu_qat_backward(x, wgu, wd, kind, dy)
+    cols = np.array([0, 7, 64, 127])
+    cd, cg, cu = ol.swiglu_qat_weight_grad_columns(x, wgu, wd, kind, dy, cols)
+    np.testing.assert_allclose(cd, dwd[:, cols], rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(cg, dwgu[cols], rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(cu, dwgu[128 + cols], rtol=1e-12, atol=1e-12)
