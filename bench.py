@@ -13,11 +13,13 @@ tokens/s and TFLOP/s) and the data-parallel encoder training step (config 5:
 16-layer QAT encoder forward+backward, gradient allreduce, AdamW commit;
 tokens/s of the fixed global batch of 32 x 2048).
 
-Multi-GPU: one process per GPU (torchrun). Configs 2-4 run one copy per rank
+Multi-GPU: one process per GPU (torchrun). Configs 1-4 run one copy per rank
 (weak scaling, no collective on their data path). Config 5 splits the global
 batch's rows over the ranks (strong scaling) and all-reduces the gradient sums
-over NCCL, bucket by bucket during the backward. Timing is the max over ranks
-of CUDA-event time between barriers.
+over NCCL (the library's own communicator, mfb_comm_*), bucket by bucket
+during the backward. Timing is the max over ranks of CUDA-event time between
+barriers; torch.distributed (gloo) carries only the barrier, the max over
+ranks and the NCCL unique id.
 
 ``--impl reference`` times the reference algorithm's CPU restatement (the
 NumPy oracle; the reference itself is JAX, which is not installed on these
@@ -76,16 +78,20 @@ class Dist:
             dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
             self.pg = dist
 
-    def nccl_group(self):
-        """A NCCL group over all ranks for the gradient allreduce (None on one GPU)."""
+    def communicator(self):
+        """The library's NCCL communicator over all ranks for the gradient exchange (None on one GPU).
+
+        Rank 0 draws the NCCL unique id; the gloo group hands it to the others.
+        """
         if not self.pg:
             return None
-        if getattr(self, "_nccl", None) is None:
-            import torch
+        if getattr(self, "_comm", None) is None:
+            from minifield_training_b200 import comm
 
-            torch.cuda.set_device(self.local)
-            self._nccl = self.pg.new_group(backend="nccl")
-        return self._nccl
+            box = [comm.unique_id() if self.rank == 0 else None]
+            self.pg.broadcast_object_list(box, src=0)
+            self._comm = comm.Communicator(self.world, self.rank, box[0], timeout_s=300.0)
+        return self._comm
 
     def barrier(self):
         if self.pg:
@@ -101,6 +107,10 @@ class Dist:
         return float(t.item())
 
     def close(self):
+        c = getattr(self, "_comm", None)
+        if c is not None:
+            c.close()
+            self._comm = None
         if self.pg:
             self.pg.destroy_process_group()
 
@@ -540,7 +550,7 @@ class EncoderStepWorkload:
         s = ctypes.c_void_p()
         _lib.call("mfb_stream_create", ctypes.byref(s))
         self.stream = s.value
-        self.model = me.EncoderStep(cfg, rows=self.rows, seed=0, group=dist.nccl_group(), stream=self.stream)
+        self.model = me.EncoderStep(cfg, rows=self.rows, seed=0, comm=dist.communicator(), stream=self.stream)
         self.batch = workloads.encoder_batch(cfg, 0, rows=self.rows, row0=dist.rank * self.rows)
         self.model.set_batch(*self.batch)
         full_seg = workloads.packed_segments(0, cfg.global_batch, cfg.length)
@@ -600,10 +610,10 @@ def _cpu_line(value, unit, sample, seconds):
             "sample": f"{sample} ({seconds:.1f} s of CPU work)"}
 
 
-def cpu_attention_sample(cfg=None, rows=None, chunk=2):
+def cpu_attention_sample(cfg=None, rows=None, chunk=2, repeats=1):
     """Time the oracle's FP32 forward+backward over ``rows`` rows of an attention config (default:
     config 2, the whole batch), ``chunk`` rows at a time (a config-2 chunk's score grids take
-    about 2.5 GB). Returns (TFLOP/s, seconds, sample text)."""
+    about 2.5 GB), ``repeats`` times. Returns (TFLOP/s, seconds, sample text)."""
     from minifield_training_b200 import workloads
     from oracle import attention as oatt
 
@@ -611,7 +621,7 @@ def cpu_attention_sample(cfg=None, rows=None, chunk=2):
     rows = cfg.batch if rows is None else rows
     inputs = workloads.attention_inputs(cfg, 0)
     dt, flops = 0.0, 0.0
-    for lo in range(0, rows, chunk):
+    for lo in [lo for _ in range(repeats) for lo in range(0, rows, chunk)]:
         q, k, v, do, mask = (x[lo:min(rows, lo + chunk)] for x in inputs[:5])
         seg = inputs[5][lo:min(rows, lo + chunk)] if inputs[5] is not None else None
         ids = oatt.bidirectional_ids(mask, seg) if cfg.packed else oatt.causal_ids(mask)
@@ -622,8 +632,9 @@ def cpu_attention_sample(cfg=None, rows=None, chunk=2):
         dt += time.perf_counter() - t0
         flops += 3.5 * 4.0 * cfg.heads * cfg.head_dim * oatt.valid_pair_count(*ids[:4])
     what = "the whole batch" if rows == cfg.batch else f"rows 0..{rows - 1}"
+    times = f", {repeats} times" if repeats > 1 else ""
     return flops / dt / 1e12, dt, (f"{cfg.name} {what} (B={rows} of {cfg.batch}, T={cfg.length}, "
-                                   f"{cfg.heads}/{cfg.kv_heads} heads), FP32 NumPy, {chunk} rows at a time")
+                                   f"{cfg.heads}/{cfg.kv_heads} heads){times}, FP32 NumPy, {chunk} rows at a time")
 
 
 def cpu_decode_sample(layers=2):
@@ -647,7 +658,7 @@ def cpu_decode_sample(layers=2):
         "FP32 NumPy (the reference's dense cached attention reads every cache slot, then masks)")
 
 
-def cpu_qat_sample(kind, tokens=256):
+def cpu_qat_sample(kind, tokens=2048):
     """Config 4 on the oracle in FP32: fake-quant of both weights once, then the GEMM chain forward +
     backward on ``tokens`` of the 16384 rows, scaled by rows. Returns (TFLOP/s, tokens/s, seconds, text)."""
     from minifield_training_b200 import workloads
@@ -668,9 +679,9 @@ def cpu_qat_sample(kind, tokens=256):
         "tokens, scaled by rows; FP32 NumPy")
 
 
-def cpu_encoder_sample():
-    """Config 5 on the oracle (torch autograd on the CPU, FP32): loss and gradients of one 2048-token
-    row through a conv layer and an attention layer at the full hidden/FFN widths, with int8 fake-quant,
+def cpu_encoder_sample(rows=2):
+    """Config 5 on the oracle (torch autograd on the CPU, FP32): loss and gradients of ``rows`` 2048-token
+    rows through a conv layer and an attention layer at the full hidden/FFN widths, with int8 fake-quant,
     scaled by FLOPs to the 16-layer step over the 32-row global batch. Returns (tokens/s, TFLOP/s,
     seconds, text)."""
     import dataclasses
@@ -683,18 +694,18 @@ def cpu_encoder_sample():
 
     torch.set_num_threads(os.cpu_count() or 1)
     full = workloads.CONFIG5
-    sub = dataclasses.replace(full, global_batch=1, layer_types=("conv", "full_attention"))
+    sub = dataclasses.replace(full, global_batch=rows, layer_types=("conv", "full_attention"))
     params = me.init_parameters(sub, 0)
-    batch = workloads.encoder_batch(sub, 0, rows=1)
+    batch = workloads.encoder_batch(sub, 0, rows=rows)
     t0 = time.perf_counter()
-    oes.loss_and_grads(sub, params, *batch, rows=1, compute_dtype=torch.float32)
+    oes.loss_and_grads(sub, params, *batch, rows=rows, compute_dtype=torch.float32)
     dt = time.perf_counter() - t0
     sub_flops = workloads.encoder_step_flops(sub, batch[2])
     full_flops = workloads.encoder_step_flops(full, workloads.packed_segments(0, full.global_batch, full.length))
     step = dt * full_flops / sub_flops
     tokens = full.global_batch * full.length
     return tokens / step, full_flops / step / 1e12, dt, (
-        f"{full.name}: 1 row x {full.length} tokens through 2 of the 16 layers (conv + attention; hidden "
+        f"{full.name}: {rows} rows x {full.length} tokens through 2 of the 16 layers (conv + attention; hidden "
         f"{full.hidden}, FFN {full.ffn}, int8 fake-quant) forward + backward, torch autograd FP32 on the CPU, "
         "scaled by FLOPs to the 16-layer 32 x 2048 step")
 
@@ -915,10 +926,10 @@ def run_ours(args, dist):
             v, dt, sample = cpu_attention_sample()
             line["cpu_baseline"] = _cpu_line(v, UNIT, sample, dt)
         if "attention_cfg1" in secondary:
-            v, dt, sample = cpu_attention_sample(workloads.CONFIG1)
+            v, dt, sample = cpu_attention_sample(workloads.CONFIG1, repeats=8)
             secondary["attention_cfg1"]["cpu_baseline"] = _cpu_line(v, UNIT, sample, dt)
         if "decode" in secondary:
-            tps, gbs, dt, sample = cpu_decode_sample()
+            tps, gbs, dt, sample = cpu_decode_sample(layers=6)
             secondary["decode"]["cpu_baseline"] = dict(_cpu_line(tps, "tokens/s", sample, dt), hbm_gbs=gbs)
         for key in ("qat", "qat_int4"):
             if key in secondary:

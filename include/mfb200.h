@@ -33,7 +33,8 @@ enum mfb_status_code {
   MFB_ERR_CUDA = 2,        /* CUDA runtime error */
   MFB_ERR_UNSUPPORTED = 3, /* valid but not implemented on this build / device */
   MFB_ERR_WORKSPACE = 4,   /* workspace pointer NULL or too small */
-  MFB_ERR_DEVICE = 5       /* a device-side status word reported an error */
+  MFB_ERR_DEVICE = 5,      /* a device-side status word reported an error */
+  MFB_ERR_COMM = 6         /* a collective failed or passed its deadline; the communicator is aborted */
 };
 
 /* ---- runtime helpers (for hosts that have no device allocator of their own) */
@@ -360,6 +361,43 @@ int mfb_cast_bf16_f32(const uint16_t* x, float* y, long long n, void* stream);
  * (src/minifield_training/layers/attention.py:100-108,
  * layers/feed_forward.py:35). n a multiple of 8; 16-byte aligned buffers. */
 int mfb_add_bf16(const uint16_t* a, const uint16_t* b, uint16_t* out, long long n, void* stream);
+
+/* ---- NCCL communicator (data-parallel exchange) -------------------------------
+ * The psum of (loss, count, gradient tree) over the data axis of the
+ * reference's training step (src/minifield_training/engine/step.py:36-78,
+ * psum at :62; shard_map over the 1-D "data" mesh :72-77), and the scalar
+ * reductions and master all-gather of the sharded AdamW transaction. One
+ * communicator per process (rank), one GPU each.
+ *
+ * mfb_comm_load dlopens NCCL from path (NULL: "libnccl.so.2") once per
+ * process and reports its version (e.g. 22803 for 2.28.3). Rank 0 draws the
+ * unique id (mfb_comm_unique_id_bytes() bytes) and the host hands it to the
+ * other ranks by any means. The communicator is non-blocking: every call
+ * below returns once its work is enqueued on the stream, and each is bounded
+ * by timeout_s -- an NCCL error or a missed deadline aborts the communicator
+ * (ncclCommAbort; NCCL's kernels on this GPU then return) and gives
+ * MFB_ERR_COMM, and an aborted communicator rejects later calls.
+ * mfb_comm_wait(comm, stream, timeout_s) waits for a stream while watching
+ * the communicator: the bounded wait a host uses instead of a stream sync
+ * when a peer may have failed. Element types and reductions: */
+enum mfb_comm_dtype { MFB_COMM_F32 = 0, MFB_COMM_F64 = 1, MFB_COMM_BF16 = 2, MFB_COMM_U8 = 3, MFB_COMM_I32 = 4 };
+enum mfb_comm_op { MFB_COMM_SUM = 0, MFB_COMM_MAX = 1, MFB_COMM_MIN = 2 };
+int mfb_comm_load(const char* path, int* version);
+size_t mfb_comm_unique_id_bytes(void);
+int mfb_comm_unique_id(void* id, size_t bytes);
+int mfb_comm_init(const void* id, size_t id_bytes, int world, int rank, double timeout_s, void** comm);
+int mfb_comm_rank(void* comm, int* rank, int* world);
+/* recv may equal send (in place). */
+int mfb_comm_allreduce(void* comm, const void* send, void* recv, size_t count, int dtype, int op, void* stream);
+/* send holds world * recv_count elements; rank r receives the reduction of block r. */
+int mfb_comm_reduce_scatter(void* comm, const void* send, void* recv, size_t recv_count, int dtype, int op,
+                            void* stream);
+/* recv holds world * send_count elements, block r from rank r; send may be recv's own block. */
+int mfb_comm_allgather(void* comm, const void* send, void* recv, size_t send_count, int dtype, void* stream);
+int mfb_comm_wait(void* comm, void* stream, double timeout_s);
+int mfb_comm_abort(void* comm);
+/* Finalizes (bounded by the communicator's timeout) and frees; NULL is a no-op. */
+int mfb_comm_destroy(void* comm);
 
 #ifdef __cplusplus
 }

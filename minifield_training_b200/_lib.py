@@ -13,7 +13,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libmfb200.so")
 
-OK, ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_DEVICE = range(6)
+OK, ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_DEVICE, ERR_COMM = range(7)
 
 QUANT_KINDS = {
     "int8-channel-absmax-v1": 0,
@@ -96,6 +96,17 @@ SIGNATURES = {
     "mfb_cast_f32_bf16": (I, [P, P, ctypes.c_longlong, P]),
     "mfb_cast_bf16_f32": (I, [P, P, LL, P]),
     "mfb_add_bf16": (I, [P, P, P, LL, P]),
+    "mfb_comm_load": (I, [ctypes.c_char_p, IP]),
+    "mfb_comm_unique_id_bytes": (SZ, []),
+    "mfb_comm_unique_id": (I, [P, SZ]),
+    "mfb_comm_init": (I, [P, SZ, I, I, ctypes.c_double, ctypes.POINTER(P)]),
+    "mfb_comm_rank": (I, [P, IP, IP]),
+    "mfb_comm_allreduce": (I, [P, P, P, SZ, I, I, P]),
+    "mfb_comm_reduce_scatter": (I, [P, P, P, SZ, I, I, P]),
+    "mfb_comm_allgather": (I, [P, P, P, SZ, I, P]),
+    "mfb_comm_wait": (I, [P, P, ctypes.c_double]),
+    "mfb_comm_abort": (I, [P]),
+    "mfb_comm_destroy": (I, [P]),
     "mfb_conv_step": (I, [P, P, P, P, I, I, P]),
     "mfb_conv_causal": (I, [P, P, P, P, P, I, I, I, P]),
 }

@@ -68,7 +68,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
     if failed:
         raise RuntimeError(f"nvcc failed for: {failed}")
     if force or jobs or _stale(LIB, objs):
-        cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode:
             sys.stderr.write(r.stdout + r.stderr)

@@ -105,9 +105,10 @@ def _project(x2, weights, positions, *, heads, kv_heads, head_dim, rope_theta, e
     v = DeviceArray((m, kv_heads, head_dim), "bfloat16")
     rq, rk = DeviceArray((m, heads), "float32"), DeviceArray((m, kv_heads), "float32")
     freqs = as_device(rope_freqs(rope_theta, head_dim), "float32", stream)
-    _lib.call("mfb_qknorm_rope_fwd", P(proj.ptr), nq, P(_gain(weights.query_norm, stream).ptr),
-              P(_gain(weights.key_norm, stream).ptr), P(positions.ptr), P(freqs.ptr), P(q.ptr), P(k.ptr), P(v.ptr),
-              P(rq.ptr), P(rk.ptr), m, heads, kv_heads, ctypes.c_float(eps), stream)
+    # Device copies are bound to names: a temporary would be freed before the launch reads it.
+    wq, wk = _gain(weights.query_norm, stream), _gain(weights.key_norm, stream)
+    _lib.call("mfb_qknorm_rope_fwd", P(proj.ptr), nq, P(wq.ptr), P(wk.ptr), P(positions.ptr), P(freqs.ptr), P(q.ptr),
+              P(k.ptr), P(v.ptr), P(rq.ptr), P(rk.ptr), m, heads, kv_heads, ctypes.c_float(eps), stream)
     return q, k, v
 
 

@@ -20,8 +20,9 @@ layer's projections are fake-quantized into fused bf16 weight buffers
 (q|k|v and gate|up rows adjacent), and the parameter arenas are ordered so the
 fused weight gradients land, FP32, straight in the gradient arena. Activations
 are kept for the backward (no rematerialization: 180 GB of HBM holds them).
-With a process group the gradient arena (plus the loss and count in its
-tail) is all-reduced bucket by bucket as each layer's backward finishes,
+With a communicator (NCCL through the library's C ABI, comm.Communicator) the
+gradient arena (plus the loss and count in its tail) is all-reduced bucket by
+bucket on a communication stream as each layer's backward is enqueued,
 overlapping the remaining backward; the AdamW commit then runs replicated.
 """
 
@@ -31,7 +32,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from .. import _lib
-from ..device import DeviceArray
+from ..device import DeviceArray, Event
 from ..optimizers import adamw
 
 P = ctypes.c_void_p
@@ -173,53 +174,46 @@ class _Layer:
 class EncoderStep:
     """One logical training step over ``rows`` local sequences of the global batch.
 
-    ``group`` (a torch.distributed process group, or None) all-reduces the
-    gradient sums, loss and count; ``stream`` is the CUDA stream handle all
-    kernels run on (and, with a group, the stream the collectives order after).
-    ``shard_optimizer`` (with a group) splits the AdamW passes across the ranks
-    and all-gathers the masters instead of every rank updating all of them.
-    On two GPUs it measured slower (the 1.5 GB all-gather outweighs the halved
-    optimizer), so the replicated transaction is the default.
+    ``comm`` (a comm.Communicator, or None) all-reduces the gradient sums,
+    loss and count; ``stream`` is the CUDA stream handle all kernels run on.
+    With a communicator the collectives run on a communication stream of the
+    step's own, ordered after the kernels they reduce by events.
+    ``shard_optimizer`` (with a communicator) splits the AdamW passes across
+    the ranks and all-gathers the masters instead of every rank updating all
+    of them. On two GPUs it measured slower (the 1.5 GB all-gather outweighs
+    the halved optimizer), so the replicated transaction is the default.
     """
 
-    def __init__(self, cfg, rows: int, *, seed: int = 0, group=None, stream=None, torch_grads=None,
-                 shard_optimizer: bool = False):
+    def __init__(self, cfg, rows: int, *, seed: int = 0, comm=None, stream=None, shard_optimizer: bool = False):
         self.cfg, self.rows, self.T = cfg, rows, cfg.length
         self.M = m = rows * cfg.length
-        self.group, self.stream = group, stream
+        self.comm, self.stream = comm, stream
         c, f, h, hk = cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads
         self.nq = (h + 2 * hk) * cfg.head_dim
         inv = inventory(cfg)
         self.layout = adamw.Layout(inv, arena_order(cfg))
         n_grad = self.layout.n_train + 4  # tail: loss sum, count
-        if torch_grads is None and group is not None:
-            # The collective library addresses the gradient buffer as a tensor.
-            import torch
-            torch_grads = torch.zeros(n_grad, dtype=torch.float32, device=f"cuda:{torch.cuda.current_device()}")
-        if torch_grads is not None:
-            grads = DeviceArray((n_grad,), "float32", ptr=torch_grads.data_ptr(), owner=False)
-            grads._base = torch_grads
-        else:
-            grads = DeviceArray.zeros((n_grad,), "float32")
+        grads = DeviceArray.zeros((n_grad,), "float32")
         self.grads = grads
         opt = adamw.AdamWConfig(cfg.learning_rate, beta1=cfg.beta1, beta2=cfg.beta2, epsilon=cfg.epsilon,
                                 weight_decay=cfg.weight_decay, clip_norm=cfg.clip_norm)
         masters = None
-        self.shard_optimizer = bool(shard_optimizer) and group is not None
+        self.shard_optimizer = bool(shard_optimizer) and comm is not None
         if self.shard_optimizer:
             # The optimizer is sharded across the ranks (each updates a slice of
-            # the masters and moments); the masters are all-gathered, so the
-            # collective library addresses them as a tensor too.
-            import torch
-            import torch.distributed as dist
-            n_master = adamw.sharded_master_elements(self.layout, dist.get_world_size(group))
-            torch_params = torch.zeros(n_master, dtype=torch.float32, device=f"cuda:{torch.cuda.current_device()}")
-            masters = DeviceArray((n_master,), "float32", ptr=torch_params.data_ptr(), owner=False)
-            masters._base = torch_params
+            # the masters and moments); the master arena holds the all-gather of
+            # every rank's equal slice.
+            masters = DeviceArray.zeros((adamw.sharded_master_elements(self.layout, comm.world),), "float32")
+        self.comm_stream = None
+        if comm is not None:
+            cs = ctypes.c_void_p()
+            _lib.call("mfb_stream_create", ctypes.byref(cs))
+            self.comm_stream = cs.value
+            self._order_events = (Event(), Event())
         self.state = adamw.initialize_state(init_parameters(cfg, seed), inv, order=arena_order(cfg), grads=grads,
                                             params=masters)
         self.loss_count = grads.view(self.layout.n_train, (2,))
-        self.transition = (adamw.make_sharded_transaction(inv, opt, group) if self.shard_optimizer
+        self.transition = (adamw.make_sharded_transaction(inv, opt, comm) if self.shard_optimizer
                            else adamw.make_transaction(inv, opt))
         self.params = self.state["params"]
         self.gviews = self.state.gradient_tree()
@@ -453,7 +447,7 @@ class EncoderStep:
         """Record the step as CUDA graphs on this step's stream (a created stream).
 
         One GPU: one graph (quantize, forward, backward, normalize, commit).
-        With a process group: the forward and the head's backward, one graph per
+        With a communicator: the forward and the head's backward, one graph per
         layer's backward (so each layer's bucket allreduce is launched between
         them), and the commit.
         """
@@ -471,7 +465,7 @@ class EncoderStep:
                 _lib.call("mfb_graph_end", P(self.stream), ctypes.byref(g))
             return g
 
-        if self.group is None:
+        if self.comm is None:
             self.graphs = {"all": rec(self._eager_local_step)}
         else:
             # A sharded AdamW transaction holds collectives between its passes:
@@ -491,22 +485,38 @@ class EncoderStep:
     def _launch(self, g):
         _lib.call("mfb_graph_launch", g, P(self.stream))
 
+    def reducer(self):
+        """A BucketReducer of this step's gradient arena over its communicator and streams."""
+        compute_done, reduced = self._order_events
+        comm, flat, cs = self.comm, self.grads, self.comm_stream
+
+        def reduce_range(lo, hi):
+            comm.allreduce(flat.view(lo, (hi - lo,)), stream=cs)
+
+        def before():  # the bucket's gradients are complete on the compute stream
+            compute_done.record(self.stream)
+            compute_done.wait_on(cs)
+
+        def after():  # the compute stream continues once every bucket is reduced
+            reduced.record(cs)
+            reduced.wait_on(self.stream)
+
+        return BucketReducer(self._buckets, reduce_range, before, after)
+
     def step(self):
         """quantize -> forward -> backward (+ bucketed allreduce) -> normalize -> AdamW commit."""
         graphs = getattr(self, "graphs", None)
         if graphs is not None:
-            if self.group is None:
+            if self.comm is None:
                 self._launch(graphs["all"])
             else:
-                import torch
-                with torch.cuda.stream(torch.cuda.ExternalStream(self.stream)):
-                    self._launch(graphs["pre"])
-                    reducer = BucketReducer(self.grads._base, self._buckets, self.group)
-                    for g, i in zip(graphs["layers"], reversed(range(len(self.layers)))):
-                        self._launch(g)
-                        reducer.layer_done(i)
-                    reducer.finish()
-                    self._launch(graphs["post"])
+                self._launch(graphs["pre"])
+                reducer = self.reducer()
+                for g, i in zip(graphs["layers"], reversed(range(len(self.layers)))):
+                    self._launch(g)
+                    reducer.layer_done(i)
+                reducer.finish()
+                self._launch(graphs["post"])
                 if self.shard_optimizer:
                     loss, div, ok = self._scalars
                     self.result = self.transition(self.state, loss, ok, divisor=div, stream=self.stream)
@@ -515,20 +525,21 @@ class EncoderStep:
             return self.result
         self.quantize()
         self.forward()
-        if self.group is not None:
-            import contextlib
-
-            import torch
-            ctx = (torch.cuda.stream(torch.cuda.ExternalStream(self.stream)) if self.stream is not None
-                   else contextlib.nullcontext())
-            with ctx:  # the collectives are ordered after the kernels on this step's stream
-                reducer = BucketReducer(self.grads._base, self._buckets, self.group)
-                self.backward(reducer.layer_done)
-                reducer.finish()
+        if self.comm is not None:
+            reducer = self.reducer()
+            self.backward(reducer.layer_done)
+            reducer.finish()
         else:
             self.backward()
         self._commit()
         return self.result
+
+    def close(self):
+        """Release the communication stream (the communicator belongs to the caller)."""
+        cs, self.comm_stream = self.comm_stream, None
+        if cs is not None and _lib._lib is not None:
+            _lib.lib().mfb_stream_sync(P(cs))
+            _lib.lib().mfb_stream_destroy(P(cs))
 
     def _normalize(self):
         loss, div, ok = self._scalars
@@ -570,22 +581,26 @@ def reduction_plan(layout, n_layers: int, total: int):
 
 
 class BucketReducer:
-    """SUM-allreduces a flat torch tensor bucket by bucket (engine/step.py:62's psum).
+    """SUM-allreduces the flat gradient buffer bucket by bucket (engine/step.py:62's psum).
 
-    ``layer_done(i)`` is called after layer i's backward is enqueued on the
-    current torch stream; its bucket's collective is then enqueued and runs
-    while the backward of the layers below it continues. ``finish()``
-    reduces the remaining ranges and makes the current stream wait for all.
+    ``reduce_range(lo, hi)`` enqueues the reduction of elements [lo, hi);
+    ``before()`` runs before each one (it orders the collective after the
+    kernels enqueued so far) and ``after()`` once at the end (it orders the
+    next kernels after every collective). ``layer_done(i)`` is called after
+    layer i's backward is enqueued: its bucket is reduced while the backward of
+    the layers below continues. ``finish()`` reduces the remaining ranges (the
+    head, the vector leaves and the loss/count tail).
     """
 
-    def __init__(self, flat, plan, group):
-        self.flat, self.group, self.works = flat, group, []
+    def __init__(self, plan, reduce_range, before=None, after=None):
+        self.reduce_range, self.before, self.after = reduce_range, before, after
         self.by_layer = {i: (lo, hi) for kind, i, lo, hi in plan if kind == "layer"}
         self.rest = [(lo, hi) for kind, _, lo, hi in plan if kind == "rest"]
 
     def _reduce(self, lo, hi):
-        import torch.distributed as dist
-        self.works.append(dist.all_reduce(self.flat[lo:hi], group=self.group, async_op=True))
+        if self.before is not None:
+            self.before()
+        self.reduce_range(lo, hi)
 
     def layer_done(self, i):
         self._reduce(*self.by_layer[i])
@@ -593,6 +608,5 @@ class BucketReducer:
     def finish(self):
         for lo, hi in self.rest:
             self._reduce(lo, hi)
-        for w in self.works:
-            w.wait()
-        self.works = []
+        if self.after is not None:
+            self.after()

@@ -398,28 +398,25 @@ def sharded_master_elements(layout, world: int) -> int:
     return max(layout.n_total, shard_slices(layout.n_train, world, 0)[2] * world, 4)
 
 
-def make_sharded_transaction(inventory: Inventory, config: AdamWConfig, group):
+def make_sharded_transaction(inventory: Inventory, config: AdamWConfig, comm):
     """The transaction of ``make_transaction`` with the elementwise passes split
-    across the data-parallel ranks of ``group`` (a torch.distributed process
-    group over NCCL): ``transition(state, active_loss, accumulation_valid, *,
-    divisor=None, stream=None)`` on the reduced gradients already in
-    ``state.arenas["grads"]``.
+    across the data-parallel ranks of ``comm`` (a comm.Communicator):
+    ``transition(state, active_loss, accumulation_valid, *, divisor=None,
+    stream=None)`` on the reduced gradients already in ``state.arenas["grads"]``.
 
     Each rank checks its slice of the state, runs the candidate and the commit
     on its slice of the trainable masters and moments, and the ranks
     all-gather the masters; the global decisions (gradient norm and flags,
     update norm and candidate flags) are SUM-allreduces of three doubles, so
     every rank reaches the same code. The moments outside a rank's slice are
-    never read or written on that rank. ``state.arenas["params"]`` must be a
-    torch-backed DeviceArray (``._base``) of ``sharded_master_elements``.
+    never read or written on that rank. ``state.arenas["params"]`` must hold
+    ``sharded_master_elements`` floats (the all-gather writes every rank's
+    whole slice).
     """
-    import torch
-    import torch.distributed as dist
-
-    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    world, rank = comm.world, comm.rank
     workspace = DeviceArray((_lib.lib().mfb_adamw_workspace_size(),), "uint8")
     result_dev = DeviceArray((6,), "int32")
-    red = torch.zeros(3, dtype=torch.float64, device=f"cuda:{torch.cuda.current_device()}")
+    red = DeviceArray((3 * 8,), "uint8")  # three float64 partials, reduced across the ranks
     scalars = {}
     names = set(inventory.names)
 
@@ -427,9 +424,8 @@ def make_sharded_transaction(inventory: Inventory, config: AdamWConfig, group):
         if not isinstance(state, State) or set(state.layout.specs) != names:
             raise ValueError("Full-weight state does not match the inventory")
         layout, a = state.layout, state.arenas
-        base = a["params"]._base
-        if base is None or base.numel() < sharded_master_elements(layout, world):
-            raise ValueError("sharded AdamW needs a torch-backed master arena of sharded_master_elements")
+        if a["params"].size < sharded_master_elements(layout, world):
+            raise ValueError("sharded AdamW needs a master arena of sharded_master_elements floats")
         loss = _device_scalar(active_loss, "float32", scalars, "loss")
         valid = _device_scalar(bool(accumulation_valid) if not isinstance(accumulation_valid, DeviceArray)
                                else accumulation_valid, "uint8", scalars, "valid")
@@ -442,21 +438,19 @@ def make_sharded_transaction(inventory: Inventory, config: AdamWConfig, group):
                       P(a["grads"].ptr), lo, hi, layout.n_train, layout.n_decayed, layout.n_total,
                       P(a["step"].ptr), P(loss.ptr), P(valid.ptr), P(divisor.ptr) if divisor is not None else None,
                       config.learning_rate, config.beta1, config.beta2, config.epsilon, config.weight_decay,
-                      config.clip_norm, P(red.data_ptr()), P(result_dev.ptr), P(workspace.ptr), workspace.nbytes,
+                      config.clip_norm, P(red.ptr), P(result_dev.ptr), P(workspace.ptr), workspace.nbytes,
                       stream)
 
-        import contextlib
-        ctx = (torch.cuda.stream(torch.cuda.ExternalStream(stream)) if stream is not None
-               else contextlib.nullcontext())
-        with ctx:  # the collectives order after this stream's kernels, and it after them
-            run(_CHECK, c_lo, c_hi)
-            dist.all_reduce(red, group=group)
-            run(_CHECK_FINALIZE, 0, 0)
-            run(_CANDIDATE, t_lo, t_hi)
-            dist.all_reduce(red[:2], group=group)
-            run(_CANDIDATE_FINALIZE, 0, 0)
-            run(_COMMIT, t_lo, t_hi)
-            dist.all_gather_into_tensor(base[:per * world], base[rank * per:(rank + 1) * per], group=group)
+        # Every collective is enqueued on ``stream``, ordered between the passes.
+        run(_CHECK, c_lo, c_hi)
+        comm.allreduce_f64(red.ptr, 3, stream=stream)
+        run(_CHECK_FINALIZE, 0, 0)
+        run(_CANDIDATE, t_lo, t_hi)
+        comm.allreduce_f64(red.ptr, 2, stream=stream)
+        run(_CANDIDATE_FINALIZE, 0, 0)
+        run(_COMMIT, t_lo, t_hi)
+        masters = a["params"]
+        comm.all_gather(masters.view(rank * per, (per,)), masters.view(0, (per * world,)), stream=stream)
         return CommitResult(state, result_dev, stream)
 
     return transition

@@ -60,10 +60,23 @@ def _worker(rank, world, port, out):
     flat = torch.randn(total, generator=g)
     expected = flat.clone()
     dist.all_reduce(expected)
-    red = me.BucketReducer(flat, plan, None)
+    events = []
+
+    def reduce_range(lo, hi):
+        events.append(("reduce", lo, hi))
+        dist.all_reduce(flat[lo:hi])  # the bucket, in place (a view of the flat buffer)
+
+    red = me.BucketReducer(plan, reduce_range, before=lambda: events.append(("before",)),
+                           after=lambda: events.append(("after",)))
     for i in reversed(range(len(TINY.layer_types))):
         red.layer_done(i)
     red.finish()
+    # Every reduction follows its ordering hook; the closing hook comes last, once.
+    assert events[-1] == ("after",) and events.count(("after",)) == 1
+    assert all(events[k] == ("before",) for k in range(0, len(events) - 1, 2))
+    reduced = sorted((e[1], e[2]) for e in events if e[0] == "reduce")
+    assert reduced[0][0] == 0 and reduced[-1][1] == total
+    assert all(a[1] == b[0] for a, b in zip(reduced, reduced[1:]))  # the ranges tile [0, total)
     out[rank] = float((flat - expected).abs().max())
     dist.destroy_process_group()
 

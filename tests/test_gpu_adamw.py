@@ -7,6 +7,7 @@ Rejections must leave every arena byte unchanged.
 """
 
 import ctypes
+import os
 
 import numpy as np
 import pytest
@@ -173,22 +174,16 @@ def test_normalized_step_divides_gradients_and_loss():
             np.testing.assert_array_equal(after[g][n], ref[0][g][n], err_msg=f"{g}/{n}")
 
 
-def _sharded_vs_full(out, port):
-    """Child process: one-rank NCCL group; the sharded transaction against the full one on equal states."""
-    import datetime
-    import os
-
-    import torch
-    import torch.distributed as dist
-
+def _sharded_vs_full(out, uid_path):
+    """Child process: one-rank communicator, full vs sharded transaction on the same state."""
+    from minifield_training_b200 import comm as mcomm
     from minifield_training_b200 import device
-    from minifield_training_b200.device import DeviceArray
+    from minifield_training_b200.device import DeviceArray, sync
     from minifield_training_b200.optimizers import adamw
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
-    torch.cuda.set_device(0)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
     device.set_device(0)
-    dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=60))
+    communicator = mcomm.Communicator(1, 0, mcomm.unique_id_via_file(uid_path, 0), timeout_s=60.0)
     rng = np.random.default_rng(3)
     shapes = {"a.matrix": (37, 53), "b.matrix": (64, 16), "c.vector": (61,), "d.frozen": (9, 7)}
     inv = adamw.build_inventory(shapes, decayed_names=frozenset({"a.matrix", "b.matrix"}),
@@ -203,10 +198,7 @@ def _sharded_vs_full(out, port):
         if bad:
             grads["b.matrix"][3, 5] = np.inf
         layout = adamw.Layout(inv)
-        n_master = adamw.sharded_master_elements(layout, 1)
-        tp = torch.zeros(n_master, dtype=torch.float32, device="cuda:0")
-        masters = DeviceArray((n_master,), "float32", ptr=tp.data_ptr(), owner=False)
-        masters._base = tp
+        masters = DeviceArray.zeros((adamw.sharded_master_elements(layout, 1),), "float32")
         states = {}
         for kind in ("full", "sharded"):
             st = adamw.initialize_state(params, inv, params=masters if kind == "sharded" else None)
@@ -217,23 +209,22 @@ def _sharded_vs_full(out, port):
                 _upload(st.arenas["grads"].view(st.layout.offsets[name], g.shape), g)
             states[kind] = st
         r_full = adamw.make_transaction(inv, cfg)(states["full"], states["full"].gradient_tree(), F(0.7), True)
-        r_sh = adamw.make_sharded_transaction(inv, cfg, dist.group.WORLD)(states["sharded"], F(0.7), True)
-        torch.cuda.synchronize()
+        r_sh = adamw.make_sharded_transaction(inv, cfg, communicator)(states["sharded"], F(0.7), True)
+        sync()
         results[bad] = ([(r.code, r.committed, r.loss, r.gradient_norm, r.update_norm) for r in (r_full, r_sh)],
                         [_read(states[k]) for k in ("full", "sharded")])
     out["results"] = results
-    dist.destroy_process_group()
+    communicator.close()
 
 
-def test_sharded_transaction_on_one_rank_matches_the_full_one():
-    """The sharded passes over a one-rank group reproduce mfb_adamw_commit bit for bit (commit and rejection)."""
-    import os
-
-    import torch.multiprocessing as mp
+def test_sharded_transaction_on_one_rank_matches_the_full_one(tmp_path):
+    """The sharded passes over a one-rank communicator reproduce mfb_adamw_commit bit for bit (commit and
+    rejection)."""
+    import multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
-    run_ranks(ctx, _sharded_vs_full, [(out, 29400 + os.getpid() % 300)], 240)
+    run_ranks(ctx, _sharded_vs_full, [(out, str(tmp_path / "nccl.id"))], 240)
     for bad, (res, arenas) in out["results"].items():
         full, sharded = res
         assert full[0] == sharded[0] and full[1] == sharded[1], (bad, full, sharded)

@@ -1,6 +1,7 @@
 """Data-parallel encoder step on two GPUs against one GPU (needs >= 2 GPUs; skipped otherwise).
 
-Two NCCL ranks each take one row of a two-row batch; after the bucketed
+Two NCCL ranks (the library's communicator, mfb_comm_*; the unique id goes
+through a file) each take one row of a two-row batch; after the bucketed
 allreduce their gradient sums, loss sum and count must equal a single GPU's
 over both rows (up to FP32 summation order: rel-L2 1e-4 per leaf), and after
 the AdamW commit both ranks must hold bit-identical masters (replicated state,
@@ -29,80 +30,74 @@ def _cfg():
                                layer_types=("conv", "full_attention"), vocab=1000)
 
 
-def _rank_graph(rank, port, out):
+def _comm(rank, uid_path):
+    from minifield_training_b200 import comm as mcomm
+    from minifield_training_b200 import device
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    device.set_device(rank)
+    return mcomm.Communicator(2, rank, mcomm.unique_id_via_file(uid_path, rank), timeout_s=120.0)
+
+
+def _rank_graph(rank, uid_path, out):
     """Two captured-graph steps per rank (forward/per-layer backward/commit graphs around the bucket allreduce)."""
     import ctypes
-    import datetime
 
-    import torch
-    import torch.distributed as dist
-
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
-    torch.cuda.set_device(rank)
-    from minifield_training_b200 import _lib, device, workloads
+    from minifield_training_b200 import _lib, workloads
     from minifield_training_b200.models import encoder as me
-    device.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=120))
+    comm = _comm(rank, uid_path)
     cfg = _cfg()
     s = ctypes.c_void_p()
     _lib.call("mfb_stream_create", ctypes.byref(s))
-    step = me.EncoderStep(cfg, rows=1, seed=0, group=dist.group.WORLD, stream=s.value)
+    step = me.EncoderStep(cfg, rows=1, seed=0, comm=comm, stream=s.value)
     step.set_batch(*workloads.encoder_batch(cfg, 7, rows=1, row0=rank))
     step.capture()
     losses = []
     for _ in range(2):
         res = step.step()
         losses.append((res.committed, res.loss))
-    torch.cuda.synchronize()
+    comm.wait(s.value)
     params = {n: v.numpy() for n, v in step.params.items() if n != "lfm2.embed_tokens.weight"}
     out[rank] = (losses, params)
-    dist.barrier()
-    dist.destroy_process_group()
+    step.close()
+    comm.close()
 
 
-def _rank(rank, port, out, shard=False):
-    import datetime
-
-    import torch
-    import torch.distributed as dist
-
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
-    torch.cuda.set_device(rank)
-    from minifield_training_b200 import device, workloads
+def _rank(rank, uid_path, out, shard=False):
+    from minifield_training_b200 import workloads
     from minifield_training_b200.models import encoder as me
-    device.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=120))
+    comm = _comm(rank, uid_path)
     cfg = _cfg()
-    step = me.EncoderStep(cfg, rows=1, seed=0, group=dist.group.WORLD, shard_optimizer=shard)
+    step = me.EncoderStep(cfg, rows=1, seed=0, comm=comm, shard_optimizer=shard)
     step.set_batch(*workloads.encoder_batch(cfg, 7, rows=1, row0=rank))
     step.quantize()
     step.forward()
-    red = me.BucketReducer(step.grads._base, step._buckets, step.group)
+    red = step.reducer()
     step.backward(red.layer_done)
     red.finish()
-    torch.cuda.synchronize()
+    comm.wait(None)
     grads = {n: v.numpy() for n, v in step.gviews.items()}
     lc = step.loss_count.numpy()
     step._commit()
     committed = step.result.committed
     params = {n: v.numpy() for n, v in step.params.items() if n != "lfm2.embed_tokens.weight"}
     out[rank] = (grads, lc, committed, params)
-    dist.barrier()
-    dist.destroy_process_group()
+    step.close()
+    comm.close()
 
 
 @pytest.mark.parametrize("shard", [False, True], ids=["replicated", "sharded_optimizer"])
-def test_two_rank_step_matches_one_gpu(shard):
+def test_two_rank_step_matches_one_gpu(shard, tmp_path):
     require_gpu()
     from minifield_training_b200 import device
     if device.device_count() < 2:
         pytest.skip("needs two GPUs")
-    import torch.multiprocessing as mp
+    import multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
-    port = 29600 + os.getpid() % 300
-    run_ranks(ctx, _rank, [(r, port, out, shard) for r in range(2)], 300)
+    uid = str(tmp_path / "nccl.id")
+    run_ranks(ctx, _rank, [(r, uid, out, shard) for r in range(2)], 300)
     # One GPU over both rows.
     from minifield_training_b200 import workloads
     from minifield_training_b200.device import sync
@@ -128,18 +123,18 @@ def test_two_rank_step_matches_one_gpu(shard):
         np.testing.assert_array_equal(p0[name], p1[name])
 
 
-def test_two_rank_graph_steps_stay_replicated_and_match_eager():
+def test_two_rank_graph_steps_stay_replicated_and_match_eager(tmp_path):
     """Captured-graph steps on two NCCL ranks: both ranks commit, stay bit-identical, and match one eager GPU."""
     require_gpu()
     from minifield_training_b200 import device
     if device.device_count() < 2:
         pytest.skip("needs two GPUs")
-    import torch.multiprocessing as mp
+    import multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
-    port = 29900 + os.getpid() % 50
-    run_ranks(ctx, _rank_graph, [(r, port, out) for r in range(2)], 300)
+    uid = str(tmp_path / "nccl.id")
+    run_ranks(ctx, _rank_graph, [(r, uid, out) for r in range(2)], 300)
     (l0, p0), (l1, p1) = out[0], out[1]
     assert all(c for c, _ in l0) and l0 == l1
     for name in p0:
