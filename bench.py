@@ -495,7 +495,6 @@ class QatWorkload:
         self.gu = DeviceArray((m, 2 * f), "bfloat16")
         self.h = DeviceArray((m, f), "bfloat16")
         self.y = DeviceArray((m, c), "bfloat16")
-        self.dh = DeviceArray((m, f), "bfloat16")
         self.dgu = DeviceArray((m, 2 * f), "bfloat16")
         self.dx = DeviceArray((m, c), "bfloat16")
         self.dw_gu = DeviceArray((2 * f, c), "float32")
@@ -517,16 +516,18 @@ class QatWorkload:
                P(self.e_gu.ptr), None)
         L.call("mfb_fakequant", P(self.w_d.ptr), self.kind, c, f, None, None, P(self.s_d.ptr), None,
                P(self.e_d.ptr), None)
-        self.gemm(self.x, K, c, self.e_gu, K, c, self.gu, 2 * f, BF, m, 2 * f, c)
-        L.call("mfb_swiglu_fwd", P(self.gu.ptr), P(self.h.ptr), m, f, None)
+        # gate|up GEMM with the SwiGLU product in its epilogue, then the down projection
+        L.call("mfb_gemm_swiglu_fwd", P(self.x.ptr), K, c, P(self.e_gu.ptr), c, P(self.gu.ptr), P(self.h.ptr), m, f,
+               c, None)
         self.gemm(self.h, K, f, self.e_d, K, f, self.y, c, BF, m, c, f)
-        self.gemm(self.dy, K, c, self.e_d, MN, f, self.dh, f, BF, m, f, c)
+        # dH = dY . W_down with the SwiGLU backward in its epilogue (writes dGU), then the weight gradients
+        L.call("mfb_gemm_swiglu_bwd", P(self.dy.ptr), K, c, P(self.e_d.ptr), MN, f, P(self.gu.ptr), P(self.dgu.ptr),
+               m, f, c, None)
         self.gemm(self.dy, MN, c, self.h, MN, f, self.dw_d, f, F32, c, f, m, mask=self.s_d)
-        L.call("mfb_swiglu_bwd", P(self.gu.ptr), P(self.dh.ptr), P(self.dgu.ptr), m, f, None)
         self.gemm(self.dgu, K, 2 * f, self.e_gu, MN, c, self.dx, c, BF, m, c, 2 * f)
         self.gemm(self.dgu, MN, 2 * f, self.x, MN, c, self.dw_gu, c, F32, 2 * f, c, m, mask=self.s_gu)
 
-    launches_per_step = 9
+    launches_per_step = 7  # two fake-quant passes, five GEMMs (two with SwiGLU epilogues)
 
 
 # ---------------------------------------------------------------------------
@@ -584,7 +585,8 @@ class EncoderStepWorkload:
 
         per_call = {"mfb_fakequant": 1, "mfb_cast_f32_bf16": 1, "mfb_embed_gather": 1, "mfb_rmsnorm_fwd": 1,
                     "mfb_rmsnorm_bwd": 2, "mfb_gemm_bf16": 1, "mfb_conv_fwd": 1, "mfb_conv_bwd": 2,
-                    "mfb_swiglu_fwd": 1, "mfb_swiglu_bwd": 1, "mfb_qknorm_rope_fwd": 1, "mfb_qknorm_rope_bwd": 3,
+                    "mfb_swiglu_fwd": 1, "mfb_swiglu_bwd": 1,
+                    "mfb_gemm_swiglu_fwd": 1, "mfb_gemm_swiglu_bwd": 1, "mfb_qknorm_rope_fwd": 1, "mfb_qknorm_rope_bwd": 3,
                     "mfb_attn_fwd": 3, "mfb_attn_bwd": 5, "mfb_head_loss": 3, "mfb_step_normalize": 1,
                     "mfb_adamw_commit": 3}
         orig, count = _lib.call, [0]

@@ -201,6 +201,23 @@ enum mfb_major { MFB_MAJOR_K = 0, MFB_MAJOR_MN = 1 };
 enum mfb_dtype { MFB_DTYPE_BF16 = 0, MFB_DTYPE_F32 = 1 };
 int mfb_gemm_bf16(const uint16_t* A, int a_major, int lda, const uint16_t* B, int b_major, int ldb, void* C,
                   int ldc, int out_dtype, int M, int N, int K, float alpha, const uint8_t* mask, void* stream);
+/* The gate|up projection of the SwiGLU block with the SwiGLU product in its
+ * epilogue (src/minifield_training/layers/feed_forward.py:24-35):
+ * gu[M, 2F] = A[M,K] . W13^T (bf16, gate columns [0,F), up [F,2F); W13 is the
+ * row-concatenation [gate; up] of the two [F, K] weights, K-major, row stride
+ * ldw) and h[M, F] = silu(gate) * up (bf16), each value rounded where the
+ * reference's bf16 graph rounds it. F a multiple of 128; gu, h, W13 16-byte
+ * aligned. Replaces mfb_gemm_bf16 + mfb_swiglu_fwd (gu is not re-read). */
+int mfb_gemm_swiglu_fwd(const uint16_t* A, int a_major, int lda, const uint16_t* W13, int ldw, uint16_t* gu,
+                        uint16_t* h, int M, int F, int K, void* stream);
+/* The down projection's input gradient with the SwiGLU backward in its
+ * epilogue: dH = dY[M,K] . Wd (Wd stored [K, F] with b_major MFB_MAJOR_MN, or
+ * [F, K] with MFB_MAJOR_K), rounded to bf16, then dgu[M, 2F] =
+ * [dH * up * silu'(gate), dH * silu(gate)] from gu[M, 2F]. dH is not stored.
+ * F a multiple of 32; gu and dgu distinct, 16-byte aligned. Replaces
+ * mfb_gemm_bf16 + mfb_swiglu_bwd. */
+int mfb_gemm_swiglu_bwd(const uint16_t* dY, int a_major, int lda, const uint16_t* Wd, int b_major, int ldb,
+                        const uint16_t* gu, uint16_t* dgu, int M, int F, int K, void* stream);
 /* The same product with a caller-owned workspace that enables split-K for
  * small M (the decode step's [batch, C] x W^T projections and logits,
  * models/lfm2_5/decode.py:356-361, layers/attention.py:281-322): when the

@@ -73,6 +73,8 @@ SIGNATURES = {
     "mfb_gemm_workspace_size": (SZ, [I, I, I]),
     "mfb_gemm_bf16_ws": (I, [P, I, I, P, I, I, P, I, I, I, I, I, F, P, I, P, SZ, P]),
     "mfb_gemm_status": (I, [IP]),
+    "mfb_gemm_swiglu_fwd": (I, [P, I, I, P, I, P, P, I, I, I, P]),
+    "mfb_gemm_swiglu_bwd": (I, [P, I, I, P, I, I, P, P, I, I, I, P]),
     "mfb_graph_begin": (I, [P]),
     "mfb_graph_end": (I, [P, ctypes.POINTER(ctypes.c_void_p)]),
     "mfb_graph_launch": (I, [P, P]),

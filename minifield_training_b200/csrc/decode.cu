@@ -487,16 +487,14 @@ int check(const void* q, const void* kc, const void* vc, const void* nk, const v
   return MFB_OK;
 }
 
-// Sets the kernel's dynamic shared-memory limit once per device and returns
-// how many CTAs of `smem` bytes fit on one SM.
+// Sets the kernel's dynamic shared-memory limit (on every call: the setting
+// belongs to the CUDA context, which a device reset replaces) and returns how
+// many CTAs of `smem` bytes fit on one SM.
 template <int G>
 int resident_ctas(int dev, size_t smem, int* occ) {
-  static bool configured[64] = {false};
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    const int smem_max = 1024 + (int)layout(MAX_B, MAX_H, 8).total;
-    MFB_CUDA_TRY(cudaFuncSetAttribute(decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max));
-    if (dev >= 0 && dev < 64) configured[dev] = true;
-  }
+  (void)dev;
+  const int smem_max = 1024 + (int)layout(MAX_B, MAX_H, 8).total;
+  MFB_CUDA_TRY(cudaFuncSetAttribute(decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max));
   MFB_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, decode_kernel<G>, THREADS, smem));
   return MFB_OK;
 }

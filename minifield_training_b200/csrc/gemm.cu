@@ -24,6 +24,15 @@
 // the main loop of the next. Every mbarrier wait is bounded; a timeout writes a
 // device status word that the host reads back (no trap, no endless spin).
 //
+// SwiGLU epilogues (layers/feed_forward.py:24-35): in the gate|up projection
+// (EPI_SWIGLU_FWD) each 256-wide B tile is the 128 gate rows and the 128
+// matching up rows of the fused [gate; up] weight (two 128-row TMA boxes), so
+// the epilogue holds gate and up of the same 128 channels and writes gu
+// (bf16, the saved activation) and h = silu(gate) * up in one pass. In the
+// down projection's input gradient (EPI_SWIGLU_BWD) the epilogue rounds the
+// dH tile to bf16, reads gate and up of its channels from gu and writes
+// dGU = [dH * up * silu'(gate), dH * silu(gate)]; dH is never stored.
+//
 // Split-K for small M (the decode step's projections: 64 rows, a handful of
 // 128x256 tiles): when a caller-owned workspace is given and the output tiles
 // fill fewer than half the SMs, the K range is cut into up to 16 slices of at
@@ -51,6 +60,7 @@ constexpr int B_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;
 constexpr int TMEM_COLS = 2 * BN;
+constexpr int EPI_PLAIN = 0, EPI_SWIGLU_FWD = 1, EPI_SWIGLU_BWD = 2;
 
 struct Args {
   void* C;
@@ -64,7 +74,76 @@ struct Args {
   float alpha;
   int k_split, kb_per;  // K slices and k-blocks per slice (1, num_k without split-K)
   float* partial;       // [k_split, M, N] FP32 partials when k_split > 1
+  int epi;              // EPI_*: plain store or a SwiGLU epilogue
+  int F;                // SwiGLU width (gate and up channels each)
+  __nv_bfloat16* h;     // EPI_SWIGLU_FWD: h [M, F], row stride F
+  const __nv_bfloat16* gu;  // EPI_SWIGLU_BWD: gu [M, 2F] read by the epilogue
 };
+
+__device__ __forceinline__ float silu_sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
+
+__device__ __forceinline__ void unpack8_bf16(const uint4& u, float* f) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 x = __bfloat1622float2(h[i]);
+    f[2 * i] = x.x;
+    f[2 * i + 1] = x.y;
+  }
+}
+
+__device__ __forceinline__ void store32_bf16(__nv_bfloat16* dst, const float* v) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 o;
+    o.x = pack_bf16(v[8 * i], v[8 * i + 1]);
+    o.y = pack_bf16(v[8 * i + 2], v[8 * i + 3]);
+    o.z = pack_bf16(v[8 * i + 4], v[8 * i + 5]);
+    o.w = pack_bf16(v[8 * i + 6], v[8 * i + 7]);
+    reinterpret_cast<uint4*>(dst)[i] = o;
+  }
+}
+
+__device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// EPI_SWIGLU_FWD, one row and 32 channels: gate and up accumulators in, gu
+// (gate at column c, up at F + c) and h out, each value rounded to bf16 where
+// the reference's bf16 graph rounds it (full_linear's output, then the product).
+__device__ __forceinline__ void swiglu_fwd_chunk(const Args& a, int row, int c, const uint32_t* g32,
+                                                 const uint32_t* u32) {
+  float g[32], u[32], h[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    g[i] = round_bf16(__uint_as_float(g32[i]) * a.alpha);
+    u[i] = round_bf16(__uint_as_float(u32[i]) * a.alpha);
+    h[i] = g[i] * silu_sigmoid(g[i]) * u[i];
+  }
+  __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)row * a.ldc;
+  store32_bf16(gu + c, g);
+  store32_bf16(gu + a.F + c, u);
+  store32_bf16(a.h + (long long)row * a.F + c, h);
+}
+
+// EPI_SWIGLU_BWD, one row and 32 channels: dH accumulator in, dGU out.
+__device__ __forceinline__ void swiglu_bwd_chunk(const Args& a, int row, int c, const uint32_t* d32) {
+  const __nv_bfloat16* gu = a.gu + (long long)row * 2 * a.F;
+  float g[32], u[32], dg[32], du[32];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    unpack8_bf16(reinterpret_cast<const uint4*>(gu + c)[i], g + 8 * i);
+    unpack8_bf16(reinterpret_cast<const uint4*>(gu + a.F + c)[i], u + 8 * i);
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float d = round_bf16(__uint_as_float(d32[i]) * a.alpha);
+    const float sg = silu_sigmoid(g[i]);
+    du[i] = d * g[i] * sg;
+    dg[i] = d * u[i] * sg * (1.f + g[i] * (1.f - sg));
+  }
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.C) + (long long)row * a.ldc;
+  store32_bf16(out + c, dg);
+  store32_bf16(out + a.F + c, du);
+}
 
 // Work item -> (m block, n block, first and end k-block).
 struct Item {
@@ -228,6 +307,20 @@ __global__ void __launch_bounds__(THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      // One stage of B: rows nb*BN.. (K-major box of BN rows or MN-major
+      // 64-row boxes), or for the SwiGLU forward the 128 gate rows and the 128
+      // up rows of channel block nb (two 128-row K-major boxes).
+      auto load_b = [&](uint32_t sb, int kb, int nb, uint32_t bar) {
+        if (args.epi == EPI_SWIGLU_FWD) {
+          tc::tma_load_2d(sb, &tb, kb * BK, nb * (BN / 2), bar);
+          tc::tma_load_2d(sb + (BN / 2) * 128, &tb, kb * BK, args.F + nb * (BN / 2), bar);
+        } else if (!args.b_mn) {
+          tc::tma_load_2d(sb, &tb, kb * BK, nb * BN, bar);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) tc::tma_load_2d(sb + j * 8192, &tb, nb * BN + 64 * j, kb * BK, bar);
+        }
+      };
       // B (the weights in a decode projection) of the first tile's first
       // stages loads before the dependency wait: a GEMM launched as a
       // programmatic dependent streams it while the previous kernel finishes.
@@ -237,16 +330,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         const Item it = item_of(args, blockIdx.x);
         pre = min(STAGES, it.kb1 - it.kb0);
         for (int i = 0; i < pre; ++i) {
-          const uint32_t sb = sbase + i * STAGE_BYTES + A_BYTES;
-          const int kb = it.kb0 + i;
           tc::mbar_expect_tx(full_bar(i), STAGE_BYTES);
-          if (!args.b_mn) {
-            tc::tma_load_2d(sb, &tb, kb * BK, it.nb * BN, full_bar(i));
-          } else {
-#pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tc::tma_load_2d(sb + j * 8192, &tb, it.nb * BN + 64 * j, kb * BK, full_bar(i));
-          }
+          load_b(sbase + i * STAGE_BYTES + A_BYTES, it.kb0 + i, it.nb, full_bar(i));
         }
       }
       wait_prerequisites();
@@ -269,14 +354,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int i = 0; i < BM / 64; ++i) tc::tma_load_2d(sa + i * 8192, &ta, mb * BM + 64 * i, kb * BK, full_bar(stage));
           }
-          if (!early) {
-            if (!args.b_mn) {
-              tc::tma_load_2d(sb, &tb, kb * BK, nb * BN, full_bar(stage));
-            } else {
-#pragma unroll
-              for (int i = 0; i < BN / 64; ++i) tc::tma_load_2d(sb + i * 8192, &tb, nb * BN + 64 * i, kb * BK, full_bar(stage));
-            }
-          }
+          if (!early) load_b(sb, kb, nb, full_bar(stage));
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -337,17 +415,31 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!tc::mbar_wait(tfull_bar(acc), acc_phase, &g_status, 5)) break;
       tc::tc_fence_after();
       const int row = mb * BM + q * 32 + lane;
+      const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
+      if (args.epi == EPI_SWIGLU_FWD) {
 #pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        uint32_t r[32];
-        tc::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + acc * BN + ch * 32, r);
-        tc::tmem_ld_wait();
-        const int col0 = nb * BN + ch * 32;
-        if (row < args.M && col0 < args.N) {
-          if (args.k_split > 1)
-            store_partial(args, ks, row, col0, r);
-          else
-            store_chunk(args, row, col0, r);
+        for (int ch = 0; ch < BN / 64; ++ch) {  // gate columns ch*32.., up columns BN/2 + ch*32..
+          uint32_t g[32], u[32];
+          tc::tmem_ld_32x32b_x32(tacc + ch * 32, g);
+          tc::tmem_ld_32x32b_x32(tacc + BN / 2 + ch * 32, u);
+          tc::tmem_ld_wait();
+          if (row < args.M) swiglu_fwd_chunk(args, row, nb * (BN / 2) + ch * 32, g, u);
+        }
+      } else {
+#pragma unroll 1
+        for (int ch = 0; ch < BN / 32; ++ch) {
+          uint32_t r[32];
+          tc::tmem_ld_32x32b_x32(tacc + ch * 32, r);
+          tc::tmem_ld_wait();
+          const int col0 = nb * BN + ch * 32;
+          if (row < args.M && col0 < args.N) {
+            if (args.epi == EPI_SWIGLU_BWD)
+              swiglu_bwd_chunk(args, row, col0, r);
+            else if (args.k_split > 1)
+              store_partial(args, ks, row, col0, r);
+            else
+              store_chunk(args, row, col0, r);
+          }
         }
       }
       tc::tc_fence_before();
@@ -570,6 +662,102 @@ extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const u
     MFB_LAUNCH_CHECK("GEMM split-K reduce");
   }
   return MFB_OK;
+}
+
+namespace {
+// Launch of the GEMM kernel with a SwiGLU epilogue (no split-K, no mask).
+int launch_swiglu(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Args& a, int tiles, cudaStream_t stream,
+                  const char* what) {
+  int dev = 0;
+  MFB_CUDA_TRY(cudaGetDevice(&dev));
+  a.k_split = 1;
+  a.kb_per = a.num_k;
+  a.alpha = 1.f;
+  MFB_CUDA_TRY(cudaFuncSetAttribute(gemm::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM));
+  const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
+  gemm::gemm_kernel<<<grid, gemm::THREADS, gemm::SMEM, stream>>>(ta, tb, a);
+  MFB_LAUNCH_CHECK(what);
+  return MFB_OK;
+}
+
+int check_swiglu_operands(const void* A, int a_major, int lda, int M, int F, int K) {
+  MFB_CHECK_ARG(M > 0 && F > 0 && K > 0, "SwiGLU GEMM needs nonempty M/F/K (%d, %d, %d)", M, F, K);
+  MFB_CHECK_ARG(A != nullptr, "NULL operand");
+  MFB_CHECK_ARG(a_major == MFB_MAJOR_K || a_major == MFB_MAJOR_MN, "bad a_major");
+  MFB_CHECK_ARG(lda % 8 == 0 && lda >= (a_major == MFB_MAJOR_K ? K : M), "lda must be a multiple of 8 and cover the operand");
+  MFB_CHECK_ARG(((uintptr_t)A & 15) == 0, "A must be 16-byte aligned (TMA)");
+  return MFB_OK;
+}
+}  // namespace
+
+extern "C" int mfb_gemm_swiglu_fwd(const uint16_t* A, int a_major, int lda, const uint16_t* W13, int ldw, uint16_t* gu,
+                                   uint16_t* h, int M, int F, int K, void* stream) {
+  int st = check_swiglu_operands(A, a_major, lda, M, F, K);
+  if (st) return st;
+  MFB_CHECK_ARG(F % (gemm::BN / 2) == 0, "SwiGLU forward needs F a multiple of %d (F=%d)", gemm::BN / 2, F);
+  MFB_CHECK_ARG(W13 && gu && h, "NULL SwiGLU buffer");
+  MFB_CHECK_ARG(ldw % 8 == 0 && ldw >= K, "ldw must be a multiple of 8 and >= K");
+  MFB_CHECK_ARG((((uintptr_t)W13 | (uintptr_t)gu | (uintptr_t)h) & 15) == 0, "W13, gu and h must be 16-byte aligned");
+  CUtensorMap ta, tb;
+  if (a_major == MFB_MAJOR_K)
+    st = tc::make_tmap_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, gemm::BM);
+  else
+    st = tc::make_tmap_bf16(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, gemm::BK);
+  if (st) return st;
+  if ((st = tc::make_tmap_bf16(&tb, W13, (uint64_t)K, (uint64_t)(2 * F), (uint64_t)ldw, gemm::BN / 2))) return st;
+  gemm::Args a{};
+  a.C = gu;
+  a.ldc = 2LL * F;
+  a.M = M;
+  a.N = 2 * F;
+  a.K = K;
+  a.a_mn = a_major == MFB_MAJOR_MN;
+  a.b_mn = 0;
+  a.num_m = cdiv(M, gemm::BM);
+  a.num_n = F / (gemm::BN / 2);
+  a.num_k = cdiv(K, gemm::BK);
+  a.epi = gemm::EPI_SWIGLU_FWD;
+  a.F = F;
+  a.h = reinterpret_cast<__nv_bfloat16*>(h);
+  return launch_swiglu(ta, tb, a, a.num_m * a.num_n, (cudaStream_t)stream, "mfb_gemm_swiglu_fwd");
+}
+
+extern "C" int mfb_gemm_swiglu_bwd(const uint16_t* dY, int a_major, int lda, const uint16_t* Wd, int b_major, int ldb,
+                                   const uint16_t* gu, uint16_t* dgu, int M, int F, int K, void* stream) {
+  int st = check_swiglu_operands(dY, a_major, lda, M, F, K);
+  if (st) return st;
+  MFB_CHECK_ARG(F % 32 == 0, "SwiGLU backward needs F a multiple of 32 (F=%d)", F);
+  MFB_CHECK_ARG(Wd && gu && dgu, "NULL SwiGLU buffer");
+  MFB_CHECK_ARG(b_major == MFB_MAJOR_K || b_major == MFB_MAJOR_MN, "bad b_major");
+  MFB_CHECK_ARG(ldb % 8 == 0 && ldb >= (b_major == MFB_MAJOR_K ? K : F), "ldb must be a multiple of 8 and cover Wd");
+  MFB_CHECK_ARG((((uintptr_t)Wd | (uintptr_t)gu | (uintptr_t)dgu) & 15) == 0, "Wd, gu and dgu must be 16-byte aligned");
+  MFB_CHECK_ARG(gu != dgu, "dgu must not alias gu");
+  CUtensorMap ta, tb;
+  if (a_major == MFB_MAJOR_K)
+    st = tc::make_tmap_bf16(&ta, dY, (uint64_t)K, (uint64_t)M, (uint64_t)lda, gemm::BM);
+  else
+    st = tc::make_tmap_bf16(&ta, dY, (uint64_t)M, (uint64_t)K, (uint64_t)lda, gemm::BK);
+  if (st) return st;
+  if (b_major == MFB_MAJOR_K)
+    st = tc::make_tmap_bf16(&tb, Wd, (uint64_t)K, (uint64_t)F, (uint64_t)ldb, gemm::BN);
+  else
+    st = tc::make_tmap_bf16(&tb, Wd, (uint64_t)F, (uint64_t)K, (uint64_t)ldb, gemm::BK);
+  if (st) return st;
+  gemm::Args a{};
+  a.C = dgu;
+  a.ldc = 2LL * F;
+  a.M = M;
+  a.N = F;
+  a.K = K;
+  a.a_mn = a_major == MFB_MAJOR_MN;
+  a.b_mn = b_major == MFB_MAJOR_MN;
+  a.num_m = cdiv(M, gemm::BM);
+  a.num_n = cdiv(F, gemm::BN);
+  a.num_k = cdiv(K, gemm::BK);
+  a.epi = gemm::EPI_SWIGLU_BWD;
+  a.F = F;
+  a.gu = reinterpret_cast<const __nv_bfloat16*>(gu);
+  return launch_swiglu(ta, tb, a, a.num_m * a.num_n, (cudaStream_t)stream, "mfb_gemm_swiglu_bwd");
 }
 
 // Reads and clears the GEMM kernels' device status word for the current

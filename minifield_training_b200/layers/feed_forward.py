@@ -5,7 +5,9 @@ feed_forward.py:24-35) under QAT (strategies/quantization.py:114-126): each
 projection master is fake-quantized, cast to bf16 and multiplied on the
 tensor cores; the weight gradients pass through the STE mask in the GEMM
 epilogue. ``w_gate_up`` is [2F, C] (gate rows, then up rows), ``w_down`` is
-[C, F]. The RMSNorm and residual around the chain are not part of it.
+[C, F]. The SwiGLU product runs in the gate|up GEMM's epilogue and its
+backward in the epilogue of the down projection's input gradient. The RMSNorm
+and residual around the chain are not part of it.
 """
 
 import ctypes
@@ -51,11 +53,14 @@ def swiglu_qat_fwd(x, w_gate_up, w_down, kind, stream=None, weights=None):
     """(y [M, C] bf16, residuals). ``weights`` reuses quantize_weights() output."""
     xd = as_device(x, "bfloat16", stream)
     w_gu, ste_gu, w_d, ste_d = weights if weights is not None else quantize_weights(w_gate_up, w_down, kind, stream)
-    m = xd.shape[0]
+    m, c = xd.shape
     f = w_d.shape[1]
-    gu = gemm_nt(xd, w_gu, stream=stream)
+    gu = DeviceArray((m, 2 * f), "bfloat16")
     h = DeviceArray((m, f), "bfloat16")
-    _lib.call("mfb_swiglu_fwd", ctypes.c_void_p(gu.ptr), ctypes.c_void_p(h.ptr), m, f, stream)
+    P = ctypes.c_void_p
+    # gate|up GEMM with silu(gate) * up in its epilogue (gu kept for the backward)
+    _lib.call("mfb_gemm_swiglu_fwd", P(xd.ptr), _lib.MAJOR_K, c, P(w_gu.ptr), c, P(gu.ptr), P(h.ptr), m, f, c,
+              stream)
     y = gemm_nt(h, w_d, stream=stream)
     return y, FfnResiduals(xd, gu, h, w_gu, ste_gu, w_d, ste_d)
 
@@ -63,13 +68,14 @@ def swiglu_qat_fwd(x, w_gate_up, w_down, kind, stream=None, weights=None):
 def swiglu_qat_bwd(res: FfnResiduals, d_y, stream=None):
     """(dx bf16 [M, C], dW_gate_up FP32 [2F, C], dW_down FP32 [C, F])."""
     dy = as_device(d_y, "bfloat16", stream)
-    m = res.x.shape[0]
+    m, c = dy.shape
     f = res.w_d.shape[1]
-    dh = gemm_nn(dy, res.w_d, stream=stream)
     dw_d = gemm_tn(dy, res.h, "float32", mask=res.ste_d, stream=stream)
     dgu = DeviceArray((m, 2 * f), "bfloat16")
-    _lib.call("mfb_swiglu_bwd", ctypes.c_void_p(res.gu.ptr), ctypes.c_void_p(dh.ptr), ctypes.c_void_p(dgu.ptr), m, f,
-              stream)
+    P = ctypes.c_void_p
+    # dH = dY . W_down with the SwiGLU backward in its epilogue (dH itself is never stored)
+    _lib.call("mfb_gemm_swiglu_bwd", P(dy.ptr), _lib.MAJOR_K, c, P(res.w_d.ptr), _lib.MAJOR_MN, f, P(res.gu.ptr),
+              P(dgu.ptr), m, f, c, stream)
     dx = gemm_nn(dgu, res.w_gu, stream=stream)
     dw_gu = gemm_tn(dgu, res.x, "float32", mask=res.ste_gu, stream=stream)
     return dx, dw_gu, dw_d

@@ -232,7 +232,6 @@ class EncoderStep:
         self.d_mid = E((m, c), bf)
         self.d_h = E((m, c), bf)
         self.d_gu = E((m, 2 * f), bf)
-        self.d_f = E((m, f), bf)
         self.d_proj = E((m, max(3 * c, self.nq)), bf)
         self.d_q, self.d_k, self.d_v = E((m, h, 64), bf), E((m, hk, 64), bf), E((m, hk, 64), bf)
         self.d_o = E((m, c), bf)
@@ -358,8 +357,9 @@ class EncoderStep:
                           self.attn_ws.nbytes, s)
                 _fwd(L.o, L.w_out, L.r, m, c, c, s)
             self._rms(L.x, L.r, self._p(p + "ffn_norm.weight"), None, L.mid, L.h2, L.rstd_ffn)
-            _fwd(L.h2, L.w13, L.gu, m, 2 * f, c, s)
-            _lib.call("mfb_swiglu_fwd", P(L.gu.ptr), P(L.a.ptr), m, f, s)
+            # gate|up GEMM with silu(gate) * up in its epilogue
+            _lib.call("mfb_gemm_swiglu_fwd", P(L.h2.ptr), _lib.MAJOR_K, c, P(L.w13.ptr), c, P(L.gu.ptr), P(L.a.ptr),
+                      m, f, c, s)
             _fwd(L.a, L.w2, L.y, m, c, f, s)
             prev = L
         self._rms(prev.mid, prev.y, self._p("lfm2.embedding_norm.weight"), self.mask, self.final, self.enc,
@@ -397,9 +397,10 @@ class EncoderStep:
         L, p = self.layers[i], _prefix(i)
         d, spare = self._grad_bufs(i)
         # FFN: x_next = mid + y.
-        _dgrad(d, L.w2, self.d_f, m, c, f, s)
         _wgrad(d, L.a, self._g(p + "feed_forward.w2.weight").ptr, L.ste2, m, c, f, s)
-        _lib.call("mfb_swiglu_bwd", P(L.gu.ptr), P(self.d_f.ptr), P(self.d_gu.ptr), m, f, s)
+        # dH = d . W2 with the SwiGLU backward in its epilogue: d_gu directly
+        _lib.call("mfb_gemm_swiglu_bwd", P(d.ptr), _lib.MAJOR_K, c, P(L.w2.ptr), _lib.MAJOR_MN, f, P(L.gu.ptr),
+                  P(self.d_gu.ptr), m, f, c, s)
         _dgrad(self.d_gu, L.w13, self.d_h, m, 2 * f, c, s)
         _wgrad(self.d_gu, L.h2, self._g(p + "feed_forward.w1.weight").ptr, L.ste13, m, 2 * f, c, s)
         self._rms_bwd(L.mid, self._p(p + "ffn_norm.weight"), L.rstd_ffn, None, self.d_h, d, self.d_mid,
