@@ -15,11 +15,12 @@
 //   MN-major: boxes {64 rows, 64 K} placed 8192 B apart (LBO), 8-K-row groups
 //             1024 B apart (SBO), K steps advance by 2048 B.
 //
-// Persistent, warp-specialised CTA (one per SM, 192 threads):
+// Persistent, warp-specialised CTA (one per SM, 320 threads):
 //   warp 0     TMA producer over a 4-stage smem ring (48 KB per stage),
 //   warp 1     TMEM allocator + single-thread tcgen05.mma issuer (128x256x16),
-//   warps 2-5  epilogue: tcgen05.ld of the 128x256 fp32 accumulator, scale,
-//              mask, convert and store.
+//   warps 2-9  epilogue, two warps per TMEM lane quarter each taking half of
+//              the tile's columns: tcgen05.ld of the 128x256 fp32
+//              accumulator, scale, mask, convert and store.
 // Two TMEM accumulators (2 x 256 columns) let the epilogue of one tile overlap
 // the main loop of the next. Every mbarrier wait is bounded; a timeout writes a
 // device status word that the host reads back (no trap, no endless spin).
@@ -54,7 +55,8 @@ namespace gemm {
 __device__ int g_status;
 
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
-constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, each storing half of a tile's columns
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -80,7 +82,9 @@ struct Args {
   const __nv_bfloat16* gu;  // EPI_SWIGLU_BWD: gu [M, 2F] read by the epilogue
 };
 
-__device__ __forceinline__ float silu_sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
+// Logistic sigmoid in the SwiGLU epilogues: the hardware exp2 and reciprocal
+// (a few ulp of FP32, far below the bf16 rounding of every value it feeds).
+__device__ __forceinline__ float silu_sigmoid(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
 __device__ __forceinline__ void unpack8_bf16(const uint4& u, float* f) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -124,14 +128,25 @@ __device__ __forceinline__ void swiglu_fwd_chunk(const Args& a, int row, int c, 
   store32_bf16(a.h + (long long)row * a.F + c, h);
 }
 
-// EPI_SWIGLU_BWD, one row and 32 channels: dH accumulator in, dGU out.
-__device__ __forceinline__ void swiglu_bwd_chunk(const Args& a, int row, int c, const uint32_t* d32) {
-  const __nv_bfloat16* gu = a.gu + (long long)row * 2 * a.F;
+// EPI_SWIGLU_BWD: gate and up of one row's 32 channels (loaded a chunk ahead).
+struct GuChunk {
+  uint4 g[4], u[4];
+};
+__device__ __forceinline__ void load_gu(const Args& a, int row, int c, GuChunk& out) {
+  const uint4* gp = reinterpret_cast<const uint4*>(a.gu + (long long)row * 2 * a.F + c);
+  const uint4* up = reinterpret_cast<const uint4*>(a.gu + (long long)row * 2 * a.F + a.F + c);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) out.g[i] = gp[i], out.u[i] = up[i];
+}
+
+// EPI_SWIGLU_BWD, one row and 32 channels: dH accumulator and gate/up in, dGU out.
+__device__ __forceinline__ void swiglu_bwd_chunk(const Args& a, int row, int c, const uint32_t* d32,
+                                                 const GuChunk& in) {
   float g[32], u[32], dg[32], du[32];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    unpack8_bf16(reinterpret_cast<const uint4*>(gu + c)[i], g + 8 * i);
-    unpack8_bf16(reinterpret_cast<const uint4*>(gu + a.F + c)[i], u + 8 * i);
+    unpack8_bf16(in.g[i], g + 8 * i);
+    unpack8_bf16(in.u[i], u + 8 * i);
   }
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
@@ -283,7 +298,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       tc::mbar_init(tfull_bar(a), 1);
-      tc::mbar_init(tempty_bar(a), 128);
+      tc::mbar_init(tempty_bar(a), 32 * EPI_WARPS);
     }
     tc::mbar_init(done_bar, 1);
     tc::mbar_fence_init();
@@ -407,6 +422,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;  // which half of the tile's columns this warp stores
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -418,24 +434,36 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
       if (args.epi == EPI_SWIGLU_FWD) {
 #pragma unroll 1
-        for (int ch = 0; ch < BN / 64; ++ch) {  // gate columns ch*32.., up columns BN/2 + ch*32..
+        for (int ch = half * (BN / 128); ch < (half + 1) * (BN / 128); ++ch) {  // gate ch*32.., up BN/2 + ch*32..
           uint32_t g[32], u[32];
           tc::tmem_ld_32x32b_x32(tacc + ch * 32, g);
           tc::tmem_ld_32x32b_x32(tacc + BN / 2 + ch * 32, u);
           tc::tmem_ld_wait();
           if (row < args.M) swiglu_fwd_chunk(args, row, nb * (BN / 2) + ch * 32, g, u);
         }
+      } else if (args.epi == EPI_SWIGLU_BWD) {
+        const int ch0 = half * (BN / 64), ch1 = ch0 + BN / 64;
+        GuChunk cur, next;
+        if (row < args.M && nb * BN + ch0 * 32 < args.N) load_gu(args, row, nb * BN + ch0 * 32, cur);
+#pragma unroll 1
+        for (int ch = ch0; ch < ch1; ++ch) {
+          uint32_t r[32];
+          tc::tmem_ld_32x32b_x32(tacc + ch * 32, r);
+          const int col0 = nb * BN + ch * 32;
+          if (ch + 1 < ch1 && row < args.M && col0 + 32 < args.N) load_gu(args, row, col0 + 32, next);
+          tc::tmem_ld_wait();
+          if (row < args.M && col0 < args.N) swiglu_bwd_chunk(args, row, col0, r, cur);
+          cur = next;
+        }
       } else {
 #pragma unroll 1
-        for (int ch = 0; ch < BN / 32; ++ch) {
+        for (int ch = half * (BN / 64); ch < (half + 1) * (BN / 64); ++ch) {
           uint32_t r[32];
           tc::tmem_ld_32x32b_x32(tacc + ch * 32, r);
           tc::tmem_ld_wait();
           const int col0 = nb * BN + ch * 32;
           if (row < args.M && col0 < args.N) {
-            if (args.epi == EPI_SWIGLU_BWD)
-              swiglu_bwd_chunk(args, row, col0, r);
-            else if (args.k_split > 1)
+            if (args.k_split > 1)
               store_partial(args, ks, row, col0, r);
             else
               store_chunk(args, row, col0, r);
