@@ -456,12 +456,12 @@ class DecodeOneWorkload:
         self.L.call("mfb_stream_destroy", self.stream)
 
     def kernels_per_step(self):
-        """Kernels one graph replay runs (a split-K GEMM sums its slices inside the one kernel)."""
+        """Kernels one graph replay runs: a split-K GEMM is the GEMM and its reduce."""
         cfg, b = self.cfg, self.batch
         c, f, nq = cfg.hidden, cfg.ffn, (cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim
 
         def gemm(n, k):
-            return 1
+            return 2 if self.L.lib().mfb_gemm_workspace_size(b, n, k) > 0 else 1
 
         n = 1 + 1 + gemm(cfg.vocab, c) + 1  # embedding gather, final norm, tied head, FP32 cast
         for kind in cfg.layer_types:

@@ -229,14 +229,8 @@ int mfb_gemm_swiglu_bwd(const uint16_t* dY, int a_major, int lda, const uint16_t
  * previous kernel on the stream (a created stream, not the legacy default
  * one): its first B tiles load while that kernel finishes, A and the output
  * wait for its completion. The caller asserts that no kernel still running on
- * the stream writes B (true of weights). MFB_GEMM_FUSED_REDUCE sums the K
- * slices inside the GEMM instead of a second kernel: the warp of the slice
- * that finishes a region of a tile last adds every slice's partial in slice
- * order (the same additions as the separate reduce) and stores C. Its
- * workspace starts with 4096 bytes of tile tickets that must be zero before
- * the first call; every call leaves them zero, and calls that share a
- * workspace must run in stream order. */
-enum mfb_gemm_flags { MFB_GEMM_PDL = 1, MFB_GEMM_FUSED_REDUCE = 2 };
+ * the stream writes B (true of weights). */
+enum mfb_gemm_flags { MFB_GEMM_PDL = 1 };
 size_t mfb_gemm_workspace_size(int M, int N, int K);
 int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const uint16_t* B, int b_major, int ldb, void* C,
                      int ldc, int out_dtype, int M, int N, int K, float alpha, const uint8_t* mask, int flags,

@@ -26,7 +26,6 @@ EMPTY_UNIFORM, EMPTY_ZERO = 0, 1
 MAJOR_K, MAJOR_MN = 0, 1
 DTYPE_BF16, DTYPE_F32 = 0, 1
 GEMM_PDL = 1
-GEMM_FUSED_REDUCE = 2
 
 P = ctypes.c_void_p
 I = ctypes.c_int

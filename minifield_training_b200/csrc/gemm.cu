@@ -76,7 +76,6 @@ struct Args {
   float alpha;
   int k_split, kb_per;  // K slices and k-blocks per slice (1, num_k without split-K)
   float* partial;       // [k_split, M, N] FP32 partials when k_split > 1
-  int* tickets;         // per-tile arrival counters (fused reduce), zero between calls
   int epi;              // EPI_*: plain store or a SwiGLU epilogue
   int F;                // SwiGLU width (gate and up channels each)
   __nv_bfloat16* h;     // EPI_SWIGLU_FWD: h [M, F], row stride F
@@ -175,8 +174,6 @@ __device__ __forceinline__ Item item_of(const Args& a, int tile) {
   return it;
 }
 
-__device__ __forceinline__ void store_chunk(const Args& a, int row, int col0, const uint32_t* r);
-
 // Raw FP32 partial of 32 columns of one row for split-K.
 __device__ __forceinline__ void store_partial(const Args& a, int ks, int row, int col0, const uint32_t* r) {
   float* c = a.partial + ((long long)ks * a.M + row) * a.N + col0;
@@ -189,39 +186,6 @@ __device__ __forceinline__ void store_partial(const Args& a, int ks, int row, in
     for (int i = 0; i < 32; ++i)
       if (col0 + i < a.N) c[i] = __uint_as_float(r[i]);
   }
-}
-
-// Fused split-K reduce (MFB_GEMM_FUSED_REDUCE): the epilogue of the slice
-// that finishes a tile last sums every slice's partial of one row's 32
-// columns in slice order -- the same additions, in the same order, as
-// splitk_reduce_kernel -- and stores C. Partials of other CTAs are read
-// through L2 (.cg) after the ticket's acquire fence.
-__device__ __forceinline__ void reduce_partials_chunk(const Args& a, int row, int col0) {
-  const float* p = a.partial + (long long)row * a.N + col0;
-  const long long slice = (long long)a.M * a.N;
-  float acc[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-  const bool vec = col0 + 32 <= a.N && (a.N & 3) == 0;
-  for (int ks = 0; ks < a.k_split; ++ks) {
-    if (vec) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(p + ks * slice) + i);
-        acc[4 * i] += v.x;
-        acc[4 * i + 1] += v.y;
-        acc[4 * i + 2] += v.z;
-        acc[4 * i + 3] += v.w;
-      }
-    } else {
-      for (int i = 0; i < 32; ++i)
-        if (col0 + i < a.N) acc[i] += __ldcg(p + ks * slice + i);
-    }
-  }
-  uint32_t r[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(acc[i]);
-  store_chunk(a, row, col0, r);  // times alpha, converted, stored (no mask with split-K)
 }
 
 // C = alpha * sum over slices of the partials, slice 0 first. One thread per
@@ -508,27 +472,6 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc::tc_fence_before();
       tc::mbar_arrive(tempty_bar(acc));
-      if (args.k_split > 1 && args.tickets) {
-        // Publish this warp's slice of the partial (its 32 rows, its half of
-        // the columns) and take that region's ticket: the warp of the slice
-        // that arrives last reduces the region and leaves the ticket at zero.
-        __threadfence();
-        __syncwarp();
-        int* ticket = args.tickets + (long long)(mb + nb * args.num_m) * EPI_WARPS + (warp - 2);
-        int old = 0;
-        if (lane == 0) old = atomicAdd(ticket, 1);
-        old = __shfl_sync(0xffffffffu, old, 0);
-        if (old == args.k_split - 1) {
-          __threadfence();
-#pragma unroll 1
-          for (int ch = half * (BN / 64); ch < (half + 1) * (BN / 64); ++ch) {
-            const int col0 = nb * BN + ch * 32;
-            if (row < args.M && col0 < args.N) reduce_partials_chunk(args, row, col0);
-          }
-          __syncwarp();
-          if (lane == 0) *ticket = 0;
-        }
-      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
@@ -633,16 +576,12 @@ int choose_split(int M, int N, int K, int sms, int* kb_per) {
 }
 }  // namespace
 
-// With MFB_GEMM_FUSED_REDUCE the workspace starts with a fixed block of tile
-// tickets (one int per tile and epilogue warp); the partials follow it.
-constexpr size_t TICKET_BYTES = 4096;
-
 extern "C" size_t mfb_gemm_workspace_size(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   int dev = 0, kb_per = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
   const int split = choose_split(M, N, K, sm_count(dev), &kb_per);
-  return split > 1 ? TICKET_BYTES + sizeof(float) * (size_t)split * M * N : 0;
+  return split > 1 ? sizeof(float) * (size_t)split * M * N : 0;
 }
 
 extern "C" int mfb_gemm_bf16(const uint16_t* A, int a_major, int lda, const uint16_t* B, int b_major, int ldb,
@@ -656,7 +595,7 @@ extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const u
                                 void* C, int ldc, int out_dtype, int M, int N, int K, float alpha,
                                 const uint8_t* mask, int flags, void* workspace, size_t workspace_bytes,
                                 void* stream) {
-  MFB_CHECK_ARG((flags & ~(MFB_GEMM_PDL | MFB_GEMM_FUSED_REDUCE)) == 0, "unknown GEMM flags %d", flags);
+  MFB_CHECK_ARG((flags & ~MFB_GEMM_PDL) == 0, "unknown GEMM flags %d", flags);
   MFB_CHECK_ARG(!(flags & MFB_GEMM_PDL) || stream != nullptr,
                 "MFB_GEMM_PDL needs a created stream, not the legacy default stream");
   MFB_CHECK_ARG(M > 0 && N > 0 && K > 0, "GEMM needs nonempty M/N/K (%d, %d, %d)", M, N, K);
@@ -703,26 +642,21 @@ extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const u
   a.k_split = 1;
   a.kb_per = a.num_k;
   a.partial = nullptr;
-  const bool fused = (flags & MFB_GEMM_FUSED_REDUCE) != 0;
-  a.tickets = nullptr;
-  if (workspace && !mask && (!fused || workspace_bytes > TICKET_BYTES)) {
+  if (workspace && !mask) {
     int kb_per = 0;
     int split = choose_split(M, N, K, sm_count(dev), &kb_per);
     const size_t slice = sizeof(float) * (size_t)M * N;
-    const size_t room = fused ? workspace_bytes - TICKET_BYTES : workspace_bytes;
-    if (split > 1 && room < slice * split) {  // a smaller workspace gets fewer slices
-      split = (int)std::min<size_t>(split, room / slice);
+    if (split > 1 && workspace_bytes < slice * split) {  // a smaller workspace gets fewer slices
+      split = (int)std::min<size_t>(split, workspace_bytes / slice);
       if (split > 1) {
         kb_per = cdiv(a.num_k, split);
         split = cdiv(a.num_k, kb_per);
       }
     }
-    const bool tickets_fit = (size_t)a.num_m * a.num_n * gemm::EPI_WARPS * sizeof(int) <= TICKET_BYTES;
-    if (split > 1 && ((uintptr_t)workspace & 15) == 0 && (!fused || tickets_fit)) {
+    if (split > 1 && ((uintptr_t)workspace & 15) == 0) {
       a.k_split = split;
       a.kb_per = kb_per;
-      a.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + (fused ? TICKET_BYTES : 0));
-      if (fused) a.tickets = static_cast<int*>(workspace);
+      a.partial = static_cast<float*>(workspace);
     }
   }
   MFB_CUDA_TRY(cudaFuncSetAttribute(gemm::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM));
@@ -744,7 +678,7 @@ extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const u
     gemm::gemm_kernel<<<grid, gemm::THREADS, gemm::SMEM, (cudaStream_t)stream>>>(ta, tb, a);
   }
   MFB_LAUNCH_CHECK("mfb_gemm_bf16");
-  if (a.k_split > 1 && !a.tickets) {
+  if (a.k_split > 1) {
     const long long total = (long long)M * N / (N % 4 == 0 ? 4 : 1);
     const int blocks = (int)std::min<long long>((total + 255) / 256, 8LL * sm_count(dev));
     if (N % 4 == 0)

@@ -183,22 +183,18 @@ class Decoder:
                 o=E((batch, h * 64), "bfloat16"), rq=E((batch, h), "float32"), rk=E((batch, hk), "float32"),
                 rstd=E((batch,), "float32"), enc=E((batch, c), "bfloat16"),
                 logits16=E((batch, cfg.vocab), "bfloat16"), logits=E((batch, cfg.vocab), "float32"),
-                ws=E((max(ws, 16),), "uint8"),
-                # zeroed once: its leading tile tickets must start at zero (every GEMM leaves them zero)
-                gemm_ws=E.zeros((max(gemm_ws, 16),), "uint8"))
+                ws=E((max(ws, 16),), "uint8"), gemm_ws=E((max(gemm_ws, 16),), "uint8"))
         return self._scratch[key]
 
     def _proj(self, x, w, out, m, n, k, B):
-        """out[m, n] = x[m, k] . w[n, k]^T (bf16); split-K through the step's workspace when m is small,
-        with the slices summed inside the GEMM (one kernel per projection).
+        """out[m, n] = x[m, k] . w[n, k]^T (bf16); split-K through the step's workspace when m is small.
 
         On a created stream it launches as a programmatic dependent: the
         weight tiles stream in while the previous kernel (norm, SwiGLU, conv
         step or attention) finishes.
         """
-        flags = _lib.GEMM_FUSED_REDUCE | (_lib.GEMM_PDL if self.stream else 0)
         _lib.call("mfb_gemm_bf16_ws", P(x.ptr), _lib.MAJOR_K, k, P(w.ptr), _lib.MAJOR_K, k, P(out.ptr), n,
-                  _lib.DTYPE_BF16, m, n, k, ctypes.c_float(1.0), None, flags,
+                  _lib.DTYPE_BF16, m, n, k, ctypes.c_float(1.0), None, _lib.GEMM_PDL if self.stream else 0,
                   P(B["gemm_ws"].ptr),
                   B["gemm_ws"].nbytes, self.stream)
 

@@ -147,8 +147,7 @@ def test_swiglu_qat_config4_full_size(kind):
 @pytest.mark.parametrize("ws_fraction", [1.0, 0.3])
 def test_split_k_gemm_for_small_m(m, n, k, ws_fraction):
     """mfb_gemm_bf16_ws: K-sliced partials summed in slice order (deterministic), any workspace size,
-    launched plainly, as a programmatic dependent (MFB_GEMM_PDL) and with the slices summed inside the
-    GEMM (MFB_GEMM_FUSED_REDUCE), all with the same result."""
+    launched plainly and as a programmatic dependent (MFB_GEMM_PDL) with the same result."""
     import ctypes
 
     from minifield_training_b200 import _lib as L
@@ -159,29 +158,20 @@ def test_split_k_gemm_for_small_m(m, n, k, ws_fraction):
     b = round_bf16(rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.05))
     ad, bd = _dev(a), _dev(b)
     need = int(L.lib().mfb_gemm_workspace_size(m, n, k))
-    ws = DeviceArray.zeros((max(16, int(need * ws_fraction) // 16 * 16),), "uint8")
+    ws = DeviceArray((max(16, int(need * ws_fraction) // 16 * 16),), "uint8")
     ref = a.astype(np.float64) @ b.astype(np.float64).T
     stream = ctypes.c_void_p()
     L.call("mfb_stream_create", ctypes.byref(stream))
     for out_dtype, code in (("float32", L.DTYPE_F32), ("bfloat16", L.DTYPE_BF16)):
         outs = []
-        # plain, as a programmatic dependent, then with the slices summed inside the GEMM (twice: its
-        # tile tickets must be back at zero for the second call)
-        for flags, s in ((0, None), (L.GEMM_PDL, stream), (L.GEMM_FUSED_REDUCE, stream),
-                         (L.GEMM_FUSED_REDUCE | L.GEMM_PDL, stream)):
+        for flags, s in ((0, None), (L.GEMM_PDL, stream)):  # plain, then as a programmatic dependent
             c = DeviceArray((m, n), out_dtype)
             L.call("mfb_gemm_bf16_ws", ctypes.c_void_p(ad.ptr), L.MAJOR_K, k, ctypes.c_void_p(bd.ptr), L.MAJOR_K, k,
                    ctypes.c_void_p(c.ptr), n, code, m, n, k, ctypes.c_float(0.5), None, flags,
                    ctypes.c_void_p(ws.ptr), ws.nbytes, s)
             L.call("mfb_stream_sync", s)
             outs.append(c.float32())
-        # Deterministic slice order: the same additions give the same bits. A partial workspace may fit one
-        # slice fewer once the fused reduce's tickets take their 4096 bytes, so across the two families
-        # only the full workspace is compared.
-        np.testing.assert_array_equal(outs[0], outs[1])
-        np.testing.assert_array_equal(outs[2], outs[3])
-        if ws_fraction == 1.0:
-            np.testing.assert_array_equal(outs[0], outs[2])
+        np.testing.assert_array_equal(outs[0], outs[1])  # deterministic slice order
         if out_dtype == "float32":
             np.testing.assert_allclose(outs[0], 0.5 * ref, rtol=1e-5, atol=1e-4 * np.sqrt(k))
         else:
