@@ -16,14 +16,26 @@
 //             1024 B apart (SBO), K steps advance by 2048 B.
 //
 // Persistent, warp-specialised CTA (one per SM, 320 threads):
-//   warp 0     TMA producer over a 4-stage smem ring (48 KB per stage),
-//   warp 1     TMEM allocator + single-thread tcgen05.mma issuer (128x256x16),
+//   warp 0     TMA producer over a shared-memory stage ring,
+//   warp 1     TMEM allocator + single-thread tcgen05.mma issuer,
 //   warps 2-9  epilogue, two warps per TMEM lane quarter each taking half of
-//              the tile's columns: tcgen05.ld of the 128x256 fp32
+//              the tile's columns: tcgen05.ld of the CTA's 128x256 fp32
 //              accumulator, scale, mask, convert and store.
 // Two TMEM accumulators (2 x 256 columns) let the epilogue of one tile overlap
 // the main loop of the next. Every mbarrier wait is bounded; a timeout writes a
 // device status word that the host reads back (no trap, no endless spin).
+//
+// Products with more than 128 output rows run on CTA pairs (clusters of two,
+// tcgen05 cta_group::2): a pair owns a 256x256 output tile, each CTA loads its
+// 128 A rows and 128 of the 256 B rows of a k-block (32 KB per stage, six
+// stages) into its own shared memory, and the even CTA issues one M=256 MMA per
+// 16-deep step that reads both CTAs' halves and accumulates each CTA's 128 rows
+// in that CTA's TMEM. Per 128x256x64 of work a CTA then streams 32 KB from L2
+// instead of 48 KB (a lone CTA loads all 256 B rows, four 48 KB stages), which
+// is what bounds the single-CTA main loop. Loads complete on the even CTA's
+// stage barrier; the MMA commits are multicast to both CTAs' stage-empty and
+// accumulator-full barriers; the odd CTA's epilogue releases an accumulator by
+// a remote arrive. No load is multicast.
 //
 // SwiGLU epilogues (layers/feed_forward.py:24-35): in the gate|up projection
 // (EPI_SWIGLU_FWD) each 256-wide B tile is the 128 gate rows and the 128
@@ -54,13 +66,10 @@ namespace gemm {
 // id of the bounded wait that gave up). Read and cleared by mfb_gemm_status.
 __device__ int g_status;
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, each storing half of a tile's columns
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN * BK * 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int EPI_PLAIN = 0, EPI_SWIGLU_FWD = 1, EPI_SWIGLU_BWD = 2;
 
@@ -77,6 +86,7 @@ struct Args {
   int k_split, kb_per;  // K slices and k-blocks per slice (1, num_k without split-K)
   float* partial;       // [k_split, M, N] FP32 partials when k_split > 1
   int epi;              // EPI_*: plain store or a SwiGLU epilogue
+  int n_fast;           // work order: n block fastest (tiles sharing A rows run together)
   int F;                // SwiGLU width (gate and up channels each)
   __nv_bfloat16* h;     // EPI_SWIGLU_FWD: h [M, F], row stride F
   const __nv_bfloat16* gu;  // EPI_SWIGLU_BWD: gu [M, 2F] read by the epilogue
@@ -160,15 +170,25 @@ __device__ __forceinline__ void swiglu_bwd_chunk(const Args& a, int row, int c, 
   store32_bf16(out + a.F + c, du);
 }
 
-// Work item -> (m block, n block, first and end k-block).
+// Work item -> (m block, n block, first and end k-block). Consecutive items
+// run at the same time on neighbouring SMs, so the fastest-varying block index
+// decides which operand they share through L2: m fastest shares a B panel, n
+// fastest an A panel. The host puts the larger operand's panels in common, so
+// that operand streams from HBM once instead of once per block of the other
+// dimension.
 struct Item {
   int mb, nb, kb0, kb1;
 };
 __device__ __forceinline__ Item item_of(const Args& a, int tile) {
   const int mn = tile % (a.num_m * a.num_n), ks = tile / (a.num_m * a.num_n);
   Item it;
-  it.mb = mn % a.num_m;
-  it.nb = mn / a.num_m;
+  if (a.n_fast) {
+    it.nb = mn % a.num_n;
+    it.mb = mn / a.num_n;
+  } else {
+    it.mb = mn % a.num_m;
+    it.nb = mn / a.num_m;
+  }
   it.kb0 = ks * a.kb_per;
   it.kb1 = min(a.num_k, it.kb0 + a.kb_per);
   return it;
@@ -276,20 +296,115 @@ __device__ __forceinline__ void store_chunk(const Args& a, int row, int col0, co
   }
 }
 
+// Shape of one CTA's share of the work. A CTA always owns 128 accumulator rows
+// and the tile's 256 columns; alone it loads all 256 B rows of a k-block, in a
+// pair (PAIR) it loads its 128 of them and the pair MMA (M = 256) reads both
+// halves, so each CTA streams 32 KB instead of 48 KB per 128x256x64 step.
+// A pair with a SwiGLU epilogue stages its epilogue through shared memory
+// (STAGED): each epilogue warp owns a ring of RING slots of SLOT bytes, one
+// 32-row x 32-column chunk per slot (64-byte swizzled bf16 boxes moved by TMA),
+// and the main loop keeps four stages to make room.
+template <bool PAIR, int EPI>
+struct Shape {
+  static constexpr bool STAGED = PAIR && EPI != EPI_PLAIN;
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
+  static constexpr int B_BYTES = B_ROWS * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = PAIR ? (STAGED ? 4 : 6) : 4;
+  // SwiGLU backward: gate and up boxes in, overwritten in place by dGate and
+  // dUp (two 2 KB boxes); forward: gate, up and h out (three boxes).
+  static constexpr int RING = EPI == EPI_SWIGLU_BWD ? 3 : 2;
+  static constexpr int SLOT = EPI == EPI_SWIGLU_BWD ? 4096 : 6144;
+  static constexpr int RING_BYTES = STAGED ? EPI_WARPS * RING * SLOT : 0;
+  static constexpr int TAIL = 512;  // mbarriers and the TMEM address slot
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + RING_BYTES + TAIL;
+  static_assert(8 * (2 * STAGES + 6 + EPI_WARPS * RING) + 4 <= TAIL, "barriers and the TMEM slot fit the tail");
+  static_assert(SMEM <= 232448, "shared memory per CTA");
+};
+
+// Byte offset of 16-byte piece j of row r in a 32 x 32 bf16 box with 64-byte
+// rows and 64-byte swizzle (piece index XOR bits 7-8 of the row's address):
+// a warp whose lanes each own one row touches every bank once per 8 lanes.
+__device__ __forceinline__ int sw64(int r, int j) { return r * 64 + ((j ^ ((r >> 1) & 3)) << 4); }
+
+__device__ __forceinline__ void box_store32(uint8_t* box, int r, const float* v) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 o;
+    o.x = pack_bf16(v[8 * j], v[8 * j + 1]);
+    o.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
+    o.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
+    o.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
+    *reinterpret_cast<uint4*>(box + sw64(r, j)) = o;
+  }
+}
+__device__ __forceinline__ void box_load32(const uint8_t* box, int r, float* v) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) unpack8_bf16(*reinterpret_cast<const uint4*>(box + sw64(r, j)), v + 8 * j);
+}
+
+// Staged EPI_SWIGLU_FWD for one row r of a chunk: gate, up and h into the
+// slot's three boxes (same rounding as swiglu_fwd_chunk).
+__device__ __forceinline__ void swiglu_fwd_box(float alpha, const uint32_t* g32, const uint32_t* u32, uint8_t* slot,
+                                               int r) {
+  float g[32], u[32], h[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    g[i] = round_bf16(__uint_as_float(g32[i]) * alpha);
+    u[i] = round_bf16(__uint_as_float(u32[i]) * alpha);
+    h[i] = g[i] * silu_sigmoid(g[i]) * u[i];
+  }
+  box_store32(slot, r, g);
+  box_store32(slot + 2048, r, u);
+  box_store32(slot + 4096, r, h);
+}
+
+// Staged EPI_SWIGLU_BWD for one row r of a chunk: gate and up read from the
+// slot, dGate and dUp written over them (same math as swiglu_bwd_chunk).
+__device__ __forceinline__ void swiglu_bwd_box(float alpha, const uint32_t* d32, uint8_t* slot, int r) {
+  float g[32], u[32], dg[32], du[32];
+  box_load32(slot, r, g);
+  box_load32(slot + 2048, r, u);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float d = round_bf16(__uint_as_float(d32[i]) * alpha);
+    const float sg = silu_sigmoid(g[i]);
+    du[i] = d * g[i] * sg;
+    dg[i] = d * u[i] * sg * (1.f + g[i] * (1.f - sg));
+  }
+  box_store32(slot, r, dg);
+  box_store32(slot + 2048, r, du);
+}
+
+// te0 / te1: the staged epilogue's tensor maps (SwiGLU backward: gu loaded,
+// dGU stored; forward: gu and h stored); unused otherwise.
+template <bool PAIR, int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, Args args) {
+    gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                const __grid_constant__ CUtensorMap te0, const __grid_constant__ CUtensorMap te1, Args args) {
+  using S = Shape<PAIR, EPI>;
+  constexpr int STAGES = S::STAGES, STAGE_BYTES = S::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   // Offset from the __shared__ array itself so accesses keep the shared state space.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t bars = sbase + STAGES * STAGE_BYTES;
+  const uint32_t ring = sbase + STAGES * STAGE_BYTES;  // staged epilogue slots (STAGED only)
+  const uint32_t bars = ring + S::RING_BYTES;
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
   auto tfull_bar = [&](int a) { return bars + 8u * (2 * STAGES + a); };
   auto tempty_bar = [&](int a) { return bars + 8u * (2 * STAGES + 2 + a); };
   const uint32_t done_bar = bars + 8u * (2 * STAGES + 4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + STAGES * STAGE_BYTES + 128);
+  // One slot-full barrier per ring slot of each epilogue warp (STAGED).
+  auto slot_bar = [&](int ew, int b) { return bars + 8u * (2 * STAGES + 6 + ew * S::RING + b); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + STAGES * STAGE_BYTES + S::RING_BYTES +
+                                                    8 * (2 * STAGES + 6 + EPI_WARPS * S::RING));
 
+  // In a pair, rank 0 issues the MMAs and owns the stage-full and
+  // accumulator-empty barriers both CTAs signal; work is walked per pair.
+  const uint32_t rank = PAIR ? tc::cluster_ctarank() : 0u;
+  const int unit = PAIR ? (int)tc::cluster_id_x() : (int)blockIdx.x;
+  const int units = PAIR ? (int)tc::cluster_count_x() : (int)gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -298,9 +413,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       tc::mbar_init(tfull_bar(a), 1);
-      tc::mbar_init(tempty_bar(a), 32 * EPI_WARPS);
+      tc::mbar_init(tempty_bar(a), (PAIR ? 2 : 1) * EPI_WARPS);  // one arrival per epilogue warp
     }
     tc::mbar_init(done_bar, 1);
+    if (S::STAGED)
+      for (int i = 0; i < EPI_WARPS * S::RING; ++i) tc::mbar_init(slot_bar(0, i), 1);
     tc::mbar_fence_init();
   }
   if (warp == 0 && lane == 0) {
@@ -308,11 +425,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc::tma_prefetch_desc(&tb);
   }
   if (warp == 1) {
-    tc::tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
-    tc::tmem_relinquish();
+    if (PAIR) {
+      tc::tmem_alloc_pair(smem_u32(tmem_slot), TMEM_COLS);
+      tc::tmem_relinquish_pair();
+    } else {
+      tc::tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+      tc::tmem_relinquish();
+    }
   }
   tc::tc_fence_before();
-  __syncthreads();
+  if (PAIR)
+    tc::cluster_sync();  // the peer's barriers are initialised before any load signals them
+  else
+    __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int num_tiles = args.num_m * args.num_n * args.k_split;
@@ -322,18 +447,37 @@ __global__ void __launch_bounds__(THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      // One stage of B: rows nb*BN.. (K-major box of BN rows or MN-major
-      // 64-row boxes), or for the SwiGLU forward the 128 gate rows and the 128
-      // up rows of channel block nb (two 128-row K-major boxes).
+      // Loads signal the leader's stage-full barrier; only the leader expects
+      // the bytes (both CTAs' loads) and arrives.
+      auto full_target = [&](int s) { return PAIR ? tc::mapa_shared(full_bar(s), 0) : full_bar(s); };
+      auto load = [&](uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+        if (PAIR)
+          tc::tma_load_2d_pair(dst, map, x, y, bar);
+        else
+          tc::tma_load_2d(dst, map, x, y, bar);
+      };
+      auto expect = [&](int s) {
+        if (rank == 0) tc::mbar_expect_tx(full_bar(s), (PAIR ? 2 : 1) * STAGE_BYTES);
+      };
+      // This CTA's B rows of one stage: rows nb*BN + rank*B_ROWS.. (K-major
+      // box or MN-major 64-row boxes), or for the SwiGLU forward the 128 gate
+      // and the 128 up rows of channel block nb (alone: two boxes; in a pair
+      // rank 0 loads the gate rows and rank 1 the up rows, so the accumulator
+      // columns are gate | up either way).
       auto load_b = [&](uint32_t sb, int kb, int nb, uint32_t bar) {
-        if (args.epi == EPI_SWIGLU_FWD) {
-          tc::tma_load_2d(sb, &tb, kb * BK, nb * (BN / 2), bar);
-          tc::tma_load_2d(sb + (BN / 2) * 128, &tb, kb * BK, args.F + nb * (BN / 2), bar);
+        if (EPI == EPI_SWIGLU_FWD) {
+          if (PAIR) {
+            load(sb, &tb, kb * BK, (int)rank * args.F + nb * (BN / 2), bar);
+          } else {
+            load(sb, &tb, kb * BK, nb * (BN / 2), bar);
+            load(sb + (BN / 2) * 128, &tb, kb * BK, args.F + nb * (BN / 2), bar);
+          }
         } else if (!args.b_mn) {
-          tc::tma_load_2d(sb, &tb, kb * BK, nb * BN, bar);
+          load(sb, &tb, kb * BK, nb * BN + (int)rank * S::B_ROWS, bar);
         } else {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j) tc::tma_load_2d(sb + j * 8192, &tb, nb * BN + 64 * j, kb * BK, bar);
+          for (int j = 0; j < S::B_ROWS / 64; ++j)
+            load(sb + j * 8192, &tb, nb * BN + (int)rank * S::B_ROWS + 64 * j, kb * BK, bar);
         }
       };
       // B (the weights in a decode projection) of the first tile's first
@@ -341,35 +485,35 @@ __global__ void __launch_bounds__(THREADS, 1)
       // programmatic dependent streams it while the previous kernel finishes.
       // A, and everything this grid writes, come after the wait.
       int pre = 0;
-      if ((int)blockIdx.x < num_tiles) {
-        const Item it = item_of(args, blockIdx.x);
+      if (unit < num_tiles) {
+        const Item it = item_of(args, unit);
         pre = min(STAGES, it.kb1 - it.kb0);
         for (int i = 0; i < pre; ++i) {
-          tc::mbar_expect_tx(full_bar(i), STAGE_BYTES);
-          load_b(sbase + i * STAGE_BYTES + A_BYTES, it.kb0 + i, it.nb, full_bar(i));
+          expect(i);
+          load_b(sbase + i * STAGE_BYTES + A_BYTES, it.kb0 + i, it.nb, full_target(i));
         }
       }
       wait_prerequisites();
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+      for (int tile = unit; ok && tile < num_tiles; tile += units) {
         const Item it = item_of(args, tile);
-        const int mb = it.mb, nb = it.nb;
+        const int mb = it.mb * (PAIR ? 2 : 1) + (int)rank, nb = it.nb;
         for (int kb = it.kb0; kb < it.kb1; ++kb) {
-          const bool early = tile == (int)blockIdx.x && kb - it.kb0 < pre;  // B already in flight
+          const bool early = tile == unit && kb - it.kb0 < pre;  // B already in flight
           if (!early) {
             if (!tc::mbar_wait(empty_bar(stage), phase ^ 1, &g_status, 1)) {
               ok = false;
               break;
             }
-            tc::mbar_expect_tx(full_bar(stage), STAGE_BYTES);
+            expect(stage);
           }
-          const uint32_t sa = sbase + stage * STAGE_BYTES, sb = sa + A_BYTES;
+          const uint32_t sa = sbase + stage * STAGE_BYTES, sb = sa + A_BYTES, bar = full_target(stage);
           if (!args.a_mn) {
-            tc::tma_load_2d(sa, &ta, kb * BK, mb * BM, full_bar(stage));
+            load(sa, &ta, kb * BK, mb * BM, bar);
           } else {
 #pragma unroll
-            for (int i = 0; i < BM / 64; ++i) tc::tma_load_2d(sa + i * 8192, &ta, mb * BM + 64 * i, kb * BK, full_bar(stage));
+            for (int i = 0; i < BM / 64; ++i) load(sa + i * 8192, &ta, mb * BM + 64 * i, kb * BK, bar);
           }
-          if (!early) load_b(sb, kb, nb, full_bar(stage));
+          if (!early) load_b(sb, kb, nb, bar);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -379,12 +523,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     // The whole warp runs the issue loop (converged); one elected lane issues.
-    {
-      const uint32_t idesc = tc::idesc_bf16_f32(BM, BN, args.a_mn, args.b_mn);
+    // In a pair only rank 0 issues.
+    if (rank == 0) {
+      const uint32_t idesc = tc::idesc_bf16_f32(PAIR ? 2 * BM : BM, BN, args.a_mn, args.b_mn);
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+      for (int tile = unit; ok && tile < num_tiles; tile += units) {
         if (!tc::mbar_wait_w(tempty_bar(acc), acc_phase ^ 1, &g_status, 2)) break;
         tc::tc_fence_after();
         const uint32_t d = tmem + acc * BN;
@@ -402,37 +547,163 @@ __global__ void __launch_bounds__(THREADS, 1)
                                           : tc::smem_desc_sw128(sa + k * 32, 16, 1024);
             const uint64_t bd = args.b_mn ? tc::smem_desc_sw128(sb + k * 2048, 8192, 1024)
                                           : tc::smem_desc_sw128(sb + k * 32, 16, 1024);
-            tc::mma_bf16_w(d, ad, bd, idesc, (kb != it.kb0 || k != 0) ? 1u : 0u);
+            const uint32_t accumulate = (kb != it.kb0 || k != 0) ? 1u : 0u;
+            if (PAIR)
+              tc::mma_bf16_pair_w(d, ad, bd, idesc, accumulate);
+            else
+              tc::mma_bf16_w(d, ad, bd, idesc, accumulate);
           }
-          tc::mma_commit_w(empty_bar(stage));
+          if (PAIR)
+            tc::mma_commit_pair_both_w(empty_bar(stage));
+          else
+            tc::mma_commit_w(empty_bar(stage));
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
-        tc::mma_commit_w(tfull_bar(acc));
+        if (PAIR)
+          tc::mma_commit_pair_both_w(tfull_bar(acc));
+        else
+          tc::mma_commit_w(tfull_bar(acc));
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
         }
       }
       // Drain: every MMA issued above has completed before TMEM is freed.
-      tc::mma_commit_w(done_bar);
+      if (PAIR)
+        tc::mma_commit_pair_w(done_bar);
+      else
+        tc::mma_commit_w(done_bar);
       tc::mbar_wait_w(done_bar, 0, &g_status, 4);
     }
+  } else if constexpr (S::STAGED) {
+    // Staged SwiGLU epilogue. This warp's region of each tile is 32 rows
+    // (TMEM lane quarter q) x half of the columns, walked in 32-column chunks;
+    // chunk i of the warp's whole sequence uses ring slot i % RING. Lane 0
+    // issues the TMA ops and commits one bulk group per chunk (empty when the
+    // chunk lies past M), so "group of chunk i - k done" is a fixed count.
+    constexpr int RING = S::RING, SLOT = S::SLOT;
+    constexpr int CH = EPI == EPI_SWIGLU_BWD ? 4 : 2;  // chunks per tile per warp
+    const int q = warp & 3, half = (warp - 2) >> 2, ew = warp - 2;
+    const uint32_t my_ring = ring + ew * RING * SLOT;
+    uint8_t* my_ring_p = smem + STAGES * STAGE_BYTES + ew * RING * SLOT;
+    // Output column (backward: dH column; forward: channel) of chunk c of a tile.
+    auto chunk_col = [&](const Item& it, int c) {
+      return EPI == EPI_SWIGLU_BWD ? it.nb * BN + half * 128 + c * 32 : it.nb * (BN / 2) + half * 64 + c * 32;
+    };
+    auto chunk_row0 = [&](const Item& it) { return (it.mb * 2 + (int)rank) * BM + q * 32; };
+    uint32_t loaded = 0, slot_phase = 0;  // per slot: a gu load in flight; its barrier parity
+    // SwiGLU backward: the gate|up load of chunk j (any lane computes whether
+    // it exists; lane 0 issues it).
+    auto issue_load = [&](int j) {
+      const int tile = unit + (j / CH) * units;
+      if (tile >= num_tiles) return;
+      const Item it = item_of(args, tile);
+      const int row0 = chunk_row0(it), col = chunk_col(it, j % CH);
+      if (row0 >= args.M || col >= args.F) return;
+      const int b = j % RING;
+      loaded |= 1u << b;
+      if (lane == 0) {
+        tc::mbar_expect_tx(slot_bar(ew, b), 2 * 2048);
+        tc::tma_load_2d(my_ring + b * SLOT, &te0, col, row0, slot_bar(ew, b));
+        tc::tma_load_2d(my_ring + b * SLOT + 2048, &te0, args.F + col, row0, slot_bar(ew, b));
+      }
+    };
+    if (EPI == EPI_SWIGLU_BWD) {
+      wait_prerequisites();  // gu comes from an earlier kernel
+      for (int j = 0; j < RING - 1; ++j) issue_load(j);
+    }
+    int acc = 0, i = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int tile = unit; ok && tile < num_tiles; tile += units) {
+      const Item it = item_of(args, tile);
+      const int row0 = chunk_row0(it);
+      if (!tc::mbar_wait_w(tfull_bar(acc), acc_phase, &g_status, 5)) break;
+      tc::tc_fence_after();
+      const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < CH; ++c, ++i) {
+        const int col = chunk_col(it, c), b = i % RING;
+        const bool live = row0 < args.M && col < args.F;
+        uint8_t* slot_p = my_ring_p + b * SLOT;
+        const uint32_t slot = my_ring + b * SLOT;
+        if (EPI == EPI_SWIGLU_BWD) {
+          uint32_t r[32];
+          tc::tmem_ld_32x32b_x32(tacc + half * 128 + c * 32, r);
+          tc::tmem_ld_wait();
+          if (live && ok) {
+            if (tc::mbar_wait_w(slot_bar(ew, b), (slot_phase >> b) & 1, &g_status, 6)) {
+              slot_phase ^= 1u << b;
+              loaded &= ~(1u << b);
+              swiglu_bwd_box(args.alpha, r, slot_p, lane);
+              tc::fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tc::tma_store_2d(&te1, slot, col, row0);
+                tc::tma_store_2d(&te1, slot + 2048, args.F + col, row0);
+              }
+            } else {
+              ok = false;
+            }
+          }
+          if (lane == 0) {
+            tc::bulk_commit_group();
+            tc::bulk_wait_group_read<1>();  // chunk i - 1's stores have left its slot
+          }
+          __syncwarp();
+          if (ok) issue_load(i + RING - 1);  // into chunk i - 1's slot
+        } else {
+          uint32_t g[32], u[32];
+          tc::tmem_ld_32x32b_x32(tacc + half * 64 + c * 32, g);
+          tc::tmem_ld_32x32b_x32(tacc + BN / 2 + half * 64 + c * 32, u);
+          tc::tmem_ld_wait();
+          if (lane == 0) tc::bulk_wait_group_read<RING - 1>();  // chunk i - RING's stores have left this slot
+          __syncwarp();
+          if (live) {
+            swiglu_fwd_box(args.alpha, g, u, slot_p, lane);
+            tc::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tc::tma_store_2d(&te0, slot, col, row0);
+              tc::tma_store_2d(&te0, slot + 2048, args.F + col, row0);
+              tc::tma_store_2d(&te1, slot + 4096, col, row0);
+            }
+          }
+          if (lane == 0) tc::bulk_commit_group();
+        }
+      }
+      // This warp's TMEM reads of the tile are done: one (remote) arrival on
+      // the leader's accumulator-empty barrier.
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive_cluster(tc::mapa_shared(tempty_bar(acc), 0));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+    // Unwind: loads still in flight (only after a timeout) land before exit,
+    // and every store has completed.
+    for (int b = 0; b < RING; ++b)
+      if (loaded & (1u << b)) tc::mbar_wait_w(slot_bar(ew, b), (slot_phase >> b) & 1, &g_status, 7);
+    if (lane == 0) tc::bulk_wait_group0();
+    __syncwarp();
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;  // which half of the tile's columns this warp stores
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    for (int tile = unit; tile < num_tiles; tile += units) {
       const Item it = item_of(args, tile);
-      const int mb = it.mb, nb = it.nb, ks = tile / (args.num_m * args.num_n);
-      if (!tc::mbar_wait(tfull_bar(acc), acc_phase, &g_status, 5)) break;
+      const int mb = it.mb * (PAIR ? 2 : 1) + (int)rank, nb = it.nb, ks = tile / (args.num_m * args.num_n);
+      if (!tc::mbar_wait_w(tfull_bar(acc), acc_phase, &g_status, 5)) break;
       tc::tc_fence_after();
       const int row = mb * BM + q * 32 + lane;
       const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
-      if (args.epi == EPI_SWIGLU_FWD) {
+      if (EPI == EPI_SWIGLU_FWD) {
 #pragma unroll 1
         for (int ch = half * (BN / 128); ch < (half + 1) * (BN / 128); ++ch) {  // gate ch*32.., up BN/2 + ch*32..
           uint32_t g[32], u[32];
@@ -441,7 +712,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc::tmem_ld_wait();
           if (row < args.M) swiglu_fwd_chunk(args, row, nb * (BN / 2) + ch * 32, g, u);
         }
-      } else if (args.epi == EPI_SWIGLU_BWD) {
+      } else if (EPI == EPI_SWIGLU_BWD) {
         const int ch0 = half * (BN / 64), ch1 = ch0 + BN / 64;
         GuChunk cur, next;
         if (row < args.M && nb * BN + ch0 * 32 < args.N) load_gu(args, row, nb * BN + ch0 * 32, cur);
@@ -470,19 +741,35 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
+      // This warp's TMEM reads are done: one arrival on the leader's
+      // accumulator-empty barrier (remote for the peer of a pair).
       tc::tc_fence_before();
-      tc::mbar_arrive(tempty_bar(acc));
+      __syncwarp();
+      if (lane == 0) {
+        if (PAIR)
+          tc::mbar_arrive_cluster(tc::mapa_shared(tempty_bar(acc), 0));
+        else
+          tc::mbar_arrive(tempty_bar(acc));
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
       }
     }
   }
+  // Both CTAs of a pair stay resident until every MMA, load and remote
+  // arrival of the pair is done; then each frees its TMEM.
   tc::tc_fence_before();
-  __syncthreads();
+  if (PAIR)
+    tc::cluster_sync();
+  else
+    __syncthreads();
   if (warp == 1) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(tmem, TMEM_COLS);
+    if (PAIR)
+      tc::tmem_dealloc_pair(tmem, TMEM_COLS);
+    else
+      tc::tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 
@@ -514,6 +801,20 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t 
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(MFB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return MFB_OK;
+}
+
+int make_tmap_bf16_box32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(MFB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(MFB_ERR_CUDA, "cuTensorMapEncodeTiled (32x32 box) failed (%d)", (int)r);
   return MFB_OK;
 }
 
@@ -584,6 +885,108 @@ extern "C" size_t mfb_gemm_workspace_size(int M, int N, int K) {
   return split > 1 ? sizeof(float) * (size_t)split * M * N : 0;
 }
 
+namespace {
+// CTA pairs of the pair kernel the device keeps resident at once (0: pairs
+// unavailable, run single CTAs). Cached per device.
+int pair_clusters(int dev) {
+  static int counts[64] = {0};
+  if (dev < 0 || dev >= 64) return 0;
+  if (counts[dev]) return counts[dev] > 0 ? counts[dev] : 0;
+  int n = 0;
+  // The largest pair configuration (a staged SwiGLU epilogue): one CTA per SM
+  // for every pair configuration.
+  auto kernel = gemm::gemm_kernel<true, gemm::EPI_SWIGLU_BWD>;
+  constexpr int smem = gemm::Shape<true, gemm::EPI_SWIGLU_BWD>::SMEM;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * (sm_count(dev) / 2));
+    cfg.blockDim = dim3(gemm::THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();  // a refused query leaves no sticky error behind
+  counts[dev] = n > 0 ? n : -1;
+  return n > 0 ? n : 0;
+}
+
+// Whether an (M rows, k_split) product runs on CTA pairs: unsplit, at least
+// two 128-row blocks of output, and a device that co-schedules the pairs.
+bool use_pair(int M, int k_split, int dev) { return k_split == 1 && M > gemm::BM && pair_clusters(dev) > 0; }
+
+// Launches gemm_kernel<PAIR, EPI> over a.num_m x a.num_n x a.k_split work
+// items (a pair's 256 rows or a CTA's 128 per m block), one persistent CTA or
+// CTA pair per SM or SM pair, optionally as a programmatic dependent launch.
+template <bool PAIR, int EPI>
+int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& te0, const CUtensorMap& te1,
+                  const gemm::Args& a, bool pdl, cudaStream_t stream, const char* what) {
+  int dev = 0;
+  MFB_CUDA_TRY(cudaGetDevice(&dev));
+  auto kernel = gemm::gemm_kernel<PAIR, EPI>;
+  constexpr int smem = gemm::Shape<PAIR, EPI>::SMEM;
+  MFB_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int tiles = a.num_m * a.num_n * a.k_split;
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (PAIR) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 2;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.gridDim = dim3(PAIR ? 2 * std::min(tiles, pair_clusters(dev)) : std::min(tiles, sm_count(dev)));
+  cfg.blockDim = dim3(gemm::THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  MFB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, ta, tb, te0, te1, a));
+  MFB_LAUNCH_CHECK(what);
+  return MFB_OK;
+}
+
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& te0, const CUtensorMap& te1,
+                const gemm::Args& a, bool pair, bool pdl, cudaStream_t stream, const char* what) {
+  switch (a.epi) {
+    case gemm::EPI_SWIGLU_FWD:
+      return pair ? launch_kernel<true, gemm::EPI_SWIGLU_FWD>(ta, tb, te0, te1, a, pdl, stream, what)
+                  : launch_kernel<false, gemm::EPI_SWIGLU_FWD>(ta, tb, te0, te1, a, pdl, stream, what);
+    case gemm::EPI_SWIGLU_BWD:
+      return pair ? launch_kernel<true, gemm::EPI_SWIGLU_BWD>(ta, tb, te0, te1, a, pdl, stream, what)
+                  : launch_kernel<false, gemm::EPI_SWIGLU_BWD>(ta, tb, te0, te1, a, pdl, stream, what);
+    default:
+      return pair ? launch_kernel<true, gemm::EPI_PLAIN>(ta, tb, te0, te1, a, pdl, stream, what)
+                  : launch_kernel<false, gemm::EPI_PLAIN>(ta, tb, te0, te1, a, pdl, stream, what);
+  }
+}
+
+// Tensor map of an A operand (K-major [M, K] or MN-major [K, M]).
+int make_tmap_a(CUtensorMap* map, const void* A, int a_major, int lda, int M, int K) {
+  if (a_major == MFB_MAJOR_K) return tc::make_tmap_bf16(map, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, gemm::BM);
+  return tc::make_tmap_bf16(map, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, gemm::BK);
+}
+// Tensor map of a B operand (K-major [N, K]: boxes of a CTA's B rows; MN-major [K, N]: 64 x 64 boxes).
+int make_tmap_b(CUtensorMap* map, const void* B, int b_major, int ldb, int N, int K, bool pair) {
+  if (b_major == MFB_MAJOR_K)
+    return tc::make_tmap_bf16(map, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb,
+                              pair ? gemm::Shape<true, gemm::EPI_PLAIN>::B_ROWS : gemm::Shape<false, gemm::EPI_PLAIN>::B_ROWS);
+  return tc::make_tmap_bf16(map, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, gemm::BK);
+}
+}  // namespace
+
 extern "C" int mfb_gemm_bf16(const uint16_t* A, int a_major, int lda, const uint16_t* B, int b_major, int ldb,
                              void* C, int ldc, int out_dtype, int M, int N, int K, float alpha, const uint8_t* mask,
                              void* stream) {
@@ -609,18 +1012,6 @@ extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const u
   MFB_CHECK_ARG(((uintptr_t)A & 15) == 0 && ((uintptr_t)B & 15) == 0, "A and B must be 16-byte aligned (TMA)");
   int dev = 0;
   MFB_CUDA_TRY(cudaGetDevice(&dev));
-  CUtensorMap ta, tb;
-  int st;
-  if (a_major == MFB_MAJOR_K)
-    st = tc::make_tmap_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, gemm::BM);
-  else
-    st = tc::make_tmap_bf16(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, gemm::BK);
-  if (st) return st;
-  if (b_major == MFB_MAJOR_K)
-    st = tc::make_tmap_bf16(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, gemm::BN);
-  else
-    st = tc::make_tmap_bf16(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, gemm::BK);
-  if (st) return st;
   gemm::Args a{};
   a.C = C;
   a.mask = mask;
@@ -631,7 +1022,6 @@ extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const u
   a.out_f32 = out_dtype == MFB_DTYPE_F32;
   a.a_mn = a_major == MFB_MAJOR_MN;
   a.b_mn = b_major == MFB_MAJOR_MN;
-  a.num_m = cdiv(M, gemm::BM);
   a.num_n = cdiv(N, gemm::BN);
   a.num_k = cdiv(K, gemm::BK);
   a.alpha = alpha;
@@ -659,25 +1049,16 @@ extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const u
       a.partial = static_cast<float*>(workspace);
     }
   }
-  MFB_CUDA_TRY(cudaFuncSetAttribute(gemm::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM));
-  const int tiles = a.num_m * a.num_n * a.k_split;
-  const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
-  if (flags & MFB_GEMM_PDL) {
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(gemm::THREADS);
-    cfg.dynamicSmemBytes = gemm::SMEM;
-    cfg.stream = (cudaStream_t)stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    MFB_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm::gemm_kernel, ta, tb, a));
-  } else {
-    gemm::gemm_kernel<<<grid, gemm::THREADS, gemm::SMEM, (cudaStream_t)stream>>>(ta, tb, a);
-  }
-  MFB_LAUNCH_CHECK("mfb_gemm_bf16");
+  const bool pair = use_pair(M, a.k_split, dev);
+  a.num_m = cdiv(M, pair ? 2 * gemm::BM : gemm::BM);
+  a.n_fast = M > N;  // A (M x K) is the larger operand
+  CUtensorMap ta, tb;
+  int st = make_tmap_a(&ta, A, a_major, lda, M, K);
+  if (st) return st;
+  if ((st = make_tmap_b(&tb, B, b_major, ldb, N, K, pair))) return st;
+  if ((st = launch_gemm(ta, tb, ta, ta, a, pair, (flags & MFB_GEMM_PDL) != 0, (cudaStream_t)stream,
+                        "mfb_gemm_bf16")))
+    return st;
   if (a.k_split > 1) {
     const long long total = (long long)M * N / (N % 4 == 0 ? 4 : 1);
     const int blocks = (int)std::min<long long>((total + 255) / 256, 8LL * sm_count(dev));
@@ -693,21 +1074,6 @@ extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const u
 }
 
 namespace {
-// Launch of the GEMM kernel with a SwiGLU epilogue (no split-K, no mask).
-int launch_swiglu(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Args& a, int tiles, cudaStream_t stream,
-                  const char* what) {
-  int dev = 0;
-  MFB_CUDA_TRY(cudaGetDevice(&dev));
-  a.k_split = 1;
-  a.kb_per = a.num_k;
-  a.alpha = 1.f;
-  MFB_CUDA_TRY(cudaFuncSetAttribute(gemm::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM));
-  const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
-  gemm::gemm_kernel<<<grid, gemm::THREADS, gemm::SMEM, stream>>>(ta, tb, a);
-  MFB_LAUNCH_CHECK(what);
-  return MFB_OK;
-}
-
 int check_swiglu_operands(const void* A, int a_major, int lda, int M, int F, int K) {
   MFB_CHECK_ARG(M > 0 && F > 0 && K > 0, "SwiGLU GEMM needs nonempty M/F/K (%d, %d, %d)", M, F, K);
   MFB_CHECK_ARG(A != nullptr, "NULL operand");
@@ -726,12 +1092,11 @@ extern "C" int mfb_gemm_swiglu_fwd(const uint16_t* A, int a_major, int lda, cons
   MFB_CHECK_ARG(W13 && gu && h, "NULL SwiGLU buffer");
   MFB_CHECK_ARG(ldw % 8 == 0 && ldw >= K, "ldw must be a multiple of 8 and >= K");
   MFB_CHECK_ARG((((uintptr_t)W13 | (uintptr_t)gu | (uintptr_t)h) & 15) == 0, "W13, gu and h must be 16-byte aligned");
+  int dev = 0;
+  MFB_CUDA_TRY(cudaGetDevice(&dev));
+  const bool pair = use_pair(M, 1, dev);
   CUtensorMap ta, tb;
-  if (a_major == MFB_MAJOR_K)
-    st = tc::make_tmap_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, gemm::BM);
-  else
-    st = tc::make_tmap_bf16(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, gemm::BK);
-  if (st) return st;
+  if ((st = make_tmap_a(&ta, A, a_major, lda, M, K))) return st;
   if ((st = tc::make_tmap_bf16(&tb, W13, (uint64_t)K, (uint64_t)(2 * F), (uint64_t)ldw, gemm::BN / 2))) return st;
   gemm::Args a{};
   a.C = gu;
@@ -741,13 +1106,21 @@ extern "C" int mfb_gemm_swiglu_fwd(const uint16_t* A, int a_major, int lda, cons
   a.K = K;
   a.a_mn = a_major == MFB_MAJOR_MN;
   a.b_mn = 0;
-  a.num_m = cdiv(M, gemm::BM);
+  a.num_m = cdiv(M, pair ? 2 * gemm::BM : gemm::BM);
   a.num_n = F / (gemm::BN / 2);
+  a.n_fast = M > 2 * F;
   a.num_k = cdiv(K, gemm::BK);
+  a.k_split = 1;
+  a.kb_per = a.num_k;
+  a.alpha = 1.f;
   a.epi = gemm::EPI_SWIGLU_FWD;
   a.F = F;
   a.h = reinterpret_cast<__nv_bfloat16*>(h);
-  return launch_swiglu(ta, tb, a, a.num_m * a.num_n, (cudaStream_t)stream, "mfb_gemm_swiglu_fwd");
+  CUtensorMap tgu = ta, th = ta;  // staged epilogue: gu and h stored by TMA
+  if (pair && ((st = tc::make_tmap_bf16_box32(&tgu, gu, 2ull * F, (uint64_t)M, 2ull * F)) ||
+               (st = tc::make_tmap_bf16_box32(&th, h, (uint64_t)F, (uint64_t)M, (uint64_t)F))))
+    return st;
+  return launch_gemm(ta, tb, tgu, th, a, pair, false, (cudaStream_t)stream, "mfb_gemm_swiglu_fwd");
 }
 
 extern "C" int mfb_gemm_swiglu_bwd(const uint16_t* dY, int a_major, int lda, const uint16_t* Wd, int b_major, int ldb,
@@ -760,17 +1133,12 @@ extern "C" int mfb_gemm_swiglu_bwd(const uint16_t* dY, int a_major, int lda, con
   MFB_CHECK_ARG(ldb % 8 == 0 && ldb >= (b_major == MFB_MAJOR_K ? K : F), "ldb must be a multiple of 8 and cover Wd");
   MFB_CHECK_ARG((((uintptr_t)Wd | (uintptr_t)gu | (uintptr_t)dgu) & 15) == 0, "Wd, gu and dgu must be 16-byte aligned");
   MFB_CHECK_ARG(gu != dgu, "dgu must not alias gu");
+  int dev = 0;
+  MFB_CUDA_TRY(cudaGetDevice(&dev));
+  const bool pair = use_pair(M, 1, dev);
   CUtensorMap ta, tb;
-  if (a_major == MFB_MAJOR_K)
-    st = tc::make_tmap_bf16(&ta, dY, (uint64_t)K, (uint64_t)M, (uint64_t)lda, gemm::BM);
-  else
-    st = tc::make_tmap_bf16(&ta, dY, (uint64_t)M, (uint64_t)K, (uint64_t)lda, gemm::BK);
-  if (st) return st;
-  if (b_major == MFB_MAJOR_K)
-    st = tc::make_tmap_bf16(&tb, Wd, (uint64_t)K, (uint64_t)F, (uint64_t)ldb, gemm::BN);
-  else
-    st = tc::make_tmap_bf16(&tb, Wd, (uint64_t)F, (uint64_t)K, (uint64_t)ldb, gemm::BK);
-  if (st) return st;
+  if ((st = make_tmap_a(&ta, dY, a_major, lda, M, K))) return st;
+  if ((st = make_tmap_b(&tb, Wd, b_major, ldb, F, K, pair))) return st;
   gemm::Args a{};
   a.C = dgu;
   a.ldc = 2LL * F;
@@ -779,13 +1147,21 @@ extern "C" int mfb_gemm_swiglu_bwd(const uint16_t* dY, int a_major, int lda, con
   a.K = K;
   a.a_mn = a_major == MFB_MAJOR_MN;
   a.b_mn = b_major == MFB_MAJOR_MN;
-  a.num_m = cdiv(M, gemm::BM);
+  a.num_m = cdiv(M, pair ? 2 * gemm::BM : gemm::BM);
   a.num_n = cdiv(F, gemm::BN);
+  a.n_fast = M > F;
   a.num_k = cdiv(K, gemm::BK);
+  a.k_split = 1;
+  a.kb_per = a.num_k;
+  a.alpha = 1.f;
   a.epi = gemm::EPI_SWIGLU_BWD;
   a.F = F;
   a.gu = reinterpret_cast<const __nv_bfloat16*>(gu);
-  return launch_swiglu(ta, tb, a, a.num_m * a.num_n, (cudaStream_t)stream, "mfb_gemm_swiglu_bwd");
+  CUtensorMap tgu = ta, tdgu = ta;  // staged epilogue: gu loaded and dGU stored by TMA
+  if (pair && ((st = tc::make_tmap_bf16_box32(&tgu, gu, 2ull * F, (uint64_t)M, 2ull * F)) ||
+               (st = tc::make_tmap_bf16_box32(&tdgu, dgu, 2ull * F, (uint64_t)M, 2ull * F))))
+    return st;
+  return launch_gemm(ta, tb, tgu, tdgu, a, pair, false, (cudaStream_t)stream, "mfb_gemm_swiglu_bwd");
 }
 
 // Reads and clears the GEMM kernels' device status word for the current

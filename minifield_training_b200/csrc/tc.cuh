@@ -205,6 +205,91 @@ __device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 
+// ---- CTA pairs (cluster of 2, tcgen05 cta_group::2) -------------------------
+// In a pair the even CTA (rank 0) issues the MMAs: A is split by rows between
+// the two CTAs' shared memory (same offsets), B by its N rows, and each CTA's
+// TMEM receives its own 128 rows of the accumulator.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;\n" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;\n" : "=r"(r));
+  return r;
+}
+// Cluster-window address of the shared variable at `addr` in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// Every thread of both CTAs: arrive (release) and wait (acquire). The
+// non-.aligned forms, so that warps need not be converged here.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\nbarrier.cluster.wait.acquire;\n" ::: "memory");
+}
+// Arrive on an mbarrier given by its cluster-window address (local or the
+// peer's), with the default release.cta semantics: it hands TMEM (ordered by
+// the tcgen05 fences around it) back to the peer, and a cluster-scope release
+// would wait for this thread's outstanding memory traffic for microseconds.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];\n" ::"r"(cluster_bar) : "memory");
+}
+// 2-D tiled load into this CTA's shared memory whose completion is counted on
+// an mbarrier of either CTA of the pair (cluster-window address). No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(cluster_bar)
+      : "memory");
+}
+// TMEM allocation shared by the pair: the same warp of both CTAs executes each
+// call; both receive the same column address.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(dst_smem), "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n" ::);
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols));
+}
+// Pair MMA (M = 256 over both CTAs), whole converged warp, one elected lane issues.
+__device__ __forceinline__ void mma_bf16_pair_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n elect.sync _|e, 0xffffffff;\n setp.ne.b32 p, %4, 0;\n"
+      " @e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrives on the mbarrier at offset `bar` in both CTAs of the pair once the
+// pair MMAs issued so far are done (the commit is multicast, the loads are not).
+__device__ __forceinline__ void mma_commit_pair_both_w(uint32_t bar) {
+  asm volatile(
+      "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n}\n" ::
+          "r"(bar),
+      "h"((uint16_t)0x3)
+      : "memory");
+}
+// Same, arriving only on this CTA's mbarrier.
+__device__ __forceinline__ void mma_commit_pair_w(uint32_t bar) {
+  asm volatile(
+      "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(bar)
+      : "memory");
+}
+
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy reads (TMA stores, tcgen05.mma operands).
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -221,7 +306,21 @@ __device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, uint32
       "r"(x), "r"(y), "r"(z), "r"(w), "r"(src)
       : "memory");
 }
+// 2-D tiled store of a shared-memory box (bulk async-group completion); the
+// box is clipped at the tensor's bounds.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];\n" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(src)
+               : "memory");
+}
+// Closes this thread's bulk async-group (an empty group when nothing is pending).
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+// At most N of this thread's most recent bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(N) : "memory");
+}
 // Every committed group has finished reading its shared-memory source.
 __device__ __forceinline__ void bulk_wait_group_read0() {
   asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
@@ -234,6 +333,9 @@ __device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk
 // `ld` elements; box = {64 inner (128 bytes), box_outer}; 128-byte swizzle.
 int make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
                    uint32_t box_outer);
+// 2-D bf16 tensor map with 32 x 32 boxes (64-byte rows) and 64-byte swizzle:
+// the staging boxes of the GEMM epilogues.
+int make_tmap_bf16_box32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld);
 // 3-D bf16 tensor map over a [rows, heads, 64] array (one 64-element head
 // vector per (row, head), rows heads*128 bytes apart), addressed as
 // {dim, row, head} so that box {64, box_rows, heads} lands in shared memory as
