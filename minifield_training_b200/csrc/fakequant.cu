@@ -134,13 +134,22 @@ __global__ void __launch_bounds__(256) fakequant_g128_kernel(const float* __rest
 }
 
 // One CTA per row (per-output-channel scale over any number of columns).
+// VEC4: cols % 4 == 0 and every buffer aligned for 4-column vectors.
+template <bool VEC4>
 __global__ void __launch_bounds__(256) fakequant_channel_kernel(const float* __restrict__ w, int kind, int rows,
                                                                 int cols, QuantOut out, Nf4Table nf4) {
   __shared__ float red[8];
   const int row = blockIdx.x;
   const float* wr = w + (size_t)row * cols;
   float m = 0.f;
-  for (int c = threadIdx.x; c < cols; c += blockDim.x) m = fmaxf(m, fabsf(wr[c]));
+  if constexpr (VEC4) {
+    for (int c = 4 * threadIdx.x; c < cols; c += 4 * blockDim.x) {
+      const float4 x = *reinterpret_cast<const float4*>(wr + c);
+      m = fmaxf(fmaxf(m, fmaxf(fabsf(x.x), fabsf(x.y))), fmaxf(fabsf(x.z), fabsf(x.w)));
+    }
+  } else {
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) m = fmaxf(m, fabsf(wr[c]));
+  }
   m = warp_max(m);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
   __syncthreads();
@@ -152,15 +161,44 @@ __global__ void __launch_bounds__(256) fakequant_channel_kernel(const float* __r
   __syncthreads();
   const float scale = group_scale(kind, red[0]);
   if (threadIdx.x == 0 && out.scales) out.scales[row] = scale;
-  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-    int8_t code;
-    uint8_t ste;
-    const float e = quantize_one(kind, wr[c], scale, nf4, code, ste);
-    const size_t i = (size_t)row * cols + c;
-    if (out.codes) out.codes[i] = code;
-    if (out.ste) out.ste[i] = ste;
-    if (out.eff_f32) out.eff_f32[i] = e;
-    if (out.eff_bf16) out.eff_bf16[i] = __float2bfloat16_rn(e);
+  if constexpr (VEC4) {
+    // Four consecutive columns per thread: one 16-byte load and one store per
+    // output (4 codes, 4 mask bytes, 8 bytes of bf16, 16 of FP32).
+    const size_t i0 = (size_t)row * cols;
+    for (int c = 4 * threadIdx.x; c < cols; c += 4 * blockDim.x) {
+      const float4 x = *reinterpret_cast<const float4*>(wr + c);
+      const float xs[4] = {x.x, x.y, x.z, x.w};
+      float e[4];
+      uint32_t codes = 0, stes = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        int8_t code;
+        uint8_t ste;
+        e[k] = quantize_one(kind, xs[k], scale, nf4, code, ste);
+        codes |= (uint32_t)(uint8_t)code << (8 * k);
+        stes |= (uint32_t)ste << (8 * k);
+      }
+      if (out.codes) *reinterpret_cast<uint32_t*>(out.codes + i0 + c) = codes;
+      if (out.ste) *reinterpret_cast<uint32_t*>(out.ste + i0 + c) = stes;
+      if (out.eff_f32) *reinterpret_cast<float4*>(out.eff_f32 + i0 + c) = make_float4(e[0], e[1], e[2], e[3]);
+      if (out.eff_bf16) {
+        uint2 p;
+        p.x = pack_bf16(e[0], e[1]);
+        p.y = pack_bf16(e[2], e[3]);
+        *reinterpret_cast<uint2*>(out.eff_bf16 + i0 + c) = p;
+      }
+    }
+  } else {
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+      int8_t code;
+      uint8_t ste;
+      const float e = quantize_one(kind, wr[c], scale, nf4, code, ste);
+      const size_t i = (size_t)row * cols + c;
+      if (out.codes) out.codes[i] = code;
+      if (out.ste) out.ste[i] = ste;
+      if (out.eff_f32) out.eff_f32[i] = e;
+      if (out.eff_bf16) out.eff_bf16[i] = __float2bfloat16_rn(e);
+    }
   }
 }
 
@@ -183,7 +221,13 @@ extern "C" int mfb_fakequant(const float* w, int kind, int rows, int cols, int8_
   QuantOut out{codes, scales, ste, eff_f32, reinterpret_cast<__nv_bfloat16*>(eff_bf16)};
   cudaStream_t s = (cudaStream_t)stream;
   if (kind == MFB_QUANT_INT8_CHANNEL) {
-    fakequant_channel_kernel<<<rows, 256, 0, s>>>(w, kind, rows, cols, out, nf4_table());
+    const bool vec4 = cols % 4 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(codes) & 3) == 0 && (reinterpret_cast<uintptr_t>(ste) & 3) == 0 &&
+                      (reinterpret_cast<uintptr_t>(eff_f32) & 15) == 0 && (reinterpret_cast<uintptr_t>(eff_bf16) & 7) == 0;
+    if (vec4)
+      fakequant_channel_kernel<true><<<rows, 256, 0, s>>>(w, kind, rows, cols, out, nf4_table());
+    else
+      fakequant_channel_kernel<false><<<rows, 256, 0, s>>>(w, kind, rows, cols, out, nf4_table());
   } else {
     MFB_CHECK_ARG((reinterpret_cast<uintptr_t>(w) & 15) == 0, "weight must be 16-byte aligned");
     const long long groups = (long long)rows * (cols / 128);

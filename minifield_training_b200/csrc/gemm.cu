@@ -344,14 +344,14 @@ __device__ __forceinline__ void box_load32(const uint8_t* box, int r, float* v) 
 }
 
 // Staged EPI_SWIGLU_FWD for one row r of a chunk: gate, up and h into the
-// slot's three boxes (same rounding as swiglu_fwd_chunk).
-__device__ __forceinline__ void swiglu_fwd_box(float alpha, const uint32_t* g32, const uint32_t* u32, uint8_t* slot,
-                                               int r) {
+// slot's three boxes (same rounding as swiglu_fwd_chunk; the SwiGLU products
+// are unscaled, alpha = 1).
+__device__ __forceinline__ void swiglu_fwd_box(const uint32_t* g32, const uint32_t* u32, uint8_t* slot, int r) {
   float g[32], u[32], h[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
-    g[i] = round_bf16(__uint_as_float(g32[i]) * alpha);
-    u[i] = round_bf16(__uint_as_float(u32[i]) * alpha);
+    g[i] = round_bf16(__uint_as_float(g32[i]));
+    u[i] = round_bf16(__uint_as_float(u32[i]));
     h[i] = g[i] * silu_sigmoid(g[i]) * u[i];
   }
   box_store32(slot, r, g);
@@ -360,14 +360,14 @@ __device__ __forceinline__ void swiglu_fwd_box(float alpha, const uint32_t* g32,
 }
 
 // Staged EPI_SWIGLU_BWD for one row r of a chunk: gate and up read from the
-// slot, dGate and dUp written over them (same math as swiglu_bwd_chunk).
-__device__ __forceinline__ void swiglu_bwd_box(float alpha, const uint32_t* d32, uint8_t* slot, int r) {
+// slot, dGate and dUp written over them (same math as swiglu_bwd_chunk, alpha = 1).
+__device__ __forceinline__ void swiglu_bwd_box(const uint32_t* d32, uint8_t* slot, int r) {
   float g[32], u[32], dg[32], du[32];
   box_load32(slot, r, g);
   box_load32(slot + 2048, r, u);
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
-    const float d = round_bf16(__uint_as_float(d32[i]) * alpha);
+    const float d = round_bf16(__uint_as_float(d32[i]));
     const float sg = silu_sigmoid(g[i]);
     du[i] = d * g[i] * sg;
     dg[i] = d * u[i] * sg * (1.f + g[i] * (1.f - sg));
@@ -595,14 +595,27 @@ __global__ void __launch_bounds__(THREADS, 1)
     };
     auto chunk_row0 = [&](const Item& it) { return (it.mb * 2 + (int)rank) * BM + q * 32; };
     uint32_t loaded = 0, slot_phase = 0;  // per slot: a gu load in flight; its barrier parity
-    // SwiGLU backward: the gate|up load of chunk j (any lane computes whether
-    // it exists; lane 0 issues it).
-    auto issue_load = [&](int j) {
-      const int tile = unit + (j / CH) * units;
-      if (tile >= num_tiles) return;
-      const Item it = item_of(args, tile);
-      const int row0 = chunk_row0(it), col = chunk_col(it, j % CH);
-      if (row0 >= args.M || col >= args.F) return;
+    // SwiGLU backward: gate|up loads run RING - 1 chunks ahead of the math.
+    // The load cursor walks the same chunk sequence; a tile's coordinates are
+    // decoded once, when the cursor enters it.
+    int ld_j = 0, ld_c = 0, ld_tile = unit, ld_row0 = 0, ld_col0 = 0;
+    auto ld_enter = [&]() {
+      if (ld_tile < num_tiles) {
+        const Item it = item_of(args, ld_tile);
+        ld_row0 = chunk_row0(it);
+        ld_col0 = chunk_col(it, 0);
+      }
+    };
+    ld_enter();
+    // The load of the cursor's chunk (every lane tracks it; lane 0 issues it).
+    auto issue_next_load = [&]() {
+      const int j = ld_j++, tile = ld_tile, row0 = ld_row0, col = ld_col0 + ld_c * 32;
+      if (++ld_c == CH) {
+        ld_c = 0;
+        ld_tile += units;
+        ld_enter();
+      }
+      if (tile >= num_tiles || row0 >= args.M || col >= args.F) return;
       const int b = j % RING;
       loaded |= 1u << b;
       if (lane == 0) {
@@ -613,7 +626,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     };
     if (EPI == EPI_SWIGLU_BWD) {
       wait_prerequisites();  // gu comes from an earlier kernel
-      for (int j = 0; j < RING - 1; ++j) issue_load(j);
+      for (int j = 0; j < RING - 1; ++j) issue_next_load();
     }
     int acc = 0, i = 0;
     uint32_t acc_phase = 0;
@@ -638,7 +651,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (tc::mbar_wait_w(slot_bar(ew, b), (slot_phase >> b) & 1, &g_status, 6)) {
               slot_phase ^= 1u << b;
               loaded &= ~(1u << b);
-              swiglu_bwd_box(args.alpha, r, slot_p, lane);
+              swiglu_bwd_box(r, slot_p, lane);
               tc::fence_proxy_async_smem();
               __syncwarp();
               if (lane == 0) {
@@ -654,7 +667,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc::bulk_wait_group_read<1>();  // chunk i - 1's stores have left its slot
           }
           __syncwarp();
-          if (ok) issue_load(i + RING - 1);  // into chunk i - 1's slot
+          if (ok) issue_next_load();  // chunk i + RING - 1, into chunk i - 1's slot
         } else {
           uint32_t g[32], u[32];
           tc::tmem_ld_32x32b_x32(tacc + half * 64 + c * 32, g);
@@ -663,7 +676,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (lane == 0) tc::bulk_wait_group_read<RING - 1>();  // chunk i - RING's stores have left this slot
           __syncwarp();
           if (live) {
-            swiglu_fwd_box(args.alpha, g, u, slot_p, lane);
+            swiglu_fwd_box(g, u, slot_p, lane);
             tc::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
