@@ -501,11 +501,18 @@ class QatWorkload:
         self.dw_d = DeviceArray((c, f), "float32")
         self.kind = _lib.QUANT_KINDS[self.kind_name]
         self.flops = 3.0 * (2.0 * m * c * 2 * f + 2.0 * m * f * c)
+        # Split-K partials for the GEMMs whose output tiles fill the GPU poorly (the weight gradients).
+        shapes = [(m, c, f), (c, f, m), (m, c, 2 * f), (2 * f, c, m)]
+        sizes = [int(_lib.lib().mfb_gemm_workspace_size(*s)) for s in shapes]
+        self.gemm_ws = DeviceArray((max(16, max(sizes)),), "uint8")
+        # Two fake-quant passes, six GEMMs (two with SwiGLU epilogues), one reduce per split GEMM.
+        self.launches_per_step = 8 + sum(1 for z in sizes if z > 0)
 
     def gemm(self, a, am, lda, b, bm, ldb, c, ldc, dt, m, n, k, mask=None):
         P = ctypes.c_void_p
-        self.L.call("mfb_gemm_bf16", P(a.ptr), am, lda, P(b.ptr), bm, ldb, P(c.ptr), ldc, dt, m, n, k,
-                    ctypes.c_float(1.0), P(mask.ptr) if mask is not None else None, None)
+        self.L.call("mfb_gemm_bf16_ws", P(a.ptr), am, lda, P(b.ptr), bm, ldb, P(c.ptr), ldc, dt, m, n, k,
+                    ctypes.c_float(1.0), P(mask.ptr) if mask is not None else None, 0, P(self.gemm_ws.ptr),
+                    self.gemm_ws.nbytes, None)
 
     def step(self):
         P = ctypes.c_void_p
@@ -526,8 +533,6 @@ class QatWorkload:
         self.gemm(self.dy, MN, c, self.h, MN, f, self.dw_d, f, F32, c, f, m, mask=self.s_d)
         self.gemm(self.dgu, K, 2 * f, self.e_gu, MN, c, self.dx, c, BF, m, c, 2 * f)
         self.gemm(self.dgu, MN, 2 * f, self.x, MN, c, self.dw_gu, c, F32, 2 * f, c, m, mask=self.s_gu)
-
-    launches_per_step = 7  # two fake-quant passes, five GEMMs (two with SwiGLU epilogues)
 
 
 # ---------------------------------------------------------------------------
@@ -551,7 +556,11 @@ class EncoderStepWorkload:
         s = ctypes.c_void_p()
         _lib.call("mfb_stream_create", ctypes.byref(s))
         self.stream = s.value
-        self.model = me.EncoderStep(cfg, rows=self.rows, seed=0, comm=dist.communicator(), stream=self.stream)
+        # With several ranks the optimizer is sharded: each rank updates the arena range it owns
+        # and broadcasts it (overlapped with the next forward), instead of every rank running the
+        # whole AdamW transaction.
+        self.model = me.EncoderStep(cfg, rows=self.rows, seed=0, comm=dist.communicator(), stream=self.stream,
+                                    shard_optimizer=dist.world > 1)
         self.batch = workloads.encoder_batch(cfg, 0, rows=self.rows, row0=dist.rank * self.rows)
         self.model.set_batch(*self.batch)
         full_seg = workloads.packed_segments(0, cfg.global_batch, cfg.length)
@@ -588,11 +597,14 @@ class EncoderStepWorkload:
                     "mfb_swiglu_fwd": 1, "mfb_swiglu_bwd": 1,
                     "mfb_gemm_swiglu_fwd": 1, "mfb_gemm_swiglu_bwd": 1, "mfb_qknorm_rope_fwd": 1, "mfb_qknorm_rope_bwd": 3,
                     "mfb_attn_fwd": 3, "mfb_attn_bwd": 5, "mfb_head_loss": 3, "mfb_step_normalize": 1,
-                    "mfb_adamw_commit": 3}
+                    "mfb_adamw_commit": 3, "mfb_adamw_shard_pass": 1}
         orig, count = _lib.call, [0]
 
         def counting(name, *a):
             count[0] += per_call.get(name, 0)
+            if name == "mfb_gemm_bf16_ws":  # the GEMM, and its reduce when the workspace lets K split
+                split = a[15] is not None and _lib.lib().mfb_gemm_workspace_size(a[9], a[10], a[11]) > 0
+                count[0] += 2 if split else 1
             return orig(name, *a)
 
         _lib.call = counting
@@ -746,11 +758,15 @@ def run_reference(args, dist):
 # ---------------------------------------------------------------------------
 
 
-def measure(dist, fn, steps, warmup, clocks=None, stream=None, end_stream=None):
+def measure(dist, fn, steps, warmup, clocks=None, stream=None, end_stream=None, settle=None):
     """Max over ranks of the mean step time, CUDA events on the launching stream.
 
     ``end_stream`` (default ``stream``) is the stream that finishes each step
-    last when a step spans several streams.
+    last when a step spans several streams. ``settle()``, when given, runs
+    before the end event: it orders the timed stream after work a step leaves
+    in flight on other streams (the sharded optimizer's master broadcasts,
+    which the next step's forward overlaps), so every timed step's work is in
+    the timed region.
     """
     from minifield_training_b200.device import Event, sync
 
@@ -765,6 +781,8 @@ def measure(dist, fn, steps, warmup, clocks=None, stream=None, end_stream=None):
     a.record(stream)
     for _ in range(steps):
         fn()
+    if settle is not None:
+        settle()
     b.record(end_stream if end_stream is not None else stream)
     sync()
     clk = clocks.stop() if clocks else None
@@ -891,7 +909,7 @@ def run_ours(args, dist):
         qat = QatWorkload(seed=dist.rank, kind=kind)
         qsteps = max(3, args.steps // 2)
         qms, _ = measure(dist, qat.step, qsteps, max(3, args.warmup // 2))
-        launches += QatWorkload.launches_per_step * qsteps
+        launches += qat.launches_per_step * qsteps
         secondary[key] = {
             "workload": workloads.CONFIG4.name, "kind": kind,
             "tokens_per_s": n * workloads.CONFIG4.tokens / (qms * 1e-3), "ms_per_step": qms,
@@ -903,9 +921,10 @@ def run_ours(args, dist):
         esteps = max(3, args.steps // 5)
         per_step = enc.count_launches()  # one eager step, counting the kernels each call launches
         enc.model.capture()  # then the step replays as CUDA graphs
-        ems, _ = measure(dist, enc.step, esteps, max(3, args.warmup // 2), stream=enc.stream)
+        ems, _ = measure(dist, enc.step, esteps, max(3, args.warmup // 2), stream=enc.stream,
+                         settle=enc.model.settle)
         launches += per_step * esteps
-        e2e_ms, _ = measure(dist, enc.e2e_step, max(3, esteps // 2), 1, stream=enc.stream)
+        e2e_ms, _ = measure(dist, enc.e2e_step, max(3, esteps // 2), 1, stream=enc.stream, settle=enc.model.settle)
         res = enc.model.result
         tflops = enc.global_flops / (ems * 1e-3) / 1e12
         secondary["encoder_step"] = {

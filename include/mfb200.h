@@ -218,13 +218,15 @@ int mfb_gemm_swiglu_fwd(const uint16_t* A, int a_major, int lda, const uint16_t*
  * mfb_gemm_bf16 + mfb_swiglu_bwd. */
 int mfb_gemm_swiglu_bwd(const uint16_t* dY, int a_major, int lda, const uint16_t* Wd, int b_major, int ldb,
                         const uint16_t* gu, uint16_t* dgu, int M, int F, int K, void* stream);
-/* The same product with a caller-owned workspace that enables split-K for
- * small M (the decode step's [batch, C] x W^T projections and logits,
- * models/lfm2_5/decode.py:356-361, layers/attention.py:281-322): when the
- * output tiles fill fewer than half the SMs and mask is NULL, K is cut into
- * slices whose FP32 partials are summed in slice order (deterministic). The
- * workspace (16-byte aligned) needs mfb_gemm_workspace_size(M, N, K) bytes for
- * the full split; a smaller one gets fewer slices, NULL or 0 none.
+/* The same product with a caller-owned workspace that enables split-K where
+ * the output tiles fill the GPU poorly: small M (the decode step's [batch, C]
+ * x W^T projections and logits, models/lfm2_5/decode.py:356-361,
+ * layers/attention.py:281-322) and the weight gradients of full_linear's VJP
+ * (kernels/linear.py:7-13: dW = dY^T X over all tokens, a few output tiles
+ * with a very deep K). K is cut into slices whose FP32 partials are summed in
+ * slice order (deterministic), then scaled and masked. The workspace (16-byte
+ * aligned) needs mfb_gemm_workspace_size(M, N, K) bytes for the full split; a
+ * smaller one gets fewer slices, NULL or 0 none.
  * flags: MFB_GEMM_PDL launches the GEMM as a programmatic dependent of the
  * previous kernel on the stream (a created stream, not the legacy default
  * one): its first B tiles load while that kernel finishes, A and the output
@@ -411,6 +413,16 @@ int mfb_comm_reduce_scatter(void* comm, const void* send, void* recv, size_t rec
                             void* stream);
 /* recv holds world * send_count elements, block r from rank r; send may be recv's own block. */
 int mfb_comm_allgather(void* comm, const void* send, void* recv, size_t send_count, int dtype, void* stream);
+/* Reduction of `count` elements of every rank's `send` into `recv` on rank
+ * `root` only (in place when send == recv), and broadcast of root's `send`
+ * into every rank's `recv` (in place likewise). A data-parallel step whose
+ * optimizer state is partitioned across the ranks reduces each gradient range
+ * to the rank that updates it and broadcasts the updated masters back, in
+ * place of the allreduce of src/minifield_training/engine/step.py:62 (the
+ * reference replicates the state on every rank). */
+int mfb_comm_reduce(void* comm, const void* send, void* recv, size_t count, int dtype, int op, int root,
+                    void* stream);
+int mfb_comm_broadcast(void* comm, const void* send, void* recv, size_t count, int dtype, int root, void* stream);
 int mfb_comm_wait(void* comm, void* stream, double timeout_s);
 int mfb_comm_abort(void* comm);
 /* Finalizes (bounded by the communicator's timeout) and frees; NULL is a no-op. */

@@ -106,6 +106,8 @@ SIGNATURES = {
     "mfb_comm_allreduce": (I, [P, P, P, SZ, I, I, P]),
     "mfb_comm_reduce_scatter": (I, [P, P, P, SZ, I, I, P]),
     "mfb_comm_allgather": (I, [P, P, P, SZ, I, P]),
+    "mfb_comm_reduce": (I, [P, P, P, SZ, I, I, I, P]),
+    "mfb_comm_broadcast": (I, [P, P, P, SZ, I, I, P]),
     "mfb_comm_wait": (I, [P, P, ctypes.c_double]),
     "mfb_comm_abort": (I, [P]),
     "mfb_comm_destroy": (I, [P]),

@@ -138,6 +138,16 @@ class Communicator:
             raise ValueError("all_gather: recv must hold world x send elements of send's type")
         _call("mfb_comm_allgather", self.handle, P(ptr), P(recv.ptr), n, dt, stream)
 
+    def reduce(self, buf: DeviceArray, root: int, op: int = SUM, stream=None):
+        """In-place reduction of ``buf`` over the ranks into rank ``root``'s copy (others unchanged)."""
+        ptr, n, dt = _ptr_count(buf)
+        _call("mfb_comm_reduce", self.handle, P(ptr), P(ptr), n, dt, op, int(root), stream)
+
+    def broadcast(self, buf: DeviceArray, root: int, stream=None):
+        """In-place broadcast of rank ``root``'s ``buf`` to every rank."""
+        ptr, n, dt = _ptr_count(buf)
+        _call("mfb_comm_broadcast", self.handle, P(ptr), P(ptr), n, dt, int(root), stream)
+
     def wait(self, stream=None, timeout_s: float = None):
         """Wait for ``stream`` while watching the communicator (raises CommError on failure or timeout)."""
         _call("mfb_comm_wait", self.handle, stream, ctypes.c_double(timeout_s or self.timeout_s))

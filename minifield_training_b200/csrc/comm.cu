@@ -39,6 +39,8 @@ struct Api {
   ncclResult_t (*ReduceScatter)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                                 cudaStream_t);
   ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+  ncclResult_t (*Reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, int, ncclComm_t, cudaStream_t);
+  ncclResult_t (*Broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
   ncclResult_t (*GroupStart)();
   ncclResult_t (*GroupEnd)();
   ncclResult_t (*GetVersion)(int*);
@@ -157,6 +159,8 @@ extern "C" int mfb_comm_load(const char* path, int* version) {
     MFB_SYM(AllReduce, "ncclAllReduce");
     MFB_SYM(ReduceScatter, "ncclReduceScatter");
     MFB_SYM(AllGather, "ncclAllGather");
+    MFB_SYM(Reduce, "ncclReduce");
+    MFB_SYM(Broadcast, "ncclBroadcast");
     MFB_SYM(GroupStart, "ncclGroupStart");
     MFB_SYM(GroupEnd, "ncclGroupEnd");
     MFB_SYM(GetVersion, "ncclGetVersion");
@@ -247,6 +251,35 @@ extern "C" int mfb_comm_allgather(void* comm, const void* send, void* recv, size
   MFB_CHECK_ARG(send_count == 0 || (send && recv), "NULL collective buffer");
   if (send_count == 0) return MFB_OK;
   return settle(c, g_api.AllGather(send, recv, send_count, t, c->nc, (cudaStream_t)stream), "all-gather");
+}
+
+extern "C" int mfb_comm_reduce(void* comm, const void* send, void* recv, size_t count, int dtype, int op, int root,
+                               void* stream) {
+  Comm* c = nullptr;
+  int st = check_comm(comm, &c);
+  if (st) return st;
+  ncclDataType_t t;
+  ncclRedOp_t r;
+  size_t bytes;
+  if ((st = map_dtype(dtype, &t, &bytes)) || (st = map_op(op, &r))) return st;
+  MFB_CHECK_ARG(root >= 0 && root < c->world, "root %d out of range for %d ranks", root, c->world);
+  MFB_CHECK_ARG(count == 0 || (send && (recv || c->rank != root)), "NULL collective buffer");
+  if (count == 0) return MFB_OK;
+  return settle(c, g_api.Reduce(send, recv, count, t, r, root, c->nc, (cudaStream_t)stream), "reduce");
+}
+
+extern "C" int mfb_comm_broadcast(void* comm, const void* send, void* recv, size_t count, int dtype, int root,
+                                  void* stream) {
+  Comm* c = nullptr;
+  int st = check_comm(comm, &c);
+  if (st) return st;
+  ncclDataType_t t;
+  size_t bytes;
+  if ((st = map_dtype(dtype, &t, &bytes))) return st;
+  MFB_CHECK_ARG(root >= 0 && root < c->world, "root %d out of range for %d ranks", root, c->world);
+  MFB_CHECK_ARG(count == 0 || (recv && (send || c->rank != root)), "NULL collective buffer");
+  if (count == 0) return MFB_OK;
+  return settle(c, g_api.Broadcast(send, recv, count, t, root, c->nc, (cudaStream_t)stream), "broadcast");
 }
 
 extern "C" int mfb_comm_wait(void* comm, void* stream, double timeout_s) {

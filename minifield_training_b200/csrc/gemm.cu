@@ -46,13 +46,13 @@
 // dH tile to bf16, reads gate and up of its channels from gu and writes
 // dGU = [dH * up * silu'(gate), dH * silu(gate)]; dH is never stored.
 //
-// Split-K for small M (the decode step's projections: 64 rows, a handful of
-// 128x256 tiles): when a caller-owned workspace is given and the output tiles
-// fill fewer than half the SMs, the K range is cut into up to 16 slices of at
-// least 256. Each (tile, slice) is a work item that writes its FP32 partial
-// [M, N] to the workspace; splitk_reduce_kernel sums the slices in slice order
-// (deterministic), scales and converts. The weights then stream through many
-// SMs instead of a few.
+// Split-K, when a caller-owned workspace is given and the output tiles fill
+// the GPU poorly: the decode step's projections (64 rows, a handful of tiles)
+// and the weight gradients (a few 256x256 pair tiles, K = the token count).
+// The K range is cut into up to 16 slices (choose_split); each (tile, slice)
+// is a work item that writes its FP32 partial [M, N] to the workspace, and
+// splitk_reduce_kernel sums the slices in slice order (deterministic), scales,
+// applies the STE mask and converts.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -208,12 +208,13 @@ __device__ __forceinline__ void store_partial(const Args& a, int ks, int row, in
   }
 }
 
-// C = alpha * sum over slices of the partials, slice 0 first. One thread per
-// 4 consecutive columns when N % 4 == 0 (float4 partial loads, issued ahead of
+// C = alpha * sum over slices of the partials, slice 0 first, times the
+// uint8 mask [M, N] when given (as store_chunk applies it). One thread per 4
+// consecutive columns when N % 4 == 0 (float4 partial loads, issued ahead of
 // the in-order adds), else one per element.
 template <bool VEC4>
 __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int k_split, int M, int N, void* C,
-                                     long long ldc, int out_f32, float alpha) {
+                                     long long ldc, int out_f32, float alpha, const uint8_t* __restrict__ mask) {
   const int per = VEC4 ? 4 : 1, cols = N / per;
   const long long total = (long long)M * cols, slice = (long long)M * N;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -233,12 +234,22 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int k_sp
         acc[0] += p[ks * slice];
       }
     }
+    float mk[4] = {1.f, 1.f, 1.f, 1.f};
+    if (mask) {
+      if (VEC4) {
+        const uchar4 m4 = *reinterpret_cast<const uchar4*>(mask + (long long)row * N + col);
+        mk[0] = m4.x, mk[1] = m4.y, mk[2] = m4.z, mk[3] = m4.w;
+      } else {
+        mk[0] = mask[(long long)row * N + col];
+      }
+    }
 #pragma unroll
     for (int e = 0; e < per; ++e) {
+      const float v = acc[e] * alpha * mk[e];
       if (out_f32)
-        reinterpret_cast<float*>(C)[row * ldc + col + e] = acc[e] * alpha;
+        reinterpret_cast<float*>(C)[row * ldc + col + e] = v;
       else
-        reinterpret_cast<__nv_bfloat16*>(C)[row * ldc + col + e] = __float2bfloat16_rn(acc[e] * alpha);
+        reinterpret_cast<__nv_bfloat16*>(C)[row * ldc + col + e] = __float2bfloat16_rn(v);
     }
   }
 }
@@ -875,14 +886,47 @@ int sm_count(int dev) {
 }  // namespace
 
 namespace {
-// K slices for an (M, N, K) product: > 1 only when the output tiles fill fewer
-// than half the SMs. A slice keeps at least SPLIT_MIN_KB 64-deep k-blocks and
-// there are at most SPLIT_MAX slices, so the FP32 partials (M x N x 4 bytes a
-// slice) stay well below the bf16 operand bytes a slice streams.
-constexpr int SPLIT_MIN_KB = 4, SPLIT_MAX = 16;
-int choose_split(int M, int N, int K, int sms, int* kb_per) {
-  const int tiles = cdiv(M, gemm::BM) * cdiv(N, gemm::BN), num_k = cdiv(K, gemm::BK);
+int pair_clusters(int dev);
+
+// K slices for an (M, N, K) product, at most SPLIT_MAX.
+//
+// Products of more than 128 rows run on CTA pairs; there the slice count s
+// minimises the modelled time ceil(tiles * s / pairs) / s (waves of one
+// slice's work, in units of one full-K pair tile at ~0.5 us per 64-deep
+// k-block) plus the partials' HBM traffic ((2s + 1) x M x N x 4 bytes at
+// ~6 TB/s: written, read back, and the output) in the same units; a larger s
+// must win by 3 %. This is what fills the GPU for the weight gradients, whose
+// few output tiles (e.g. 1024 x 1024 = 16 pair tiles) run K = 65536 deep.
+// Each slice keeps at least SPLIT_MIN_KB_PAIR k-blocks.
+//
+// Smaller products (the decode projections, single-CTA tiles): > 1 only when
+// the tiles fill fewer than half the SMs, slices of at least SPLIT_MIN_KB
+// k-blocks, so the FP32 partials stay well below the bf16 operand bytes a
+// slice streams.
+constexpr int SPLIT_MIN_KB = 4, SPLIT_MIN_KB_PAIR = 8, SPLIT_MAX = 16;
+int choose_split(int M, int N, int K, int dev, int* kb_per) {
+  const int num_k = cdiv(K, gemm::BK);
   *kb_per = num_k;
+  const int pairs = M > gemm::BM ? pair_clusters(dev) : 0;
+  if (pairs > 0) {
+    const int tiles = cdiv(M, 2 * gemm::BM) * cdiv(N, gemm::BN);
+    const double tile_us = 0.5 * num_k, bytes = 4.0 * M * N;
+    double best_t = 0.0;
+    int best = 1;
+    for (int s = 1; s <= SPLIT_MAX && (s == 1 || num_k / s >= SPLIT_MIN_KB_PAIR); ++s) {
+      const double waves = (double)cdiv(tiles * s, pairs) / s;
+      const double t = waves + (s > 1 ? (2.0 * s + 1.0) * bytes / 6.0e6 / tile_us : 0.0);
+      if (s == 1 || t < 0.97 * best_t) {
+        best_t = t;
+        best = s;
+      }
+    }
+    if (best == 1) return 1;
+    *kb_per = cdiv(num_k, best);
+    return cdiv(num_k, *kb_per);
+  }
+  const int sms = sm_count(dev);
+  const int tiles = cdiv(M, gemm::BM) * cdiv(N, gemm::BN);
   if (2 * tiles > sms || num_k < 2 * SPLIT_MIN_KB) return 1;
   int split = std::min(std::min(num_k / SPLIT_MIN_KB, sms / tiles), SPLIT_MAX);
   *kb_per = cdiv(num_k, split);
@@ -894,7 +938,7 @@ extern "C" size_t mfb_gemm_workspace_size(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   int dev = 0, kb_per = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
-  const int split = choose_split(M, N, K, sm_count(dev), &kb_per);
+  const int split = choose_split(M, N, K, dev, &kb_per);
   return split > 1 ? sizeof(float) * (size_t)split * M * N : 0;
 }
 
@@ -929,9 +973,9 @@ int pair_clusters(int dev) {
   return n > 0 ? n : 0;
 }
 
-// Whether an (M rows, k_split) product runs on CTA pairs: unsplit, at least
-// two 128-row blocks of output, and a device that co-schedules the pairs.
-bool use_pair(int M, int k_split, int dev) { return k_split == 1 && M > gemm::BM && pair_clusters(dev) > 0; }
+// Whether an M-row product runs on CTA pairs: at least two 128-row blocks of
+// output and a device that co-schedules the pairs.
+bool use_pair(int M, int dev) { return M > gemm::BM && pair_clusters(dev) > 0; }
 
 // Launches gemm_kernel<PAIR, EPI> over a.num_m x a.num_n x a.k_split work
 // items (a pair's 256 rows or a CTA's 128 per m block), one persistent CTA or
@@ -1045,9 +1089,9 @@ extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const u
   a.k_split = 1;
   a.kb_per = a.num_k;
   a.partial = nullptr;
-  if (workspace && !mask) {
+  if (workspace) {
     int kb_per = 0;
-    int split = choose_split(M, N, K, sm_count(dev), &kb_per);
+    int split = choose_split(M, N, K, dev, &kb_per);
     const size_t slice = sizeof(float) * (size_t)M * N;
     if (split > 1 && workspace_bytes < slice * split) {  // a smaller workspace gets fewer slices
       split = (int)std::min<size_t>(split, workspace_bytes / slice);
@@ -1062,7 +1106,7 @@ extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const u
       a.partial = static_cast<float*>(workspace);
     }
   }
-  const bool pair = use_pair(M, a.k_split, dev);
+  const bool pair = use_pair(M, dev);
   a.num_m = cdiv(M, pair ? 2 * gemm::BM : gemm::BM);
   a.n_fast = M > N;  // A (M x K) is the larger operand
   CUtensorMap ta, tb;
@@ -1073,14 +1117,15 @@ extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const u
                         "mfb_gemm_bf16")))
     return st;
   if (a.k_split > 1) {
-    const long long total = (long long)M * N / (N % 4 == 0 ? 4 : 1);
+    const bool vec4 = N % 4 == 0 && ((uintptr_t)mask & 3) == 0;
+    const long long total = (long long)M * N / (vec4 ? 4 : 1);
     const int blocks = (int)std::min<long long>((total + 255) / 256, 8LL * sm_count(dev));
-    if (N % 4 == 0)
+    if (vec4)
       gemm::splitk_reduce_kernel<true><<<blocks, 256, 0, (cudaStream_t)stream>>>(a.partial, a.k_split, M, N, C,
-                                                                                ldc, a.out_f32, alpha);
+                                                                                ldc, a.out_f32, alpha, mask);
     else
       gemm::splitk_reduce_kernel<false><<<blocks, 256, 0, (cudaStream_t)stream>>>(a.partial, a.k_split, M, N, C,
-                                                                                 ldc, a.out_f32, alpha);
+                                                                                 ldc, a.out_f32, alpha, mask);
     MFB_LAUNCH_CHECK("GEMM split-K reduce");
   }
   return MFB_OK;
@@ -1107,7 +1152,7 @@ extern "C" int mfb_gemm_swiglu_fwd(const uint16_t* A, int a_major, int lda, cons
   MFB_CHECK_ARG((((uintptr_t)W13 | (uintptr_t)gu | (uintptr_t)h) & 15) == 0, "W13, gu and h must be 16-byte aligned");
   int dev = 0;
   MFB_CUDA_TRY(cudaGetDevice(&dev));
-  const bool pair = use_pair(M, 1, dev);
+  const bool pair = use_pair(M, dev);
   CUtensorMap ta, tb;
   if ((st = make_tmap_a(&ta, A, a_major, lda, M, K))) return st;
   if ((st = tc::make_tmap_bf16(&tb, W13, (uint64_t)K, (uint64_t)(2 * F), (uint64_t)ldw, gemm::BN / 2))) return st;
@@ -1148,7 +1193,7 @@ extern "C" int mfb_gemm_swiglu_bwd(const uint16_t* dY, int a_major, int lda, con
   MFB_CHECK_ARG(gu != dgu, "dgu must not alias gu");
   int dev = 0;
   MFB_CUDA_TRY(cudaGetDevice(&dev));
-  const bool pair = use_pair(M, 1, dev);
+  const bool pair = use_pair(M, dev);
   CUtensorMap ta, tb;
   if ((st = make_tmap_a(&ta, dY, a_major, lda, M, K))) return st;
   if ((st = make_tmap_b(&tb, Wd, b_major, ldb, F, K, pair))) return st;

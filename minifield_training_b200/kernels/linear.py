@@ -14,11 +14,13 @@ from .. import _lib
 from ..device import DeviceArray, as_device
 
 
-def _gemm(a, a_major, lda, b, b_major, ldb, c, ldc, out_dtype, m, n, k, alpha=1.0, mask=None, stream=None):
+def _gemm(a, a_major, lda, b, b_major, ldb, c, ldc, out_dtype, m, n, k, alpha=1.0, mask=None, stream=None,
+          ws=None):
     p = ctypes.c_void_p
     _lib.call(
-        "mfb_gemm_bf16", p(a.ptr), a_major, lda, p(b.ptr), b_major, ldb, p(c.ptr), ldc, out_dtype, m, n, k,
-        ctypes.c_float(alpha), p(mask.ptr) if mask is not None else None, stream,
+        "mfb_gemm_bf16_ws", p(a.ptr), a_major, lda, p(b.ptr), b_major, ldb, p(c.ptr), ldc, out_dtype, m, n, k,
+        ctypes.c_float(alpha), p(mask.ptr) if mask is not None else None, 0, p(ws.ptr) if ws is not None else None,
+        ws.nbytes if ws is not None else 0, stream,
     )
 
 
@@ -43,12 +45,16 @@ def gemm_nn(a: DeviceArray, b: DeviceArray, out_dtype="bfloat16", stream=None) -
 
 
 def gemm_tn(a: DeviceArray, b: DeviceArray, out_dtype="float32", mask=None, stream=None) -> DeviceArray:
-    """C[M,N] = A[K,M]^T . B[K,N] (both read MN-major in place), optional mask."""
+    """C[M,N] = A[K,M]^T . B[K,N] (both read MN-major in place), optional mask. The weight
+    gradient: few output tiles over a deep K (the tokens), so K is split through a workspace
+    when that fills the GPU better (its release waits for the product)."""
     k, m = a.shape
     n = b.shape[1]
     c = DeviceArray((m, n), out_dtype)
+    need = int(_lib.lib().mfb_gemm_workspace_size(m, n, k))
+    ws = DeviceArray((need,), "uint8") if need else None
     _gemm(a, _lib.MAJOR_MN, m, b, _lib.MAJOR_MN, n, c, n, _lib.DTYPE_BF16 if out_dtype == "bfloat16" else _lib.DTYPE_F32,
-          m, n, k, mask=mask, stream=stream)
+          m, n, k, mask=mask, stream=stream, ws=ws)
     return c
 
 

@@ -117,10 +117,11 @@ def rope_freqs(theta: float, head_dim: int = 64) -> np.ndarray:
         np.float32)
 
 
-def _gemm(a, a_major, lda, b, b_major, ldb, c, ldc, f32, m, n, k, mask=None, stream=None):
-    _lib.call("mfb_gemm_bf16", P(a), a_major, lda, P(b), b_major, ldb, P(c), ldc,
+def _gemm(a, a_major, lda, b, b_major, ldb, c, ldc, f32, m, n, k, mask=None, stream=None, ws=None):
+    _lib.call("mfb_gemm_bf16_ws", P(a), a_major, lda, P(b), b_major, ldb, P(c), ldc,
               _lib.DTYPE_F32 if f32 else _lib.DTYPE_BF16, m, n, k, ctypes.c_float(1.0),
-              P(mask) if mask is not None else None, stream)
+              P(mask) if mask is not None else None, 0, P(ws.ptr) if ws is not None else None,
+              ws.nbytes if ws is not None else 0, stream)
 
 
 def _fwd(x, w, out, m, n, k, stream):
@@ -133,10 +134,12 @@ def _dgrad(dy, w, out, m, n, k, stream):
     _gemm(dy.ptr, _lib.MAJOR_K, n, w.ptr, _lib.MAJOR_MN, k, out.ptr, k, False, m, k, n, stream=stream)
 
 
-def _wgrad(dy, x, out_ptr, ste, m, n, k, stream):
-    """out[n, k] (FP32) = dy[m, n]^T . x[m, k], times the STE mask."""
+def _wgrad(dy, x, out_ptr, ste, m, n, k, stream, ws=None):
+    """out[n, k] (FP32) = dy[m, n]^T . x[m, k], times the STE mask. These products have few
+    output tiles and K = the token count: ``ws`` (mfb_gemm_workspace_size bytes) lets the GEMM
+    split K so that every SM pair gets work."""
     _gemm(dy.ptr, _lib.MAJOR_MN, n, x.ptr, _lib.MAJOR_MN, k, out_ptr, k, True, n, k, m,
-          mask=ste.ptr if ste is not None else None, stream=stream)
+          mask=ste.ptr if ste is not None else None, stream=stream, ws=ws)
 
 
 @dataclass
@@ -178,10 +181,15 @@ class EncoderStep:
     loss and count; ``stream`` is the CUDA stream handle all kernels run on.
     With a communicator the collectives run on a communication stream of the
     step's own, ordered after the kernels they reduce by events.
-    ``shard_optimizer`` (with a communicator) splits the AdamW passes across
-    the ranks and all-gathers the masters instead of every rank updating all
-    of them. On two GPUs it measured slower (the 1.5 GB all-gather outweighs
-    the halved optimizer), so the replicated transaction is the default.
+    ``shard_optimizer`` (with a communicator) partitions the optimizer state:
+    each rank owns a contiguous, bucket-aligned range of the trainable arena
+    (``owner_ranges``); each gradient bucket is reduced to its owner instead
+    of all-reduced, the AdamW passes run on the owned range (their global
+    decisions are allreduces of three doubles), and the owners broadcast the
+    updated masters at the end of the step. The next step's forward waits for
+    each layer's masters just before that layer, so the broadcast overlaps the
+    forward; ``settle()`` orders other work after it. Moments outside a rank's
+    range are never touched on that rank.
     """
 
     def __init__(self, cfg, rows: int, *, seed: int = 0, comm=None, stream=None, shard_optimizer: bool = False):
@@ -197,24 +205,31 @@ class EncoderStep:
         self.grads = grads
         opt = adamw.AdamWConfig(cfg.learning_rate, beta1=cfg.beta1, beta2=cfg.beta2, epsilon=cfg.epsilon,
                                 weight_decay=cfg.weight_decay, clip_norm=cfg.clip_norm)
-        masters = None
+        self._buckets = reduction_plan(self.layout, len(cfg.layer_types), n_grad)
         self.shard_optimizer = bool(shard_optimizer) and comm is not None
         if self.shard_optimizer:
-            # The optimizer is sharded across the ranks (each updates a slice of
-            # the masters and moments); the master arena holds the all-gather of
-            # every rank's equal slice.
-            masters = DeviceArray.zeros((adamw.sharded_master_elements(self.layout, comm.world),), "float32")
+            # Each rank owns a contiguous, bucket-aligned range of the trainable
+            # arena: gradients are reduced to their owner, the AdamW passes run
+            # on the owned range, and the owners broadcast the updated masters.
+            self._owners = owner_ranges(self._buckets, self.layout.n_train, comm.world)
+            self._bcast_plan = broadcast_plan(self._buckets, self.layout.n_train, self._owners)
+            self._bcast_events = {key: Event() for key, _ in self._bcast_plan}
+            self._gather_start = Event()
+            self._pending = False
         self.comm_stream = None
         if comm is not None:
             cs = ctypes.c_void_p()
             _lib.call("mfb_stream_create", ctypes.byref(cs))
             self.comm_stream = cs.value
             self._order_events = (Event(), Event())
-        self.state = adamw.initialize_state(init_parameters(cfg, seed), inv, order=arena_order(cfg), grads=grads,
-                                            params=masters)
+        self.state = adamw.initialize_state(init_parameters(cfg, seed), inv, order=arena_order(cfg), grads=grads)
         self.loss_count = grads.view(self.layout.n_train, (2,))
-        self.transition = (adamw.make_sharded_transaction(inv, opt, comm) if self.shard_optimizer
-                           else adamw.make_transaction(inv, opt))
+        if self.shard_optimizer:
+            lo, hi = self._owners[comm.rank]
+            check_hi = self.layout.n_total if comm.rank == comm.world - 1 else hi
+            self.transition = adamw.make_sharded_transaction(inv, opt, comm, slices=(lo, check_hi, lo, hi))
+        else:
+            self.transition = adamw.make_transaction(inv, opt)
         self.params = self.state["params"]
         self.gviews = self.state.gradient_tree()
         self.quant = _lib.QUANT_KINDS[cfg.quant] if cfg.quant else None
@@ -237,6 +252,9 @@ class EncoderStep:
         self.d_o = E((m, c), bf)
         ws = max(_lib.lib().mfb_norm_workspace_size(m, c), _lib.lib().mfb_encoder_workspace_size(c, cfg.classes))
         self.ws = E((ws,), "uint8")
+        # Split-K partials of the weight-gradient GEMMs (out features x in features, K = m tokens).
+        wg = [(c, f), (2 * f, c), (c, c), (3 * c, c), (self.nq, c)]
+        self.gemm_ws = E((max(16, max(int(_lib.lib().mfb_gemm_workspace_size(n, k, m)) for n, k in wg)),), "uint8")
         aws = _lib.lib().mfb_attn_workspace_size(rows, self.T, self.T, h, hk, cfg.head_dim)
         self.attn_ws = E((max(aws, 16),), "uint8")
         self.result = None
@@ -260,7 +278,6 @@ class EncoderStep:
             L.w2, L.ste2 = E((c, f), bf), E((c, f), "uint8")
             self.layers.append(L)
         self.head_eff = E((cfg.classes, c), bf)
-        self._buckets = reduction_plan(self.layout, len(self.layers), self.grads.size)
         # Initialization ran on the default stream; a created (non-blocking)
         # step stream does not order after it, so finish it here.
         _lib.call("mfb_device_sync")
@@ -284,26 +301,32 @@ class EncoderStep:
             _lib.call("mfb_fakequant", P(w.ptr), self.quant, rows, cols, None, None, P(s.ptr), None, P(e.ptr),
                       self.stream)
 
-    def quantize(self):
-        """Effective bf16 weights and STE masks of every projection for this step."""
+    def _quantize_layer(self, i):
         c, f = self.cfg.hidden, self.cfg.ffn
-        for i, L in enumerate(self.layers):
-            p = _prefix(i)
-            self._quantize(p + "feed_forward.w1.weight", L.w13, L.ste13, 0)
-            self._quantize(p + "feed_forward.w3.weight", L.w13, L.ste13, f)
-            self._quantize(p + "feed_forward.w2.weight", L.w2, L.ste2, 0)
-            if L.kind == "conv":
-                self._quantize(p + "conv.in_proj.weight", L.w_in, L.ste_in, 0)
-                self._quantize(p + "conv.out_proj.weight", L.w_out, L.ste_out, 0)
-            else:
-                kv = self.cfg.kv_heads * self.cfg.head_dim
-                self._quantize(p + "self_attn.q_proj.weight", L.w_in, L.ste_in, 0)
-                self._quantize(p + "self_attn.k_proj.weight", L.w_in, L.ste_in, c)
-                self._quantize(p + "self_attn.v_proj.weight", L.w_in, L.ste_in, c + kv)
-                self._quantize(p + "self_attn.out_proj.weight", L.w_out, L.ste_out, 0)
+        L, p = self.layers[i], _prefix(i)
+        self._quantize(p + "feed_forward.w1.weight", L.w13, L.ste13, 0)
+        self._quantize(p + "feed_forward.w3.weight", L.w13, L.ste13, f)
+        self._quantize(p + "feed_forward.w2.weight", L.w2, L.ste2, 0)
+        if L.kind == "conv":
+            self._quantize(p + "conv.in_proj.weight", L.w_in, L.ste_in, 0)
+            self._quantize(p + "conv.out_proj.weight", L.w_out, L.ste_out, 0)
+        else:
+            kv = self.cfg.kv_heads * self.cfg.head_dim
+            self._quantize(p + "self_attn.q_proj.weight", L.w_in, L.ste_in, 0)
+            self._quantize(p + "self_attn.k_proj.weight", L.w_in, L.ste_in, c)
+            self._quantize(p + "self_attn.v_proj.weight", L.w_in, L.ste_in, c + kv)
+            self._quantize(p + "self_attn.out_proj.weight", L.w_out, L.ste_out, 0)
+
+    def _quantize_head(self):
         # The head is not a model projection: full_linear casts its master to bf16.
         hw = self._p("head.weight")
         _lib.call("mfb_cast_f32_bf16", P(hw.ptr), P(self.head_eff.ptr), hw.size, self.stream)
+
+    def quantize(self):
+        """Effective bf16 weights and STE masks of every projection for this step."""
+        for i in range(len(self.layers)):
+            self._quantize_layer(i)
+        self._quantize_head()
 
     def set_batch(self, ids, mask, seg, pos, labels):
         """Upload one local batch (int32 [rows, T] host arrays) and build the attention ids."""
@@ -327,41 +350,51 @@ class EncoderStep:
                   P(rstd.ptr), self.M, self.cfg.hidden, ctypes.c_float(self.cfg.norm_eps), self.stream)
 
     def forward(self):
-        cfg, m, c, f, s = self.cfg, self.M, self.cfg.hidden, self.cfg.ffn, self.stream
+        self._fwd_embed()
+        for i in range(len(self.layers)):
+            self._fwd_layer(i)
+        self._fwd_final()
+
+    def _fwd_embed(self):
+        cfg, m, c = self.cfg, self.M, self.cfg.hidden
         emb = self._p("lfm2.embed_tokens.weight")
-        _lib.call("mfb_embed_gather", P(emb.ptr), P(self.ids.ptr), P(self.x0.ptr), m, c, cfg.vocab, s)
-        prev = None
-        for i, L in enumerate(self.layers):
-            p = _prefix(i)
-            opmask = self.mask if L.kind == "conv" else None
-            if prev is None:
-                _lib.call("mfb_memcpy_d2d", P(L.x.ptr), P(self.x0.ptr), L.x.nbytes, s)
-                self._rms(L.x, None, self._p(p + "operator_norm.weight"), opmask, None, L.h, L.rstd_op)
-            else:
-                self._rms(prev.mid, prev.y, self._p(p + "operator_norm.weight"), opmask, L.x, L.h, L.rstd_op)
-            if L.kind == "conv":
-                _fwd(L.h, L.w_in, L.proj, m, 3 * c, c, s)
-                _lib.call("mfb_conv_fwd", P(L.proj.ptr), P(self._p(p + "conv.conv.weight").ptr), P(self.seg.ptr),
-                          P(L.mixed.ptr), m, self.T, c, s)
-                _fwd(L.mixed, L.w_out, L.r, m, c, c, s)
-            else:
-                _fwd(L.h, L.w_in, L.proj, m, self.nq, c, s)
-                _lib.call("mfb_qknorm_rope_fwd", P(L.proj.ptr), self.nq, P(self._p(p + "self_attn.q_layernorm.weight").ptr),
-                          P(self._p(p + "self_attn.k_layernorm.weight").ptr), P(self.pos.ptr), P(self.freqs.ptr),
-                          P(L.q.ptr), P(L.k.ptr), P(L.v.ptr), P(L.rstd_q.ptr), P(L.rstd_k.ptr), m, cfg.heads,
-                          cfg.kv_heads, ctypes.c_float(cfg.norm_eps), s)
-                causal, off, pol = self.attn_flags
-                _lib.call("mfb_attn_fwd", P(L.q.ptr), P(L.k.ptr), P(L.v.ptr), P(L.o.ptr), P(L.lse.ptr),
-                          P(self.qid.ptr), P(self.kid.ptr), self.rows, self.T, self.T, cfg.heads, cfg.kv_heads,
-                          cfg.head_dim, causal, off, pol, ctypes.c_float(cfg.head_dim ** -0.5), P(self.attn_ws.ptr),
-                          self.attn_ws.nbytes, s)
-                _fwd(L.o, L.w_out, L.r, m, c, c, s)
-            self._rms(L.x, L.r, self._p(p + "ffn_norm.weight"), None, L.mid, L.h2, L.rstd_ffn)
-            # gate|up GEMM with silu(gate) * up in its epilogue
-            _lib.call("mfb_gemm_swiglu_fwd", P(L.h2.ptr), _lib.MAJOR_K, c, P(L.w13.ptr), c, P(L.gu.ptr), P(L.a.ptr),
-                      m, f, c, s)
-            _fwd(L.a, L.w2, L.y, m, c, f, s)
-            prev = L
+        _lib.call("mfb_embed_gather", P(emb.ptr), P(self.ids.ptr), P(self.x0.ptr), m, c, cfg.vocab, self.stream)
+
+    def _fwd_layer(self, i):
+        cfg, m, c, f, s = self.cfg, self.M, self.cfg.hidden, self.cfg.ffn, self.stream
+        L, p = self.layers[i], _prefix(i)
+        prev = self.layers[i - 1] if i > 0 else None
+        opmask = self.mask if L.kind == "conv" else None
+        if prev is None:
+            _lib.call("mfb_memcpy_d2d", P(L.x.ptr), P(self.x0.ptr), L.x.nbytes, s)
+            self._rms(L.x, None, self._p(p + "operator_norm.weight"), opmask, None, L.h, L.rstd_op)
+        else:
+            self._rms(prev.mid, prev.y, self._p(p + "operator_norm.weight"), opmask, L.x, L.h, L.rstd_op)
+        if L.kind == "conv":
+            _fwd(L.h, L.w_in, L.proj, m, 3 * c, c, s)
+            _lib.call("mfb_conv_fwd", P(L.proj.ptr), P(self._p(p + "conv.conv.weight").ptr), P(self.seg.ptr),
+                      P(L.mixed.ptr), m, self.T, c, s)
+            _fwd(L.mixed, L.w_out, L.r, m, c, c, s)
+        else:
+            _fwd(L.h, L.w_in, L.proj, m, self.nq, c, s)
+            _lib.call("mfb_qknorm_rope_fwd", P(L.proj.ptr), self.nq, P(self._p(p + "self_attn.q_layernorm.weight").ptr),
+                      P(self._p(p + "self_attn.k_layernorm.weight").ptr), P(self.pos.ptr), P(self.freqs.ptr),
+                      P(L.q.ptr), P(L.k.ptr), P(L.v.ptr), P(L.rstd_q.ptr), P(L.rstd_k.ptr), m, cfg.heads,
+                      cfg.kv_heads, ctypes.c_float(cfg.norm_eps), s)
+            causal, off, pol = self.attn_flags
+            _lib.call("mfb_attn_fwd", P(L.q.ptr), P(L.k.ptr), P(L.v.ptr), P(L.o.ptr), P(L.lse.ptr),
+                      P(self.qid.ptr), P(self.kid.ptr), self.rows, self.T, self.T, cfg.heads, cfg.kv_heads,
+                      cfg.head_dim, causal, off, pol, ctypes.c_float(cfg.head_dim ** -0.5), P(self.attn_ws.ptr),
+                      self.attn_ws.nbytes, s)
+            _fwd(L.o, L.w_out, L.r, m, c, c, s)
+        self._rms(L.x, L.r, self._p(p + "ffn_norm.weight"), None, L.mid, L.h2, L.rstd_ffn)
+        # gate|up GEMM with silu(gate) * up in its epilogue
+        _lib.call("mfb_gemm_swiglu_fwd", P(L.h2.ptr), _lib.MAJOR_K, c, P(L.w13.ptr), c, P(L.gu.ptr), P(L.a.ptr),
+                  m, f, c, s)
+        _fwd(L.a, L.w2, L.y, m, c, f, s)
+
+    def _fwd_final(self):
+        prev = self.layers[-1]
         self._rms(prev.mid, prev.y, self._p("lfm2.embedding_norm.weight"), self.mask, self.final, self.enc,
                   self.rstd_final)
 
@@ -397,26 +430,26 @@ class EncoderStep:
         L, p = self.layers[i], _prefix(i)
         d, spare = self._grad_bufs(i)
         # FFN: x_next = mid + y.
-        _wgrad(d, L.a, self._g(p + "feed_forward.w2.weight").ptr, L.ste2, m, c, f, s)
+        _wgrad(d, L.a, self._g(p + "feed_forward.w2.weight").ptr, L.ste2, m, c, f, s, self.gemm_ws)
         # dH = d . W2 with the SwiGLU backward in its epilogue: d_gu directly
         _lib.call("mfb_gemm_swiglu_bwd", P(d.ptr), _lib.MAJOR_K, c, P(L.w2.ptr), _lib.MAJOR_MN, f, P(L.gu.ptr),
                   P(self.d_gu.ptr), m, f, c, s)
         _dgrad(self.d_gu, L.w13, self.d_h, m, 2 * f, c, s)
-        _wgrad(self.d_gu, L.h2, self._g(p + "feed_forward.w1.weight").ptr, L.ste13, m, 2 * f, c, s)
+        _wgrad(self.d_gu, L.h2, self._g(p + "feed_forward.w1.weight").ptr, L.ste13, m, 2 * f, c, s, self.gemm_ws)
         self._rms_bwd(L.mid, self._p(p + "ffn_norm.weight"), L.rstd_ffn, None, self.d_h, d, self.d_mid,
                       self._g(p + "ffn_norm.weight"))
         # Operator: mid = x + r.
         if L.kind == "conv":
             _dgrad(self.d_mid, L.w_out, self.d_o, m, c, c, s)
-            _wgrad(self.d_mid, L.mixed, self._g(p + "conv.out_proj.weight").ptr, L.ste_out, m, c, c, s)
+            _wgrad(self.d_mid, L.mixed, self._g(p + "conv.out_proj.weight").ptr, L.ste_out, m, c, c, s, self.gemm_ws)
             _lib.call("mfb_conv_bwd", P(L.proj.ptr), P(self._p(p + "conv.conv.weight").ptr), P(self.seg.ptr),
                       P(self.d_o.ptr), P(self.d_proj.ptr), P(self._g(p + "conv.conv.weight").ptr), 0, m, self.T,
                       c, P(self.ws.ptr), self.ws.nbytes, s)
             _dgrad(self.d_proj, L.w_in, self.d_h, m, 3 * c, c, s)
-            _wgrad(self.d_proj, L.h, self._g(p + "conv.in_proj.weight").ptr, L.ste_in, m, 3 * c, c, s)
+            _wgrad(self.d_proj, L.h, self._g(p + "conv.in_proj.weight").ptr, L.ste_in, m, 3 * c, c, s, self.gemm_ws)
         else:
             _dgrad(self.d_mid, L.w_out, self.d_o, m, c, c, s)
-            _wgrad(self.d_mid, L.o, self._g(p + "self_attn.out_proj.weight").ptr, L.ste_out, m, c, c, s)
+            _wgrad(self.d_mid, L.o, self._g(p + "self_attn.out_proj.weight").ptr, L.ste_out, m, c, c, s, self.gemm_ws)
             causal, off, pol = self.attn_flags
             _lib.call("mfb_attn_bwd", P(L.q.ptr), P(L.k.ptr), P(L.v.ptr), P(L.o.ptr), P(L.lse.ptr),
                       P(self.d_o.ptr), P(self.d_q.ptr), P(self.d_k.ptr), P(self.d_v.ptr), P(self.qid.ptr),
@@ -430,7 +463,8 @@ class EncoderStep:
                       P(self._g(p + "self_attn.k_layernorm.weight").ptr), 0, m, cfg.heads, cfg.kv_heads,
                       P(self.ws.ptr), self.ws.nbytes, s)
             _dgrad(self.d_proj, L.w_in, self.d_h, m, self.nq, c, s)
-            _wgrad(self.d_proj, L.h, self._g(p + "self_attn.q_proj.weight").ptr, L.ste_in, m, self.nq, c, s)
+            _wgrad(self.d_proj, L.h, self._g(p + "self_attn.q_proj.weight").ptr,
+                   L.ste_in, m, self.nq, c, s, self.gemm_ws)
         opmask = self.mask if L.kind == "conv" else None
         self._rms_bwd(L.x, self._p(p + "operator_norm.weight"), L.rstd_op, opmask, self.d_h, self.d_mid, spare,
                       self._g(p + "operator_norm.weight"))
@@ -449,8 +483,12 @@ class EncoderStep:
 
         One GPU: one graph (quantize, forward, backward, normalize, commit).
         With a communicator: the forward and the head's backward, one graph per
-        layer's backward (so each layer's bucket allreduce is launched between
-        them), and the commit.
+        layer's backward (so each layer's bucket reduction is launched between
+        them), and the commit (replicated optimizer) or the normalization
+        (sharded optimizer, whose passes hold collectives). With the sharded
+        optimizer the forward is one graph per layer (that layer's
+        quantization and forward), so each waits only for its own masters'
+        broadcast from the previous step.
         """
         if getattr(self, "graphs", None) is not None:
             return
@@ -468,13 +506,17 @@ class EncoderStep:
 
         if self.comm is None:
             self.graphs = {"all": rec(self._eager_local_step)}
+            self._result_dev = self.result._dev
+        elif self.shard_optimizer:
+            self.graphs = {"embed": rec(self._fwd_embed),
+                           "fwd": [rec(lambda i=i: self._fwd_layer_quantized(i)) for i in range(len(self.layers))],
+                           "head": rec(self._head_part),
+                           "layers": [rec(lambda i=i: self._bwd_layer(i)) for i in reversed(range(len(self.layers)))],
+                           "post": rec(self._normalize)}
         else:
-            # A sharded AdamW transaction holds collectives between its passes:
-            # it then runs after the "post" graph, outside the graphs.
             self.graphs = {"pre": rec(lambda: (self.quantize(), self.forward(), self._bwd_head())),
                            "layers": [rec(lambda i=i: self._bwd_layer(i)) for i in reversed(range(len(self.layers)))],
-                           "post": rec(self._normalize if self.shard_optimizer else self._commit)}
-        if not self.shard_optimizer:
+                           "post": rec(self._commit)}
             self._result_dev = self.result._dev
 
     def _eager_local_step(self):
@@ -486,13 +528,85 @@ class EncoderStep:
     def _launch(self, g):
         _lib.call("mfb_graph_launch", g, P(self.stream))
 
+    # ---- sharded optimizer: owned ranges and the masters' broadcast -----------------
+    def _fwd_layer_quantized(self, i):
+        self._quantize_layer(i)
+        self._fwd_layer(i)
+
+    def _head_part(self):
+        self._fwd_final()
+        self._quantize_head()
+        self._bwd_head()
+
+    def _await(self, key):
+        """The compute stream waits for the broadcast of ``key``'s masters (if one is pending)."""
+        if self._pending:
+            self._bcast_events[key].wait_on(self.stream)
+
+    def _broadcast_masters(self):
+        """Every owner broadcasts its updated masters, in the next forward's order, on the
+        communication stream after the commit; one event per range group."""
+        comm, cs, params = self.comm, self.comm_stream, self.state.arenas["params"]
+        self._gather_start.record(self.stream)
+        self._gather_start.wait_on(cs)
+        for key, pieces in self._bcast_plan:
+            for lo, hi, root in pieces:
+                comm.broadcast(params.view(lo, (hi - lo,)), root, stream=cs)
+            self._bcast_events[key].record(cs)
+        self._pending = True
+
+    def settle(self):
+        """Order the compute stream after the last step's master broadcasts (sharded optimizer):
+        afterwards every rank's masters are complete for work on that stream."""
+        if self.shard_optimizer and self._pending:
+            self._bcast_events["head"].wait_on(self.stream)  # the last broadcast on the stream
+            self._pending = False
+
+    def grad_owner(self, name):
+        """The rank whose gradient of leaf ``name`` is reduced (sharded optimizer; 0 otherwise)."""
+        if not self.shard_optimizer:
+            return 0
+        off = self.layout.offsets[name]
+        return next(r for r, (lo, hi) in enumerate(self._owners) if lo <= off < hi)
+
+    def _sharded_step(self, run):
+        """One step with the sharded optimizer; ``run(key, i)`` launches a piece (graph or eager)."""
+        run("embed", None)
+        self._await("vectors")
+        for i in range(len(self.layers)):
+            self._await(("layer", i))
+            run("fwd", i)
+        self._await("head")
+        self._pending = False
+        run("head", None)
+        reducer = self.reducer()
+        for i in reversed(range(len(self.layers))):
+            run("layers", i)
+            reducer.layer_done(i)
+        reducer.finish()
+        run("post", None)
+        loss, div, ok = self._scalars
+        self.result = self.transition(self.state, loss, ok, divisor=div, stream=self.stream)
+        self._broadcast_masters()
+        return self.result
+
     def reducer(self):
-        """A BucketReducer of this step's gradient arena over its communicator and streams."""
+        """A BucketReducer of this step's gradient arena over its communicator and streams:
+        allreduces, or with the sharded optimizer reductions to each range's owner (and an
+        allreduce of the loss/count tail)."""
         compute_done, reduced = self._order_events
         comm, flat, cs = self.comm, self.grads, self.comm_stream
+        n_train = self.layout.n_train
 
         def reduce_range(lo, hi):
-            comm.allreduce(flat.view(lo, (hi - lo,)), stream=cs)
+            if not self.shard_optimizer:
+                comm.allreduce(flat.view(lo, (hi - lo,)), stream=cs)
+                return
+            for x, y, root in owner_reductions(lo, hi, self._owners, n_train):
+                if root is None:
+                    comm.allreduce(flat.view(x, (y - x,)), stream=cs)
+                else:
+                    comm.reduce(flat.view(x, (y - x,)), root, stream=cs)
 
         def before():  # the bucket's gradients are complete on the compute stream
             compute_done.record(self.stream)
@@ -505,8 +619,29 @@ class EncoderStep:
         return BucketReducer(self._buckets, reduce_range, before, after)
 
     def step(self):
-        """quantize -> forward -> backward (+ bucketed allreduce) -> normalize -> AdamW commit."""
+        """quantize -> forward -> backward (+ bucketed gradient reduction) -> normalize -> AdamW commit.
+
+        With the sharded optimizer the step ends by enqueueing the masters'
+        broadcast; the next step's forward waits for it layer by layer, and
+        ``settle()`` orders any other work after it."""
         graphs = getattr(self, "graphs", None)
+        if self.shard_optimizer:
+            if graphs is not None:
+                def run(key, i):
+                    g = graphs[key]
+                    if key == "layers":
+                        g = g[len(self.layers) - 1 - i]
+                    elif key == "fwd":
+                        g = g[i]
+                    self._launch(g)
+            else:
+                eager = {"embed": lambda i: self._fwd_embed(), "fwd": self._fwd_layer_quantized,
+                         "head": lambda i: self._head_part(), "layers": self._bwd_layer,
+                         "post": lambda i: self._normalize()}
+
+                def run(key, i):
+                    eager[key](i)
+            return self._sharded_step(run)
         if graphs is not None:
             if self.comm is None:
                 self._launch(graphs["all"])
@@ -518,10 +653,6 @@ class EncoderStep:
                     reducer.layer_done(i)
                 reducer.finish()
                 self._launch(graphs["post"])
-                if self.shard_optimizer:
-                    loss, div, ok = self._scalars
-                    self.result = self.transition(self.state, loss, ok, divisor=div, stream=self.stream)
-                    return self.result
             self.result = adamw.CommitResult(self.state, self._result_dev, self.stream)
             return self.result
         self.quantize()
@@ -549,10 +680,13 @@ class EncoderStep:
                   self.stream)
 
     def _commit(self):
+        """Normalize and commit (the replicated transaction; with the sharded optimizer the owned
+        range's passes, then the masters' broadcast)."""
         self._normalize()
         loss, div, ok = self._scalars
         if self.shard_optimizer:
             self.result = self.transition(self.state, loss, ok, divisor=div, stream=self.stream)
+            self._broadcast_masters()
         else:
             self.result = self.transition(self.state, self.gviews, loss, ok, divisor=div, stream=self.stream)
 
@@ -579,6 +713,64 @@ def reduction_plan(layout, n_layers: int, total: int):
     if total > hi_all:
         plan.append(("rest", -1, hi_all, total))
     return plan
+
+
+def _round4(n):
+    return (n + 3) // 4 * 4
+
+
+def owner_ranges(plan, n_train: int, world: int):
+    """[lo, hi) of the trainable arena owned by each rank: contiguous ranges
+    tiling [0, n_train) whose cuts fall on bucket starts (the head range, a
+    layer's matrices, the vector leaves), each cut the bucket start nearest an
+    equal share. A bucket therefore belongs to one rank, except that a range
+    may hold several. Starts are multiples of 4 (leaf offsets)."""
+    layers = [(lo, hi) for kind, _, lo, hi in plan if kind == "layer"]
+    starts = sorted({0} | {lo for lo, _ in layers} | {_round4(max(hi for _, hi in layers))})
+    starts = [x for x in starts if x < n_train]
+    cuts = [0]
+    for k in range(1, world):
+        target = k * n_train / world
+        cand = [x for x in starts if x >= cuts[-1]]
+        cuts.append(min(cand, key=lambda x: abs(x - target)) if cand else n_train)
+    cuts.append(n_train)
+    return [(cuts[r], cuts[r + 1]) for r in range(world)]
+
+
+def owner_reductions(lo: int, hi: int, owners, n_train: int):
+    """The collectives that reduce gradient range [lo, hi) under the sharded optimizer:
+    (x, y, root) reductions of each owned piece to its owner, then (x, y, None) an
+    allreduce of the part past the trainable arena (the loss/count tail every rank
+    needs)."""
+    out = []
+    for r, (a, b) in enumerate(owners):
+        x, y = max(lo, a), min(hi, b)
+        if x < y:
+            out.append((x, y, r))
+    if hi > n_train:
+        out.append((max(lo, n_train), hi, None))
+    return out
+
+
+def broadcast_plan(plan, n_train: int, owners):
+    """Master ranges to broadcast after a sharded commit, in the order the next
+    forward needs them: the vector leaves (every layer's norm gains), layers
+    0, 1, ..., then the head. Each entry is (key, [(lo, hi, owner rank)])."""
+    def pieces(lo, hi):
+        out = []
+        for r, (a, b) in enumerate(owners):
+            x, y = max(lo, a), min(hi, b, n_train)
+            if x < y:
+                out.append((x, y, r))
+        return out
+
+    layers = {i: (lo, hi) for kind, i, lo, hi in plan if kind == "layer"}
+    lo_all = min(lo for lo, _ in layers.values())
+    hi_all = max(hi for _, hi in layers.values())
+    out = [("vectors", pieces(hi_all, n_train))]
+    out += [(("layer", i), pieces(*layers[i])) for i in sorted(layers)]
+    out.append(("head", pieces(0, lo_all)))
+    return out
 
 
 class BucketReducer:

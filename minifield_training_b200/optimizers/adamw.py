@@ -398,7 +398,7 @@ def sharded_master_elements(layout, world: int) -> int:
     return max(layout.n_total, shard_slices(layout.n_train, world, 0)[2] * world, 4)
 
 
-def make_sharded_transaction(inventory: Inventory, config: AdamWConfig, comm):
+def make_sharded_transaction(inventory: Inventory, config: AdamWConfig, comm, slices=None):
     """The transaction of ``make_transaction`` with the elementwise passes split
     across the data-parallel ranks of ``comm`` (a comm.Communicator):
     ``transition(state, active_loss, accumulation_valid, *, divisor=None,
@@ -412,6 +412,12 @@ def make_sharded_transaction(inventory: Inventory, config: AdamWConfig, comm):
     never read or written on that rank. ``state.arenas["params"]`` must hold
     ``sharded_master_elements`` floats (the all-gather writes every rank's
     whole slice).
+
+    ``slices`` = (check_lo, check_hi, lo, hi) replaces the equal slices with
+    the caller's partition (check ranges tiling [0, n_total), update ranges
+    tiling [0, n_train) across the ranks, starts multiples of 4) and leaves
+    the masters un-gathered: the caller brings every rank's updated range to
+    the others (a data-parallel step overlaps that with its next forward).
     """
     world, rank = comm.world, comm.rank
     workspace = DeviceArray((_lib.lib().mfb_adamw_workspace_size(),), "uint8")
@@ -424,14 +430,17 @@ def make_sharded_transaction(inventory: Inventory, config: AdamWConfig, comm):
         if not isinstance(state, State) or set(state.layout.specs) != names:
             raise ValueError("Full-weight state does not match the inventory")
         layout, a = state.layout, state.arenas
-        if a["params"].size < sharded_master_elements(layout, world):
+        if slices is None and a["params"].size < sharded_master_elements(layout, world):
             raise ValueError("sharded AdamW needs a master arena of sharded_master_elements floats")
         loss = _device_scalar(active_loss, "float32", scalars, "loss")
         valid = _device_scalar(bool(accumulation_valid) if not isinstance(accumulation_valid, DeviceArray)
                                else accumulation_valid, "uint8", scalars, "valid")
         P = ctypes.c_void_p
-        c_lo, c_hi, _ = shard_slices(layout.n_total, world, rank)
-        t_lo, t_hi, per = shard_slices(layout.n_train, world, rank)
+        if slices is None:
+            c_lo, c_hi, _ = shard_slices(layout.n_total, world, rank)
+            t_lo, t_hi, per = shard_slices(layout.n_train, world, rank)
+        else:
+            c_lo, c_hi, t_lo, t_hi = slices
 
         def run(pass_id, lo, hi):
             _lib.call("mfb_adamw_shard_pass", pass_id, P(a["params"].ptr), P(a["m"].ptr), P(a["v"].ptr),
@@ -449,8 +458,9 @@ def make_sharded_transaction(inventory: Inventory, config: AdamWConfig, comm):
         comm.allreduce_f64(red.ptr, 2, stream=stream)
         run(_CANDIDATE_FINALIZE, 0, 0)
         run(_COMMIT, t_lo, t_hi)
-        masters = a["params"]
-        comm.all_gather(masters.view(rank * per, (per,)), masters.view(0, (per * world,)), stream=stream)
+        if slices is None:
+            masters = a["params"]
+            comm.all_gather(masters.view(rank * per, (per,)), masters.view(0, (per * world,)), stream=stream)
         return CommitResult(state, result_dev, stream)
 
     return transition

@@ -109,3 +109,86 @@ def test_sharded_master_arena_holds_the_all_gather():
     for world in (1, 2, 8):
         per = adamw.shard_slices(layout.n_train, world, 0)[2]
         assert adamw.sharded_master_elements(layout, world) >= max(layout.n_total, per * world)
+
+
+def _leaf_ranges(layout):
+    return [(layout.offsets[n], layout.offsets[n] + layout.size(n)) for n in layout.trainable]
+
+
+@pytest.mark.parametrize("cfg", [workloads.CONFIG5, TINY], ids=["config5", "tiny"])
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_owner_ranges_tile_the_trainable_arena_at_bucket_starts(cfg, world):
+    """Sharded optimizer: contiguous owned ranges tiling [0, n_train), cut only at bucket starts
+    (so no leaf is split between owners), and within one bucket of an equal share."""
+    layout = adamw.Layout(me.inventory(cfg), me.arena_order(cfg))
+    plan = me.reduction_plan(layout, len(cfg.layer_types), layout.n_train + 4)
+    owners = me.owner_ranges(plan, layout.n_train, world)
+    assert len(owners) == world and owners[0][0] == 0 and owners[-1][1] == layout.n_train
+    assert all(a[1] == b[0] for a, b in zip(owners, owners[1:]))
+    assert all(lo <= hi and lo % 4 == 0 for lo, hi in owners)
+    for lo, hi in _leaf_ranges(layout):
+        assert sum(1 for a, b in owners if a <= lo and hi <= b) == 1, (lo, hi)
+    if cfg is workloads.CONFIG5 and world in (2, 4, 8):
+        biggest = max(hi - lo for kind, _, lo, hi in plan if kind == "layer")
+        assert max(hi - lo for lo, hi in owners) <= layout.n_train / world + biggest
+
+
+@pytest.mark.parametrize("world", [1, 2, 8])
+def test_broadcast_plan_sends_every_master_once_from_its_owner(world):
+    layout = adamw.Layout(me.inventory(workloads.CONFIG5), me.arena_order(workloads.CONFIG5))
+    n_layers = len(workloads.CONFIG5.layer_types)
+    plan = me.reduction_plan(layout, n_layers, layout.n_train + 4)
+    owners = me.owner_ranges(plan, layout.n_train, world)
+    bplan = me.broadcast_plan(plan, layout.n_train, owners)
+    assert [k for k, _ in bplan] == ["vectors"] + [("layer", i) for i in range(n_layers)] + ["head"]
+    cover = np.zeros(layout.n_train, np.int8)
+    for _, pieces in bplan:
+        for lo, hi, r in pieces:
+            assert owners[r][0] <= lo < hi <= owners[r][1]
+            cover[lo:hi] += 1
+    assert cover.max() == 1
+    for lo, hi in _leaf_ranges(layout):
+        assert (cover[lo:hi] == 1).all(), (lo, hi)
+
+
+def _owner_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    layout = adamw.Layout(me.inventory(TINY), me.arena_order(TINY))
+    total = layout.n_train + 4
+    plan = me.reduction_plan(layout, len(TINY.layer_types), total)
+    owners = me.owner_ranges(plan, layout.n_train, world)
+    g = torch.Generator().manual_seed(rank)
+    flat = torch.randn(total, generator=g)
+    expected = flat.clone()
+    dist.all_reduce(expected)
+
+    def reduce_range(lo, hi):
+        for x, y, root in me.owner_reductions(lo, hi, owners, layout.n_train):
+            if root is None:
+                dist.all_reduce(flat[x:y])
+            else:
+                buf = flat[x:y].clone()
+                dist.reduce(buf, dst=root)
+                if rank == root:
+                    flat[x:y] = buf
+
+    red = me.BucketReducer(plan, reduce_range)
+    for i in reversed(range(len(TINY.layer_types))):
+        red.layer_done(i)
+    red.finish()
+    lo, hi = owners[rank]
+    out[rank] = (float((flat[lo:hi] - expected[lo:hi]).abs().max()) if hi > lo else 0.0,
+                 float((flat[layout.n_train:] - expected[layout.n_train:]).abs().max()))
+    dist.destroy_process_group()
+
+
+def test_owner_reductions_give_each_owner_the_full_sum_on_three_gloo_ranks():
+    """Sharded optimizer: reducing every bucket to its owners (and allreducing the loss/count tail)
+    leaves each rank's owned range, and the tail, equal to a full allreduce."""
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    port = 29900 + os.getpid() % 90
+    run_ranks(ctx, _owner_worker, [(r, 3, port, out) for r in range(3)], 120)
+    for r in range(3):
+        assert out[r][0] < 1e-5 and out[r][1] < 1e-5, out[r]

@@ -7,7 +7,9 @@ over both rows (up to FP32 summation order: rel-L2 1e-4 per leaf), and after
 the AdamW commit both ranks must hold bit-identical masters (replicated state,
 engine/step.py:62 and the data-parallel known answers' replication checks),
 with the replicated transaction and with the optimizer sharded across the
-ranks (its masters all-gathered).
+ranks (each rank owns a bucket-aligned range: its gradients are reduced to it,
+it updates it, and it broadcasts the masters back, overlapped with the next
+step's forward).
 Ranks run as child processes; NCCL's NVLS is off, as for every multi-rank
 test on this pool.
 """
@@ -39,8 +41,8 @@ def _comm(rank, uid_path):
     return mcomm.Communicator(2, rank, mcomm.unique_id_via_file(uid_path, rank), timeout_s=120.0)
 
 
-def _rank_graph(rank, uid_path, out):
-    """Two captured-graph steps per rank (forward/per-layer backward/commit graphs around the bucket allreduce)."""
+def _rank_graph(rank, uid_path, out, shard=False):
+    """Two captured-graph steps per rank (forward/per-layer backward/commit graphs around the bucket reductions)."""
     import ctypes
 
     from minifield_training_b200 import _lib, workloads
@@ -49,13 +51,14 @@ def _rank_graph(rank, uid_path, out):
     cfg = _cfg()
     s = ctypes.c_void_p()
     _lib.call("mfb_stream_create", ctypes.byref(s))
-    step = me.EncoderStep(cfg, rows=1, seed=0, comm=comm, stream=s.value)
+    step = me.EncoderStep(cfg, rows=1, seed=0, comm=comm, stream=s.value, shard_optimizer=shard)
     step.set_batch(*workloads.encoder_batch(cfg, 7, rows=1, row0=rank))
     step.capture()
     losses = []
     for _ in range(2):
         res = step.step()
         losses.append((res.committed, res.loss))
+    step.settle()  # the sharded optimizer's last master broadcast
     comm.wait(s.value)
     params = {n: v.numpy() for n, v in step.params.items() if n != "lfm2.embed_tokens.weight"}
     out[rank] = (losses, params)
@@ -79,9 +82,12 @@ def _rank(rank, uid_path, out, shard=False):
     grads = {n: v.numpy() for n, v in step.gviews.items()}
     lc = step.loss_count.numpy()
     step._commit()
+    step.settle()
+    comm.wait(None)
     committed = step.result.committed
     params = {n: v.numpy() for n, v in step.params.items() if n != "lfm2.embed_tokens.weight"}
-    out[rank] = (grads, lc, committed, params)
+    owners = {n: step.grad_owner(n) for n in grads}
+    out[rank] = (grads, lc, committed, params, owners)
     step.close()
     comm.close()
 
@@ -109,21 +115,25 @@ def test_two_rank_step_matches_one_gpu(shard, tmp_path):
     ref.forward()
     ref.backward()
     sync()
-    g0, lc0, c0, p0 = out[0]
-    g1, lc1, c1, p1 = out[1]
+    g0, lc0, c0, p0, own = out[0]
+    g1, lc1, c1, p1, _ = out[1]
     np.testing.assert_allclose(lc0, ref.loss_count.numpy(), rtol=1e-4)
     np.testing.assert_array_equal(lc0, lc1)
     for name, v in ref.gviews.items():
         r = v.numpy().astype(np.float64)
-        np.testing.assert_array_equal(g0[name], g1[name])
-        err = np.linalg.norm(g0[name] - r) / max(np.linalg.norm(r), 1e-30)
+        # Replicated: both ranks hold the sum. Sharded: the leaf's owner does (the other keeps its own part).
+        g = (g0, g1)[own[name]][name]
+        if not shard:
+            np.testing.assert_array_equal(g0[name], g1[name])
+        err = np.linalg.norm(g - r) / max(np.linalg.norm(r), 1e-30)
         assert err < 1e-4, (name, err)
     assert c0 and c1
     for name in p0:
         np.testing.assert_array_equal(p0[name], p1[name])
 
 
-def test_two_rank_graph_steps_stay_replicated_and_match_eager(tmp_path):
+@pytest.mark.parametrize("shard", [False, True], ids=["replicated", "sharded_optimizer"])
+def test_two_rank_graph_steps_stay_replicated_and_match_eager(shard, tmp_path):
     """Captured-graph steps on two NCCL ranks: both ranks commit, stay bit-identical, and match one eager GPU."""
     require_gpu()
     from minifield_training_b200 import device
@@ -134,7 +144,7 @@ def test_two_rank_graph_steps_stay_replicated_and_match_eager(tmp_path):
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
     uid = str(tmp_path / "nccl.id")
-    run_ranks(ctx, _rank_graph, [(r, uid, out) for r in range(2)], 300)
+    run_ranks(ctx, _rank_graph, [(r, uid, out, shard) for r in range(2)], 300)
     (l0, p0), (l1, p1) = out[0], out[1]
     assert all(c for c, _ in l0) and l0 == l1
     for name in p0:

@@ -188,3 +188,46 @@ def test_split_k_workspace_is_needed_only_for_few_tiles():
     assert L.lib().mfb_gemm_workspace_size(64, 1024, 6656) > 0
     assert L.lib().mfb_gemm_workspace_size(16384, 13312, 1024) == 0  # enough tiles: no split
     assert L.lib().mfb_gemm_workspace_size(64, 1024, 64) == 0  # one k-block: nothing to split
+    # Weight gradients over 65536 tokens: 16 and 104 pair tiles get K slices.
+    assert L.lib().mfb_gemm_workspace_size(1024, 1024, 65536) > 0
+    assert L.lib().mfb_gemm_workspace_size(1024, 6656, 65536) > 0
+
+
+@pytest.mark.parametrize("m,n,k", [(1024, 1024, 8192), (520, 776, 4100)])
+def test_split_k_weight_gradient_on_pairs(m, n, k):
+    """The weight-gradient layout (dW = dY^T X: both operands MN-major, FP32 out, STE mask) on CTA
+    pairs with K slices: equal to the FP64 product within FP32 summation noise, to the unsplit
+    product within the same, and deterministic across calls."""
+    import ctypes
+
+    from minifield_training_b200 import _lib as L
+    from minifield_training_b200.device import DeviceArray
+
+    rng = np.random.default_rng(m + n + k)
+    dy = round_bf16(rng.standard_normal((k, m), dtype=np.float32))  # [tokens, out]
+    x = round_bf16(rng.standard_normal((k, n), dtype=np.float32))   # [tokens, in]
+    mask = (rng.random((m, n)) > 0.1).astype(np.uint8)
+    dyd, xd = _dev(dy), _dev(x)
+    md = DeviceArray.from_numpy(mask, "uint8")
+    need = int(L.lib().mfb_gemm_workspace_size(m, n, k))
+    assert need > 0
+    ws = DeviceArray((need,), "uint8")
+    ref = (dy.astype(np.float64).T @ x.astype(np.float64)) * mask
+
+    def run(workspace):
+        c = DeviceArray((m, n), "float32")
+        L.call("mfb_gemm_bf16_ws", ctypes.c_void_p(dyd.ptr), L.MAJOR_MN, m, ctypes.c_void_p(xd.ptr), L.MAJOR_MN, n,
+               ctypes.c_void_p(c.ptr), n, L.DTYPE_F32, m, n, k, ctypes.c_float(1.0), ctypes.c_void_p(md.ptr), 0,
+               ctypes.c_void_p(workspace.ptr) if workspace is not None else None,
+               workspace.nbytes if workspace is not None else 0, None)
+        return c.float32()
+
+    split_a, split_b, whole = run(ws), run(ws), run(None)
+    np.testing.assert_array_equal(split_a, split_b)
+    tol = 1e-4 * np.sqrt(k)
+    np.testing.assert_allclose(split_a, ref, rtol=1e-5, atol=tol)
+    np.testing.assert_allclose(split_a, whole, rtol=1e-5, atol=tol)
+    assert np.all(split_a[mask == 0] == 0)
+    st = ctypes.c_int()
+    L.call("mfb_gemm_status", ctypes.byref(st))
+    assert st.value == 0
