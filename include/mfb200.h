@@ -225,8 +225,11 @@ int mfb_gemm_swiglu_bwd(const uint16_t* dY, int a_major, int lda, const uint16_t
  * (kernels/linear.py:7-13: dW = dY^T X over all tokens, a few output tiles
  * with a very deep K). K is cut into slices whose FP32 partials are summed in
  * slice order (deterministic), then scaled and masked. The workspace (16-byte
- * aligned) needs mfb_gemm_workspace_size(M, N, K) bytes for the full split; a
- * smaller one gets fewer slices, NULL or 0 none.
+ * aligned) needs mfb_gemm_workspace_size(M, N, K) bytes for the full split of
+ * the unmasked product; a smaller one gets fewer slices, NULL or 0 none.
+ * Unmasked products of at most 64 rows run as C^T = B A^T internally (the
+ * weight rows fill the tensor core's 128-row side, C is stored transposed),
+ * so a wide projection of a decode batch needs no split at all.
  * flags: MFB_GEMM_PDL launches the GEMM as a programmatic dependent of the
  * previous kernel on the stream (a created stream, not the legacy default
  * one): its first B tiles load while that kernel finishes, A and the output

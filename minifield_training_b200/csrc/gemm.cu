@@ -70,7 +70,6 @@ constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, each storing half of a tile's columns
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int A_BYTES = BM * BK * 2;
-constexpr int TMEM_COLS = 2 * BN;
 constexpr int EPI_PLAIN = 0, EPI_SWIGLU_FWD = 1, EPI_SWIGLU_BWD = 2;
 
 struct Args {
@@ -87,6 +86,9 @@ struct Args {
   float* partial;       // [k_split, M, N] FP32 partials when k_split > 1
   int epi;              // EPI_*: plain store or a SwiGLU epilogue
   int n_fast;           // work order: n block fastest (tiles sharing A rows run together)
+  int swapped;          // the product runs as D = B . A^T (weights as the MMA's M side): D[r][s] is
+                        // stored at C[s * ldc + r], and the weights (A here) stream before the
+                        // programmatic-dependency wait
   int F;                // SwiGLU width (gate and up channels each)
   __nv_bfloat16* h;     // EPI_SWIGLU_FWD: h [M, F], row stride F
   const __nv_bfloat16* gu;  // EPI_SWIGLU_BWD: gu [M, 2F] read by the epilogue
@@ -214,7 +216,8 @@ __device__ __forceinline__ void store_partial(const Args& a, int ks, int row, in
 // the in-order adds), else one per element.
 template <bool VEC4>
 __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int k_split, int M, int N, void* C,
-                                     long long ldc, int out_f32, float alpha, const uint8_t* __restrict__ mask) {
+                                     long long ldc, int out_f32, float alpha, const uint8_t* __restrict__ mask,
+                                     int trans) {
   const int per = VEC4 ? 4 : 1, cols = N / per;
   const long long total = (long long)M * cols, slice = (long long)M * N;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -246,10 +249,29 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int k_sp
 #pragma unroll
     for (int e = 0; e < per; ++e) {
       const float v = acc[e] * alpha * mk[e];
+      // Swapped products (trans): partial element (row, col) is C's (col, row).
+      const long long at = trans ? (long long)(col + e) * ldc + row : row * ldc + col + e;
       if (out_f32)
-        reinterpret_cast<float*>(C)[row * ldc + col + e] = v;
+        reinterpret_cast<float*>(C)[at] = v;
       else
-        reinterpret_cast<__nv_bfloat16*>(C)[row * ldc + col + e] = __float2bfloat16_rn(v);
+        reinterpret_cast<__nv_bfloat16*>(C)[at] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+// Swapped products: D[row][col0 + i] goes to C[(col0 + i) * ldc + row]; a
+// warp's lanes hold consecutive rows, so each store instruction writes one
+// contiguous run of C.
+__device__ __forceinline__ void store_chunk_t(const Args& a, int row, int col0, const uint32_t* r) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int col = col0 + i;
+    if (col < a.N) {
+      const float v = __uint_as_float(r[i]) * a.alpha;
+      if (a.out_f32)
+        reinterpret_cast<float*>(a.C)[(long long)col * a.ldc + row] = v;
+      else
+        reinterpret_cast<__nv_bfloat16*>(a.C)[(long long)col * a.ldc + row] = __float2bfloat16_rn(v);
     }
   }
 }
@@ -315,13 +337,16 @@ __device__ __forceinline__ void store_chunk(const Args& a, int row, int col0, co
 // (STAGED): each epilogue warp owns a ring of RING slots of SLOT bytes, one
 // 32-row x 32-column chunk per slot (64-byte swizzled bf16 boxes moved by TMA),
 // and the main loop keeps four stages to make room.
-template <bool PAIR, int EPI>
+// TN: the tile's N (256; 64 for swapped products, whose N is a handful of
+// activation rows, with more stages for the weight stream).
+template <bool PAIR, int EPI, int TN = BN>
 struct Shape {
   static constexpr bool STAGED = PAIR && EPI != EPI_PLAIN;
-  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
+  static constexpr int B_ROWS = PAIR ? TN / 2 : TN;
   static constexpr int B_BYTES = B_ROWS * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = PAIR ? (STAGED ? 4 : 6) : 4;
+  static constexpr int STAGES = PAIR ? (STAGED ? 4 : 6) : (TN == BN ? 4 : 8);
+  static constexpr int TMEM_COLS = 2 * TN;
   // SwiGLU backward: gate and up boxes in, overwritten in place by dGate and
   // dUp (two 2 KB boxes); forward: gate, up and h out (three boxes).
   static constexpr int RING = EPI == EPI_SWIGLU_BWD ? 3 : 2;
@@ -389,11 +414,12 @@ __device__ __forceinline__ void swiglu_bwd_box(const uint32_t* d32, uint8_t* slo
 
 // te0 / te1: the staged epilogue's tensor maps (SwiGLU backward: gu loaded,
 // dGU stored; forward: gu and h stored); unused otherwise.
-template <bool PAIR, int EPI>
+template <bool PAIR, int EPI, int TN = BN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                 const __grid_constant__ CUtensorMap te0, const __grid_constant__ CUtensorMap te1, Args args) {
-  using S = Shape<PAIR, EPI>;
+  using S = Shape<PAIR, EPI, TN>;
+  constexpr int TMEM_COLS = S::TMEM_COLS;
   constexpr int STAGES = S::STAGES, STAGE_BYTES = S::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   // Offset from the __shared__ array itself so accesses keep the shared state space.
@@ -470,7 +496,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       auto expect = [&](int s) {
         if (rank == 0) tc::mbar_expect_tx(full_bar(s), (PAIR ? 2 : 1) * STAGE_BYTES);
       };
-      // This CTA's B rows of one stage: rows nb*BN + rank*B_ROWS.. (K-major
+      // This CTA's B rows of one stage: rows nb*TN + rank*B_ROWS.. (K-major
       // box or MN-major 64-row boxes), or for the SwiGLU forward the 128 gate
       // and the 128 up rows of channel block nb (alone: two boxes; in a pair
       // rank 0 loads the gate rows and rank 1 the up rows, so the accumulator
@@ -478,30 +504,44 @@ __global__ void __launch_bounds__(THREADS, 1)
       auto load_b = [&](uint32_t sb, int kb, int nb, uint32_t bar) {
         if (EPI == EPI_SWIGLU_FWD) {
           if (PAIR) {
-            load(sb, &tb, kb * BK, (int)rank * args.F + nb * (BN / 2), bar);
+            load(sb, &tb, kb * BK, (int)rank * args.F + nb * (TN / 2), bar);
           } else {
-            load(sb, &tb, kb * BK, nb * (BN / 2), bar);
-            load(sb + (BN / 2) * 128, &tb, kb * BK, args.F + nb * (BN / 2), bar);
+            load(sb, &tb, kb * BK, nb * (TN / 2), bar);
+            load(sb + (TN / 2) * 128, &tb, kb * BK, args.F + nb * (TN / 2), bar);
           }
         } else if (!args.b_mn) {
-          load(sb, &tb, kb * BK, nb * BN + (int)rank * S::B_ROWS, bar);
+          load(sb, &tb, kb * BK, nb * TN + (int)rank * S::B_ROWS, bar);
         } else {
 #pragma unroll
           for (int j = 0; j < S::B_ROWS / 64; ++j)
-            load(sb + j * 8192, &tb, nb * BN + (int)rank * S::B_ROWS + 64 * j, kb * BK, bar);
+            load(sb + j * 8192, &tb, nb * TN + (int)rank * S::B_ROWS + 64 * j, kb * BK, bar);
         }
       };
-      // B (the weights in a decode projection) of the first tile's first
-      // stages loads before the dependency wait: a GEMM launched as a
-      // programmatic dependent streams it while the previous kernel finishes.
-      // A, and everything this grid writes, come after the wait.
+      auto load_a = [&](uint32_t sa, int kb, int mb, uint32_t bar) {
+        if (!args.a_mn) {
+          load(sa, &ta, kb * BK, mb * BM, bar);
+        } else {
+#pragma unroll
+          for (int i = 0; i < BM / 64; ++i) load(sa + i * 8192, &ta, mb * BM + 64 * i, kb * BK, bar);
+        }
+      };
+      // The weights (B; A of a swapped product) of the first tile's first
+      // stages load before the dependency wait: a GEMM launched as a
+      // programmatic dependent streams them while the previous kernel
+      // finishes. The activations, and everything this grid writes, come
+      // after the wait.
+      const bool w_is_a = args.swapped != 0;
       int pre = 0;
       if (unit < num_tiles) {
         const Item it = item_of(args, unit);
         pre = min(STAGES, it.kb1 - it.kb0);
         for (int i = 0; i < pre; ++i) {
           expect(i);
-          load_b(sbase + i * STAGE_BYTES + A_BYTES, it.kb0 + i, it.nb, full_target(i));
+          const uint32_t sa = sbase + i * STAGE_BYTES;
+          if (w_is_a)
+            load_a(sa, it.kb0 + i, it.mb * (PAIR ? 2 : 1) + (int)rank, full_target(i));
+          else
+            load_b(sa + A_BYTES, it.kb0 + i, it.nb, full_target(i));
         }
       }
       wait_prerequisites();
@@ -509,7 +549,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const Item it = item_of(args, tile);
         const int mb = it.mb * (PAIR ? 2 : 1) + (int)rank, nb = it.nb;
         for (int kb = it.kb0; kb < it.kb1; ++kb) {
-          const bool early = tile == unit && kb - it.kb0 < pre;  // B already in flight
+          const bool early = tile == unit && kb - it.kb0 < pre;  // weights already in flight
           if (!early) {
             if (!tc::mbar_wait(empty_bar(stage), phase ^ 1, &g_status, 1)) {
               ok = false;
@@ -518,13 +558,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             expect(stage);
           }
           const uint32_t sa = sbase + stage * STAGE_BYTES, sb = sa + A_BYTES, bar = full_target(stage);
-          if (!args.a_mn) {
-            load(sa, &ta, kb * BK, mb * BM, bar);
-          } else {
-#pragma unroll
-            for (int i = 0; i < BM / 64; ++i) load(sa + i * 8192, &ta, mb * BM + 64 * i, kb * BK, bar);
-          }
-          if (!early) load_b(sb, kb, nb, bar);
+          if (!early || !w_is_a) load_a(sa, kb, mb, bar);
+          if (!early || w_is_a) load_b(sb, kb, nb, bar);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -536,14 +571,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     // The whole warp runs the issue loop (converged); one elected lane issues.
     // In a pair only rank 0 issues.
     if (rank == 0) {
-      const uint32_t idesc = tc::idesc_bf16_f32(PAIR ? 2 * BM : BM, BN, args.a_mn, args.b_mn);
+      const uint32_t idesc = tc::idesc_bf16_f32(PAIR ? 2 * BM : BM, TN, args.a_mn, args.b_mn);
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
       for (int tile = unit; ok && tile < num_tiles; tile += units) {
         if (!tc::mbar_wait_w(tempty_bar(acc), acc_phase ^ 1, &g_status, 2)) break;
         tc::tc_fence_after();
-        const uint32_t d = tmem + acc * BN;
+        const uint32_t d = tmem + acc * TN;
         const Item it = item_of(args, tile);
         for (int kb = it.kb0; kb < it.kb1; ++kb) {
           if (!tc::mbar_wait_w(full_bar(stage), phase, &g_status, 3)) {
@@ -602,7 +637,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t* my_ring_p = smem + STAGES * STAGE_BYTES + ew * RING * SLOT;
     // Output column (backward: dH column; forward: channel) of chunk c of a tile.
     auto chunk_col = [&](const Item& it, int c) {
-      return EPI == EPI_SWIGLU_BWD ? it.nb * BN + half * 128 + c * 32 : it.nb * (BN / 2) + half * 64 + c * 32;
+      return EPI == EPI_SWIGLU_BWD ? it.nb * TN + half * 128 + c * 32 : it.nb * (TN / 2) + half * 64 + c * 32;
     };
     auto chunk_row0 = [&](const Item& it) { return (it.mb * 2 + (int)rank) * BM + q * 32; };
     uint32_t loaded = 0, slot_phase = 0;  // per slot: a gu load in flight; its barrier parity
@@ -647,7 +682,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int row0 = chunk_row0(it);
       if (!tc::mbar_wait_w(tfull_bar(acc), acc_phase, &g_status, 5)) break;
       tc::tc_fence_after();
-      const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
+      const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + acc * TN;
 #pragma unroll 1
       for (int c = 0; c < CH; ++c, ++i) {
         const int col = chunk_col(it, c), b = i % RING;
@@ -682,7 +717,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         } else {
           uint32_t g[32], u[32];
           tc::tmem_ld_32x32b_x32(tacc + half * 64 + c * 32, g);
-          tc::tmem_ld_32x32b_x32(tacc + BN / 2 + half * 64 + c * 32, u);
+          tc::tmem_ld_32x32b_x32(tacc + TN / 2 + half * 64 + c * 32, u);
           tc::tmem_ld_wait();
           if (lane == 0) tc::bulk_wait_group_read<RING - 1>();  // chunk i - RING's stores have left this slot
           __syncwarp();
@@ -726,25 +761,25 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!tc::mbar_wait_w(tfull_bar(acc), acc_phase, &g_status, 5)) break;
       tc::tc_fence_after();
       const int row = mb * BM + q * 32 + lane;
-      const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
+      const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + acc * TN;
       if (EPI == EPI_SWIGLU_FWD) {
 #pragma unroll 1
-        for (int ch = half * (BN / 128); ch < (half + 1) * (BN / 128); ++ch) {  // gate ch*32.., up BN/2 + ch*32..
+        for (int ch = half * (TN / 128); ch < (half + 1) * (TN / 128); ++ch) {  // gate ch*32.., up TN/2 + ch*32..
           uint32_t g[32], u[32];
           tc::tmem_ld_32x32b_x32(tacc + ch * 32, g);
-          tc::tmem_ld_32x32b_x32(tacc + BN / 2 + ch * 32, u);
+          tc::tmem_ld_32x32b_x32(tacc + TN / 2 + ch * 32, u);
           tc::tmem_ld_wait();
-          if (row < args.M) swiglu_fwd_chunk(args, row, nb * (BN / 2) + ch * 32, g, u);
+          if (row < args.M) swiglu_fwd_chunk(args, row, nb * (TN / 2) + ch * 32, g, u);
         }
       } else if (EPI == EPI_SWIGLU_BWD) {
-        const int ch0 = half * (BN / 64), ch1 = ch0 + BN / 64;
+        const int ch0 = half * (TN / 64), ch1 = ch0 + TN / 64;
         GuChunk cur, next;
-        if (row < args.M && nb * BN + ch0 * 32 < args.N) load_gu(args, row, nb * BN + ch0 * 32, cur);
+        if (row < args.M && nb * TN + ch0 * 32 < args.N) load_gu(args, row, nb * TN + ch0 * 32, cur);
 #pragma unroll 1
         for (int ch = ch0; ch < ch1; ++ch) {
           uint32_t r[32];
           tc::tmem_ld_32x32b_x32(tacc + ch * 32, r);
-          const int col0 = nb * BN + ch * 32;
+          const int col0 = nb * TN + ch * 32;
           if (ch + 1 < ch1 && row < args.M && col0 + 32 < args.N) load_gu(args, row, col0 + 32, next);
           tc::tmem_ld_wait();
           if (row < args.M && col0 < args.N) swiglu_bwd_chunk(args, row, col0, r, cur);
@@ -752,14 +787,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       } else {
 #pragma unroll 1
-        for (int ch = half * (BN / 64); ch < (half + 1) * (BN / 64); ++ch) {
+        for (int ch = half * (TN / 64); ch < (half + 1) * (TN / 64); ++ch) {
           uint32_t r[32];
           tc::tmem_ld_32x32b_x32(tacc + ch * 32, r);
           tc::tmem_ld_wait();
-          const int col0 = nb * BN + ch * 32;
+          const int col0 = nb * TN + ch * 32;
           if (row < args.M && col0 < args.N) {
             if (args.k_split > 1)
               store_partial(args, ks, row, col0, r);
+            else if (args.swapped)
+              store_chunk_t(args, row, col0, r);
             else
               store_chunk(args, row, col0, r);
           }
@@ -904,10 +941,10 @@ int pair_clusters(int dev);
 // k-blocks, so the FP32 partials stay well below the bf16 operand bytes a
 // slice streams.
 constexpr int SPLIT_MIN_KB = 4, SPLIT_MIN_KB_PAIR = 8, SPLIT_MAX = 16;
-int choose_split(int M, int N, int K, int dev, int* kb_per) {
+int choose_split(int M, int N, int K, int dev, int* kb_per, bool single = false) {
   const int num_k = cdiv(K, gemm::BK);
   *kb_per = num_k;
-  const int pairs = M > gemm::BM ? pair_clusters(dev) : 0;
+  const int pairs = M > gemm::BM && !single ? pair_clusters(dev) : 0;
   if (pairs > 0) {
     const int tiles = cdiv(M, 2 * gemm::BM) * cdiv(N, gemm::BN);
     const double tile_us = 0.5 * num_k, bytes = 4.0 * M * N;
@@ -934,11 +971,23 @@ int choose_split(int M, int N, int K, int dev, int* kb_per) {
 }
 }  // namespace
 
+namespace {
+// Products of at most SWAP_M rows without a mask (the decode step's [batch, C]
+// projections) run swapped: D = B . A^T with the weights' rows on the MMA's
+// 128-row side and the few activation rows as a SWAP_TN-wide N tile, stored
+// transposed into C. The weight rows then fill the tiles (the unswapped tile
+// would use 64 of its 128 rows) and the wide projections need no K split.
+constexpr int SWAP_M = 64, SWAP_TN = 64;
+bool swapped_shape(int M, const void* mask) { return M <= SWAP_M && mask == nullptr; }
+}  // namespace
+
 extern "C" size_t mfb_gemm_workspace_size(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   int dev = 0, kb_per = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
-  const int split = choose_split(M, N, K, dev, &kb_per);
+  // The need of the unmasked product (swapped when M <= SWAP_M); a masked one
+  // of so few rows may get fewer slices from it.
+  const int split = M <= SWAP_M ? choose_split(N, M, K, dev, &kb_per, true) : choose_split(M, N, K, dev, &kb_per);
   return split > 1 ? sizeof(float) * (size_t)split * M * N : 0;
 }
 
@@ -980,13 +1029,13 @@ bool use_pair(int M, int dev) { return M > gemm::BM && pair_clusters(dev) > 0; }
 // Launches gemm_kernel<PAIR, EPI> over a.num_m x a.num_n x a.k_split work
 // items (a pair's 256 rows or a CTA's 128 per m block), one persistent CTA or
 // CTA pair per SM or SM pair, optionally as a programmatic dependent launch.
-template <bool PAIR, int EPI>
+template <bool PAIR, int EPI, int TN = gemm::BN>
 int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& te0, const CUtensorMap& te1,
                   const gemm::Args& a, bool pdl, cudaStream_t stream, const char* what) {
   int dev = 0;
   MFB_CUDA_TRY(cudaGetDevice(&dev));
-  auto kernel = gemm::gemm_kernel<PAIR, EPI>;
-  constexpr int smem = gemm::Shape<PAIR, EPI>::SMEM;
+  auto kernel = gemm::gemm_kernel<PAIR, EPI, TN>;
+  constexpr int smem = gemm::Shape<PAIR, EPI, TN>::SMEM;
   MFB_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int tiles = a.num_m * a.num_n * a.k_split;
   cudaLaunchConfig_t cfg{};
@@ -1025,6 +1074,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
       return pair ? launch_kernel<true, gemm::EPI_SWIGLU_BWD>(ta, tb, te0, te1, a, pdl, stream, what)
                   : launch_kernel<false, gemm::EPI_SWIGLU_BWD>(ta, tb, te0, te1, a, pdl, stream, what);
     default:
+      if (a.swapped) return launch_kernel<false, gemm::EPI_PLAIN, SWAP_TN>(ta, tb, te0, te1, a, pdl, stream, what);
       return pair ? launch_kernel<true, gemm::EPI_PLAIN>(ta, tb, te0, te1, a, pdl, stream, what)
                   : launch_kernel<false, gemm::EPI_PLAIN>(ta, tb, te0, te1, a, pdl, stream, what);
   }
@@ -1036,10 +1086,12 @@ int make_tmap_a(CUtensorMap* map, const void* A, int a_major, int lda, int M, in
   return tc::make_tmap_bf16(map, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, gemm::BK);
 }
 // Tensor map of a B operand (K-major [N, K]: boxes of a CTA's B rows; MN-major [K, N]: 64 x 64 boxes).
-int make_tmap_b(CUtensorMap* map, const void* B, int b_major, int ldb, int N, int K, bool pair) {
+int make_tmap_b(CUtensorMap* map, const void* B, int b_major, int ldb, int N, int K, bool pair, int rows = 0) {
   if (b_major == MFB_MAJOR_K)
     return tc::make_tmap_bf16(map, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb,
-                              pair ? gemm::Shape<true, gemm::EPI_PLAIN>::B_ROWS : gemm::Shape<false, gemm::EPI_PLAIN>::B_ROWS);
+                              rows ? rows
+                                   : (pair ? gemm::Shape<true, gemm::EPI_PLAIN>::B_ROWS
+                                           : gemm::Shape<false, gemm::EPI_PLAIN>::B_ROWS));
   return tc::make_tmap_bf16(map, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, gemm::BK);
 }
 }  // namespace
@@ -1069,17 +1121,25 @@ extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const u
   MFB_CHECK_ARG(((uintptr_t)A & 15) == 0 && ((uintptr_t)B & 15) == 0, "A and B must be 16-byte aligned (TMA)");
   int dev = 0;
   MFB_CUDA_TRY(cudaGetDevice(&dev));
+  // The kernel computes D[KM, KN]: C itself, or C^T for a swapped product.
+  const bool swap = swapped_shape(M, mask);
+  const int KM = swap ? N : M, KN = swap ? M : N;
+  const uint16_t* KA = swap ? B : A;
+  const uint16_t* KB = swap ? A : B;
+  const int ka_major = swap ? b_major : a_major, kb_major = swap ? a_major : b_major;
+  const int klda = swap ? ldb : lda, kldb = swap ? lda : ldb;
   gemm::Args a{};
   a.C = C;
   a.mask = mask;
   a.ldc = ldc;
-  a.M = M;
-  a.N = N;
+  a.M = KM;
+  a.N = KN;
   a.K = K;
   a.out_f32 = out_dtype == MFB_DTYPE_F32;
-  a.a_mn = a_major == MFB_MAJOR_MN;
-  a.b_mn = b_major == MFB_MAJOR_MN;
-  a.num_n = cdiv(N, gemm::BN);
+  a.a_mn = ka_major == MFB_MAJOR_MN;
+  a.b_mn = kb_major == MFB_MAJOR_MN;
+  a.swapped = swap;
+  a.num_n = cdiv(KN, swap ? SWAP_TN : gemm::BN);
   a.num_k = cdiv(K, gemm::BK);
   a.alpha = alpha;
   {
@@ -1091,7 +1151,7 @@ extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const u
   a.partial = nullptr;
   if (workspace) {
     int kb_per = 0;
-    int split = choose_split(M, N, K, dev, &kb_per);
+    int split = choose_split(KM, KN, K, dev, &kb_per, swap);
     const size_t slice = sizeof(float) * (size_t)M * N;
     if (split > 1 && workspace_bytes < slice * split) {  // a smaller workspace gets fewer slices
       split = (int)std::min<size_t>(split, workspace_bytes / slice);
@@ -1106,26 +1166,26 @@ extern "C" int mfb_gemm_bf16_ws(const uint16_t* A, int a_major, int lda, const u
       a.partial = static_cast<float*>(workspace);
     }
   }
-  const bool pair = use_pair(M, dev);
-  a.num_m = cdiv(M, pair ? 2 * gemm::BM : gemm::BM);
-  a.n_fast = M > N;  // A (M x K) is the larger operand
+  const bool pair = !swap && use_pair(M, dev);
+  a.num_m = cdiv(KM, pair ? 2 * gemm::BM : gemm::BM);
+  a.n_fast = KM > KN;  // A (KM x K) is the larger operand
   CUtensorMap ta, tb;
-  int st = make_tmap_a(&ta, A, a_major, lda, M, K);
+  int st = make_tmap_a(&ta, KA, ka_major, klda, KM, K);
   if (st) return st;
-  if ((st = make_tmap_b(&tb, B, b_major, ldb, N, K, pair))) return st;
+  if ((st = make_tmap_b(&tb, KB, kb_major, kldb, KN, K, pair, swap ? SWAP_TN : 0))) return st;
   if ((st = launch_gemm(ta, tb, ta, ta, a, pair, (flags & MFB_GEMM_PDL) != 0, (cudaStream_t)stream,
                         "mfb_gemm_bf16")))
     return st;
   if (a.k_split > 1) {
-    const bool vec4 = N % 4 == 0 && ((uintptr_t)mask & 3) == 0;
-    const long long total = (long long)M * N / (vec4 ? 4 : 1);
+    const bool vec4 = KN % 4 == 0 && ((uintptr_t)mask & 3) == 0;
+    const long long total = (long long)KM * KN / (vec4 ? 4 : 1);
     const int blocks = (int)std::min<long long>((total + 255) / 256, 8LL * sm_count(dev));
     if (vec4)
-      gemm::splitk_reduce_kernel<true><<<blocks, 256, 0, (cudaStream_t)stream>>>(a.partial, a.k_split, M, N, C,
-                                                                                ldc, a.out_f32, alpha, mask);
+      gemm::splitk_reduce_kernel<true><<<blocks, 256, 0, (cudaStream_t)stream>>>(a.partial, a.k_split, KM, KN, C,
+                                                                                ldc, a.out_f32, alpha, mask, swap);
     else
-      gemm::splitk_reduce_kernel<false><<<blocks, 256, 0, (cudaStream_t)stream>>>(a.partial, a.k_split, M, N, C,
-                                                                                 ldc, a.out_f32, alpha, mask);
+      gemm::splitk_reduce_kernel<false><<<blocks, 256, 0, (cudaStream_t)stream>>>(a.partial, a.k_split, KM, KN, C,
+                                                                                 ldc, a.out_f32, alpha, mask, swap);
     MFB_LAUNCH_CHECK("GEMM split-K reduce");
   }
   return MFB_OK;

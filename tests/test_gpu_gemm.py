@@ -188,6 +188,8 @@ def test_split_k_workspace_is_needed_only_for_few_tiles():
     assert L.lib().mfb_gemm_workspace_size(64, 1024, 6656) > 0
     assert L.lib().mfb_gemm_workspace_size(16384, 13312, 1024) == 0  # enough tiles: no split
     assert L.lib().mfb_gemm_workspace_size(64, 1024, 64) == 0  # one k-block: nothing to split
+    # A 64-row product runs swapped: the 13312 weight rows give 104 tiles, no split.
+    assert L.lib().mfb_gemm_workspace_size(64, 13312, 1024) == 0
     # Weight gradients over 65536 tokens: 16 and 104 pair tiles get K slices.
     assert L.lib().mfb_gemm_workspace_size(1024, 1024, 65536) > 0
     assert L.lib().mfb_gemm_workspace_size(1024, 6656, 65536) > 0
