@@ -937,10 +937,10 @@ int pair_clusters(int dev);
 // Each slice keeps at least SPLIT_MIN_KB_PAIR k-blocks.
 //
 // Smaller products (the decode projections, single-CTA tiles): > 1 only when
-// the tiles fill fewer than half the SMs, slices of at least SPLIT_MIN_KB
-// k-blocks, so the FP32 partials stay well below the bf16 operand bytes a
-// slice streams.
-constexpr int SPLIT_MIN_KB = 4, SPLIT_MIN_KB_PAIR = 8, SPLIT_MAX = 16;
+// the tiles fill fewer than half the SMs and a tile is deep enough to be
+// worth a reduce launch, slices of at least SPLIT_MIN_KB k-blocks, so the FP32
+// partials stay well below the bf16 operand bytes a slice streams.
+constexpr int SPLIT_MIN_KB = 4, SPLIT_MIN_KB_PAIR = 8, SPLIT_MAX = 16, SPLIT_MIN_TILE_KB = 30;
 int choose_split(int M, int N, int K, int dev, int* kb_per, bool single = false) {
   const int num_k = cdiv(K, gemm::BK);
   *kb_per = num_k;
@@ -964,7 +964,10 @@ int choose_split(int M, int N, int K, int dev, int* kb_per, bool single = false)
   }
   const int sms = sm_count(dev);
   const int tiles = cdiv(M, gemm::BM) * cdiv(N, gemm::BN);
-  if (2 * tiles > sms || num_k < 2 * SPLIT_MIN_KB) return 1;
+  // A tile that streams in a few microseconds (under SPLIT_MIN_TILE_KB
+  // k-blocks, ~0.27 us each on one SM) is not split: the reduce launch would
+  // cost more than the slices save.
+  if (2 * tiles > sms || num_k < 2 * SPLIT_MIN_KB || num_k < SPLIT_MIN_TILE_KB) return 1;
   int split = std::min(std::min(num_k / SPLIT_MIN_KB, sms / tiles), SPLIT_MAX);
   *kb_per = cdiv(num_k, split);
   return cdiv(num_k, *kb_per);
