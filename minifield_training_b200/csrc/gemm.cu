@@ -46,9 +46,14 @@
 // dH tile to bf16, reads gate and up of its channels from gu and writes
 // dGU = [dH * up * silu'(gate), dH * silu(gate)]; dH is never stored.
 //
+// Products of at most 64 rows without a mask (the decode step's [batch, C]
+// projections) run swapped: D = B . A^T, the weight rows on the MMA's 128-row
+// side and the batch as a 64-wide N tile, D stored transposed into C; the
+// weights are the operand loaded ahead of a programmatic-dependency wait.
+//
 // Split-K, when a caller-owned workspace is given and the output tiles fill
-// the GPU poorly: the decode step's projections (64 rows, a handful of tiles)
-// and the weight gradients (a few 256x256 pair tiles, K = the token count).
+// the GPU poorly: deep decode projections (w2) and the weight gradients (a
+// few 256x256 pair tiles, K = the token count).
 // The K range is cut into up to 16 slices (choose_split); each (tile, slice)
 // is a work item that writes its FP32 partial [M, N] to the workspace, and
 // splitk_reduce_kernel sums the slices in slice order (deterministic), scales,

@@ -187,7 +187,9 @@ class Decoder:
         return self._scratch[key]
 
     def _proj(self, x, w, out, m, n, k, B):
-        """out[m, n] = x[m, k] . w[n, k]^T (bf16); split-K through the step's workspace when m is small.
+        """out[m, n] = x[m, k] . w[n, k]^T (bf16). With the batch's few rows the library runs the product
+        swapped (the weight rows on the tensor core's 128-row side) and splits K through the step's
+        workspace only for a deep weight (w2).
 
         On a created stream it launches as a programmatic dependent: the
         weight tiles stream in while the previous kernel (norm, SwiGLU, conv

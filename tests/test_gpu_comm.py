@@ -5,8 +5,10 @@ deadline passes while the stream is still busy (queued GEMMs that finish on
 their own) aborts the communicator and raises CommError, and the aborted
 communicator rejects later calls; a communicator whose second rank never
 joins fails its initialisation at the deadline instead of waiting for ever.
-Two GPUs (skipped on one): SUM all-reduce, reduce-scatter and all-gather
-across two processes give the exact sums and blocks. NVLS stays off.
+Two GPUs (skipped on one): SUM all-reduce, reduce-scatter, all-gather,
+reduce to a root and broadcast from a root across two processes give the exact
+sums and blocks (the non-root's reduce buffer keeps its own values). NVLS stays
+off.
 """
 
 import ctypes
@@ -35,6 +37,8 @@ def _child_one_rank(uid_path, out):
     c.all_gather(a, g)
     r = DeviceArray((1000,), "float32")
     c.reduce_scatter(g, r)
+    c.reduce(r, 0)
+    c.broadcast(r, 0)
     c.wait()
     out["values"] = (a.numpy(), g.numpy(), r.numpy())
     c.close()
@@ -128,8 +132,12 @@ def _child_two_ranks(rank, uid_path, out):
     c.all_gather(DeviceArray.from_numpy(x, "float32"), g)
     d = DeviceArray.from_numpy(np.array([rank + 0.5, -rank, 3.0], np.float64).view(np.uint8), "uint8")
     c.allreduce_f64(d.ptr, 3, op=comm.MAX)
+    red = DeviceArray.from_numpy(x, "float32")
+    c.reduce(red, 1)  # the sum lands on rank 1 only
+    b = DeviceArray.from_numpy(x, "float32")
+    c.broadcast(b, 0)  # rank 0's values everywhere
     c.wait()
-    out[rank] = (x, a.numpy(), r.numpy(), g.numpy(), d.numpy().view(np.float64))
+    out[rank] = (x, a.numpy(), r.numpy(), g.numpy(), d.numpy().view(np.float64), red.numpy(), b.numpy())
     c.close()
 
 
@@ -144,7 +152,7 @@ def test_two_rank_collectives_are_exact(tmp_path):
     out = ctx.Manager().dict()
     uid = str(tmp_path / "nccl.id")
     run_ranks(ctx, _child_two_ranks, [(r, uid, out) for r in range(2)], 240)
-    (x0, a0, r0, g0, d0), (x1, a1, r1, g1, d1) = out[0], out[1]
+    (x0, a0, r0, g0, d0, red0, b0), (x1, a1, r1, g1, d1, red1, b1) = out[0], out[1]
     total = x0 + x1  # a two-term float32 sum is the same in either order
     np.testing.assert_array_equal(a0, total)
     np.testing.assert_array_equal(a1, total)
@@ -154,3 +162,7 @@ def test_two_rank_collectives_are_exact(tmp_path):
         np.testing.assert_array_equal(g, np.concatenate((x0, x1)))
     for d in (d0, d1):
         np.testing.assert_array_equal(d, [1.5, 0.0, 3.0])
+    np.testing.assert_array_equal(red1, total)
+    np.testing.assert_array_equal(red0, x0)
+    np.testing.assert_array_equal(b0, x0)
+    np.testing.assert_array_equal(b1, x0)
