@@ -228,7 +228,9 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(const float* __restrict
 //   warp 1      TMEM owner and MMA issuer (whole warp, one elected lane).
 //   warps 2-5   softmax for query head h0, warps 6-9 for h0 + 1: one thread
 //               per query row (TMEM lane quarter = warp % 4), reading its S row
-//               with tcgen05.ld.
+//               with tcgen05.ld; at the end each warp's normalised O rows go
+//               into its head's Q buffer and a whole tile leaves as one TMA
+//               store per head (a partial tile stores rows).
 // Per live key tile j and head g:
 //   S_g = Q_g K_j^T           SS MMA, M=128 N=128 K=64 -> TMEM (128 columns)
 //   softmax: the thread loads its 128-value S row with one wait, takes the
@@ -298,7 +300,7 @@ __device__ __forceinline__ bool tile_full128(const Params& p, const Range& qr, c
 // 10 warps: the sub-partitions holding 3 warps cap registers at 168 per thread.
 __global__ void __launch_bounds__(TF_THREADS, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                       const __grid_constant__ CUtensorMap tv, Params p) {
+                       const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to, Params p) {
   extern __shared__ uint8_t smem_raw[];
   // Offset from the __shared__ array itself so accesses keep the shared state space.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -648,24 +650,40 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       vm0 /= (float)p.S;
       vm1 /= (float)p.S;
     }
-    __nv_bfloat16* orow = p.o + (((long long)b * p.T + t) * p.H + h) * HD;
+    // Normalised bf16 pairs, packed in place into ou[0, 32).
 #pragma unroll
-    for (int c8 = 0; c8 < 8; ++c8) {
-      uint4 u;
-      uint32_t* w = reinterpret_cast<uint32_t*>(&u);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int d = c8 * 8 + 2 * e;
-        float a0 = __uint_as_float(ou[d]) * inv, a1 = __uint_as_float(ou[d + 1]) * inv;
-        if (need_uniform) {
-          const float u0 = __shfl_sync(0xffffffffu, vm0, d >> 1), u1 = __shfl_sync(0xffffffffu, vm1, d >> 1);
-          if (empty) a0 = u0, a1 = u1;
-        }
-        w[e] = pack_bf16(a0, a1);
+    for (int e = 0; e < 32; ++e) {
+      float a0 = __uint_as_float(ou[2 * e]) * inv, a1 = __uint_as_float(ou[2 * e + 1]) * inv;
+      if (need_uniform) {
+        const float u0 = __shfl_sync(0xffffffffu, vm0, e), u1 = __shfl_sync(0xffffffffu, vm1, e);
+        if (empty) a0 = u0, a1 = u1;
       }
-      if (t < p.T) *reinterpret_cast<uint4*>(orow + c8 * 8) = u;
+      ou[e] = pack_bf16(a0, a1);
     }
     if (t < p.T) p.lse[((long long)b * p.H + h) * p.T + t] = empty ? -INFINITY : M + __log2f(l);
+    if (q0 + TQ <= p.T) {
+      // Whole tile: rows into the head's Q buffer (every product that read it
+      // has completed: o_full follows them) in the TMA tile layout, then one
+      // TMA store per head. All eight softmax warps reach the barrier.
+      uint8_t* stage = smem + TF_Q_OFF + g * 16384;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8)
+        *reinterpret_cast<uint4*>(stage + r * 128 + ((c8 ^ (r & 7)) << 4)) =
+            make_uint4(ou[4 * c8], ou[4 * c8 + 1], ou[4 * c8 + 2], ou[4 * c8 + 3]);
+      tc::fence_proxy_async_smem();
+      asm volatile("bar.sync 1, 256;\n" ::: "memory");
+      if (warp == 2 && lane == 0) {
+        tc::tma_store_2d(&to, sb + TF_Q_OFF, h0 * 64, b * p.T + q0);
+        tc::tma_store_2d(&to, sb + TF_Q_OFF + 16384, (h0 + 1) * 64, b * p.T + q0);
+        tc::bulk_commit_group();
+        tc::bulk_wait_group0();
+      }
+    } else if (t < p.T) {
+      __nv_bfloat16* orow = p.o + (((long long)b * p.T + t) * p.H + h) * HD;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8)
+        *reinterpret_cast<uint4*>(orow + c8 * 8) = make_uint4(ou[4 * c8], ou[4 * c8 + 1], ou[4 * c8 + 2], ou[4 * c8 + 3]);
+    }
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -690,7 +708,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 //               sub-items (half 0 / half 1 of every item): one key row (TMEM
 //               lane) per thread, 32 of the sub-item's 64 query columns per
 //               warp, two warps of a group per TMEM lane quarter. Prologue: K
-//               and V rows into TMEM; epilogue: dK/dV rows out.
+//               and V rows into TMEM; epilogue: dK/dV rows into the first Q/dO
+//               stage, out as two TMA stores (partial tiles store rows).
 //   warps 18-21 dQ flush: add each item's dQ tile into the FP32 accumulator
 //               while the next item is computed: TMEM -> swizzled shared
 //               staging -> TMA tensor reduce-add (the reductions run in the
@@ -777,7 +796,8 @@ __device__ __forceinline__ void ds_chunk(const uint32_t (&sx)[N], const uint32_t
 __global__ void __launch_bounds__(TB_THREADS, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                        const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                       const __grid_constant__ CUtensorMap tdq, Params p) {
+                       const __grid_constant__ CUtensorMap tdq, const __grid_constant__ CUtensorMap tdk,
+                       const __grid_constant__ CUtensorMap tdv, Params p) {
   extern __shared__ uint8_t smem_raw[];
   // Offset from the __shared__ array itself so accesses keep the shared state space.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -1103,8 +1123,15 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
     }
     // Epilogue: after the last products, dK (times the logit scale) and dV
     // (plus the uniform-row term) for this key row, this warp's TB_CW dims.
+    // A whole 128-key tile goes through the first Q/dO stage (free once every
+    // product has completed) in the TMA tile layout and leaves as two TMA
+    // stores; a partial tile stores its rows. Every softmax-gradient warp
+    // reaches the staging barrier, whatever its waits returned.
     const bool done_ok = ok && tc::mbar_wait(done_bar, 0, status, 38);
-    if (__all_sync(0xffffffffu, done_ok)) {
+    const bool go = __all_sync(0xffffffffu, done_ok);
+    const bool whole = s0 + TK <= p.S;
+    uint4 ka[TB_CW / 8], va[TB_CW / 8];
+    if (go) {
       tc::tc_fence_after();
       uint32_t kv[TB_CW], vv[TB_CW];
 #pragma unroll
@@ -1113,29 +1140,48 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
         tc::tmem_ld_32x32b_x16(tmem + lane_off + 256 + wq * TB_CW + c, vv + c);
       }
       tc::tmem_ld_wait();
-      if (s < p.S) {
-        const long long off = (((long long)b * p.S + s) * p.Hk + hk) * HD + wq * TB_CW;
-        const float* uv = p.uvec + ((long long)b * p.Hk + hk) * HD + wq * TB_CW;
-        const bool uni = p.policy == MFB_EMPTY_UNIFORM;
+      const float* uv = p.uvec + ((long long)b * p.Hk + hk) * HD + wq * TB_CW;
+      const bool uni = p.policy == MFB_EMPTY_UNIFORM;
+#pragma unroll
+      for (int c8 = 0; c8 < TB_CW / 8; ++c8) {
+        uint32_t* aw = reinterpret_cast<uint32_t*>(&ka[c8]);
+        uint32_t* cw = reinterpret_cast<uint32_t*>(&va[c8]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d = c8 * 8 + 2 * e;
+          const float k0 = nitems > 0 ? __uint_as_float(kv[d]) * p.scale : 0.f;
+          const float k1 = nitems > 0 ? __uint_as_float(kv[d + 1]) * p.scale : 0.f;
+          float v0 = nitems > 0 ? __uint_as_float(vv[d]) : 0.f;
+          float v1 = nitems > 0 ? __uint_as_float(vv[d + 1]) : 0.f;
+          if (uni) v0 += uv[d], v1 += uv[d + 1];
+          aw[e] = pack_bf16(k0, k1);
+          cw[e] = pack_bf16(v0, v1);
+        }
+      }
+    }
+    if (whole) {
+      if (go) {
 #pragma unroll
         for (int c8 = 0; c8 < TB_CW / 8; ++c8) {
-          uint4 a, c;
-          uint32_t* aw = reinterpret_cast<uint32_t*>(&a);
-          uint32_t* cw = reinterpret_cast<uint32_t*>(&c);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int d = c8 * 8 + 2 * e;
-            const float k0 = nitems > 0 ? __uint_as_float(kv[d]) * p.scale : 0.f;
-            const float k1 = nitems > 0 ? __uint_as_float(kv[d + 1]) * p.scale : 0.f;
-            float v0 = nitems > 0 ? __uint_as_float(vv[d]) : 0.f;
-            float v1 = nitems > 0 ? __uint_as_float(vv[d + 1]) : 0.f;
-            if (uni) v0 += uv[d], v1 += uv[d + 1];
-            aw[e] = pack_bf16(k0, k1);
-            cw[e] = pack_bf16(v0, v1);
-          }
-          *reinterpret_cast<uint4*>(p.dk + off + c8 * 8) = a;
-          *reinterpret_cast<uint4*>(p.dv + off + c8 * 8) = c;
+          const uint32_t off = r * 128 + ((((wq * TB_CW) / 8 + c8) ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(smem + TB_QD_OFF + off) = ka[c8];
+          *reinterpret_cast<uint4*>(smem + TB_QD_OFF + 16384 + off) = va[c8];
         }
+      }
+      tc::fence_proxy_async_smem();
+      asm volatile("bar.sync 1, %0;\n" ::"r"(32 * TB_SM_WARPS) : "memory");
+      if (warp == 2 && lane == 0) {
+        tc::tma_store_2d(&tdk, sb + TB_QD_OFF, hk * 64, b * p.S + s0);
+        tc::tma_store_2d(&tdv, sb + TB_QD_OFF + 16384, hk * 64, b * p.S + s0);
+        tc::bulk_commit_group();
+        tc::bulk_wait_group0();
+      }
+    } else if (go && s < p.S) {
+      const long long off = (((long long)b * p.S + s) * p.Hk + hk) * HD + wq * TB_CW;
+#pragma unroll
+      for (int c8 = 0; c8 < TB_CW / 8; ++c8) {
+        *reinterpret_cast<uint4*>(p.dk + off + c8 * 8) = ka[c8];
+        *reinterpret_cast<uint4*>(p.dv + off + c8 * 8) = va[c8];
       }
     }
   } else {
@@ -1313,6 +1359,7 @@ int launch_ranges(const Params& p, const int* qid, const int* kid, cudaStream_t 
   return MFB_OK;
 }
 
+
 }  // namespace attn
 }  // namespace mfb
 
@@ -1400,18 +1447,20 @@ extern "C" int mfb_attn_fwd(const uint16_t* q, const uint16_t* k, const uint16_t
   p.kid = kid;
   cudaStream_t s = (cudaStream_t)stream;
   if ((st = launch_ranges(p, qid, kid, s))) return st;
-  MFB_CHECK_ARG(((uintptr_t)q & 15) == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0,
-                "q/k/v must be 16-byte aligned");
-  CUtensorMap tq, tk, tv;
+  MFB_CHECK_ARG(((uintptr_t)q & 15) == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0 &&
+                    ((uintptr_t)o & 15) == 0,
+                "q/k/v/o must be 16-byte aligned");
+  CUtensorMap tq, tk, tv, to;
   if ((st = tc::make_tmap_bf16(&tq, q, (uint64_t)H * HD, (uint64_t)B * T, (uint64_t)H * HD, TQ))) return st;
   if ((st = tc::make_tmap_bf16(&tk, k, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
   if ((st = tc::make_tmap_bf16(&tv, v, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
+  if ((st = tc::make_tmap_bf16(&to, o, (uint64_t)H * HD, (uint64_t)B * T, (uint64_t)H * HD, TQ))) return st;
   MFB_CHECK_ARG(S <= TF_MAX_TILES * TK, "key length %d above the supported %d", S, TF_MAX_TILES * TK);
   if ((st = set_smem((const void*)attn_fwd_tc_kernel, TF_SMEM))) return st;
   schedule_kernel<<<1, 1024, 0, s>>>(p, 0, w.order);
   MFB_LAUNCH_CHECK("attention forward schedule");
   const long long fwd_ctas = (long long)B * cdiv(T, TQ) * (H / TF_HPB);
-  attn_fwd_tc_kernel<<<(unsigned)fwd_ctas, TF_THREADS, TF_SMEM, s>>>(tq, tk, tv, p);
+  attn_fwd_tc_kernel<<<(unsigned)fwd_ctas, TF_THREADS, TF_SMEM, s>>>(tq, tk, tv, to, p);
   MFB_LAUNCH_CHECK("mfb_attn_fwd");
   return MFB_OK;
 }
@@ -1447,19 +1496,21 @@ extern "C" int mfb_attn_bwd(const uint16_t* q, const uint16_t* k, const uint16_t
   MFB_LAUNCH_CHECK("attention backward preprocess");
   MFB_CHECK_ARG(T <= TF_MAX_TILES * TQ, "query length %d above the supported %d", T, TF_MAX_TILES * TQ);
   MFB_CHECK_ARG(((uintptr_t)q & 15) == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0 &&
-                    ((uintptr_t)d_o & 15) == 0,
-                "q/k/v/d_o must be 16-byte aligned");
-  CUtensorMap tq, tk, tv, tdo, tdq;
+                    ((uintptr_t)d_o & 15) == 0 && ((uintptr_t)dk & 15) == 0 && ((uintptr_t)dv & 15) == 0,
+                "q/k/v/d_o/dk/dv must be 16-byte aligned");
+  CUtensorMap tq, tk, tv, tdo, tdq, tdk, tdv;
   if ((st = tc::make_tmap_bf16(&tq, q, (uint64_t)H * HD, (uint64_t)B * T, (uint64_t)H * HD, TQ))) return st;
   if ((st = tc::make_tmap_bf16(&tdo, d_o, (uint64_t)H * HD, (uint64_t)B * T, (uint64_t)H * HD, TQ))) return st;
   if ((st = tc::make_tmap_f32_rows_heads(&tdq, w.dq_acc, H, (uint64_t)T, (uint64_t)B, 32))) return st;
   if ((st = tc::make_tmap_bf16(&tk, k, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
   if ((st = tc::make_tmap_bf16(&tv, v, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
+  if ((st = tc::make_tmap_bf16(&tdk, dk, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
+  if ((st = tc::make_tmap_bf16(&tdv, dv, (uint64_t)Hk * HD, (uint64_t)B * S, (uint64_t)Hk * HD, TK))) return st;
   if ((st = set_smem((const void*)attn_bwd_tc_kernel, TB_SMEM))) return st;
   schedule_kernel<<<1, 1024, 0, s>>>(p, 1, w.order);
   MFB_LAUNCH_CHECK("attention backward schedule");
   const long long bwd_ctas = (long long)B * cdiv(S, TK) * Hk;
-  attn_bwd_tc_kernel<<<(unsigned)bwd_ctas, TB_THREADS, TB_SMEM, s>>>(tq, tk, tv, tdo, tdq, p);
+  attn_bwd_tc_kernel<<<(unsigned)bwd_ctas, TB_THREADS, TB_SMEM, s>>>(tq, tk, tv, tdo, tdq, tdk, tdv, p);
   MFB_LAUNCH_CHECK("attention backward");
   const long long n4 = (long long)B * T * H * HD / 4;
   dq_convert_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, s>>>(w.dq_acc, reinterpret_cast<__nv_bfloat16*>(dq), n4,
