@@ -122,9 +122,13 @@ __global__ void ids_kernel(int mode, const int* __restrict__ mask, const int* __
   }
 }
 
-// Per-64-block id ranges for queries (z = 0) and keys (z = 1).
+// Per-64-block id ranges for queries (z = 0) and keys (z = 1); the first CTA
+// also clears `clear_n` floats at `clear` (the backward's uniform-row
+// accumulator, which the pre-pass that follows adds into).
 __global__ void ranges_kernel(const int* __restrict__ qid, const int* __restrict__ kid, Range* qr, Range* kr, int B,
-                              int T, int S, int nqb, int nkb) {
+                              int T, int S, int nqb, int nkb, float* clear, int clear_n) {
+  if (clear && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+    for (int i = threadIdx.x; i < clear_n; i += blockDim.x) clear[i] = 0.f;
   const int which = blockIdx.z;
   const int n = which ? S : T;
   const int nb = which ? nkb : nqb;
@@ -1316,18 +1320,31 @@ Params make_params(const Workspace& w, int B, int T, int S, int H, int Hk, int c
 // first keeps the last wave short). Forward items are (query tile, batch row)
 // weighted by their live key tiles, backward items (key tile, batch row) by
 // their live query tiles -- the same tile test the kernels use. One CTA,
-// counting sort over the tile counts.
+// counting sort over the tile counts. The range records are staged in shared
+// memory with coalesced loads and each weight is computed once, when they fit
+// (SCHED_RANGES records, SCHED_ITEMS items); otherwise they are read from the
+// workspace.
+constexpr int SCHED_RANGES = 1536;
+constexpr int SCHED_ITEMS = 4096;
 __global__ void __launch_bounds__(1024) schedule_kernel(Params p, int backward, int* order) {
   __shared__ int hist[TF_MAX_TILES + 1], base[TF_MAX_TILES + 1];
+  __shared__ Range sr[SCHED_RANGES];
+  __shared__ int wt[SCHED_ITEMS];
   const int ntq = cdiv(p.T, TQ), nkt = cdiv(p.S, TK);
   const int per = backward ? nkt : ntq, other = backward ? ntq : nkt;
   const int n = p.B * per;
+  const int nqr = p.B * p.nqb, nr = nqr + p.B * p.nkb;
+  const bool staged = nr <= SCHED_RANGES, keep = n <= SCHED_ITEMS;
+  if (staged)
+    for (int i = threadIdx.x; i < nr; i += blockDim.x) sr[i] = i < nqr ? p.qr[i] : p.kr[i - nqr];
   for (int i = threadIdx.x; i <= other; i += blockDim.x) hist[i] = 0;
   __syncthreads();
+  const Range* qbase = staged ? sr : p.qr;
+  const Range* kbase = staged ? sr + nqr : p.kr;
   auto weight = [&](int it) {
     const int t = it % per, b = it / per;
-    const Range* qrs = p.qr + (long long)b * p.nqb;
-    const Range* krs = p.kr + (long long)b * p.nkb;
+    const Range* qrs = qbase + (long long)b * p.nqb;
+    const Range* krs = kbase + (long long)b * p.nkb;
     int c = 0;
     if (backward) {
       const Range kr = range128(krs, p.nkb, t);
@@ -1338,7 +1355,11 @@ __global__ void __launch_bounds__(1024) schedule_kernel(Params p, int backward, 
     }
     return c;
   };
-  for (int it = threadIdx.x; it < n; it += blockDim.x) atomicAdd(&hist[weight(it)], 1);
+  for (int it = threadIdx.x; it < n; it += blockDim.x) {
+    const int w = weight(it);
+    if (keep) wt[it] = w;
+    atomicAdd(&hist[w], 1);
+  }
   __syncthreads();
   if (threadIdx.x == 0) {  // weights are tile counts, at most `other`
     int acc = 0;
@@ -1348,13 +1369,14 @@ __global__ void __launch_bounds__(1024) schedule_kernel(Params p, int backward, 
     }
   }
   __syncthreads();
-  for (int it = threadIdx.x; it < n; it += blockDim.x) order[atomicAdd(&base[weight(it)], 1)] = it;
+  for (int it = threadIdx.x; it < n; it += blockDim.x) order[atomicAdd(&base[keep ? wt[it] : weight(it)], 1)] = it;
 }
 
-int launch_ranges(const Params& p, const int* qid, const int* kid, cudaStream_t s) {
+int launch_ranges(const Params& p, const int* qid, const int* kid, cudaStream_t s, float* clear = nullptr,
+                  int clear_n = 0) {
   dim3 grid(max(p.nqb, p.nkb), p.B, 2);
   ranges_kernel<<<grid, 64, 0, s>>>(qid, kid, const_cast<Range*>(p.qr), const_cast<Range*>(p.kr), p.B, p.T, p.S,
-                                    p.nqb, p.nkb);
+                                    p.nqb, p.nkb, clear, clear_n);
   MFB_LAUNCH_CHECK("attention ranges");
   return MFB_OK;
 }
@@ -1489,8 +1511,7 @@ extern "C" int mfb_attn_bwd(const uint16_t* q, const uint16_t* k, const uint16_t
   p.qid = qid;
   p.kid = kid;
   cudaStream_t s = (cudaStream_t)stream;
-  if ((st = launch_ranges(p, qid, kid, s))) return st;
-  MFB_CUDA_TRY(cudaMemsetAsync(w.uvec, 0, sizeof(float) * (size_t)B * Hk * HD, s));
+  if ((st = launch_ranges(p, qid, kid, s, w.uvec, B * Hk * HD))) return st;
   const long long rows = (long long)B * T * H;
   attn_bwd_pre_kernel<<<(unsigned)((rows + 31) / 32), 256, 0, s>>>(p);
   MFB_LAUNCH_CHECK("attention backward preprocess");
