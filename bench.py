@@ -271,7 +271,7 @@ class AttentionWorkload:
         self.fwd()
         self.bwd()
 
-    launches_per_step = 9  # ids, ranges, schedule, fwd, ranges, schedule, bwd-pre, bwd-main, dq-convert
+    launches_per_step = 8  # ids, ranges, schedule, fwd, bwd-pre (with the ranges), schedule, bwd-main, dq-convert
 
     def capture_graphs(self):
         """Capture the step, the forward alone and the backward alone as CUDA graphs on a created
@@ -596,7 +596,7 @@ class EncoderStepWorkload:
                     "mfb_rmsnorm_bwd": 2, "mfb_gemm_bf16": 1, "mfb_conv_fwd": 1, "mfb_conv_bwd": 2,
                     "mfb_swiglu_fwd": 1, "mfb_swiglu_bwd": 1,
                     "mfb_gemm_swiglu_fwd": 1, "mfb_gemm_swiglu_bwd": 1, "mfb_qknorm_rope_fwd": 1, "mfb_qknorm_rope_bwd": 3,
-                    "mfb_attn_fwd": 3, "mfb_attn_bwd": 5, "mfb_head_loss": 3, "mfb_step_normalize": 1,
+                    "mfb_attn_fwd": 3, "mfb_attn_bwd": 4, "mfb_head_loss": 3, "mfb_step_normalize": 1,
                     "mfb_adamw_commit": 3, "mfb_adamw_shard_pass": 1}
         orig, count = _lib.call, [0]
 
@@ -838,7 +838,7 @@ def run_ours(args, dist):
         timer = Timer()
         fwd_ms = dist.max(timer.time(att.fwd, args.steps))
         bwd_ms = dist.max(timer.time(att.bwd, args.steps))
-        launches += 3 * args.steps + 5 * args.steps
+        launches += 3 * args.steps + 4 * args.steps
         roofline = attention_roofline(att, fwd_ms, bwd_ms, tf_burst, peak_kind, traffic)
         e2e = attention_e2e(att, dist, args.steps, n)
         line.update(value=value, ms_per_step=ms, tensor_peak_frac=value / n / tf_burst, roofline=roofline, e2e=e2e)
@@ -858,7 +858,7 @@ def run_ours(args, dist):
         ms1, _ = measure(dist, lambda: a1.replay("step"), args.steps, args.warmup, stream=a1.stream)
         f1, _ = measure(dist, lambda: a1.replay("fwd"), args.steps, 2, stream=a1.stream)
         b1, _ = measure(dist, lambda: a1.replay("bwd"), args.steps, 2, stream=a1.stream)
-        launches += (9 + 3 + 5) * args.steps
+        launches += (8 + 3 + 4) * args.steps
         a1.release_graphs()
         e2e1 = attention_e2e(a1, dist, args.steps, n)
         tflops1 = n * a1.total_flops / (ms1 * 1e-3) / 1e12

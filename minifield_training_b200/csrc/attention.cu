@@ -122,13 +122,9 @@ __global__ void ids_kernel(int mode, const int* __restrict__ mask, const int* __
   }
 }
 
-// Per-64-block id ranges for queries (z = 0) and keys (z = 1); the first CTA
-// also clears `clear_n` floats at `clear` (the backward's uniform-row
-// accumulator, which the pre-pass that follows adds into).
+// Per-64-block id ranges for queries (z = 0) and keys (z = 1).
 __global__ void ranges_kernel(const int* __restrict__ qid, const int* __restrict__ kid, Range* qr, Range* kr, int B,
-                              int T, int S, int nqb, int nkb, float* clear, int clear_n) {
-  if (clear && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
-    for (int i = threadIdx.x; i < clear_n; i += blockDim.x) clear[i] = 0.f;
+                              int T, int S, int nqb, int nkb) {
   const int which = blockIdx.z;
   const int n = which ? S : T;
   const int nb = which ? nkb : nqb;
@@ -169,7 +165,45 @@ __global__ void ranges_kernel(const int* __restrict__ qid, const int* __restrict
 
 // dsum[b,h,t] = sum_d dO * O; uniform-policy empty rows add dO/S to uvec[b,hk];
 // and the row's FP32 dQ accumulator is zeroed for the main kernel's reductions.
-__global__ void __launch_bounds__(256) attn_bwd_pre_kernel(Params p) {
+// Blocks from `npre` on compute the per-64 id ranges instead (four 64-id
+// blocks each, queries then keys: ranges_kernel's work), so that
+// latency-bound work overlaps the bandwidth-bound pre-pass.
+__global__ void __launch_bounds__(256) attn_bwd_pre_kernel(Params p, const int* __restrict__ qid,
+                                                           const int* __restrict__ kid, int npre) {
+  if (blockIdx.x >= npre) {
+    __shared__ int sl[8], sh[8], sz[8];
+    const int grp = threadIdx.x >> 6, half = (threadIdx.x >> 5) & 1;
+    const int nqr = p.B * p.nqb, nr = nqr + p.B * p.nkb;
+    const int rb = (blockIdx.x - npre) * 4 + grp;
+    const bool keys = rb >= nqr;
+    const int k = keys ? rb - nqr : rb, nb = keys ? p.nkb : p.nqb, n = keys ? p.S : p.T;
+    const int b = k / nb, blk = k % nb;
+    const int pos = blk * 64 + (threadIdx.x & 63);
+    const int v = (rb < nr && pos < n) ? (keys ? kid : qid)[(long long)b * n + pos] : 0;
+    int lo = v != 0 ? v : kIntMax;
+    int hi = v != 0 ? v : kIntMin;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+      hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    const int zero = __any_sync(0xffffffffu, v == 0) ? 1 : 0;
+    if ((threadIdx.x & 31) == 0) {
+      sl[2 * grp + half] = lo;
+      sh[2 * grp + half] = hi;
+      sz[2 * grp + half] = zero;
+    }
+    __syncthreads();
+    if ((threadIdx.x & 63) == 0 && rb < nr) {
+      Range r;
+      r.lo = min(sl[2 * grp], sl[2 * grp + 1]);
+      r.hi = max(sh[2 * grp], sh[2 * grp + 1]);
+      r.full = (!sz[2 * grp] && !sz[2 * grp + 1] && r.lo == r.hi) ? 1 : 0;
+      r.pad = 0;
+      const_cast<Range*>(keys ? p.kr : p.qr)[(long long)b * nb + blk] = r;
+    }
+    return;
+  }
   const long long row = (long long)blockIdx.x * 32 + (threadIdx.x >> 3);  // (b, t, h) flattened as bthd rows
   const int sub = threadIdx.x & 7;
   const long long nrows = (long long)p.B * p.T * p.H;
@@ -1372,11 +1406,10 @@ __global__ void __launch_bounds__(1024) schedule_kernel(Params p, int backward, 
   for (int it = threadIdx.x; it < n; it += blockDim.x) order[atomicAdd(&base[keep ? wt[it] : weight(it)], 1)] = it;
 }
 
-int launch_ranges(const Params& p, const int* qid, const int* kid, cudaStream_t s, float* clear = nullptr,
-                  int clear_n = 0) {
+int launch_ranges(const Params& p, const int* qid, const int* kid, cudaStream_t s) {
   dim3 grid(max(p.nqb, p.nkb), p.B, 2);
   ranges_kernel<<<grid, 64, 0, s>>>(qid, kid, const_cast<Range*>(p.qr), const_cast<Range*>(p.kr), p.B, p.T, p.S,
-                                    p.nqb, p.nkb, clear, clear_n);
+                                    p.nqb, p.nkb);
   MFB_LAUNCH_CHECK("attention ranges");
   return MFB_OK;
 }
@@ -1511,9 +1544,12 @@ extern "C" int mfb_attn_bwd(const uint16_t* q, const uint16_t* k, const uint16_t
   p.qid = qid;
   p.kid = kid;
   cudaStream_t s = (cudaStream_t)stream;
-  if ((st = launch_ranges(p, qid, kid, s, w.uvec, B * Hk * HD))) return st;
+  // The uniform-row accumulator is read and written only under the uniform
+  // empty-row policy.
+  if (empty_policy == MFB_EMPTY_UNIFORM) MFB_CUDA_TRY(cudaMemsetAsync(w.uvec, 0, sizeof(float) * (size_t)B * Hk * HD, s));
   const long long rows = (long long)B * T * H;
-  attn_bwd_pre_kernel<<<(unsigned)((rows + 31) / 32), 256, 0, s>>>(p);
+  const long long npre = (rows + 31) / 32, nranges = (long long)B * (p.nqb + p.nkb);
+  attn_bwd_pre_kernel<<<(unsigned)(npre + (nranges + 3) / 4), 256, 0, s>>>(p, qid, kid, (int)npre);
   MFB_LAUNCH_CHECK("attention backward preprocess");
   MFB_CHECK_ARG(T <= TF_MAX_TILES * TQ, "query length %d above the supported %d", T, TF_MAX_TILES * TQ);
   MFB_CHECK_ARG(((uintptr_t)q & 15) == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0 &&
