@@ -276,3 +276,28 @@ def test_rows_of_one_warp_that_rescale_differently():
     ids = oatt.bidirectional_ids(mask, None)
     out, grads = oracle_attention(q, k, v, ids, do)
     _check(r, out, grads, "divergent rescale")
+
+
+def test_wide_batch_matches_the_same_rows_in_smaller_calls():
+    """Rows are independent, so a batch split into smaller calls must give the same results.
+
+    24 rows of 4096 tokens make 3072 per-64 id-range records: more than the
+    work-order kernel stages in shared memory (1536), so it reads them from the
+    workspace; calls of 8 rows (1024 records) take the staged path. Each O, dK
+    and dV value comes from one CTA in a fixed order whatever the work order,
+    so those agree bit for bit; dQ is summed by reduce-adds in arrival order
+    and agrees to the gradient gate.
+    """
+    from minifield_training_b200 import workloads
+
+    b, t = 24, 4096
+    q, k, v, do = _qkvd(21, b, t, t, h=2, hk=1)
+    seg = workloads.packed_segments(23, b, t, lo=32, hi=1024)
+    mask = (seg != 0).astype(np.int32)
+    whole = gpu_attention(BIDIR, q, k, v, do, mask=mask, seg=seg)
+    for r0 in range(0, b, 8):
+        rows = slice(r0, r0 + 8)
+        part = gpu_attention(BIDIR, q[rows], k[rows], v[rows], do[rows], mask=mask[rows], seg=seg[rows])
+        for name in ("out", "dk", "dv"):
+            np.testing.assert_array_equal(whole[name][rows], part[name], err_msg=f"{name} rows {r0}-{r0 + 7}")
+        assert_close(whole["dq"][rows], part["dq"], scaled=True, what=f"dq rows {r0}-{r0 + 7}")
