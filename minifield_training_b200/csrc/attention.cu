@@ -702,7 +702,10 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     if (q0 + TQ <= p.T) {
       // Whole tile: rows into the head's Q buffer (every product that read it
       // has completed: o_full follows them) in the TMA tile layout, then one
-      // TMA store per head. All eight softmax warps reach the barrier.
+      // TMA store per head. All eight softmax warps reach the barrier. A tile
+      // without live key tiles issues no products, so nothing else has waited
+      // for the Q load that could still land on the staged rows: wait for it.
+      tc::mbar_wait(q_full, 0, status, 22);
       uint8_t* stage = smem + TF_Q_OFF + g * 16384;
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8)

@@ -301,3 +301,30 @@ def test_wide_batch_matches_the_same_rows_in_smaller_calls():
         for name in ("out", "dk", "dv"):
             np.testing.assert_array_equal(whole[name][rows], part[name], err_msg=f"{name} rows {r0}-{r0 + 7}")
         assert_close(whole["dq"][rows], part["dq"], scaled=True, what=f"dq rows {r0}-{r0 + 7}")
+
+
+def test_whole_query_tiles_without_live_keys():
+    """Whole 128-row query tiles with no valid key still write their rows.
+
+    Such a tile issues no products, and its rows take the empty-row policy:
+    zeros for the bidirectional operator (the second tile is all padding,
+    segment id 0) and
+    the uniform average over all keys for the causal one (batch row 1 masks
+    every key). Its O rows go through the same shared staging and TMA store as
+    any whole tile, after the tile's Q load has landed in that buffer.
+    """
+    t = 256
+    q, k, v, do = _qkvd(31, 2, t, t)
+    seg = np.zeros((2, t), np.int32)
+    seg[:, :100] = 1  # segment id 0 from token 100 on: padding queries with no valid key
+    mask = (seg != 0).astype(np.int32)
+    r = gpu_attention(BIDIR, q, k, v, do, mask=mask, seg=seg)
+    out, grads = oracle_attention(q, k, v, oatt.bidirectional_ids(mask, seg), do)
+    _check(r, out, grads, "bidirectional, padded second tile")
+    assert np.all(r["out"][:, 128:] == 0)
+
+    mask = np.ones((2, t), np.int32)
+    mask[1, :] = 0
+    r = gpu_attention(CAUSAL, q, k, v, do, mask=mask)
+    out, grads = oracle_attention(q, k, v, oatt.causal_ids(mask), do)
+    _check(r, out, grads, "causal, row without valid keys")
