@@ -278,29 +278,31 @@ def test_rows_of_one_warp_that_rescale_differently():
     _check(r, out, grads, "divergent rescale")
 
 
-def test_wide_batch_matches_the_same_rows_in_smaller_calls():
+@pytest.mark.parametrize("b, t, rows", [(24, 4096, 8), (520, 1024, 260)])
+def test_wide_batch_matches_the_same_rows_in_smaller_calls(b, t, rows):
     """Rows are independent, so a batch split into smaller calls must give the same results.
 
     24 rows of 4096 tokens make 3072 per-64 id-range records: more than the
     work-order kernel stages in shared memory (1536), so it reads them from the
-    workspace; calls of 8 rows (1024 records) take the staged path. Each O, dK
-    and dV value comes from one CTA in a fixed order whatever the work order,
-    so those agree bit for bit; dQ is summed by reduce-adds in arrival order
-    and agrees to the gradient gate.
+    workspace; calls of 8 rows (1024 records) take the staged path. 520 rows of
+    1024 tokens make 4160 work items per call: more than the kernel keeps
+    weights for (4096), so it computes each weight twice; calls of 260 rows
+    (2080 items) keep them. Each O, dK and dV value comes from one CTA in a
+    fixed order whatever the work order, so those agree bit for bit; dQ is
+    summed by reduce-adds in arrival order and agrees to the gradient gate.
     """
     from minifield_training_b200 import workloads
 
-    b, t = 24, 4096
     q, k, v, do = _qkvd(21, b, t, t, h=2, hk=1)
     seg = workloads.packed_segments(23, b, t, lo=32, hi=1024)
     mask = (seg != 0).astype(np.int32)
     whole = gpu_attention(BIDIR, q, k, v, do, mask=mask, seg=seg)
-    for r0 in range(0, b, 8):
-        rows = slice(r0, r0 + 8)
-        part = gpu_attention(BIDIR, q[rows], k[rows], v[rows], do[rows], mask=mask[rows], seg=seg[rows])
+    for r0 in range(0, b, rows):
+        sl = slice(r0, r0 + rows)
+        part = gpu_attention(BIDIR, q[sl], k[sl], v[sl], do[sl], mask=mask[sl], seg=seg[sl])
         for name in ("out", "dk", "dv"):
-            np.testing.assert_array_equal(whole[name][rows], part[name], err_msg=f"{name} rows {r0}-{r0 + 7}")
-        assert_close(whole["dq"][rows], part["dq"], scaled=True, what=f"dq rows {r0}-{r0 + 7}")
+            np.testing.assert_array_equal(whole[name][sl], part[name], err_msg=f"{name} rows {r0}-{r0 + rows - 1}")
+        assert_close(whole["dq"][sl], part["dq"], scaled=True, what=f"dq rows {r0}-{r0 + rows - 1}")
 
 
 def test_whole_query_tiles_without_live_keys():
