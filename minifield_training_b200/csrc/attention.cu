@@ -260,7 +260,8 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(const float* __restrict
 //
 // CTA = (128 query rows, the two query heads of one GQA pair, batch row).
 // Warp roles (320 threads):
-//   warp 0      TMA producer (lane 0): both Q tiles once, then K/V tiles
+//   warp 0      TMA producer: both Q tiles (thread 0, right after the barrier
+//               set-up, so the load overlaps the prologue), then K/V tiles
 //               through a 3-stage ring (128 keys x 64 dims, 128-byte swizzle);
 //               all lanes stage each key tile's ids and run table.
 //   warp 1      TMEM owner and MMA issuer (whole warp, one elected lane).
@@ -382,6 +383,10 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     }
     tc::mbar_init(done_bar, 1);
     tc::mbar_fence_init();
+    // Q does not depend on the live-tile list: its load overlaps the prologue.
+    tc::mbar_expect_tx(q_full, 2 * 16384);
+    tc::tma_load_2d(sb + TF_Q_OFF, &tq, h0 * 64, b * p.T + q0, q_full);
+    tc::tma_load_2d(sb + TF_Q_OFF + 16384, &tq, (h0 + 1) * 64, b * p.T + q0, q_full);
   }
   if (warp == 0) {
     // Live key tiles of this query tile, in order, with their "no mask" flag.
@@ -423,9 +428,6 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       tc::tma_prefetch_desc(&tq);
       tc::tma_prefetch_desc(&tk);
       tc::tma_prefetch_desc(&tv);
-      tc::mbar_expect_tx(q_full, 2 * 16384);
-      tc::tma_load_2d(sb + TF_Q_OFF, &tq, h0 * 64, b * p.T + q0, q_full);
-      tc::tma_load_2d(sb + TF_Q_OFF + 16384, &tq, (h0 + 1) * 64, b * p.T + q0, q_full);
     }
     for (int it = 0; it < ntiles; ++it) {
       const int j = list[1 + it] & 0xFFFF;
@@ -741,9 +743,10 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 // heads x live 128-row query tiles ("items"), each split into two 64-query
 // sub-items so the tensor core works on one sub-item while the
 // softmax-gradient warps work on the other. Warp roles (704 threads):
-//   warp 0      producer: K and V once; per item the Q and dO tiles (TMA, three
-//               stages) and the per-query lse, dsum and query id (loaded one
-//               item ahead).
+//   warp 0      producer: K and V once (thread 0, right after the barrier
+//               set-up, so the load overlaps the prologue); per item the Q and
+//               dO tiles (TMA, three stages) and the per-query lse, dsum and
+//               query id (loaded one item ahead).
 //   warp 1      TMEM owner and MMA issuer (whole warp, one elected lane).
 //   warps 2-17  softmax-gradient, two groups of eight taking alternate
 //               sub-items (half 0 / half 1 of every item): one key row (TMEM
@@ -883,6 +886,10 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
     tc::mbar_init(done_bar, 1);
     tc::mbar_init(kv_tm, 32 * TB_SM_WARPS);
     tc::mbar_fence_init();
+    // K and V do not depend on the item list: their load overlaps the prologue.
+    tc::mbar_expect_tx(kv_full, 2 * 16384);
+    tc::tma_load_2d(sb + TB_K_OFF, &tk, hk * 64, b * p.S + s0, kv_full);
+    tc::tma_load_2d(sb + TB_V_OFF, &tv, hk * 64, b * p.S + s0, kv_full);
   }
   if (warp == 0) {
     int count = 0;
@@ -916,9 +923,6 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       tc::tma_prefetch_desc(&tk);
       tc::tma_prefetch_desc(&tv);
       tc::tma_prefetch_desc(&tdo);
-      tc::mbar_expect_tx(kv_full, 2 * 16384);
-      tc::tma_load_2d(sb + TB_K_OFF, &tk, hk * 64, b * p.S + s0, kv_full);
-      tc::tma_load_2d(sb + TB_V_OFF, &tv, hk * 64, b * p.S + s0, kv_full);
     }
     // Column data (lse, dsum, query id) of an item, loaded one item ahead so
     // that the global-load latency overlaps the wait for a free stage.
