@@ -719,7 +719,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         tc::tma_store_2d(&to, sb + TF_Q_OFF, h0 * 64, b * p.T + q0);
         tc::tma_store_2d(&to, sb + TF_Q_OFF + 16384, (h0 + 1) * 64, b * p.T + q0);
         tc::bulk_commit_group();
-        tc::bulk_wait_group0();
+        tc::bulk_wait_group_read0();  // the staging must outlive the reads; the writes complete with the grid
       }
     } else if (t < p.T) {
       __nv_bfloat16* orow = p.o + (((long long)b * p.T + t) * p.H + h) * HD;
@@ -1219,7 +1219,7 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
         tc::tma_store_2d(&tdk, sb + TB_QD_OFF, hk * 64, b * p.S + s0);
         tc::tma_store_2d(&tdv, sb + TB_QD_OFF + 16384, hk * 64, b * p.S + s0);
         tc::bulk_commit_group();
-        tc::bulk_wait_group0();
+        tc::bulk_wait_group_read0();  // the staging must outlive the reads; the writes complete with the grid
       }
     } else if (go && s < p.S) {
       const long long off = (((long long)b * p.S + s) * p.Hk + hk) * HD + wq * TB_CW;
