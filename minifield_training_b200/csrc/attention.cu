@@ -745,8 +745,9 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 // softmax-gradient warps work on the other. Warp roles (704 threads):
 //   warp 0      producer: K and V once (thread 0, right after the barrier
 //               set-up, so the load overlaps the prologue); per item the Q and
-//               dO tiles (TMA, three stages) and the per-query lse, dsum and
-//               query id (loaded one item ahead).
+//               dO tiles (TMA, three stages; item 0's as soon as the warp has
+//               built the item list) and the per-query lse, dsum and query id
+//               (loaded one item ahead).
 //   warp 1      TMEM owner and MMA issuer (whole warp, one elected lane).
 //   warps 2-17  softmax-gradient, two groups of eight taking alternate
 //               sub-items (half 0 / half 1 of every item): one key row (TMEM
@@ -906,6 +907,13 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       count += __popc(bal);
     }
     if (lane == 0) list[0] = count;
+    __syncwarp();
+    if (lane == 0 && count > 0) {  // item 0's Q and dO: the load overlaps the rest of the prologue
+      const int q0 = (list[1] & 0xFFFF) * TQ;
+      tc::mbar_expect_tx(qd_full(0), 2 * 16384);
+      tc::tma_load_2d(sb + TB_QD_OFF, &tq, (hk * p.G) * 64, b * p.T + q0, qd_full(0));
+      tc::tma_load_2d(sb + TB_QD_OFF + 16384, &tdo, (hk * p.G) * 64, b * p.T + q0, qd_full(0));
+    }
   } else if (warp == 1) {
     tc::tmem_alloc(smem_u32(tmem_slot), 512);
     tc::tmem_relinquish();
@@ -951,7 +959,7 @@ __global__ void __launch_bounds__(TB_THREADS, 1)
       const int entry = list[1 + it % nlive];
       const int q0 = (entry & 0xFFFF) * TQ;
       if (!tc::mbar_wait(qd_empty(st), ph ^ 1, status, 31)) break;
-      if (lane == 0) {
+      if (lane == 0 && it > 0) {  // item 0's tiles were requested before the prologue barrier
         const uint32_t qb_ = sb + TB_QD_OFF + st * 32768;
         tc::mbar_expect_tx(qd_full(st), 2 * 16384);
         tc::tma_load_2d(qb_, &tq, h * 64, b * p.T + q0, qd_full(st));
